@@ -1,0 +1,240 @@
+#!/usr/bin/env python3
+"""Generate the golden vectors in this folder from the REFERENCE itself.
+
+Run once in a container that has the reference checkout (the GPU box does not):
+
+    make -C oracle ref REF=<reference checkout>
+    python tests/golden/make_golden.py --reference <reference checkout>
+
+Inputs are seeded; codes come from the reference's own NF24 packer
+(scripts/native_linear_rnf8_avx512_patch.py:75-87, imported from the checkout)
+and every output from the reference's own AVX-512 kernels compiled into
+oracle/_ref.  The fixtures pin (a) the oracle restatement in oracle/oracle.c,
+(b) this repository's packer and (c) the CUDA kernels, all without needing the
+reference at test time.  Case shapes follow the reference's smoke tests
+(scripts/smoke_native_rnf8_avx512.py:21-80 and
+scripts/bench_native_sdpa_avx512_exact.py:146-161) with small head counts so the
+fixtures stay a few hundred KB.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+REF_LIBS = REPO / "oracle" / "_ref"
+
+VP, I, I64, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
+
+
+def ptr(a):
+    return None if a is None else a.ctypes.data_as(VP)
+
+
+def bind(lib, name, args):
+    fn = getattr(lib, name)
+    fn.argtypes = args
+    fn.restype = I
+    return fn
+
+
+def check(status, name):
+    if status != 0:
+        raise RuntimeError(f"{name} -> {status}")
+
+
+def gemm_cases(torch, pack, codebook, gemm_lib):
+    full = bind(gemm_lib, "triposplat_gemm_rnf8_avx512", [VP] * 10 + [I] * 7)
+    tail = bind(gemm_lib, "triposplat_gemm_rnf8_avx512_tail", [VP] * 10 + [I] * 7)
+    rng = bind(gemm_lib, "triposplat_gemm_rnf8_avx512_range", [VP] * 10 + [I] * 9)
+    cases = {
+        # (M, K, N, start, count); seeds follow the reference smoke (19 + stages + n)
+        "gemm_25x96x64": (25, 96, 64, 0, None),
+        "gemm_40x96x64": (40, 96, 64, 0, None),
+        "gemm_10x96x64": (10, 96, 64, 0, None),
+        "gemm_3x96x5_tail": (3, 96, 5, 0, None),
+        "gemm_7x100x7_tail": (7, 100, 7, 0, None),
+        "gemm_33x160x96_range32_48": (33, 160, 96, 32, 48),
+        "gemm_130x256x144": (130, 256, 144, 0, None),
+    }
+    for name, (m, k, n, start, count) in cases.items():
+        torch.manual_seed(19 + 3 + n + m)
+        x = torch.randn(m, k, dtype=torch.float32)
+        w = torch.randn(n, k, dtype=torch.float32) * 0.03
+        b = torch.randn(n, dtype=torch.float32) * 0.01
+        codes, scales, _ = pack(w, codebook)
+        c01 = codes[0].numpy()
+        q2 = codes[1].numpy()
+        sc = scales[0].numpy()
+        xn, bn = x.numpy(), b.numpy()
+        cb = codebook.numpy()
+        if count is None:
+            out = np.empty((m, n), np.float32)
+            fn = tail if n % 16 else full
+            check(fn(ptr(xn), ptr(c01), ptr(q2), ptr(q2), ptr(sc), ptr(sc), ptr(sc), ptr(cb),
+                     ptr(bn), ptr(out), m, k, n, k, n, 2, 3), name)
+        else:
+            out = np.empty((m, count), np.float32)
+            check(rng(ptr(xn), ptr(c01), ptr(q2), ptr(q2), ptr(sc), ptr(sc), ptr(sc), ptr(cb),
+                      ptr(bn), ptr(out), m, k, n, start, count, k, count, 2, 3), name)
+        np.savez_compressed(HERE / f"{name}.npz", x=xn, w=w.numpy(), bias=bn, code01_t=c01,
+                            q2_t=q2, scale=sc, out=out, start=start,
+                            count=-1 if count is None else count)
+
+
+def sdpa_cases(torch, sdpa_lib, packed_lib):
+    fn = bind(sdpa_lib, "triposplat_sdpa_f32_avx512_exact_q8t512", [VP] * 5 + [I] * 8)
+    pk_fn = bind(packed_lib, "triposplat_sdpa_f32_avx512_exact_q8t512_packed_blhd",
+                 [VP] * 5 + [I] * 9)
+    cases = {
+        # name: (B, H, Lq, Lk, bias spec)
+        "sdpa_self256": (1, 2, 256, 256, None),
+        "sdpa_masked256": (1, 2, 256, 256, ("onehot", 7, 2.0)),
+        "sdpa_cross193x256": (1, 2, 193, 256, None),
+        "sdpa_cross5x17_bias": (2, 2, 5, 17, ("randn",)),
+        "sdpa_q3_k1": (1, 3, 3, 1, None),
+        "sdpa_q70_k700_bias": (1, 2, 70, 700, ("randn",)),
+    }
+    gen = torch.Generator(device="cpu").manual_seed(0)
+    for name, (B, H, lq, lk, bspec) in cases.items():
+        q = torch.randn((B, H, lq, 64), generator=gen).numpy()
+        k = torch.randn((B, H, lk, 64), generator=gen).numpy()
+        v = torch.randn((B, H, lk, 64), generator=gen).numpy()
+        bias = None
+        if bspec is not None:
+            if bspec[0] == "onehot":
+                bias = np.zeros(lk, np.float32)
+                bias[bspec[1]] = bspec[2]
+            else:
+                bias = torch.randn((lk,), generator=gen).numpy()
+        out = np.empty((B, H, lq, 64), np.float32)
+        check(fn(ptr(q), ptr(k), ptr(v), ptr(bias), ptr(out), B, H, lq, lk, 64,
+                 int(bias is not None), 0 if bias is None else lk, 2), name)
+        lkp = (lk + 15) // 16 * 16
+        packk = np.zeros((B, H, 64, lkp), np.float32)
+        packv = np.zeros((B, H, 64, lkp), np.float32)
+        packk[..., :lk] = k.transpose(0, 1, 3, 2)
+        packv[..., :lk] = v.transpose(0, 1, 3, 2)
+        out_blhd = np.empty((B, lq, H, 64), np.float32)
+        check(pk_fn(ptr(q), ptr(packk), ptr(packv), ptr(bias), ptr(out_blhd), B, H, lq, lk, 64,
+                    lkp, int(bias is not None), 0 if bias is None else lk, 2), name + "_packed")
+        extra = {} if bias is None else {"bias": bias}
+        np.savez_compressed(HERE / f"{name}.npz", q=q, k=k, v=v, out=out, out_blhd=out_blhd,
+                            **extra)
+
+
+def elementwise_cases(torch):
+    nr = __import__("ctypes").CDLL(str(REF_LIBS / "libref_norm_rope.so"))
+    act = ctypes.CDLL(str(REF_LIBS / "libref_activations.so"))
+    blk = ctypes.CDLL(str(REF_LIBS / "libref_block_elementwise.so"))
+    smp = ctypes.CDLL(str(REF_LIBS / "libref_sampler.so"))
+    qkv = ctypes.CDLL(str(REF_LIBS / "libref_qkv_postprocess_v2.so"))
+    ln = bind(nr, "triposplat_layernorm_f32_avx512", [VP] * 4 + [I64, I, F, I, I])
+    rms = bind(nr, "triposplat_multihead_rmsnorm_f32_avx512", [VP] * 3 + [I64, I, I, F, I])
+    rope = bind(nr, "triposplat_rope_complex_f32_avx512", [VP] * 3 + [I64, I, I])
+    gelu = bind(act, "triposplat_gelu_tanh_f32_avx512", [VP] * 2 + [I64, I])
+    silu = bind(act, "triposplat_silu_f32_avx512", [VP] * 2 + [I64, I])
+    mod = bind(blk, "triposplat_modulate_inplace_f32_avx512", [VP] * 3 + [I] * 4)
+    gres = bind(blk, "triposplat_gated_residual_inplace_f32_avx512", [VP] * 3 + [I] * 4)
+    add = bind(blk, "triposplat_add_inplace_f32_avx512", [VP] * 2 + [I64, I])
+    cfg = bind(smp, "triposplat_cfg_combine_inplace_f32_avx512", [VP] * 3 + [I, I64, I])
+    eul = bind(smp, "triposplat_euler_update_inplace_f32_avx512", [VP] * 3 + [I, I64, I])
+    post = bind(qkv, "triposplat_qkv_rope_rmsnorm_pack_f32_avx512_v2", [VP] * 7 + [I] * 7)
+    g = torch.Generator(device="cpu").manual_seed(1)
+
+    def rn(*shape, s=1.0):
+        return (torch.randn(shape, generator=g) * s).numpy().astype(np.float32)
+
+    data = {}
+    x = rn(5, 1000)
+    w, b = 1.0 + rn(1000, s=0.02), rn(1000, s=0.1)
+    out = np.empty_like(x)
+    check(ln(ptr(x), ptr(w), ptr(b), ptr(out), 5, 1000, 1e-6, 1, 2), "ln")
+    out2 = np.empty_like(x)
+    check(ln(ptr(x), None, None, ptr(out2), 5, 1000, 1e-5, 0, 2), "ln_noaff")
+    data.update(ln_x=x, ln_w=w, ln_b=b, ln_out=out, ln_out_noaffine=out2)
+
+    x = rn(3, 7, 4, 64)
+    gam = 1.0 + rn(4, 64, s=0.1)
+    out = np.empty_like(x)
+    check(rms(ptr(x), ptr(gam), ptr(out), 21, 4, 64, 1e-12, 2), "rms")
+    data.update(rms_x=x, rms_gamma=gam, rms_out=out)
+
+    x, f = rn(6, 64), rn(6, 64)
+    out = np.empty_like(x)
+    check(rope(ptr(x), ptr(f), ptr(out), 6, 64, 2), "rope")
+    data.update(rope_x=x, rope_f=f, rope_out=out)
+
+    x = np.concatenate([rn(997, s=3.0), np.array([0.0, -12.0, 12.0], np.float32)])
+    out = np.empty_like(x)
+    check(gelu(ptr(x), ptr(out), x.size, 2), "gelu")
+    out_s = np.empty_like(x)
+    check(silu(ptr(x), ptr(out_s), x.size, 2), "silu")
+    data.update(act_x=x, gelu_out=out, silu_out=out_s)
+
+    h, sc, sh = rn(2, 9, 48), rn(2, 48, s=0.2), rn(2, 48, s=0.2)
+    hm = h.copy()
+    check(mod(ptr(hm), ptr(sc), ptr(sh), 2, 9, 48, 2), "mod")
+    base, delta, gate = rn(2, 9, 48), rn(2, 9, 48), rn(2, 48)
+    bo, do = base.copy(), delta.copy()
+    check(gres(ptr(bo), ptr(do), ptr(gate), 2, 9, 48, 2), "gres")
+    ao = base.copy()
+    check(add(ptr(ao), ptr(delta), ao.size, 2), "add")
+    data.update(mod_h=h, mod_scale=sc, mod_shift=sh, mod_out=hm, gres_base=base,
+                gres_delta=delta, gres_gate=gate, gres_base_out=bo, gres_delta_out=do,
+                add_out=ao)
+
+    pos, neg = rn(2, 333), rn(2, 333)
+    guid = np.array([3.0, 1.5], np.float32)
+    po = pos.copy()
+    check(cfg(ptr(po), ptr(neg), ptr(guid), 2, 333, 2), "cfg")
+    dt = np.array([0.05, 0.1], np.float32)
+    so = pos.copy()
+    check(eul(ptr(so), ptr(neg), ptr(dt), 2, 333, 2), "euler")
+    data.update(cfg_pos=pos, cfg_neg=neg, cfg_g=guid, cfg_out=po, euler_dt=dt, euler_out=so)
+
+    B, L, H, D, Lp = 2, 19, 2, 64, 32
+    qkv_in = rn(B, L, 3, H, D)
+    ang = rn(1, L, H, D // 2)
+    freqs = np.stack([np.cos(ang), np.sin(ang)], -1).reshape(1, L, H, D).astype(np.float32)
+    qg, kg = 1.0 + rn(H, D, s=0.1), 1.0 + rn(H, D, s=0.1)
+    qo = np.empty((B, H, L, D), np.float32)
+    pk = np.full((B, H, D, Lp), 7.0, np.float32)
+    pv = np.full((B, H, D, Lp), 7.0, np.float32)
+    check(post(ptr(qkv_in), ptr(freqs), ptr(qg), ptr(kg), ptr(qo), ptr(pk), ptr(pv),
+               B, L, H, D, Lp, 1, 2), "qkv_post")
+    data.update(post_qkv=qkv_in, post_freqs=freqs, post_qg=qg, post_kg=kg, post_q=qo,
+                post_pk=pk, post_pv=pv)
+    np.savez_compressed(HERE / "elementwise.npz", **data)
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True, type=Path)
+    args = ap.parse_args()
+    sys.path.insert(0, str(args.reference / "scripts"))
+    import torch
+    from native_linear_nf8_avx512_patch import make_nf8_codebook  # reference packer
+    from native_linear_rnf8_avx512_patch import quantize_nf24_i16_per_output_channel
+
+    def pack(w, cb):
+        codes, scales, err = quantize_nf24_i16_per_output_channel(w, cb)
+        return [codes[0], codes[1]], scales, err
+
+    codebook = make_nf8_codebook(torch)
+    np.save(HERE / "nf8_codebook.npy", codebook.numpy())
+    gemm_cases(torch, pack, codebook, ctypes.CDLL(str(REF_LIBS / "libref_gemm_nf24_i16.so")))
+    sdpa_cases(torch, ctypes.CDLL(str(REF_LIBS / "libref_sdpa_q8t512.so")),
+               ctypes.CDLL(str(REF_LIBS / "libref_sdpa_q8t512_packed.so")))
+    elementwise_cases(torch)
+    print("golden fixtures written to", HERE)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,61 @@
+"""Pin the CPU oracle (oracle/oracle.c) to golden vectors made by the reference's
+own AVX-512 kernels (tests/golden/make_golden.py)."""
+import numpy as np
+import pytest
+
+GEMM_CASES = ["gemm_25x96x64", "gemm_40x96x64", "gemm_10x96x64", "gemm_3x96x5_tail",
+              "gemm_7x100x7_tail", "gemm_33x160x96_range32_48", "gemm_130x256x144"]
+SDPA_CASES = ["sdpa_self256", "sdpa_masked256", "sdpa_cross193x256", "sdpa_cross5x17_bias",
+              "sdpa_q3_k1", "sdpa_q70_k700_bias"]
+
+
+@pytest.mark.parametrize("case", GEMM_CASES)
+def test_gemm_oracle_bit_exact(oracle, golden, case):
+    g = golden(case)
+    count = int(g["count"])
+    out = oracle.gemm_nf24(g["x"], g["code01_t"], g["q2_t"], g["scale"], g["bias"],
+                           start=int(g["start"]), count=None if count < 0 else count)
+    # same decode and the same in-order fmaf chain as the reference: bit-identical
+    np.testing.assert_array_equal(out, g["out"])
+
+
+@pytest.mark.parametrize("case", SDPA_CASES)
+def test_sdpa_oracle_matches_reference(oracle, golden, case):
+    g = golden(case)
+    out = oracle.sdpa(g["q"], g["k"], g["v"], bias=g.get("bias"))
+    # expf vs the reference's polynomial exp and a different reduction order
+    np.testing.assert_allclose(out, g["out"], rtol=0, atol=2e-6)
+    assert np.sqrt(np.mean((out - g["out"]) ** 2)) < 2e-7
+    blhd = oracle.sdpa(g["q"], g["k"], g["v"], bias=g.get("bias"), out_blhd=True)
+    np.testing.assert_allclose(blhd, g["out_blhd"], rtol=0, atol=2e-6)
+
+
+def test_elementwise_oracle(oracle, golden):
+    g = golden("elementwise")
+    tol = dict(rtol=2e-6, atol=2e-6)
+    np.testing.assert_allclose(oracle.layernorm(g["ln_x"], g["ln_w"], g["ln_b"], 1e-6), g["ln_out"], **tol)
+    np.testing.assert_allclose(oracle.layernorm(g["ln_x"], eps=1e-5), g["ln_out_noaffine"], **tol)
+    np.testing.assert_allclose(oracle.multihead_rmsnorm(g["rms_x"], g["rms_gamma"]), g["rms_out"], **tol)
+    np.testing.assert_allclose(oracle.rope_complex(g["rope_x"], g["rope_f"]), g["rope_out"], **tol)
+    np.testing.assert_allclose(oracle.gelu_tanh(g["act_x"]), g["gelu_out"], **tol)
+    np.testing.assert_allclose(oracle.silu(g["act_x"]), g["silu_out"], **tol)
+    np.testing.assert_allclose(oracle.modulate(g["mod_h"], g["mod_scale"], g["mod_shift"]), g["mod_out"], **tol)
+    b, d = oracle.gated_residual(g["gres_base"], g["gres_delta"], g["gres_gate"])
+    np.testing.assert_allclose(b, g["gres_base_out"], **tol)
+    np.testing.assert_allclose(d, g["gres_delta_out"], **tol)
+    np.testing.assert_allclose(oracle.add(g["gres_base"], g["gres_delta"]), g["add_out"], **tol)
+    np.testing.assert_allclose(oracle.cfg_combine(g["cfg_pos"], g["cfg_neg"], g["cfg_g"]), g["cfg_out"], **tol)
+    np.testing.assert_allclose(oracle.euler_update(g["cfg_pos"], g["cfg_neg"], g["euler_dt"]), g["euler_out"], **tol)
+    q, pk, pv = oracle.qkv_rope_rmsnorm_pack(g["post_qkv"], g["post_freqs"], g["post_qg"], g["post_kg"], Lp=32)
+    np.testing.assert_allclose(q, g["post_q"], **tol)
+    np.testing.assert_allclose(pk, g["post_pk"], **tol)
+    np.testing.assert_array_equal(pv, g["post_pv"])
+
+
+def test_oracle_error_codes(oracle):
+    x = np.zeros((2, 4), np.float32)
+    c = np.zeros((4, 16), np.int16)
+    q = np.zeros((4, 16), np.int8)
+    s = np.zeros(16, np.float32)
+    with pytest.raises(RuntimeError):
+        oracle.gemm_nf24(x, c, q, s, s, start=8, count=16)  # range overflow -> -3
