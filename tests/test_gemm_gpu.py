@@ -1,0 +1,130 @@
+"""NF24 GEMM parity: CUDA (through the C-ABI) vs the oracle / reference golden vectors.
+
+Tolerance (fp32 semantics, split-precision tensor cores): max |y - y_ref| <= 2e-5 + 2e-5*|y_ref|,
+the reference smoke test's own rtol = atol = 2e-5 (scripts/smoke_native_rnf8_avx512.py:58).
+The scalar tail path reproduces the reference's operation order and must be bit-identical.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+RTOL = ATOL = 2e-5
+
+
+def _cuda(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def _pack(torch_w):
+    from nf24_pack import quantize_nf24_i16_per_output_channel
+
+    codes, scales, _ = quantize_nf24_i16_per_output_channel(torch_w)
+    return codes[0].numpy(), codes[1].numpy(), scales[0].numpy()
+
+
+def _run(x, c01, q2, sc, bias, start=0, count=None):
+    from nf24_linear import nf24_linear
+
+    y = nf24_linear(_cuda(x), _cuda(c01), _cuda(q2), _cuda(sc), _cuda(bias), start=start, count=count)
+    torch.cuda.synchronize()
+    return y.cpu().numpy()
+
+
+def _assert_close(y, ref):
+    err = np.abs(y - ref)
+    bound = ATOL + RTOL * np.abs(ref)
+    assert np.isfinite(y).all()
+    assert (err <= bound).all(), f"max err {err.max():.3e} (worst ratio {(err / bound).max():.2f})"
+
+
+@pytest.mark.parametrize("case", ["gemm_25x96x64", "gemm_40x96x64", "gemm_10x96x64",
+                                  "gemm_3x96x5_tail", "gemm_7x100x7_tail",
+                                  "gemm_33x160x96_range32_48", "gemm_130x256x144"])
+def test_gemm_golden(golden, case):
+    g = golden(case)
+    count = int(g["count"])
+    y = _run(g["x"], g["code01_t"], g["q2_t"], g["scale"], g["bias"], start=int(g["start"]),
+             count=None if count < 0 else count)
+    if g["code01_t"].shape[1] % 16:
+        np.testing.assert_array_equal(y, g["out"])  # reference-order scalar kernel
+    else:
+        _assert_close(y, g["out"])
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 1024, 1024), (3, 64, 16), (257, 1000, 3072),
+                                   (300, 4096, 1024), (513, 1024, 4096), (64, 1024, 6144),
+                                   (2, 1024, 6144)])
+def test_gemm_vs_oracle(oracle, M, K, N):
+    g = torch.Generator().manual_seed(M * 7 + N)
+    x = torch.randn(M, K, generator=g).numpy()
+    w = torch.randn(N, K, generator=g) * 0.02
+    b = (torch.randn(N, generator=g) * 0.01).numpy()
+    c01, q2, sc = _pack(w)
+    ref = oracle.gemm_nf24(x, c01, q2, sc, b)
+    _assert_close(_run(x, c01, q2, sc, b), ref)
+
+
+def test_gemm_range_windows(oracle):
+    g = torch.Generator().manual_seed(5)
+    M, K, N = 200, 1024, 3072
+    x = torch.randn(M, K, generator=g).numpy()
+    c01, q2, sc = _pack(torch.randn(N, K, generator=g) * 0.02)
+    b = (torch.randn(N, generator=g) * 0.01).numpy()
+    for start, count in ((0, 1024), (1024, 1024), (2048, 1024), (16, 48), (3056, 16)):
+        ref = oracle.gemm_nf24(x, c01, q2, sc, b, start=start, count=count)
+        _assert_close(_run(x, c01, q2, sc, b, start=start, count=count), ref)
+
+
+def test_gemm_row_scale_extremes(oracle):
+    """Rows of very different magnitude exercise the per-row pre-scale of the split."""
+    g = torch.Generator().manual_seed(9)
+    M, K, N = 64, 512, 256
+    x = torch.randn(M, K, generator=g)
+    mags = torch.tensor([10.0 ** e for e in range(-8, 8)]).repeat(4)
+    x = (x * mags[:, None]).numpy()
+    x[5, :] = 0.0
+    c01, q2, sc = _pack(torch.randn(N, K, generator=g) * 0.02)
+    b = np.zeros(N, np.float32)
+    ref = oracle.gemm_nf24(x, c01, q2, sc, b)
+    y = _run(x, c01, q2, sc, b)
+    scale = np.abs(x).max(axis=1, keepdims=True) * 0.02 * np.sqrt(K) + 1e-30
+    assert (np.abs(y - ref) / scale).max() < 2e-6
+    assert (y[5] == 0).all()
+
+
+def test_gemm_full_config1_vs_oracle(oracle):
+    """BASELINE config 1 at full size: M=4096, K=1024, N=3072."""
+    g = torch.Generator().manual_seed(0)
+    M, K, N = 4096, 1024, 3072
+    x = torch.randn(M, K, generator=g).numpy()
+    c01, q2, sc = _pack(torch.randn(N, K, generator=g) * 0.02)
+    b = (torch.randn(N, generator=g) * 0.01).numpy()
+    ref = oracle.gemm_nf24(x, c01, q2, sc, b)
+    y = _run(x, c01, q2, sc, b)
+    _assert_close(y, ref)
+    assert float(np.sqrt(np.mean((y - ref) ** 2))) < 1e-6
+
+
+def test_gemm_error_codes():
+    import _native
+
+    lib = _native.load()
+    dev = torch.zeros(4096, device="cuda")
+    p = dev.data_ptr()
+    f = lib.triposplat_gemm_rnf8_avx512
+    fr = lib.triposplat_gemm_rnf8_avx512_range
+    assert f(None, p, p, p, p, p, p, p, p, p, 2, 16, 16, 16, 16, 0, 3) == -1
+    assert f(p, p, p, p, p, p, p, p, p, p, 0, 16, 16, 16, 16, 0, 3) == -2
+    assert f(p, p, p, p, p, p, p, p, p, p, 2, 16, 16, 16, 16, 0, 2) == -2
+    assert f(p, p, p, p, p, p, p, p, p, p, 2, 16, 16, 8, 16, 0, 3) == -3
+    assert fr(p, p, p, p, p, p, p, p, p, p, 2, 16, 64, 48, 32, 16, 32, 0, 3) == -3
+    assert fr(p, p, p, p, p, p, p, p, p, p, 2, 16, 64, 8, 16, 16, 16, 0, 3) == -4
+    host = np.zeros(4096, np.float32)
+    hp = host.ctypes.data
+    assert f(hp, p, p, p, p, p, p, p, p, p, 2, 16, 16, 16, 16, 0, 3) == -9
+    assert lib.triposplat_gemm_rnf8_avx512_residual_mode() == 4
+    assert lib.triposplat_b200_status() == 0

@@ -1,0 +1,98 @@
+"""Loader and thin ctypes bindings for ``libtriposplat_b200.so``.
+
+The library is the product: every hot-path call in this package goes through it.
+There is no CPU or PyTorch fallback — if the library is missing or no CUDA
+device is present, ``load()`` raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from functools import lru_cache
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+DEFAULT_LIBRARY = HERE / "libtriposplat_b200.so"
+
+VP = ctypes.c_void_p
+I = ctypes.c_int
+I64 = ctypes.c_int64
+F = ctypes.c_float
+U64P = ctypes.POINTER(ctypes.c_uint64)
+
+# name -> (argtypes, restype); mirrors include/triposplat_b200.h
+SIGNATURES: dict[str, tuple[list, object]] = {
+    # runtime
+    "triposplat_b200_set_stream": ([VP], None),
+    "triposplat_b200_get_stream": ([], VP),
+    "triposplat_b200_status": ([], I),
+    "triposplat_b200_clear_status": ([], None),
+    "triposplat_b200_workspace_reserve": ([ctypes.c_uint64], I),
+    "triposplat_b200_workspace_stats": ([U64P, U64P], I),
+    "triposplat_b200_workspace_release": ([], None),
+    "triposplat_b200_abi_version": ([], I),
+    # NF24 GEMM
+    "triposplat_gemm_rnf8_avx512": ([VP] * 10 + [I] * 7, I),
+    "triposplat_gemm_rnf8_avx512_range": ([VP] * 10 + [I] * 9, I),
+    "triposplat_gemm_rnf8_avx512_tail": ([VP] * 10 + [I] * 7, I),
+    "triposplat_gemm_rnf8_avx512_row_tile": ([], I),
+    "triposplat_gemm_rnf8_avx512_residual_mode": ([], I),
+}
+
+
+def library_path(path: str | os.PathLike | None = None) -> Path:
+    p = Path(path or os.environ.get("TRIPOSPLAT_B200_LIBRARY", DEFAULT_LIBRARY))
+    return p.resolve()
+
+
+@lru_cache(maxsize=4)
+def _load(path: str) -> ctypes.CDLL:
+    if not Path(path).is_file():
+        raise FileNotFoundError(
+            f"{path} is missing: build it with `python triposplat-cpu-avx512_b200/build_lib.py`")
+    lib = ctypes.CDLL(path)
+    for name, (args, res) in SIGNATURES.items():
+        fn = getattr(lib, name, None)
+        if fn is None:
+            continue
+        fn.argtypes = args
+        fn.restype = res
+    return lib
+
+
+def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
+    return _load(str(library_path(path)))
+
+
+def bind(lib: ctypes.CDLL, name: str, args, res=I):
+    fn = getattr(lib, name)
+    fn.argtypes = args
+    fn.restype = res
+    return fn
+
+
+def use_current_stream(lib: ctypes.CDLL) -> None:
+    """Queue the library's next launches on PyTorch's current CUDA stream."""
+    import torch
+
+    lib.triposplat_b200_set_stream(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+
+
+def check_status(lib: ctypes.CDLL) -> None:
+    st = int(lib.triposplat_b200_status())
+    if st != 0:
+        raise RuntimeError(f"a CUDA kernel of libtriposplat_b200 gave up on a wait (device status {st})")
+
+
+def require_cuda(*tensors, what: str = "tensor") -> None:
+    import torch
+
+    for t in tensors:
+        if t is None:
+            continue
+        if t.device.type != "cuda":
+            raise ValueError(f"{what} must be a CUDA tensor, got {t.device}")
+        if not t.is_contiguous():
+            raise ValueError(f"{what} must be contiguous")
+    if not torch.cuda.is_available():
+        raise RuntimeError("no CUDA device")

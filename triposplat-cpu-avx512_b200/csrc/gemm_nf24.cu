@@ -1,0 +1,491 @@
+// NF24 int16 dequant GEMM for sm_100a:  Y[M, count] = X[M, K] . W[:, start:start+count] + b
+//
+// Weight semantics (reference scripts/gemm_nf24_i16_avx512.c:26-33):
+//   W[k, n] = scale[n] * (256 * q01[k, n] + q2[k, n]),   q01 int16 [K, N], q2 int8 [K, N]
+//
+// Design.
+//  * X (fp32) is split once per call by `nf24_split_rows` into two exact-sum fp16 planes
+//    X' = hi + lo after an exact per-row power-of-two pre-scale (undone in the epilogue),
+//    so fp16's range never clips and hi + lo carries ~22 significant bits.
+//  * W/256 = q01 + q2/256 is split into two fp16 operands that are EXACT for every code
+//    |q01| <= 1023 (the packer emits |q01| <= 636):
+//        A1 = 2*floor(q01/2)          (even integer)
+//        A2 = (q01 & 1) + q2/256      (multiple of 1/256 in [-0.5, 1.5))
+//    Both are built from the raw codes with integer/bit operations and one HFMA2 each
+//    (magic-exponent construction), in registers, and written straight into tensor memory.
+//  * The tcgen05 MMA computes the TRANSPOSED product D[n, m] = sum_k A[n, k] * X'[m, k]
+//    with A (weights) read from TMEM and X' (hi or lo plane, TMA-loaded with 128-B
+//    swizzle) from shared memory:  4 MMAs per k-step (A1.hi, A1.lo, A2.hi, A2.lo).
+//  * Accuracy: the tensor core's fp32 accumulation truncates, so an error that grows
+//    linearly with the number of accumulation steps builds up in a long-lived accumulator
+//    (measured: rmse 1.8e-5 relative at K = 4096, 16x the fp32 reference).  Each k-block
+//    (64 k) is therefore accumulated into a FRESH TMEM partial (double-buffered) and
+//    promoted into round-to-nearest fp32 running sums held in the epilogue warps'
+//    registers, which keeps the error at the level of a 64-long dot product.
+//    Epilogue: y = sum * rowscale[m] * 256*scale[n] + bias[n].
+//
+// Warp roles (448 threads, one CTA per SM):
+//   warp 0       TMA producer (codes and X planes)
+//   warp 1       TMEM allocator + single-thread MMA issuer
+//   warps 2..5   weight decoders (raw codes smem -> registers -> TMEM)
+//   warps 6..13  promotion + epilogue; two warps per TMEM lane quarter, 96 tokens each
+//
+// Columns whose layout TMA cannot address (N % 16 != 0, unaligned pointers) go to
+// `nf24_gemm_simt`, which reproduces the reference's scalar tail kernel
+// (scripts/gemm_nf24_i16_avx512_tail.c:32-47) operation for operation.
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+#include "runtime.h"
+
+namespace tsb {
+namespace gemm {
+
+constexpr int BN = 128;  // weight columns per CTA = TMEM lanes = MMA M
+constexpr int BM = 192;  // tokens per CTA = MMA N
+constexpr int BK = 64;   // k per stage: one 128-B swizzle row of fp16
+constexpr int XS = 3;    // X stages (hi + lo planes)
+constexpr int CS = 3;    // raw-code stages
+constexpr int AS = 2;    // decoded-weight stages in TMEM
+constexpr int X_PLANE = BM * BK * 2;       // 24 KB
+constexpr int X_STAGE = 2 * X_PLANE;       // 48 KB
+constexpr int C16_BYTES = BK * BN * 2;     // 16 KB
+constexpr int C8_BYTES = BK * BN;          //  8 KB
+constexpr int C_STAGE = C16_BYTES + C8_BYTES;
+constexpr int NUM_EPI_WARPS = 8;
+constexpr int EPI_COLS = BM / 2;  // tokens per epilogue warp
+constexpr int NUM_THREADS = 32 * (6 + NUM_EPI_WARPS);
+constexpr int TMEM_COLS = 512;
+constexpr int ACC_COL = 0;        // 2 partial buffers x BM fp32 columns
+constexpr int A_COL = 2 * BM;     // AS stages x (32 cols A1 + 32 cols A2)
+static_assert(A_COL + AS * 64 <= TMEM_COLS, "TMEM budget");
+constexpr int NUM_BARS = 2 * XS + 2 * CS + 2 * AS + 5;
+constexpr int SMEM_BYTES = 1024 /*align slack*/ + XS * X_STAGE + CS * C_STAGE + BM * 4 +
+                           NUM_BARS * 8 + 16;
+
+struct Params {
+  const float* rscale;  // [M] inverse row pre-scale of the split X
+  const float* scale;   // [N]
+  const float* bias;    // [N]
+  float* out;           // [M, stride_out]
+  int M, K, N, start, count, stride_out;
+  int* status;
+};
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    nf24_gemm_tc(const __grid_constant__ CUtensorMap tm_xhi,
+                 const __grid_constant__ CUtensorMap tm_xlo,
+                 const __grid_constant__ CUtensorMap tm_c16,
+                 const __grid_constant__ CUtensorMap tm_c8, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* xs = smem;
+  uint8_t* cs = xs + XS * X_STAGE;
+  float* rs_s = reinterpret_cast<float*>(cs + CS * C_STAGE);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(rs_s + BM);
+  uint64_t* x_full = bars;
+  uint64_t* x_empty = x_full + XS;
+  uint64_t* c_full = x_empty + XS;
+  uint64_t* c_empty = c_full + CS;
+  uint64_t* a_full = c_empty + CS;
+  uint64_t* a_empty = a_full + AS;
+  uint64_t* acc_full = a_empty + AS;  // [2]
+  uint64_t* acc_free = acc_full + 2;  // [2]
+  uint64_t* mma_done = acc_free + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t warp = warp_id();
+  const uint32_t lane = lane_id();
+  const int n0 = blockIdx.x * BN;  // local column (within [0, count))
+  const int m0 = blockIdx.y * BM;
+  const int kblocks = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < XS; ++i) { mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], 1); }
+    for (int i = 0; i < CS; ++i) { mbar_init(&c_full[i], 1); mbar_init(&c_empty[i], 4); }
+    for (int i = 0; i < AS; ++i) { mbar_init(&a_full[i], 4); mbar_init(&a_empty[i], 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_free[i], NUM_EPI_WARPS); }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_xhi);
+    tma_prefetch_desc(&tm_xlo);
+    tma_prefetch_desc(&tm_c16);
+    tma_prefetch_desc(&tm_c8);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp >= 6) {
+    for (int i = threadIdx.x - 192; i < BM; i += 32 * NUM_EPI_WARPS)
+      rs_s[i] = (m0 + i < p.M) ? p.rscale[m0 + i] : 0.0f;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (elect_one()) {
+      int last_c[CS], last_x[XS];
+      for (int i = 0; i < CS; ++i) last_c[i] = -1;
+      for (int i = 0; i < XS; ++i) last_x[i] = -1;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        const int c = kb % CS, x = kb % XS;
+        if (kb >= CS &&
+            !mbar_wait(&c_empty[c], ((kb / CS) & 1) ^ 1, p.status, kDevTimeoutProducer, abort_flag))
+          break;
+        uint8_t* cdst = cs + c * C_STAGE;
+        mbar_arrive_expect_tx(&c_full[c], C_STAGE);
+        tma_load_2d(cdst, &tm_c16, &c_full[c], p.start + n0, kb * BK);
+        tma_load_2d(cdst + C16_BYTES, &tm_c8, &c_full[c], p.start + n0, kb * BK);
+        last_c[c] = kb;
+        if (kb >= XS &&
+            !mbar_wait(&x_empty[x], ((kb / XS) & 1) ^ 1, p.status, kDevTimeoutProducer, abort_flag))
+          break;
+        uint8_t* xdst = xs + x * X_STAGE;
+        mbar_arrive_expect_tx(&x_full[x], X_STAGE);
+        tma_load_2d(xdst, &tm_xhi, &x_full[x], kb * BK, m0);
+        tma_load_2d(xdst + X_PLANE, &tm_xlo, &x_full[x], kb * BK, m0);
+        last_x[x] = kb;
+      }
+      if (*abort_flag) {
+        // never leave the CTA while a bulk copy may still write its shared memory
+        for (int i = 0; i < CS; ++i)
+          if (last_c[i] >= 0) mbar_wait(&c_full[i], (last_c[i] / CS) & 1, p.status, kDevTimeoutProducer, nullptr);
+        for (int i = 0; i < XS; ++i)
+          if (last_x[i] >= 0) mbar_wait(&x_full[i], (last_x[i] / XS) & 1, p.status, kDevTimeoutProducer, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (elect_one()) {
+      constexpr uint32_t idesc = idesc_f16_f32(BN, BM);
+      bool ok = true;
+      for (int kb = 0; kb < kblocks && ok; ++kb) {
+        const int x = kb % XS, a = kb % AS, b = kb & 1;
+        ok = mbar_wait(&x_full[x], (kb / XS) & 1, p.status, kDevTimeoutMma, abort_flag) &&
+             mbar_wait(&a_full[a], (kb / AS) & 1, p.status, kDevTimeoutMma, abort_flag) &&
+             (kb < 2 || mbar_wait(&acc_free[b], ((kb >> 1) & 1) ^ 1, p.status, kDevTimeoutMma, abort_flag));
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t hi = smem_u32(xs + x * X_STAGE);
+        const uint32_t lo = hi + X_PLANE;
+        const uint32_t a_col = tmem + A_COL + a * 64;
+        const uint32_t d = tmem + ACC_COL + b * BM;
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          const uint64_t dhi = sw128_kmajor_desc(hi + kk * 32);
+          const uint64_t dlo = sw128_kmajor_desc(lo + kk * 32);
+          const uint32_t a1 = a_col + kk * 8;
+          const uint32_t a2 = a_col + 32 + kk * 8;
+          mma_f16_ts(d, a1, dhi, idesc, kk != 0);  // fresh partial per k-block
+          mma_f16_ts(d, a1, dlo, idesc, 1);
+          mma_f16_ts(d, a2, dhi, idesc, 1);
+          mma_f16_ts(d, a2, dlo, idesc, 1);
+        }
+        mma_commit(&x_empty[x]);
+        mma_commit(&a_empty[a]);
+        mma_commit(&acc_full[b]);
+      }
+      // Retire every issued MMA before teardown frees TMEM (also on the error path).
+      mma_commit(mma_done);
+      mbar_wait(mma_done, 0, p.status, kDevTimeoutMma, nullptr);
+    }
+  } else if (warp < 6) {
+    // ---------------- weight decoders ----------------
+    const uint32_t sub = warp & 3;  // TMEM lane quarter this warp may touch
+    const int nl = sub * 32 + lane;
+    const uint32_t lane_base = (sub * 32) << 16;
+    const __half2 two = __floats2half2_rn(2.0f, 2.0f);
+    const __half2 m3072 = __floats2half2_rn(-3072.0f, -3072.0f);
+    const __half2 inv256 = __floats2half2_rn(1.0f / 256.0f, 1.0f / 256.0f);
+    const __half2 m4p5 = __floats2half2_rn(-4.5f, -4.5f);
+    for (int kb = 0; kb < kblocks; ++kb) {
+      const int c = kb % CS, a = kb % AS;
+      bool ok = mbar_wait(&c_full[c], (kb / CS) & 1, p.status, kDevTimeoutConsumer, abort_flag);
+      if (ok && kb >= AS)
+        ok = mbar_wait(&a_empty[a], ((kb / AS) & 1) ^ 1, p.status, kDevTimeoutConsumer, abort_flag);
+      // the tcgen05 st below is warp-collective: leave the loop as a whole warp
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const uint16_t* c16 = reinterpret_cast<const uint16_t*>(cs + c * C_STAGE);
+      const uint8_t* c8 = cs + c * C_STAGE + C16_BYTES;
+      uint32_t r1[32], r2[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const uint32_t v0 = c16[(2 * i) * BN + nl];
+        const uint32_t v1 = c16[(2 * i + 1) * BN + nl];
+        const uint32_t b0 = c8[(2 * i) * BN + nl];
+        const uint32_t b1 = c8[(2 * i + 1) * BN + nl];
+        const uint32_t pq = v0 | (v1 << 16);
+        const uint32_t pc = b0 | (b1 << 16);
+        const uint32_t f1 = ((pq >> 1) & 0x03FF03FFu) ^ 0x66006600u;
+        const uint32_t f2 = (((pq << 8) & 0x01000100u) | pc) ^ 0x64806480u;
+        r1[i] = h2_bits(__hfma2(bits_h2(f1), two, m3072));
+        r2[i] = h2_bits(__hfma2(bits_h2(f2), inv256, m4p5));
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&c_empty[c]);
+      const uint32_t taddr = tmem + lane_base + A_COL + a * 64;
+      tmem_st32(taddr, r1);
+      tmem_st32(taddr + 32, r2);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a_full[a]);
+    }
+  } else {
+    // ---------------- promotion + epilogue ----------------
+    const uint32_t sub = warp & 3;
+    const int half = (warp - 6) >> 2;  // which 96-token half of the tile
+    const int nl = sub * 32 + lane;
+    const uint32_t lane_base = (sub * 32) << 16;
+    float sum[EPI_COLS];
+#pragma unroll
+    for (int j = 0; j < EPI_COLS; ++j) sum[j] = 0.0f;
+    bool ok = true;
+    for (int kb = 0; kb < kblocks; ++kb) {
+      const int b = kb & 1;
+      ok = mbar_wait(&acc_full[b], (kb >> 1) & 1, p.status, kDevTimeoutEpilogue, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t col = tmem + lane_base + ACC_COL + b * BM + half * EPI_COLS;
+#pragma unroll
+      for (int q = 0; q < EPI_COLS / 16; ++q) {
+        uint32_t r[16];
+        tmem_ld16(col + q * 16, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) sum[q * 16 + j] += __uint_as_float(r[j]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_free[b]);
+    }
+    if (ok) {
+      const int nloc = n0 + nl;
+      if (nloc < p.count) {
+        const float sc = p.scale[p.start + nloc] * 256.0f;
+        const float bi = p.bias[p.start + nloc];
+        float* out_col = p.out + nloc;
+        const int mbase = m0 + half * EPI_COLS;
+#pragma unroll
+        for (int j = 0; j < EPI_COLS; ++j) {
+          const int m = mbase + j;
+          if (m < p.M)
+            out_col[(int64_t)m * p.stride_out] = fmaf(sum[j] * rs_s[half * EPI_COLS + j], sc, bi);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// X fp32 [M, K] (row stride stride_x) -> hi, lo fp16 [M, Kp] and rscale [M].
+// One warp per row; the row is pre-scaled by 2^s so its max lands in [2^14, 2^15).
+__global__ void nf24_split_rows(const float* __restrict__ x, int M, int K, int Kp, int stride_x,
+                                __half* __restrict__ hi, __half* __restrict__ lo,
+                                float* __restrict__ rscale) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const float* xr = x + (int64_t)row * stride_x;
+  float mx = 0.0f;
+  for (int k = lane; k < K; k += 32) mx = fmaxf(mx, fabsf(xr[k]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  int shift = 0;
+  if (mx > 0.0f && mx <= 3.402823466e38f) {
+    shift = 14 - ilogbf(mx);
+    shift = shift < -60 ? -60 : (shift > 60 ? 60 : shift);
+  }
+  __half* hr = hi + (int64_t)row * Kp;
+  __half* lr = lo + (int64_t)row * Kp;
+  for (int k = lane * 2; k < Kp; k += 64) {
+    float a = (k < K) ? ldexpf(xr[k], shift) : 0.0f;
+    float b = (k + 1 < K) ? ldexpf(xr[k + 1], shift) : 0.0f;
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(a - hf.x, b - hf.y);
+    *reinterpret_cast<__half2*>(hr + k) = h;
+    *reinterpret_cast<__half2*>(lr + k) = l;
+  }
+  if (lane == 0) rscale[row] = ldexpf(1.0f, -shift);
+}
+
+// Reference-order scalar kernel: one thread per output, acc = bias, then an in-order
+// fmaf chain over k with w = (float)(256*q01 + q2) * scale[n].
+__global__ void nf24_gemm_simt(const float* __restrict__ x, const int16_t* __restrict__ c01,
+                               const int8_t* __restrict__ q2, const float* __restrict__ scale,
+                               const float* __restrict__ bias, float* __restrict__ out, int M,
+                               int K, int N, int start, int count, int stride_x, int stride_out) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  const int m = blockIdx.y;
+  if (j >= count || m >= M) return;
+  const int n = start + j;
+  const float* xr = x + (int64_t)m * stride_x;
+  const float sc = scale[n];
+  float acc = bias[n];
+  for (int k = 0; k < K; ++k) {
+    const int32_t q = (int32_t)c01[(int64_t)k * N + n] * 256 + (int32_t)q2[(int64_t)k * N + n];
+    acc = fmaf(xr[k], __fmul_rn((float)q, sc), acc);
+  }
+  out[(int64_t)m * stride_out + j] = acc;
+}
+
+}  // namespace gemm
+
+// Host launcher shared by the full / range / tail entry points.
+static int gemm_launch(const float* x, const int16_t* c01, const int8_t* q2, const float* scale,
+                       const float* bias, float* out, int M, int K, int N, int start, int count,
+                       int stride_x, int stride_out, bool allow_tc) {
+  using namespace gemm;
+  int st = entry_check();
+  if (st != kOk) return st;
+  if (!is_device_pointer(x) || !is_device_pointer(c01) || !is_device_pointer(q2) ||
+      !is_device_pointer(scale) || !is_device_pointer(bias) || !is_device_pointer(out))
+    return kNotDevicePointer;
+  cudaStream_t stream = current_stream();
+  const bool aligned = ((reinterpret_cast<uintptr_t>(c01) | reinterpret_cast<uintptr_t>(q2)) & 15) == 0;
+  const bool tc = allow_tc && (N % 16 == 0) && (start % 16 == 0) && aligned;
+  if (!tc) {
+    dim3 grid((count + 127) / 128, M);
+    nf24_gemm_simt<<<grid, 128, 0, stream>>>(x, c01, q2, scale, bias, out, M, K, N, start, count,
+                                             stride_x, stride_out);
+    return launch_status();
+  }
+  const int Kp = (K + 7) & ~7;
+  const size_t plane = (size_t)M * Kp * 2;
+  uint8_t* ws = static_cast<uint8_t*>(workspace(2 * plane + (size_t)M * 4 + 256, stream));
+  if (!ws) return kWorkspace;
+  __half* hi = reinterpret_cast<__half*>(ws);
+  __half* lo = reinterpret_cast<__half*>(ws + plane);
+  float* rscale = reinterpret_cast<float*>(ws + 2 * plane);
+  nf24_split_rows<<<(M + 7) / 8, 256, 0, stream>>>(x, M, K, Kp, stride_x, hi, lo, rscale);
+  if ((st = launch_status()) != kOk) return st;
+
+  CUtensorMap m_hi, m_lo, m_c16, m_c8;
+  {
+    const uint64_t dims[2] = {(uint64_t)Kp, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)Kp * 2};
+    const uint32_t box[2] = {BK, BM};
+    if (!encode_tmap(&m_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, hi, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tmap(&m_lo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, lo, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B))
+      return kLaunchFailed;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)K};
+    const uint64_t s16[1] = {(uint64_t)N * 2};
+    const uint64_t s8[1] = {(uint64_t)N};
+    const uint32_t box[2] = {BN, BK};
+    if (!encode_tmap(&m_c16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<int16_t*>(c01), dims,
+                     s16, box, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode_tmap(&m_c8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(q2), dims, s8,
+                     box, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return kLaunchFailed;
+  }
+  {
+    static uint64_t attr_done = 0;  // one bit per device ordinal
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(attr_done >> dev & 1)) {
+      cudaFuncSetAttribute(nf24_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+      attr_done |= 1ull << dev;
+    }
+  }
+  Params prm{rscale, scale, bias, out, M, K, N, start, count, stride_out, device_status()};
+  dim3 grid((count + BN - 1) / BN, (M + BM - 1) / BM);
+  nf24_gemm_tc<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(m_hi, m_lo, m_c16, m_c8, prm);
+  return launch_status();
+}
+
+}  // namespace tsb
+
+// ---------------------------------------------------------------------------
+// C-ABI (same names, argument lists and status codes as the reference library
+// libtriposplat_gemm_nf24_i16_avx512.so).  Pointers are CUDA device pointers;
+// the work is queued on the stream set by triposplat_b200_set_stream (default
+// stream otherwise).  `threads` is accepted and ignored.  For NF24, codes0_t is
+// the int16 q01 [K, N] plane, codes1_t (== codes2_t) the int8 q2 [K, N] plane and
+// scales0 (== scales1 == scales2) the per-column scale; codebook is not read.
+// ---------------------------------------------------------------------------
+extern "C" {
+
+// scripts/gemm_nf24_i16_avx512.c:151-197
+int triposplat_gemm_rnf8_avx512_range(const float* x, const uint8_t* codes0_t,
+                                      const uint8_t* codes1_t, const uint8_t* codes2_t,
+                                      const float* scales0, const float* scales1,
+                                      const float* scales2, const float* codebook,
+                                      const float* bias, float* out, int M, int K, int N,
+                                      int output_start, int output_count, int stride_x,
+                                      int stride_out, int threads, int stages) {
+  (void)threads;
+  if (!x || !codes0_t || !codes1_t || !codes2_t || !scales0 || !scales1 || !scales2 ||
+      !codebook || !bias || !out)
+    return tsb::kNullPointer;
+  if (M <= 0 || K <= 0 || N <= 0 || output_start < 0 || output_count <= 0 || stages != 3)
+    return tsb::kBadDims;
+  if (output_start + output_count > N || stride_x < K || stride_out < output_count)
+    return tsb::kBadRange;
+  if ((output_start & 15) != 0 || (output_count & 15) != 0) return tsb::kBadAlignment;
+  return tsb::gemm_launch(x, reinterpret_cast<const int16_t*>(codes0_t),
+                          reinterpret_cast<const int8_t*>(codes1_t), scales0, bias, out, M, K, N,
+                          output_start, output_count, stride_x, stride_out, true);
+}
+
+// scripts/gemm_nf24_i16_avx512.c:199-220
+int triposplat_gemm_rnf8_avx512(const float* x, const uint8_t* codes0_t, const uint8_t* codes1_t,
+                                const uint8_t* codes2_t, const float* scales0,
+                                const float* scales1, const float* scales2,
+                                const float* codebook, const float* bias, float* out, int M,
+                                int K, int N, int stride_x, int stride_out, int threads,
+                                int stages) {
+  return triposplat_gemm_rnf8_avx512_range(x, codes0_t, codes1_t, codes2_t, scales0, scales1,
+                                           scales2, codebook, bias, out, M, K, N, 0, N, stride_x,
+                                           stride_out, threads, stages);
+}
+
+// scripts/gemm_nf24_i16_avx512_tail.c:8-49 (any N; the reference-order scalar kernel)
+int triposplat_gemm_rnf8_avx512_tail(const float* x, const uint8_t* codes0_t,
+                                     const uint8_t* codes1_t, const uint8_t* codes2_t,
+                                     const float* scales0, const float* scales1,
+                                     const float* scales2, const float* codebook,
+                                     const float* bias, float* out, int M, int K, int N,
+                                     int stride_x, int stride_out, int threads, int stages) {
+  (void)threads;
+  if (!x || !codes0_t || !codes1_t || !codes2_t || !scales0 || !scales1 || !scales2 ||
+      !codebook || !bias || !out)
+    return tsb::kNullPointer;
+  if (M <= 0 || K <= 0 || N <= 0 || stride_x < K || stride_out < N || stages != 3)
+    return tsb::kBadDims;
+  return tsb::gemm_launch(x, reinterpret_cast<const int16_t*>(codes0_t),
+                          reinterpret_cast<const int8_t*>(codes1_t), scales0, bias, out, M, K, N,
+                          0, N, stride_x, stride_out, false);
+}
+
+// scripts/gemm_nf24_i16_avx512.c:222-224: rows per CTA tile here (the CPU returns ROW_TILE)
+int triposplat_gemm_rnf8_avx512_row_tile(void) { return tsb::gemm::BM; }
+
+// scripts/gemm_nf24_i16_avx512.c:226-228: 4 = nf24_i16
+int triposplat_gemm_rnf8_avx512_residual_mode(void) { return 4; }
+
+}  // extern "C"

@@ -1,0 +1,195 @@
+// Library runtime: stream selection, device status word, workspaces, TMA maps.
+#include <cudaTypedefs.h>
+
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include "runtime.h"
+
+namespace tsb {
+
+namespace {
+
+thread_local cudaStream_t t_stream = nullptr;
+
+struct DeviceState {
+  int* host_status = nullptr;    // pinned, mapped
+  int* device_status = nullptr;  // device view of host_status
+  std::map<cudaStream_t, std::pair<void*, size_t>> workspaces;
+  uint64_t allocations = 0;
+  int sms = 0;
+};
+
+std::mutex g_mutex;
+std::map<int, DeviceState> g_devices;
+
+DeviceState* state_for_current_device() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  DeviceState& st = g_devices[dev];
+  if (st.host_status == nullptr) {
+    int* h = nullptr;
+    if (cudaHostAlloc(reinterpret_cast<void**>(&h), sizeof(int), cudaHostAllocMapped) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    *h = 0;
+    int* d = nullptr;
+    if (cudaHostGetDevicePointer(reinterpret_cast<void**>(&d), h, 0) != cudaSuccess) {
+      cudaGetLastError();
+      cudaFreeHost(h);
+      return nullptr;
+    }
+    st.host_status = h;
+    st.device_status = d;
+    cudaDeviceGetAttribute(&st.sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return &st;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+}  // namespace
+
+cudaStream_t current_stream() { return t_stream; }
+
+int* device_status() {
+  DeviceState* st = state_for_current_device();
+  return st ? st->device_status : nullptr;
+}
+
+int host_status() {
+  DeviceState* st = state_for_current_device();
+  if (!st) return 0;
+  return *reinterpret_cast<volatile int*>(st->host_status);
+}
+
+int sm_count() {
+  DeviceState* st = state_for_current_device();
+  return st ? st->sms : 148;
+}
+
+void* workspace(size_t bytes, cudaStream_t stream) {
+  DeviceState* st = state_for_current_device();
+  if (!st) return nullptr;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  auto& slot = st->workspaces[stream];
+  if (slot.first != nullptr && slot.second >= bytes) return slot.first;
+  // Growing: the previous buffer may still be read by work queued on `stream`.
+  if (slot.first != nullptr) {
+    cudaStreamSynchronize(stream);
+    cudaFree(slot.first);
+    slot.first = nullptr;
+    slot.second = 0;
+  }
+  size_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
+  want = (want + 0xFFFFF) & ~static_cast<size_t>(0xFFFFF);
+  void* p = nullptr;
+  if (cudaMalloc(&p, want) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  slot.first = p;
+  slot.second = want;
+  st->allocations += 1;
+  return p;
+}
+
+bool is_device_pointer(const void* p) {
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged ||
+         (attr.type == cudaMemoryTypeHost && attr.devicePointer != nullptr);
+}
+
+int entry_check() {
+  DeviceState* st = state_for_current_device();
+  if (!st) return kNoDevice;
+  if (*reinterpret_cast<volatile int*>(st->host_status) != 0) return kDeviceFault;
+  return kOk;
+}
+
+int launch_status() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? kOk : kLaunchFailed;
+}
+
+bool encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, void* base,
+                 const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                 CUtensorMapSwizzle swizzle) {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+  });
+  if (!g_encode) return false;
+  cuuint32_t elem_strides[5] = {1, 1, 1, 1, 1};
+  CUresult r = g_encode(map, dtype, rank, base, reinterpret_cast<const cuuint64_t*>(dims),
+                        reinterpret_cast<const cuuint64_t*>(strides_bytes),
+                        reinterpret_cast<const cuuint32_t*>(box), elem_strides,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+}  // namespace tsb
+
+// ---------------------------------------------------------------------------
+// C-ABI: runtime controls (no reference counterpart; the CPU library needs no
+// stream and keeps its workspace thread-local)
+// ---------------------------------------------------------------------------
+extern "C" {
+
+void triposplat_b200_set_stream(void* stream) {
+  tsb::t_stream = reinterpret_cast<cudaStream_t>(stream);
+}
+
+void* triposplat_b200_get_stream(void) { return reinterpret_cast<void*>(tsb::t_stream); }
+
+int triposplat_b200_status(void) { return tsb::host_status(); }
+
+void triposplat_b200_clear_status(void) {
+  tsb::DeviceState* st = tsb::state_for_current_device();
+  if (st) *reinterpret_cast<volatile int*>(st->host_status) = 0;
+}
+
+int triposplat_b200_workspace_reserve(uint64_t bytes) {
+  return tsb::workspace(bytes, tsb::t_stream) ? 0 : tsb::kWorkspace;
+}
+
+int triposplat_b200_workspace_stats(uint64_t* allocations, uint64_t* capacity_bytes) {
+  if (!allocations || !capacity_bytes) return tsb::kNullPointer;
+  tsb::DeviceState* st = tsb::state_for_current_device();
+  if (!st) return tsb::kNoDevice;
+  std::lock_guard<std::mutex> lock(tsb::g_mutex);
+  uint64_t cap = 0;
+  for (auto& kv : st->workspaces) cap += kv.second.second;
+  *allocations = st->allocations;
+  *capacity_bytes = cap;
+  return 0;
+}
+
+void triposplat_b200_workspace_release(void) {
+  tsb::DeviceState* st = tsb::state_for_current_device();
+  if (!st) return;
+  cudaDeviceSynchronize();
+  std::lock_guard<std::mutex> lock(tsb::g_mutex);
+  for (auto& kv : st->workspaces)
+    if (kv.second.first) cudaFree(kv.second.first);
+  st->workspaces.clear();
+}
+
+int triposplat_b200_abi_version(void) { return 1; }
+
+}  // extern "C"

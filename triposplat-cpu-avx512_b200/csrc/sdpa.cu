@@ -1,0 +1,646 @@
+// Exact scaled-dot-product attention for sm_100a, head_dim 64, scale 1/8:
+//   O = softmax(0.125 * Q K^T + bias_key) V
+// (reference scripts/native_sdpa_avx512_exact_q8t512.c:137-332; packed-K/V, BLHD-output
+// variant scripts/native_sdpa_avx512_exact_q8t512_packed.c:3-158).
+//
+// Split precision.  fp32 inputs are split into two fp16 planes (hi + lo, ~22 significant
+// bits) after an exact power-of-two pre-scale (per query row for Q; per 128-key tile for
+// K and V), and each product is formed with three tensor-core passes
+// (hi.hi + hi.lo + lo.hi; the lo.lo term is ~2^-22 relative and dropped):
+//   S = Qh Kh^T + Qh Kl^T + Ql Kh^T                (tcgen05, A/B from shared memory)
+//   O_t = Ph Vh + Ph Vl + Pl Vh                     (tcgen05, P from tensor memory)
+// The pre-scales fold into constants the softmax already multiplies by, so they are free.
+//
+// Exact online softmax.  Keys are processed in tiles of 128; per tile the softmax warps
+// take the running max m, rescale factor alpha = 2^(m_old - m_new), p = 2^(s*log2e - m),
+// the fp32 row sum, and merge the tile's fp32 output O_t (read back from TMEM) into
+// register accumulators: O = O*alpha + O_t * vscale_t.  No Lq x Lk matrix is ever
+// materialised and no score is skipped.
+//
+// CTA: one (b, h) and 128 query rows, 192 threads, two CTAs per SM.
+//   warp 0      TMA producer (Q once, K and V^T tiles)
+//   warp 1      TMEM allocator + MMA issuer
+//   warps 2..5  softmax / merge / epilogue, thread = query row = TMEM lane
+// TMEM (256 columns): S / P tile at 0..127 (P overwrites S in place: for every 16-key
+// chunk, P_hi goes to its first 8 columns and P_lo to the next 8), O_t double buffer at
+// 128..191 and 192..255.
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+#include "runtime.h"
+
+namespace tsb {
+namespace sdpa {
+
+constexpr int D = 64;
+constexpr int BQ = 128;
+constexpr int BKV = 128;
+constexpr int NUM_THREADS = 192;
+constexpr int TMEM_COLS = 256;
+constexpr int S_COL = 0;
+constexpr int O_COL = 128;
+constexpr int PLANE = 128 * D * 2;  // 16 KB: one 128 x 64 fp16 tile
+constexpr int SMEM_BYTES = 1024 + 6 * PLANE + 2 * BKV * 4 + 32 * 8 + 16;
+constexpr float LOG2E = 1.4426950408889634f;
+
+struct Params {
+  const float* qinv;  // [BH * Lq]   inverse pre-scale of each query row
+  const float* kinv;  // [BH * T]    inverse pre-scale of each key tile
+  const float* vinv;  // [BH * T]
+  const float* bias;  // nullable; bias for (bh, key j) = bias[bh * bias_bh_stride + j]
+  long long bias_bh_stride;
+  float* out;
+  int H, Lq, Lk, T;
+  int out_blhd;
+  int* status;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 2)
+    sdpa_fwd_tc(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant__ CUtensorMap tm_qlo,
+                const __grid_constant__ CUtensorMap tm_khi, const __grid_constant__ CUtensorMap tm_klo,
+                const __grid_constant__ CUtensorMap tm_vhi, const __grid_constant__ CUtensorMap tm_vlo,
+                const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* q_hi = smem;
+  uint8_t* q_lo = q_hi + PLANE;
+  uint8_t* k_hi = q_lo + PLANE;
+  uint8_t* k_lo = k_hi + PLANE;
+  uint8_t* v_hi = k_lo + PLANE;  // two [64 dims x 64 keys] swizzled blocks
+  uint8_t* v_lo = v_hi + PLANE;
+  float* bias_s = reinterpret_cast<float*>(v_lo + PLANE);  // [2][BKV], log2 units
+  uint64_t* bars = reinterpret_cast<uint64_t*>(bias_s + 2 * BKV);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = bars + 2;
+  uint64_t* v_full = bars + 3;
+  uint64_t* v_empty = bars + 4;
+  uint64_t* s_full = bars + 5;
+  uint64_t* p_full = bars + 6;
+  uint64_t* o_full = bars + 7;  // [2]
+  uint64_t* o_free = bars + 9;  // [2]
+  uint64_t* mma_done = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t warp = warp_id();
+  const uint32_t lane = lane_id();
+  const int bh = blockIdx.y;
+  const int q0 = blockIdx.x * BQ;
+  const int T = p.T;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 12; ++i) mbar_init(&bars[i], 1);
+    mbar_init(p_full, 4);
+    mbar_init(&o_free[0], 4);
+    mbar_init(&o_free[1], 4);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_qhi); tma_prefetch_desc(&tm_qlo);
+    tma_prefetch_desc(&tm_khi); tma_prefetch_desc(&tm_klo);
+    tma_prefetch_desc(&tm_vhi); tma_prefetch_desc(&tm_vlo);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (elect_one()) {
+      int issued_k = -1, issued_v = -1;
+      mbar_arrive_expect_tx(q_full, 2 * PLANE);
+      tma_load_3d(q_hi, &tm_qhi, q_full, 0, q0, bh);
+      tma_load_3d(q_lo, &tm_qlo, q_full, 0, q0, bh);
+      for (int t = 0; t < T; ++t) {
+        if (t >= 1 && !mbar_wait(k_empty, (t - 1) & 1, p.status, kDevTimeoutProducer, abort_flag)) break;
+        mbar_arrive_expect_tx(k_full, 2 * PLANE);
+        tma_load_3d(k_hi, &tm_khi, k_full, 0, t * BKV, bh);
+        tma_load_3d(k_lo, &tm_klo, k_full, 0, t * BKV, bh);
+        issued_k = t;
+        if (t >= 1 && !mbar_wait(v_empty, (t - 1) & 1, p.status, kDevTimeoutProducer, abort_flag)) break;
+        mbar_arrive_expect_tx(v_full, 2 * PLANE);
+        tma_load_3d(v_hi, &tm_vhi, v_full, t * BKV, 0, bh);
+        tma_load_3d(v_hi + PLANE / 2, &tm_vhi, v_full, t * BKV + 64, 0, bh);
+        tma_load_3d(v_lo, &tm_vlo, v_full, t * BKV, 0, bh);
+        tma_load_3d(v_lo + PLANE / 2, &tm_vlo, v_full, t * BKV + 64, 0, bh);
+        issued_v = t;
+      }
+      if (*abort_flag) {
+        mbar_wait(q_full, 0, p.status, kDevTimeoutProducer, nullptr);
+        if (issued_k >= 0) mbar_wait(k_full, issued_k & 1, p.status, kDevTimeoutProducer, nullptr);
+        if (issued_v >= 0) mbar_wait(v_full, issued_v & 1, p.status, kDevTimeoutProducer, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (elect_one()) {
+      constexpr uint32_t idesc_s = idesc_f16_f32(BQ, BKV);
+      constexpr uint32_t idesc_o = idesc_f16_f32(BQ, D);
+      bool ok = mbar_wait(q_full, 0, p.status, kDevTimeoutMma, abort_flag);
+      const uint32_t qh = smem_u32(q_hi), ql = smem_u32(q_lo);
+      const uint32_t kh = smem_u32(k_hi), kl = smem_u32(k_lo);
+      const uint32_t vh = smem_u32(v_hi), vl = smem_u32(v_lo);
+      for (int t = 0; t < T && ok; ++t) {
+        ok = mbar_wait(k_full, t & 1, p.status, kDevTimeoutMma, abort_flag) &&
+             (t == 0 || mbar_wait(&o_full[(t - 1) & 1], ((t - 1) >> 1) & 1, p.status, kDevTimeoutMma, abort_flag));
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t a_h = sw128_kmajor_desc(qh + kk * 32);
+          const uint64_t a_l = sw128_kmajor_desc(ql + kk * 32);
+          const uint64_t b_h = sw128_kmajor_desc(kh + kk * 32);
+          const uint64_t b_l = sw128_kmajor_desc(kl + kk * 32);
+          mma_f16_ss(tmem + S_COL, a_h, b_h, idesc_s, kk != 0);
+          mma_f16_ss(tmem + S_COL, a_h, b_l, idesc_s, 1);
+          mma_f16_ss(tmem + S_COL, a_l, b_h, idesc_s, 1);
+        }
+        mma_commit(k_empty);
+        mma_commit(s_full);
+        ok = mbar_wait(p_full, t & 1, p.status, kDevTimeoutMma, abort_flag) &&
+             mbar_wait(v_full, t & 1, p.status, kDevTimeoutMma, abort_flag) &&
+             (t < 2 || mbar_wait(&o_free[t & 1], ((t >> 1) & 1) ^ 1, p.status, kDevTimeoutMma, abort_flag));
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t o = tmem + O_COL + (t & 1) * D;
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk) {
+          const uint32_t ph = tmem + S_COL + kk * 16;  // P_hi for keys 16kk..16kk+15
+          const uint32_t pl = ph + 8;                  // P_lo
+          const uint32_t voff = (kk >> 2) * (PLANE / 2) + (kk & 3) * 32;
+          const uint64_t b_h = sw128_kmajor_desc(vh + voff);
+          const uint64_t b_l = sw128_kmajor_desc(vl + voff);
+          mma_f16_ts(o, ph, b_h, idesc_o, kk != 0);
+          mma_f16_ts(o, ph, b_l, idesc_o, 1);
+          mma_f16_ts(o, pl, b_h, idesc_o, 1);
+        }
+        mma_commit(v_empty);
+        mma_commit(&o_full[t & 1]);
+      }
+      mma_commit(mma_done);
+      mbar_wait(mma_done, 0, p.status, kDevTimeoutMma, nullptr);
+    }
+  } else {
+    // ---------------- softmax, merge, epilogue ----------------
+    const uint32_t sub = warp & 3;
+    const int r = sub * 32 + lane;  // query row within the tile == TMEM lane
+    const int tid = threadIdx.x - 64;
+    const uint32_t lane_base = (sub * 32) << 16;
+    const int qrow = q0 + r;
+    const bool row_valid = qrow < p.Lq;
+    const float cq = 0.125f * LOG2E * (row_valid ? p.qinv[(int64_t)bh * p.Lq + qrow] : 0.0f);
+    const float* bias_row = p.bias ? p.bias + (int64_t)bh * p.bias_bh_stride : nullptr;
+    float o_acc[D];
+#pragma unroll
+    for (int d = 0; d < D; ++d) o_acc[d] = 0.0f;
+    float m_run = -INFINITY, l_run = 0.0f, alpha_prev = 0.0f;
+    bool ok = true;
+    for (int t = 0; t < T; ++t) {
+      {
+        const int j = t * BKV + tid;
+        float b = -INFINITY;
+        if (j < p.Lk) b = bias_row ? bias_row[j] * LOG2E : 0.0f;
+        bias_s[(t & 1) * BKV + tid] = b;
+      }
+      named_bar_sync(1, 128);
+      const float* bt = bias_s + (t & 1) * BKV;
+      ok = mbar_wait(s_full, t & 1, p.status, kDevTimeoutConsumer, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+      tc_fence_after();
+      const float c2 = cq * p.kinv[(int64_t)bh * T + t];
+      // pass 1: tile max
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int ch = 0; ch < BKV / 32; ++ch) {
+        uint32_t s[32];
+        tmem_ld32(tmem + lane_base + S_COL + ch * 32, s);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) mx = fmaxf(mx, fmaf(__uint_as_float(s[j]), c2, bt[ch * 32 + j]));
+      }
+      const float m_new = fmaxf(m_run, mx);
+      const float m_use = (m_new == -INFINITY) ? 0.0f : m_new;
+      const float alpha = ex2(m_run - m_use);
+      // pass 2: p = 2^(s - m), row sum, fp16 hi/lo split written over S as the PV A operand
+      float psum = 0.0f;
+#pragma unroll 1
+      for (int ch = 0; ch < BKV / 16; ++ch) {
+        uint32_t s[16], ph[8], pl[8];
+        tmem_ld16(tmem + lane_base + S_COL + ch * 16, s);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; j += 2) {
+          const float p0 = ex2(fmaf(__uint_as_float(s[j]), c2, bt[ch * 16 + j]) - m_use);
+          const float p1 = ex2(fmaf(__uint_as_float(s[j + 1]), c2, bt[ch * 16 + j + 1]) - m_use);
+          psum += p0 + p1;
+          const __half2 h = __floats2half2_rn(p0, p1);
+          const float2 hf = __half22float2(h);
+          const __half2 lo = __floats2half2_rn(p0 - hf.x, p1 - hf.y);
+          ph[j >> 1] = *reinterpret_cast<const uint32_t*>(&h);
+          pl[j >> 1] = *reinterpret_cast<const uint32_t*>(&lo);
+        }
+        const uint32_t dst = tmem + lane_base + S_COL + ch * 16;
+        asm volatile(
+            "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(dst),
+            "r"(ph[0]), "r"(ph[1]), "r"(ph[2]), "r"(ph[3]), "r"(ph[4]), "r"(ph[5]), "r"(ph[6]),
+            "r"(ph[7])
+            : "memory");
+        asm volatile(
+            "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(dst + 8),
+            "r"(pl[0]), "r"(pl[1]), "r"(pl[2]), "r"(pl[3]), "r"(pl[4]), "r"(pl[5]), "r"(pl[6]),
+            "r"(pl[7])
+            : "memory");
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      l_run = l_run * alpha + psum;
+      m_run = m_use;
+      // merge the previous tile's P.V while the tensor core works on this one
+      if (t >= 1) {
+        const int pb = (t - 1) & 1;
+        ok = mbar_wait(&o_full[pb], ((t - 1) >> 1) & 1, p.status, kDevTimeoutConsumer, abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        tc_fence_after();
+        const float vs = p.vinv[(int64_t)bh * T + t - 1];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t o[32];
+          tmem_ld32(tmem + lane_base + O_COL + pb * D + hh * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int d = 0; d < 32; ++d)
+            o_acc[hh * 32 + d] = fmaf(__uint_as_float(o[d]), vs, o_acc[hh * 32 + d] * alpha_prev);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&o_free[pb]);
+      }
+      alpha_prev = alpha;
+    }
+    if (ok) {
+      const int pb = (T - 1) & 1;
+      ok = mbar_wait(&o_full[pb], ((T - 1) >> 1) & 1, p.status, kDevTimeoutEpilogue, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        tc_fence_after();
+        const float vs = p.vinv[(int64_t)bh * T + T - 1];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t o[32];
+          tmem_ld32(tmem + lane_base + O_COL + pb * D + hh * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int d = 0; d < 32; ++d)
+            o_acc[hh * 32 + d] = fmaf(__uint_as_float(o[d]), vs, o_acc[hh * 32 + d] * alpha_prev);
+        }
+        if (row_valid) {
+          const float inv = 1.0f / l_run;
+          const int b = bh / p.H, h = bh % p.H;
+          float* dst = p.out_blhd ? p.out + (((int64_t)b * p.Lq + qrow) * p.H + h) * D
+                                  : p.out + ((int64_t)bh * p.Lq + qrow) * D;
+#pragma unroll
+          for (int d = 0; d < D; d += 4)
+            *reinterpret_cast<float4*>(dst + d) =
+                make_float4(o_acc[d] * inv, o_acc[d + 1] * inv, o_acc[d + 2] * inv, o_acc[d + 3] * inv);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Pre-split kernels
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int pow2_shift(float mx) {
+  if (!(mx > 0.0f) || !(mx <= 3.402823466e38f)) return 0;
+  int s = 14 - ilogbf(mx);
+  return s < -60 ? -60 : (s > 60 ? 60 : s);
+}
+
+// Q [BH, Lq, 64] fp32 -> hi/lo fp16 [BH, Lq, 64], qinv [BH*Lq].  One warp per row.
+__global__ void sdpa_split_q(const float* __restrict__ q, int64_t rows, __half* __restrict__ hi,
+                             __half* __restrict__ lo, float* __restrict__ qinv) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float2 v = *reinterpret_cast<const float2*>(q + row * D + lane * 2);
+  float mx = fmaxf(fabsf(v.x), fabsf(v.y));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const int s = pow2_shift(mx);
+  const float a = ldexpf(v.x, s), b = ldexpf(v.y, s);
+  const __half2 h = __floats2half2_rn(a, b);
+  const float2 hf = __half22float2(h);
+  *reinterpret_cast<__half2*>(hi + row * D + lane * 2) = h;
+  *reinterpret_cast<__half2*>(lo + row * D + lane * 2) = __floats2half2_rn(a - hf.x, b - hf.y);
+  if (lane == 0) qinv[row] = ldexpf(1.0f, -s);
+}
+
+// One CTA per (bh, 128-key tile): K -> hi/lo [BH, Lkt, 64]; V -> transposed hi/lo
+// [BH, 64, Lkt]; one power-of-two pre-scale per tile for each.  Keys >= Lk are zero.
+// Element (j, d) of K (or V) is read at base + bh*bh_stride + j*j_stride + d*d_stride,
+// which covers both the [B,H,Lk,64] layout and the packed [B,H,64,Lkp] one.
+__global__ void __launch_bounds__(256) sdpa_split_kv(
+    const float* __restrict__ k, const float* __restrict__ v, int64_t bh_stride, int64_t j_stride,
+    int64_t d_stride, int Lk, int Lkt, __half* __restrict__ khi, __half* __restrict__ klo,
+    __half* __restrict__ vhi, __half* __restrict__ vlo, float* __restrict__ kinv,
+    float* __restrict__ vinv) {
+  __shared__ float vt[BKV][D + 1];
+  __shared__ float red[2][8];
+  const int t = blockIdx.x, bh = blockIdx.y, T = gridDim.x;
+  const int j0 = t * BKV;
+  const float* kb = k + (int64_t)bh * bh_stride;
+  const float* vb = v + (int64_t)bh * bh_stride;
+  float kmx = 0.0f, vmx = 0.0f;
+  for (int e = threadIdx.x; e < BKV * D; e += 256) {
+    int j, d;
+    if (d_stride == 1) { j = e / D; d = e % D; } else { d = e / BKV; j = e % BKV; }
+    const int jj = j0 + j;
+    float kv = 0.0f, vv = 0.0f;
+    if (jj < Lk) {
+      kv = kb[(int64_t)jj * j_stride + (int64_t)d * d_stride];
+      vv = vb[(int64_t)jj * j_stride + (int64_t)d * d_stride];
+    }
+    vt[j][d] = vv;
+    kmx = fmaxf(kmx, fabsf(kv));
+    vmx = fmaxf(vmx, fabsf(vv));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    kmx = fmaxf(kmx, __shfl_xor_sync(0xffffffffu, kmx, o));
+    vmx = fmaxf(vmx, __shfl_xor_sync(0xffffffffu, vmx, o));
+  }
+  if ((threadIdx.x & 31) == 0) { red[0][threadIdx.x >> 5] = kmx; red[1][threadIdx.x >> 5] = vmx; }
+  __syncthreads();
+  kmx = red[0][0]; vmx = red[1][0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) { kmx = fmaxf(kmx, red[0][w]); vmx = fmaxf(vmx, red[1][w]); }
+  const int sk = pow2_shift(kmx), sv = pow2_shift(vmx);
+  // K rows: thread handles (row j, 8 dims); reads are L1/L2 hits from the first pass
+  for (int e = threadIdx.x; e < BKV * (D / 8); e += 256) {
+    const int j = e / (D / 8), d0 = (e % (D / 8)) * 8;
+    const int jj = j0 + j;
+    __align__(16) __half h8[8];
+    __align__(16) __half l8[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float x = jj < Lk ? ldexpf(kb[(int64_t)jj * j_stride + (int64_t)(d0 + i) * d_stride], sk) : 0.0f;
+      const __half hh = __float2half_rn(x);
+      h8[i] = hh;
+      l8[i] = __float2half_rn(x - __half2float(hh));
+    }
+    const int64_t off = ((int64_t)bh * Lkt + jj) * D + d0;
+    *reinterpret_cast<uint4*>(khi + off) = *reinterpret_cast<uint4*>(h8);
+    *reinterpret_cast<uint4*>(klo + off) = *reinterpret_cast<uint4*>(l8);
+  }
+  // V transposed: thread handles (dim d, 8 keys)
+  for (int e = threadIdx.x; e < D * (BKV / 8); e += 256) {
+    const int d = e / (BKV / 8), jb = (e % (BKV / 8)) * 8;
+    __align__(16) __half h8[8];
+    __align__(16) __half l8[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float x = ldexpf(vt[jb + i][d], sv);
+      const __half hh = __float2half_rn(x);
+      h8[i] = hh;
+      l8[i] = __float2half_rn(x - __half2float(hh));
+    }
+    const int64_t off = ((int64_t)bh * D + d) * Lkt + j0 + jb;
+    *reinterpret_cast<uint4*>(vhi + off) = *reinterpret_cast<uint4*>(h8);
+    *reinterpret_cast<uint4*>(vlo + off) = *reinterpret_cast<uint4*>(l8);
+  }
+  if (threadIdx.x == 0) {
+    kinv[(int64_t)bh * T + t] = ldexpf(1.0f, -sk);
+    vinv[(int64_t)bh * T + t] = ldexpf(1.0f, -sv);
+  }
+}
+
+}  // namespace sdpa
+
+struct SdpaCounters {
+  uint64_t calls = 0, enqueue_ns = 0, split_ns = 0, attn_ns = 0;
+};
+static SdpaCounters g_sdpa;
+
+static uint64_t now_ns() {
+  timespec ts;
+  clock_gettime(CLOCK_MONOTONIC, &ts);
+  return (uint64_t)ts.tv_sec * 1000000000ull + ts.tv_nsec;
+}
+
+// k/v element (bh, j, d) at base + bh*bh_stride + j*j_stride + d*d_stride
+static int sdpa_launch(const float* q, const float* k, const float* v, int64_t bh_stride,
+                       int64_t j_stride, int64_t d_stride, const float* bias,
+                       int64_t bias_bh_stride, float* out, int B, int H, int Lq, int Lk,
+                       int out_blhd) {
+  using namespace sdpa;
+  const uint64_t t0 = now_ns();
+  int st = entry_check();
+  if (st != kOk) return st;
+  if (!is_device_pointer(q) || !is_device_pointer(k) || !is_device_pointer(v) ||
+      !is_device_pointer(out) || (bias && !is_device_pointer(bias)))
+    return kNotDevicePointer;
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15) return kBadAlignment;
+  cudaStream_t stream = current_stream();
+  const int64_t BH = (int64_t)B * H;
+  const int T = (Lk + BKV - 1) / BKV;
+  const int Lkt = T * BKV;
+  const size_t qplane = (size_t)BH * Lq * D * 2;
+  const size_t kplane = (size_t)BH * Lkt * D * 2;
+  auto al = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+  const size_t off_qlo = al(qplane), off_qinv = off_qlo + al(qplane);
+  const size_t off_khi = off_qinv + al((size_t)BH * Lq * 4);
+  const size_t off_klo = off_khi + al(kplane), off_vhi = off_klo + al(kplane);
+  const size_t off_vlo = off_vhi + al(kplane), off_kinv = off_vlo + al(kplane);
+  const size_t off_vinv = off_kinv + al((size_t)BH * T * 4);
+  const size_t total = off_vinv + al((size_t)BH * T * 4);
+  uint8_t* ws = static_cast<uint8_t*>(workspace(total, stream));
+  if (!ws) return kWorkspace;
+  __half* qhi = reinterpret_cast<__half*>(ws);
+  __half* qlo = reinterpret_cast<__half*>(ws + off_qlo);
+  float* qinv = reinterpret_cast<float*>(ws + off_qinv);
+  __half* khi = reinterpret_cast<__half*>(ws + off_khi);
+  __half* klo = reinterpret_cast<__half*>(ws + off_klo);
+  __half* vhi = reinterpret_cast<__half*>(ws + off_vhi);
+  __half* vlo = reinterpret_cast<__half*>(ws + off_vlo);
+  float* kinv = reinterpret_cast<float*>(ws + off_kinv);
+  float* vinv = reinterpret_cast<float*>(ws + off_vinv);
+
+  const int64_t qrows = BH * Lq;
+  sdpa_split_q<<<(unsigned)((qrows + 7) / 8), 256, 0, stream>>>(q, qrows, qhi, qlo, qinv);
+  sdpa_split_kv<<<dim3(T, (unsigned)BH), 256, 0, stream>>>(k, v, bh_stride, j_stride, d_stride, Lk,
+                                                           Lkt, khi, klo, vhi, vlo, kinv, vinv);
+  if ((st = launch_status()) != kOk) return st;
+  const uint64_t t1 = now_ns();
+
+  CUtensorMap m_qhi, m_qlo, m_khi, m_klo, m_vhi, m_vlo;
+  const uint32_t box_rows[3] = {64, 128, 1};
+  const uint32_t box_vt[3] = {64, 64, 1};
+  {
+    const uint64_t dims[3] = {D, (uint64_t)Lq, (uint64_t)BH};
+    const uint64_t strides[2] = {D * 2, (uint64_t)Lq * D * 2};
+    if (!encode_tmap(&m_qhi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, qhi, dims, strides, box_rows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tmap(&m_qlo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, qlo, dims, strides, box_rows, CU_TENSOR_MAP_SWIZZLE_128B))
+      return kLaunchFailed;
+  }
+  {
+    const uint64_t dims[3] = {D, (uint64_t)Lkt, (uint64_t)BH};
+    const uint64_t strides[2] = {D * 2, (uint64_t)Lkt * D * 2};
+    if (!encode_tmap(&m_khi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, khi, dims, strides, box_rows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tmap(&m_klo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, klo, dims, strides, box_rows, CU_TENSOR_MAP_SWIZZLE_128B))
+      return kLaunchFailed;
+  }
+  {
+    const uint64_t dims[3] = {(uint64_t)Lkt, D, (uint64_t)BH};
+    const uint64_t strides[2] = {(uint64_t)Lkt * 2, (uint64_t)Lkt * D * 2};
+    if (!encode_tmap(&m_vhi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, vhi, dims, strides, box_vt, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tmap(&m_vlo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, vlo, dims, strides, box_vt, CU_TENSOR_MAP_SWIZZLE_128B))
+      return kLaunchFailed;
+  }
+  {
+    static uint64_t attr_done = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(attr_done >> dev & 1)) {
+      cudaFuncSetAttribute(sdpa_fwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+      attr_done |= 1ull << dev;
+    }
+  }
+  Params prm{qinv, kinv, vinv, bias, (long long)bias_bh_stride, out, H, Lq, Lk, T, out_blhd, device_status()};
+  dim3 grid((Lq + BQ - 1) / BQ, (unsigned)BH);
+  sdpa_fwd_tc<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(m_qhi, m_qlo, m_khi, m_klo, m_vhi, m_vlo, prm);
+  st = launch_status();
+  const uint64_t t2 = now_ns();
+  g_sdpa.calls += 1;
+  g_sdpa.split_ns += t1 - t0;
+  g_sdpa.attn_ns += t2 - t1;
+  return st;
+}
+
+}  // namespace tsb
+
+// ---------------------------------------------------------------------------
+// C-ABI.  Same names, argument lists and status codes as the reference SDPA
+// libraries; pointers are CUDA device pointers, `threads` is ignored, work is
+// queued on the stream set by triposplat_b200_set_stream.
+// ---------------------------------------------------------------------------
+extern "C" {
+
+// scripts/native_sdpa_avx512_exact_q8t512.c:137-166 (q/k/v/out [B,H,L,64]; bias [Lk] shared)
+int triposplat_sdpa_f32_avx512_exact_q8t512(const float* q, const float* k, const float* v,
+                                            const float* key_bias_or_null, float* out, int B,
+                                            int H, int Lq, int Lk, int D, int has_key_bias,
+                                            int key_bias_len, int threads) {
+  (void)threads;
+  if (!q || !k || !v || !out) return tsb::kNullPointer;
+  if (B <= 0 || H <= 0 || Lq <= 0 || Lk <= 0 || D != 64) return tsb::kBadDims;
+  if (has_key_bias && (!key_bias_or_null || key_bias_len != Lk)) return tsb::kBadRange;
+  return tsb::sdpa_launch(q, k, v, (int64_t)Lk * 64, 64, 1,
+                          has_key_bias ? key_bias_or_null : nullptr, 0, out, B, H, Lq, Lk, 0);
+}
+
+// scripts/native_sdpa_avx512_exact_q8t512.c:334-351 (alias)
+int triposplat_sdpa_f32(const float* q, const float* k, const float* v, const float* bias,
+                        float* out, int B, int H, int Lq, int Lk, int D, int has_key_bias,
+                        int key_bias_len, int threads) {
+  return triposplat_sdpa_f32_avx512_exact_q8t512(q, k, v, bias, out, B, H, Lq, Lk, D,
+                                                 has_key_bias, key_bias_len, threads);
+}
+
+// scripts/native_sdpa_avx512_exact_q8.c:52 (the strict-baseline kernel's symbol, same math)
+int triposplat_sdpa_f32_avx512_exact_q8(const float* q, const float* k, const float* v,
+                                        const float* bias, float* out, int B, int H, int Lq,
+                                        int Lk, int D, int has_key_bias, int key_bias_len,
+                                        int threads) {
+  return triposplat_sdpa_f32_avx512_exact_q8t512(q, k, v, bias, out, B, H, Lq, Lk, D,
+                                                 has_key_bias, key_bias_len, threads);
+}
+
+// scripts/native_sdpa_avx512_exact_q8t512_packed.c:3-21 (packed K/V [B,H,64,Lkp], out [B,Lq,H,64])
+int triposplat_sdpa_f32_avx512_exact_q8t512_packed_blhd(
+    const float* q, const float* packed_k, const float* packed_v, const float* key_bias_or_null,
+    float* out_blhd, int B, int H, int Lq, int Lk, int D, int Lkp, int has_key_bias,
+    int key_bias_len, int threads) {
+  (void)threads;
+  if (!q || !packed_k || !packed_v || !out_blhd) return tsb::kNullPointer;
+  if (B <= 0 || H <= 0 || Lq <= 0 || Lk <= 0 || D != 64 || Lkp < Lk || (Lkp & 15) != 0)
+    return tsb::kBadDims;
+  if (has_key_bias && (!key_bias_or_null || key_bias_len != Lk)) return tsb::kBadRange;
+  return tsb::sdpa_launch(q, packed_k, packed_v, (int64_t)64 * Lkp, 1, Lkp,
+                          has_key_bias ? key_bias_or_null : nullptr, 0, out_blhd, B, H, Lq, Lk, 1);
+}
+
+// scripts/native_sdpa_avx512_exact_q8t512_packed.c:160-162
+int triposplat_sdpa_packed_output_is_blhd(void) { return 1; }
+
+// No reference counterpart: per-(b,h) key bias [B*H, Lk] (bias_bh_stride elements apart,
+// 0 = one shared [Lk] row) and a choice of BHLD (0) or BLHD (1) output.
+int triposplat_sdpa_f32_cuda_bias_bh(const float* q, const float* k, const float* v,
+                                     const float* bias, long long bias_bh_stride, float* out,
+                                     int B, int H, int Lq, int Lk, int out_blhd) {
+  if (!q || !k || !v || !out) return tsb::kNullPointer;
+  if (B <= 0 || H <= 0 || Lq <= 0 || Lk <= 0 || bias_bh_stride < 0) return tsb::kBadDims;
+  if (bias && bias_bh_stride != 0 && bias_bh_stride < Lk) return tsb::kBadRange;
+  return tsb::sdpa_launch(q, k, v, (int64_t)Lk * 64, 64, 1, bias, bias_bh_stride, out, B, H, Lq,
+                          Lk, out_blhd ? 1 : 0);
+}
+
+// scripts/native_sdpa_avx512_exact_q8t512.c:64-70: tile sizes of this implementation
+int triposplat_sdpa_key_tile(void) { return tsb::sdpa::BKV; }
+int triposplat_sdpa_query_block(void) { return tsb::sdpa::BQ; }
+
+// scripts/native_sdpa_avx512_exact_q8t512.c:77-100.  On the GPU the call is asynchronous:
+// allocate_ns is 0, pack_ns is the host time to validate and enqueue the split kernels,
+// compute_ns the host time to encode and enqueue the attention kernel, free_ns is 0.
+void triposplat_sdpa_q8t512_profile_reset(void) { tsb::g_sdpa = tsb::SdpaCounters(); }
+
+int triposplat_sdpa_q8t512_profile_get(uint64_t* calls, uint64_t* allocate_ns, uint64_t* pack_ns,
+                                       uint64_t* compute_ns, uint64_t* free_ns) {
+  if (!calls || !allocate_ns || !pack_ns || !compute_ns || !free_ns) return tsb::kNullPointer;
+  *calls = tsb::g_sdpa.calls;
+  *allocate_ns = 0;
+  *pack_ns = tsb::g_sdpa.split_ns;
+  *compute_ns = tsb::g_sdpa.attn_ns;
+  *free_ns = 0;
+  return 0;
+}
+
+// scripts/native_sdpa_avx512_exact_q8t512.c:51-62 -> the library-wide workspace
+int triposplat_b200_workspace_stats(uint64_t* allocations, uint64_t* capacity_bytes);
+void triposplat_b200_workspace_release(void);
+
+int triposplat_sdpa_q8t512_workspace_stats(uint64_t* allocations, uint64_t* capacity_bytes) {
+  return triposplat_b200_workspace_stats(allocations, capacity_bytes);
+}
+
+void triposplat_sdpa_q8t512_workspace_release(void) { triposplat_b200_workspace_release(); }
+
+}  // extern "C"
