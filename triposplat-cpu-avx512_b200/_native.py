@@ -37,6 +37,19 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "triposplat_gemm_rnf8_avx512_tail": ([VP] * 10 + [I] * 7, I),
     "triposplat_gemm_rnf8_avx512_row_tile": ([], I),
     "triposplat_gemm_rnf8_avx512_residual_mode": ([], I),
+    # exact SDPA
+    "triposplat_sdpa_f32_avx512_exact_q8t512": ([VP] * 5 + [I] * 8, I),
+    "triposplat_sdpa_f32_avx512_exact_q8": ([VP] * 5 + [I] * 8, I),
+    "triposplat_sdpa_f32": ([VP] * 5 + [I] * 8, I),
+    "triposplat_sdpa_f32_avx512_exact_q8t512_packed_blhd": ([VP] * 5 + [I] * 9, I),
+    "triposplat_sdpa_f32_cuda_bias_bh": ([VP] * 4 + [ctypes.c_longlong, VP] + [I] * 5, I),
+    "triposplat_sdpa_packed_output_is_blhd": ([], I),
+    "triposplat_sdpa_key_tile": ([], I),
+    "triposplat_sdpa_query_block": ([], I),
+    "triposplat_sdpa_q8t512_profile_reset": ([], None),
+    "triposplat_sdpa_q8t512_profile_get": ([U64P] * 5, I),
+    "triposplat_sdpa_q8t512_workspace_stats": ([U64P, U64P], I),
+    "triposplat_sdpa_q8t512_workspace_release": ([], None),
 }
 
 

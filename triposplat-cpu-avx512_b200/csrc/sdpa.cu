@@ -40,7 +40,7 @@ constexpr int TMEM_COLS = 256;
 constexpr int S_COL = 0;
 constexpr int O_COL = 128;
 constexpr int PLANE = 128 * D * 2;  // 16 KB: one 128 x 64 fp16 tile
-constexpr int SMEM_BYTES = 1024 + 6 * PLANE + 2 * BKV * 4 + 32 * 8 + 16;
+constexpr int SMEM_BYTES = 1024 + 6 * PLANE + 4 * BKV * 4 + 32 * 8 + 16;
 constexpr float LOG2E = 1.4426950408889634f;
 
 struct Params {
@@ -61,10 +61,6 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-__device__ __forceinline__ void named_bar_sync(int id, int count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
 __global__ void __launch_bounds__(NUM_THREADS, 2)
     sdpa_fwd_tc(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant__ CUtensorMap tm_qlo,
                 const __grid_constant__ CUtensorMap tm_khi, const __grid_constant__ CUtensorMap tm_klo,
@@ -79,8 +75,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
   uint8_t* k_lo = k_hi + PLANE;
   uint8_t* v_hi = k_lo + PLANE;  // two [64 dims x 64 keys] swizzled blocks
   uint8_t* v_lo = v_hi + PLANE;
-  float* bias_s = reinterpret_cast<float*>(v_lo + PLANE);  // [2][BKV], log2 units
-  uint64_t* bars = reinterpret_cast<uint64_t*>(bias_s + 2 * BKV);
+  float* bias_s = reinterpret_cast<float*>(v_lo + PLANE);  // [4 warps][BKV], log2 units
+  uint64_t* bars = reinterpret_cast<uint64_t*>(bias_s + 4 * BKV);
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;
   uint64_t* k_empty = bars + 2;
@@ -101,10 +97,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
   const int T = p.T;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 12; ++i) mbar_init(&bars[i], 1);
-    mbar_init(p_full, 4);
+    for (int i = 0; i < 6; ++i) mbar_init(&bars[i], 1);  // q/k/v full+empty, s_full
+    mbar_init(p_full, 4);                                 // one arrival per softmax warp
+    mbar_init(&o_full[0], 1);
+    mbar_init(&o_full[1], 1);
     mbar_init(&o_free[0], 4);
     mbar_init(&o_free[1], 4);
+    mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -202,7 +201,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     // ---------------- softmax, merge, epilogue ----------------
     const uint32_t sub = warp & 3;
     const int r = sub * 32 + lane;  // query row within the tile == TMEM lane
-    const int tid = threadIdx.x - 64;
     const uint32_t lane_base = (sub * 32) << 16;
     const int qrow = q0 + r;
     const bool row_valid = qrow < p.Lq;
@@ -214,14 +212,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     float m_run = -INFINITY, l_run = 0.0f, alpha_prev = 0.0f;
     bool ok = true;
     for (int t = 0; t < T; ++t) {
-      {
-        const int j = t * BKV + tid;
+      // key bias (+ -inf past Lk) for this tile, staged in a warp-private buffer so no
+      // cross-warp barrier is needed (a warp may leave the loop early on an error)
+      float* bt = bias_s + sub * BKV;
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < BKV / 32; ++i) {
+        const int jl = i * 32 + lane;
+        const int j = t * BKV + jl;
         float b = -INFINITY;
         if (j < p.Lk) b = bias_row ? bias_row[j] * LOG2E : 0.0f;
-        bias_s[(t & 1) * BKV + tid] = b;
+        bt[jl] = b;
       }
-      named_bar_sync(1, 128);
-      const float* bt = bias_s + (t & 1) * BKV;
+      __syncwarp();
       ok = mbar_wait(s_full, t & 1, p.status, kDevTimeoutConsumer, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
