@@ -1,0 +1,179 @@
+/*
+ * triposplat_b200.h — C ABI of libtriposplat_b200.so, the B200 (sm_100a) implementation of
+ * the TripoSplat flow-model hot path: NF24 int16 dequant GEMM, exact SDPA, and the
+ * prologue / epilogue kernels around them.
+ *
+ * Drop-in contract.  Every function below that cites a reference file keeps that
+ * function's name, argument list, argument meaning and status codes, so the reference's
+ * ctypes bindings (scripts/native_linear_rnf8_avx512_patch.py:201-210,
+ * scripts/native_sdpa_ctypes.py:14-20, the norm/GELU/SiLU/block/sampler patches) bind this
+ * library unchanged.  Differences, all deliberate:
+ *   - every float / code pointer is a CUDA device pointer (device, managed or mapped
+ *     memory); a host-only pointer returns -9 instead of being dereferenced;
+ *   - work is queued asynchronously on the calling thread's stream
+ *     (triposplat_b200_set_stream, default: the legacy default stream); the call returns
+ *     once the work is enqueued;
+ *   - the trailing `threads` argument is accepted and ignored.
+ *
+ * Status codes: 0 ok; -1 null pointer; -2 bad dimension / stages; -3 bad range / bias
+ * length; -4 alignment (range start/count not a multiple of 16, or an unaligned q/out
+ * pointer for SDPA); -5 workspace allocation failed; -9 pointer not device-accessible;
+ * -10 kernel launch failed; -11 an earlier kernel of this library gave up on a bounded
+ * wait (see triposplat_b200_status); -12 no usable CUDA device.
+ */
+#ifndef TRIPOSPLAT_B200_H
+#define TRIPOSPLAT_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- runtime controls --
+ * No reference counterpart: the CPU library has no streams and a thread-local workspace. */
+
+/* Stream (cudaStream_t) used by this thread's subsequent calls; NULL = legacy default. */
+void triposplat_b200_set_stream(void* stream);
+void* triposplat_b200_get_stream(void);
+/* Non-zero once a kernel of this library recorded a bounded-wait timeout (host-mapped
+ * status word, readable without synchronising); entry points then return -11. */
+int triposplat_b200_status(void);
+void triposplat_b200_clear_status(void);
+/* Pre-size the library workspace of the current (device, stream), e.g. before capturing
+ * the calls into a CUDA graph, so no call grows it later. */
+int triposplat_b200_workspace_reserve(uint64_t bytes);
+int triposplat_b200_workspace_stats(uint64_t* allocations, uint64_t* capacity_bytes);
+void triposplat_b200_workspace_release(void);
+int triposplat_b200_abi_version(void);
+
+/* ---------------------------------------------------------------- NF24 GEMM ----------
+ * Y[M, N] = X[M, K] . W + bias,  W[k, n] = scale[n] * (256*q01[k, n] + q2[k, n]).
+ * For NF24: codes0_t = int16 q01 [K, N]; codes1_t = codes2_t = int8 q2 [K, N];
+ * scales0 = scales1 = scales2 = scale [N]; codebook is not read (any non-null pointer);
+ * stages must be 3.  X fp32 with row stride stride_x; out fp32 with row stride stride_out. */
+
+/* replaces scripts/gemm_nf24_i16_avx512.c:199-220 */
+int triposplat_gemm_rnf8_avx512(const float* x, const uint8_t* codes0_t, const uint8_t* codes1_t,
+                                const uint8_t* codes2_t, const float* scales0,
+                                const float* scales1, const float* scales2,
+                                const float* codebook, const float* bias, float* out, int M,
+                                int K, int N, int stride_x, int stride_out, int threads,
+                                int stages);
+
+/* replaces scripts/gemm_nf24_i16_avx512.c:151-197; out is [M, output_count] */
+int triposplat_gemm_rnf8_avx512_range(const float* x, const uint8_t* codes0_t,
+                                      const uint8_t* codes1_t, const uint8_t* codes2_t,
+                                      const float* scales0, const float* scales1,
+                                      const float* scales2, const float* codebook,
+                                      const float* bias, float* out, int M, int K, int N,
+                                      int output_start, int output_count, int stride_x,
+                                      int stride_out, int threads, int stages);
+
+/* replaces scripts/gemm_nf24_i16_avx512_tail.c:8-49 (any N; reference operation order) */
+int triposplat_gemm_rnf8_avx512_tail(const float* x, const uint8_t* codes0_t,
+                                     const uint8_t* codes1_t, const uint8_t* codes2_t,
+                                     const float* scales0, const float* scales1,
+                                     const float* scales2, const float* codebook,
+                                     const float* bias, float* out, int M, int K, int N,
+                                     int stride_x, int stride_out, int threads, int stages);
+
+/* replaces scripts/gemm_nf24_i16_avx512.c:222-224 (rows per CTA tile here) */
+int triposplat_gemm_rnf8_avx512_row_tile(void);
+/* replaces scripts/gemm_nf24_i16_avx512.c:226-228; returns 4 (= nf24_i16) */
+int triposplat_gemm_rnf8_avx512_residual_mode(void);
+
+/* ---------------------------------------------------------------- exact SDPA ---------
+ * O = softmax(0.125 * Q K^T + key_bias) V, head_dim 64, q/k/v/out [B, H, L, 64] fp32. */
+
+/* replaces scripts/native_sdpa_avx512_exact_q8t512.c:137-332; key bias [Lk] shared by all (b,h) */
+int triposplat_sdpa_f32_avx512_exact_q8t512(const float* q, const float* k, const float* v,
+                                            const float* key_bias_or_null, float* out, int B,
+                                            int H, int Lq, int Lk, int D, int has_key_bias,
+                                            int key_bias_len, int threads);
+/* replaces scripts/native_sdpa_avx512_exact_q8t512.c:334-351 (alias) */
+int triposplat_sdpa_f32(const float* q, const float* k, const float* v, const float* bias,
+                        float* out, int B, int H, int Lq, int Lk, int D, int has_key_bias,
+                        int key_bias_len, int threads);
+/* replaces scripts/native_sdpa_avx512_exact_q8.c:52 (same mathematics) */
+int triposplat_sdpa_f32_avx512_exact_q8(const float* q, const float* k, const float* v,
+                                        const float* bias, float* out, int B, int H, int Lq,
+                                        int Lk, int D, int has_key_bias, int key_bias_len,
+                                        int threads);
+/* replaces scripts/native_sdpa_avx512_exact_q8t512_packed.c:3-158:
+ * packed K/V [B, H, 64, Lkp] (Lkp >= Lk, Lkp % 16 == 0), output [B, Lq, H, 64] */
+int triposplat_sdpa_f32_avx512_exact_q8t512_packed_blhd(
+    const float* q, const float* packed_k, const float* packed_v, const float* key_bias_or_null,
+    float* out_blhd, int B, int H, int Lq, int Lk, int D, int Lkp, int has_key_bias,
+    int key_bias_len, int threads);
+/* replaces scripts/native_sdpa_avx512_exact_q8t512_packed.c:160-162; returns 1 */
+int triposplat_sdpa_packed_output_is_blhd(void);
+/* No reference counterpart: per-(b,h) key bias rows bias_bh_stride elements apart
+ * (0 = one shared [Lk] row, NULL = no bias) and BHLD (0) / BLHD (1) output. */
+int triposplat_sdpa_f32_cuda_bias_bh(const float* q, const float* k, const float* v,
+                                     const float* bias, long long bias_bh_stride, float* out,
+                                     int B, int H, int Lq, int Lk, int out_blhd);
+/* replace scripts/native_sdpa_avx512_exact_q8t512.c:64-70 (tile sizes used here) */
+int triposplat_sdpa_key_tile(void);
+int triposplat_sdpa_query_block(void);
+/* replace scripts/native_sdpa_avx512_exact_q8t512.c:77-100; GPU timings are host enqueue
+ * times (pack_ns = split kernels, compute_ns = attention kernel), allocate/free are 0 */
+void triposplat_sdpa_q8t512_profile_reset(void);
+int triposplat_sdpa_q8t512_profile_get(uint64_t* calls, uint64_t* allocate_ns, uint64_t* pack_ns,
+                                       uint64_t* compute_ns, uint64_t* free_ns);
+/* replace scripts/native_sdpa_avx512_exact_q8t512.c:51-62 (library-wide workspace) */
+int triposplat_sdpa_q8t512_workspace_stats(uint64_t* allocations, uint64_t* capacity_bytes);
+void triposplat_sdpa_q8t512_workspace_release(void);
+
+/* ---------------------------------------------------------------- prologue / epilogue - */
+
+/* replaces scripts/native_norm_rope_avx512.c:13-49 */
+int triposplat_layernorm_f32_avx512(const float* input, const float* weight, const float* bias,
+                                    float* output, int64_t rows, int cols, float eps,
+                                    int has_affine, int threads);
+/* replaces scripts/native_norm_rope_avx512.c:51-83 */
+int triposplat_multihead_rmsnorm_f32_avx512(const float* input, const float* gamma, float* output,
+                                            int64_t outer, int heads, int dim, float eps,
+                                            int threads);
+/* replaces scripts/native_norm_rope_avx512.c:85-110 */
+int triposplat_rope_complex_f32_avx512(const float* input, const float* freqs_interleaved,
+                                       float* output, int64_t vectors, int dim, int threads);
+/* replaces scripts/native_gelu_avx512.c:44-68 */
+int triposplat_gelu_tanh_f32_avx512(const float* input, float* output, int64_t count, int threads);
+/* replaces scripts/native_silu_avx512_extra.c:28-45 */
+int triposplat_silu_f32_avx512(const float* input, float* output, int64_t count, int threads);
+/* replaces scripts/native_block_elementwise_avx512.c:9-22 */
+int triposplat_modulate_inplace_f32_avx512(float* h, const float* scale, const float* shift,
+                                           int batch, int rows, int cols, int threads);
+/* replaces scripts/native_block_elementwise_avx512.c:24-35 */
+int triposplat_gated_residual_inplace_f32_avx512(float* base, float* delta, const float* gate,
+                                                 int batch, int rows, int cols, int threads);
+/* replaces scripts/native_block_elementwise_avx512.c:37-46 */
+int triposplat_add_inplace_f32_avx512(float* base, const float* delta, int64_t count, int threads);
+/* replaces scripts/native_sampler_avx512.c:19-54 */
+int triposplat_cfg_combine_inplace_f32_avx512(float* positive, const float* negative,
+                                              const float* guidance, int batch,
+                                              int64_t elements_per_batch, int threads);
+/* replaces scripts/native_sampler_avx512.c:56-89 */
+int triposplat_euler_update_inplace_f32_avx512(float* sample, const float* prediction,
+                                               const float* dt, int batch,
+                                               int64_t elements_per_batch, int threads);
+/* replaces scripts/native_qkv_postprocess_v2_avx512.c:45-105 */
+int triposplat_qkv_rope_rmsnorm_pack_f32_avx512_v2(const float* qkv, const float* frequencies,
+                                                   const float* q_gamma, const float* k_gamma,
+                                                   float* q_bhld, float* packed_k,
+                                                   float* packed_v, int B, int L, int H, int D,
+                                                   int L_padded, int frequency_batches,
+                                                   int threads);
+/* replaces scripts/native_qkv_postprocess_v2_avx512.c:107-191 (selected_indices is a
+ * device pointer; it is copied back once to validate it as the reference does) */
+int triposplat_q_kv_selected_rope_rmsnorm_pack_f32_avx512_v2(
+    const float* q, const float* kv, const float* frequencies, const int64_t* selected_indices,
+    const float* q_gamma, const float* k_gamma, float* q_bhld, float* packed_k, float* packed_v,
+    int B, int Lq, int Lk, int H, int D, int Lk_padded, int frequency_batches, int threads);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TRIPOSPLAT_B200_H */

@@ -50,6 +50,19 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "triposplat_sdpa_q8t512_profile_get": ([U64P] * 5, I),
     "triposplat_sdpa_q8t512_workspace_stats": ([U64P, U64P], I),
     "triposplat_sdpa_q8t512_workspace_release": ([], None),
+    # prologue / epilogue kernels
+    "triposplat_layernorm_f32_avx512": ([VP] * 4 + [I64, I, F, I, I], I),
+    "triposplat_multihead_rmsnorm_f32_avx512": ([VP] * 3 + [I64, I, I, F, I], I),
+    "triposplat_rope_complex_f32_avx512": ([VP] * 3 + [I64, I, I], I),
+    "triposplat_gelu_tanh_f32_avx512": ([VP] * 2 + [I64, I], I),
+    "triposplat_silu_f32_avx512": ([VP] * 2 + [I64, I], I),
+    "triposplat_modulate_inplace_f32_avx512": ([VP] * 3 + [I] * 4, I),
+    "triposplat_gated_residual_inplace_f32_avx512": ([VP] * 3 + [I] * 4, I),
+    "triposplat_add_inplace_f32_avx512": ([VP] * 2 + [I64, I], I),
+    "triposplat_cfg_combine_inplace_f32_avx512": ([VP] * 3 + [I, I64, I], I),
+    "triposplat_euler_update_inplace_f32_avx512": ([VP] * 3 + [I, I64, I], I),
+    "triposplat_qkv_rope_rmsnorm_pack_f32_avx512_v2": ([VP] * 7 + [I] * 7, I),
+    "triposplat_q_kv_selected_rope_rmsnorm_pack_f32_avx512_v2": ([VP] * 9 + [I] * 8, I),
 }
 
 
