@@ -1,0 +1,330 @@
+#!/usr/bin/env python3
+"""Benchmark: s20 CFG flow sampling of the synthetic 28-block NF24 flow model on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+A step is one CFG sampler step (one forward of the batch-2 [cond, uncond] pair through
+28 blocks and 206 NF24 Linears, then CFG combine + Euler update) for one image per GPU.
+Multi-GPU (torchrun, one process per GPU): every rank samples its own image (weak
+scaling, replicas; no collective on the data path); timing is the max over ranks.
+
+Reported metric: seconds per image for 20-step sampling (lower is better), whole job:
+value = (max-over-ranks time of K steps) / K * 20 / N.  Also reported: the end-to-end
+number through the public sampler API with host buffers (H2D of each step's inputs, D2H
+of its result), the roofline of the dominant kernel (the attention kernel), per-kernel
+device time, and, on rank 0 at N=1, the reference CPU path timed on this host.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+PKG = REPO / "triposplat-cpu-avx512_b200"
+sys.path[:0] = [str(PKG), str(REPO / "oracle")]
+
+METRIC = "s20 CFG sampling sec/image; NF24 GEMM & exact-SDPA TFLOP/s vs roofline"
+UNIT = "s/image"
+SAMPLER_STEPS = 20
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.is_file():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+def profiled_traffic():
+    """DRAM bytes per attention launch from the committed ncu summary, if present."""
+    f = REPO / "profiles" / "sdpa_fwd_tc_config2a.md"
+    if not f.is_file():
+        return None
+    for line in f.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_full_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str):
+        self.uuid = uuid
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.uuid, f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.rows = []
+        if self.proc is None:
+            return False
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        for line in out.splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 8:
+                self.rows.append(parts)
+        return False
+
+    def summary(self):
+        rows = getattr(self, "rows", [])
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in rows for n, v in zip(names, r[4:8]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows),
+                "power_w_max": max((float(r[2]) for r in rows if r[2].replace(".", "").isdigit()), default=None)}
+
+
+def cpu_baseline(spec, seconds):
+    import cpu_block
+
+    try:
+        r = cpu_block.time_sample(spec, min_seconds=seconds, max_reps=3)
+    except Exception as exc:  # noqa: BLE001 - reported, not fatal
+        return {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "unavailable",
+                "sample": f"reference CPU block could not run: {exc}"}
+    return {"value": round(r["sec_per_image"], 2), "unit": UNIT, "cores": r["threads"], "kind": r["kind"],
+            "sample": (f"one full-size block of the CFG-pair forward (B=2, L=8193, 1374 cond tokens) "
+                       f"through the reference's AVX-512 kernels, median of {r['reps']} runs = "
+                       f"{r['block_seconds']:.3f} s; sec/image = 20 steps x forward/block flops "
+                       f"({r['block_flops'] / 1e12:.3f} TFLOP per block)")}
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU kernels on the host cores, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from flow_model import FlowSpec
+    import cpu_block
+
+    spec = FlowSpec()
+    if not cpu_block._RefKernels.available():
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "reference AVX-512 kernels not built or host CPU lacks AVX-512"}))
+        return 0
+    blk = cpu_block.CpuBlock(spec)
+    for _ in range(max(0, min(args.warmup, 1))):
+        blk.run()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        blk.run()
+        times.append(time.perf_counter() - t0)
+    t_block = sum(times) / len(times)
+    value = cpu_block.sec_per_image_from_block(spec, t_block, blk.block_flops())
+    sample = (f"each step = one full-size block of the CFG-pair forward (B=2, L=8193) through "
+              f"the reference's AVX-512 kernels; sec/image = 20 x forward/block flops x mean block time")
+    line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t_block * 1e3, 3), "higher_is_better": False, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "s20 CFG flow sampling, synthetic 28-block NF24 flow model",
+                       "parallelism": "host CPU (OpenMP)"},
+            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": blk.th,
+                             "kind": "reference", "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+
+    import _native
+    from flow_model import CfgEulerSampler, FlowModelB200, FlowSpec, make_weights
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    spec = FlowSpec()
+    lib = _native.load()
+    weights = make_weights(spec, seed=0, device=str(dev))
+    model = FlowModelB200(weights, device=str(dev))
+    sampler = CfgEulerSampler(model, steps=SAMPLER_STEPS, guidance=3.0, shift=3.0)
+
+    # per-rank image: seeded inputs in pinned host memory (also the e2e source buffers)
+    g = torch.Generator().manual_seed(1000 + rank)
+    h_lat = torch.randn(1, spec.latent_tokens, spec.latent_dim, generator=g).pin_memory()
+    h_cam = torch.randn(1, 1, spec.camera_dim, generator=g).pin_memory()
+    h_cond = torch.randn(1, spec.cond_tokens, spec.cond_dim, generator=g).pin_memory()
+    h_neg = torch.zeros(1, spec.cond_tokens, spec.cond_dim).pin_memory()
+    h_out_lat = torch.empty(spec.latent_tokens, spec.latent_dim).pin_memory()
+    h_out_cam = torch.empty(1, spec.camera_dim).pin_memory()
+    sampler.load(h_lat.to(dev), h_cam.to(dev), h_cond.to(dev), h_neg.to(dev))
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- warm-up (untimed)
+    for i in range(args.warmup):
+        sampler.step(i % SAMPLER_STEPS)
+    torch.cuda.synchronize()
+    _native.check_status(lib)
+
+    # ---- timed region: K sampler steps, inputs resident in HBM
+    uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    launches0 = int(lib.triposplat_b200_launch_count())
+    lib.triposplat_b200_profile_enable(1)
+    with ClockSampler(uuid) as clk:
+        start.record()
+        for i in range(args.steps):
+            sampler.step((args.warmup + i) % SAMPLER_STEPS)
+        stop.record()
+        torch.cuda.synchronize()
+    lib.triposplat_b200_profile_enable(0)
+    barrier()
+    launches = int(lib.triposplat_b200_launch_count()) - launches0
+    prof = _native.profile_collect(lib)
+    ms_total = max_over_ranks(start.elapsed_time(stop))
+    _native.check_status(lib)
+
+    # ---- end-to-end through the public sampler API with host buffers
+    h2d = sum(t.numel() * 4 for t in (h_lat, h_cam, h_cond, h_neg))
+    d2h = (h_out_lat.numel() + h_out_cam.numel()) * 4
+    barrier()
+    torch.cuda.synchronize()
+    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    for i in range(args.steps):
+        sampler.load(h_lat, h_cam, h_cond, h_neg)  # H2D from pinned host memory
+        sampler.step((args.warmup + i) % SAMPLER_STEPS)
+        h_out_lat.copy_(sampler.x_lat[0], non_blocking=True)
+        h_out_cam.copy_(sampler.x_cam[0], non_blocking=True)
+    e_stop.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e_start.elapsed_time(e_stop))
+    finite = bool(torch.isfinite(h_out_lat).all()) and bool(torch.isfinite(h_out_cam).all())
+
+    # ---- report
+    ms_step = ms_total / args.steps
+    value = ms_step / 1e3 * SAMPLER_STEPS / world
+    e2e_value = e2e_ms / args.steps / 1e3 * SAMPLER_STEPS / world
+    flops = spec.flops_per_forward(batch=2)
+    peaks, peak_src = load_peaks()
+    attn = prof["sdpa_attn"]
+    L, Mc, BH = spec.seq, spec.cond_tokens, 2 * spec.heads
+    attn_flops_per_step = spec.blocks * 4.0 * BH * L * (L + Mc) * spec.head_dim
+    achieved = None
+    if attn["launches"]:
+        launches_per_step = attn["launches"] / args.steps
+        achieved = attn_flops_per_step / launches_per_step / (attn["ms"] / attn["launches"] / 1e3) / 1e12
+    peak = float(peaks.get("bf16_tflops_sustained") or peaks["bf16_tflops"])
+    traffic_full = profiled_traffic()
+    kernels = {k: {"launches_per_step": round(v["launches"] / args.steps, 2),
+                   "ms_per_step": round(v["ms"] / args.steps, 3),
+                   "share": round(v["ms"] / max(1e-9, sum(x["ms"] for x in prof.values())), 4)}
+               for k, v in prof.items()}
+    gemm = prof["gemm_tc"]
+    line = {
+        "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded Gaussian latent/camera/condition; random-init weights packed to NF24)",
+        "config": {"workload": "s20 CFG flow sampling, synthetic 28-block NF24 flow model (BASELINE config 5)",
+                   "blocks": spec.blocks, "linears": len(spec.linears()), "hidden": spec.hidden,
+                   "heads": spec.heads, "mlp": spec.mlp, "latent_tokens": spec.latent_tokens,
+                   "seq": spec.seq, "cond_tokens": Mc, "sampler_steps": SAMPLER_STEPS,
+                   "guidance": 3.0, "shift": 3.0, "global_batch": f"{world} image(s) x CFG pair",
+                   "parallelism": f"replicas x{world} (one image per GPU, no data-path collective)",
+                   "l2": "no flush: every step streams 1.4 GB of NF24 weights and ~1 GB of "
+                         "activations, far above the 126 MB L2"},
+        "tflops_logical_per_gpu": round(flops["total"] / (ms_step / 1e3) / 1e12, 1),
+        "roofline": {"kernel": "sdpa_fwd_tc (exact SDPA, self + cross)", "bound": "tensor",
+                     "achieved": None if achieved is None else round(achieved, 1),
+                     "peak": peak, "unit": "TFLOP/s",
+                     "frac": None if achieved is None else round(achieved / peak, 4),
+                     "peak_source": f"bf16_tflops_sustained, {peak_src}",
+                     "flops": "algorithmic 4*B*H*Lq*Lk*64 per launch (3 split-fp16 tensor passes each)",
+                     "tensor_pipe_frac": None if achieved is None else round(3 * achieved / peak, 4),
+                     "traffic": traffic_full},
+        "gemm": {"kernel": "nf24_gemm_tc", "launches_per_step": round(gemm["launches"] / args.steps, 1),
+                 "ms_per_step": round(gemm["ms"] / args.steps, 3),
+                 "achieved_tflops_logical": round(flops["gemm"] / (gemm["ms"] / args.steps / 1e3) / 1e12, 1)
+                 if gemm["ms"] else None},
+        "kernels": kernels,
+        "gpu_launches": launches,
+        "clocks": clk.summary(),
+        "e2e": {"value": round(e2e_value, 4), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "finite": finite,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(spec, args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

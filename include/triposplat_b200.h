@@ -46,6 +46,14 @@ int triposplat_b200_workspace_reserve(uint64_t bytes);
 int triposplat_b200_workspace_stats(uint64_t* allocations, uint64_t* capacity_bytes);
 void triposplat_b200_workspace_release(void);
 int triposplat_b200_abi_version(void);
+/* Number of kernels this library has launched in this process (all devices). */
+uint64_t triposplat_b200_launch_count(void);
+/* While enabled, every launch is bracketed by CUDA events on its stream. */
+void triposplat_b200_profile_enable(int on);
+/* Waits for the bracketed launches recorded so far and returns, per kernel family
+ * (0 GEMM tensor-core, 1 GEMM activation split, 2 GEMM scalar tail, 3 SDPA attention,
+ * 4 SDPA split, 5 elementwise; n entries), the launch count and summed device ms. */
+int triposplat_b200_profile_collect(uint64_t* launches, double* total_ms, int n);
 
 /* ---------------------------------------------------------------- NF24 GEMM ----------
  * Y[M, N] = X[M, K] . W + bias,  W[k, n] = scale[n] * (256*q01[k, n] + q2[k, n]).
@@ -171,6 +179,17 @@ int triposplat_q_kv_selected_rope_rmsnorm_pack_f32_avx512_v2(
     const float* q, const float* kv, const float* frequencies, const int64_t* selected_indices,
     const float* q_gamma, const float* k_gamma, float* q_bhld, float* packed_k, float* packed_v,
     int B, int Lq, int Lk, int H, int D, int Lk_padded, int frequency_batches, int threads);
+/* replaces scripts/native_embeddings_avx512.c:97-125: out[b] = [cos(t_b f) | sin(t_b f) | 0] */
+int triposplat_timestep_embedding_f32_avx512(const float* timesteps, const float* frequencies,
+                                             float* output, int batch, int half_dim,
+                                             int output_dim, int threads);
+/* No reference counterpart: the selected-query post-process without RoPE or an index list
+ * (cross-attention: condition tokens carry no position).  q [B,Lq,H,64], kv [B,Lk,2,H,64]
+ * -> q_bhld [B,H,Lq,64], packed k/v [B,H,64,Lk_padded]; k and q get 8/max(||x||,1e-12)*gamma. */
+int triposplat_b200_q_kv_rmsnorm_pack_f32(const float* q, const float* kv, const float* q_gamma,
+                                          const float* k_gamma, float* q_bhld, float* packed_k,
+                                          float* packed_v, int B, int Lq, int Lk, int H,
+                                          int Lk_padded);
 
 #ifdef __cplusplus
 }

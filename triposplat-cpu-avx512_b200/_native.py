@@ -31,6 +31,9 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "triposplat_b200_workspace_stats": ([U64P, U64P], I),
     "triposplat_b200_workspace_release": ([], None),
     "triposplat_b200_abi_version": ([], I),
+    "triposplat_b200_launch_count": ([], ctypes.c_uint64),
+    "triposplat_b200_profile_enable": ([I], None),
+    "triposplat_b200_profile_collect": ([U64P, ctypes.POINTER(ctypes.c_double), I], I),
     # NF24 GEMM
     "triposplat_gemm_rnf8_avx512": ([VP] * 10 + [I] * 7, I),
     "triposplat_gemm_rnf8_avx512_range": ([VP] * 10 + [I] * 9, I),
@@ -63,6 +66,8 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "triposplat_euler_update_inplace_f32_avx512": ([VP] * 3 + [I, I64, I], I),
     "triposplat_qkv_rope_rmsnorm_pack_f32_avx512_v2": ([VP] * 7 + [I] * 7, I),
     "triposplat_q_kv_selected_rope_rmsnorm_pack_f32_avx512_v2": ([VP] * 9 + [I] * 8, I),
+    "triposplat_b200_q_kv_rmsnorm_pack_f32": ([VP] * 7 + [I] * 5, I),
+    "triposplat_timestep_embedding_f32_avx512": ([VP] * 3 + [I] * 4, I),
 }
 
 
@@ -122,3 +127,16 @@ def require_cuda(*tensors, what: str = "tensor") -> None:
             raise ValueError(f"{what} must be contiguous")
     if not torch.cuda.is_available():
         raise RuntimeError("no CUDA device")
+
+
+KERNEL_FAMILIES = ("gemm_tc", "gemm_split", "gemm_simt", "sdpa_attn", "sdpa_split", "elementwise")
+
+
+def profile_collect(lib) -> dict:
+    n = len(KERNEL_FAMILIES)
+    launches = (ctypes.c_uint64 * n)()
+    ms = (ctypes.c_double * n)()
+    st = lib.triposplat_b200_profile_collect(launches, ms, n)
+    if st != 0:
+        raise RuntimeError(f"profile_collect returned {st}")
+    return {k: {"launches": int(launches[i]), "ms": float(ms[i])} for i, k in enumerate(KERNEL_FAMILIES)}

@@ -181,7 +181,7 @@ __global__ void __launch_bounds__(256) qkv_post_k(
       const int t = t0 + i;
       float2 ky = make_float2(0.0f, 0.0f), vy = make_float2(0.0f, 0.0f);
       if (t < Lk) {
-        const float* f = freqs + (((int64_t)fbb * Lk + t) * H + h) * 64;
+        const float* f = freqs ? freqs + (((int64_t)fbb * Lk + t) * H + h) * 64 : nullptr;
         const float* ks;
         const float* vs;
         if (kSelected) {  // kv [B, Lk, 2, H, 64]
@@ -195,7 +195,7 @@ __global__ void __launch_bounds__(256) qkv_post_k(
           reinterpret_cast<float2*>(q_bhld + ((int64_t)bh * Lq + t) * 64)[lane] = qy;
         }
         ky = rope_rms64(reinterpret_cast<const float2*>(ks)[lane],
-                        reinterpret_cast<const float2*>(f)[lane], gk);
+                        f ? reinterpret_cast<const float2*>(f)[lane] : make_float2(1.0f, 0.0f), gk);
         vy = reinterpret_cast<const float2*>(vs)[lane];
       }
       kt[2 * lane][i] = ky.x;
@@ -217,12 +217,27 @@ __global__ void __launch_bounds__(256) qkv_post_k(
     for (int i = warp; i < 64; i += 8) {
       const int qi = tile * 64 + i;
       if (qi >= Lq) break;
-      const int64_t key = sel[qi];
-      const float* f = freqs + (((int64_t)fbb * Lk + key) * H + h) * 64;
+      float2 fr = make_float2(1.0f, 0.0f);  // no frequencies: identity rotation
+      if (freqs) {
+        const int64_t key = sel[qi];
+        fr = reinterpret_cast<const float2*>(freqs + (((int64_t)fbb * Lk + key) * H + h) * 64)[lane];
+      }
       const float2 qx = reinterpret_cast<const float2*>(qsrc + (((int64_t)b * Lq + qi) * H + h) * 64)[lane];
-      reinterpret_cast<float2*>(q_bhld + ((int64_t)bh * Lq + qi) * 64)[lane] =
-          rope_rms64(qx, reinterpret_cast<const float2*>(f)[lane], gq);
+      reinterpret_cast<float2*>(q_bhld + ((int64_t)bh * Lq + qi) * 64)[lane] = rope_rms64(qx, fr, gq);
     }
+  }
+}
+
+// [cos(t*f) | sin(t*f) | 0...] per sample  (scripts/native_embeddings_avx512.c:97-125)
+__global__ void timestep_embed_k(const float* __restrict__ t, const float* __restrict__ f,
+                                 float* __restrict__ out, int batch, int half, int out_dim) {
+  const int b = blockIdx.x;
+  if (b >= batch) return;
+  for (int i = threadIdx.x; i < out_dim; i += blockDim.x) {
+    float v = 0.0f;
+    if (i < half) v = cosf(t[b] * f[i]);
+    else if (i < 2 * half) v = sinf(t[b] * f[i - half]);
+    out[(int64_t)b * out_dim + i] = v;
   }
 }
 
@@ -250,8 +265,9 @@ int triposplat_layernorm_f32_avx512(const float* input, const float* weight, con
   if (rows <= 0 || cols <= 0 || eps < 0.0f) return kBadDims;
   if (has_affine && (!weight || !bias)) return kBadRange;
   TSB_PREAMBLE();
-  layernorm_k<<<grid_for(rows, 8), 256, 0, current_stream()>>>(input, weight, bias, output, rows,
-                                                               cols, eps, has_affine);
+  { LaunchScope _scope(kKElementwise, current_stream());
+    layernorm_k<<<grid_for(rows, 8), 256, 0, current_stream()>>>(input, weight, bias, output, rows,
+                                                               cols, eps, has_affine); }
   return launch_status();
 }
 
@@ -264,8 +280,9 @@ int triposplat_multihead_rmsnorm_f32_avx512(const float* input, const float* gam
   if (outer <= 0 || heads <= 0 || dim <= 0 || eps < 0.0f) return kBadDims;
   TSB_PREAMBLE();
   const int64_t vectors = outer * heads;
-  rmsnorm_k<<<grid_for(vectors, 8), 256, 0, current_stream()>>>(input, gamma, output, vectors,
-                                                                heads, dim, eps);
+  { LaunchScope _scope(kKElementwise, current_stream());
+    rmsnorm_k<<<grid_for(vectors, 8), 256, 0, current_stream()>>>(input, gamma, output, vectors,
+                                                                heads, dim, eps); }
   return launch_status();
 }
 
@@ -277,9 +294,10 @@ int triposplat_rope_complex_f32_avx512(const float* input, const float* freqs_in
   if (vectors <= 0 || dim <= 0 || (dim & 1) != 0) return kBadDims;
   TSB_PREAMBLE();
   const int64_t pairs = vectors * dim / 2;
-  rope_k<<<grid_for(pairs, 256), 256, 0, current_stream()>>>(
+  { LaunchScope _scope(kKElementwise, current_stream());
+    rope_k<<<grid_for(pairs, 256), 256, 0, current_stream()>>>(
       reinterpret_cast<const float2*>(input), reinterpret_cast<const float2*>(freqs_interleaved),
-      reinterpret_cast<float2*>(output), pairs);
+      reinterpret_cast<float2*>(output), pairs); }
   return launch_status();
 }
 
@@ -289,7 +307,8 @@ int triposplat_gelu_tanh_f32_avx512(const float* input, float* output, int64_t c
   if (!input || !output) return kNullPointer;
   if (count <= 0) return kBadDims;
   TSB_PREAMBLE();
-  gelu_k<<<grid_for(count, 256), 256, 0, current_stream()>>>(input, output, count);
+  { LaunchScope _scope(kKElementwise, current_stream());
+    gelu_k<<<grid_for(count, 256), 256, 0, current_stream()>>>(input, output, count); }
   return launch_status();
 }
 
@@ -299,7 +318,8 @@ int triposplat_silu_f32_avx512(const float* input, float* output, int64_t count,
   if (!input || !output) return kNullPointer;
   if (count <= 0) return kBadDims;
   TSB_PREAMBLE();
-  silu_k<<<grid_for(count, 256), 256, 0, current_stream()>>>(input, output, count);
+  { LaunchScope _scope(kKElementwise, current_stream());
+    silu_k<<<grid_for(count, 256), 256, 0, current_stream()>>>(input, output, count); }
   return launch_status();
 }
 
@@ -311,7 +331,8 @@ int triposplat_modulate_inplace_f32_avx512(float* h, const float* scale, const f
   if (batch <= 0 || rows <= 0 || cols <= 0) return kBadDims;
   TSB_PREAMBLE();
   const int64_t n = (int64_t)batch * rows * cols;
-  modulate_k<<<grid_for(n, 256), 256, 0, current_stream()>>>(h, scale, shift, rows, cols, n);
+  { LaunchScope _scope(kKElementwise, current_stream());
+    modulate_k<<<grid_for(n, 256), 256, 0, current_stream()>>>(h, scale, shift, rows, cols, n); }
   return launch_status();
 }
 
@@ -323,7 +344,8 @@ int triposplat_gated_residual_inplace_f32_avx512(float* base, float* delta, cons
   if (batch <= 0 || rows <= 0 || cols <= 0) return kBadDims;
   TSB_PREAMBLE();
   const int64_t n = (int64_t)batch * rows * cols;
-  gated_residual_k<<<grid_for(n, 256), 256, 0, current_stream()>>>(base, delta, gate, rows, cols, n);
+  { LaunchScope _scope(kKElementwise, current_stream());
+    gated_residual_k<<<grid_for(n, 256), 256, 0, current_stream()>>>(base, delta, gate, rows, cols, n); }
   return launch_status();
 }
 
@@ -333,7 +355,8 @@ int triposplat_add_inplace_f32_avx512(float* base, const float* delta, int64_t c
   if (!base || !delta) return kNullPointer;
   if (count <= 0) return kBadDims;
   TSB_PREAMBLE();
-  add_k<<<grid_for(count, 256), 256, 0, current_stream()>>>(base, delta, count);
+  { LaunchScope _scope(kKElementwise, current_stream());
+    add_k<<<grid_for(count, 256), 256, 0, current_stream()>>>(base, delta, count); }
   return launch_status();
 }
 
@@ -346,8 +369,9 @@ int triposplat_cfg_combine_inplace_f32_avx512(float* positive, const float* nega
   if (batch <= 0 || elements_per_batch <= 0) return kBadDims;
   TSB_PREAMBLE();
   const int64_t n = (int64_t)batch * elements_per_batch;
-  cfg_k<<<grid_for(n, 256), 256, 0, current_stream()>>>(positive, negative, guidance,
-                                                        elements_per_batch, n);
+  { LaunchScope _scope(kKElementwise, current_stream());
+    cfg_k<<<grid_for(n, 256), 256, 0, current_stream()>>>(positive, negative, guidance,
+                                                        elements_per_batch, n); }
   return launch_status();
 }
 
@@ -360,8 +384,9 @@ int triposplat_euler_update_inplace_f32_avx512(float* sample, const float* predi
   if (batch <= 0 || elements_per_batch <= 0) return kBadDims;
   TSB_PREAMBLE();
   const int64_t n = (int64_t)batch * elements_per_batch;
-  euler_k<<<grid_for(n, 256), 256, 0, current_stream()>>>(sample, prediction, dt,
-                                                          elements_per_batch, n);
+  { LaunchScope _scope(kKElementwise, current_stream());
+    euler_k<<<grid_for(n, 256), 256, 0, current_stream()>>>(sample, prediction, dt,
+                                                          elements_per_batch, n); }
   return launch_status();
 }
 
@@ -380,9 +405,10 @@ int triposplat_qkv_rope_rmsnorm_pack_f32_avx512_v2(const float* qkv, const float
     return kBadDims;
   TSB_PREAMBLE();
   const int tiles = (L_padded + 63) / 64;
-  qkv_post_k<false><<<dim3(tiles, B * H), 256, 0, current_stream()>>>(
+  { LaunchScope _scope(kKElementwise, current_stream());
+    qkv_post_k<false><<<dim3(tiles, B * H), 256, 0, current_stream()>>>(
       nullptr, qkv, frequencies, nullptr, q_gamma, k_gamma, q_bhld, packed_k, packed_v, H, L, L,
-      L_padded, frequency_batches, tiles);
+      L_padded, frequency_batches, tiles); }
   return launch_status();
 }
 
@@ -418,10 +444,47 @@ int triposplat_q_kv_selected_rope_rmsnorm_pack_f32_avx512_v2(
   const int kv_tiles = (Lk_padded + 63) / 64;
   const int q_tiles = (Lq + 63) / 64;
   const int tiles = kv_tiles > q_tiles ? kv_tiles : q_tiles;
-  qkv_post_k<true><<<dim3(tiles, B * H), 256, 0, s>>>(q, kv, frequencies, selected_indices,
+  { LaunchScope _scope(kKElementwise, current_stream());
+    qkv_post_k<true><<<dim3(tiles, B * H), 256, 0, s>>>(q, kv, frequencies, selected_indices,
                                                      q_gamma, k_gamma, q_bhld, packed_k, packed_v,
                                                      H, Lq, Lk, Lk_padded, frequency_batches,
-                                                     kv_tiles);
+                                                     kv_tiles); }
+  return launch_status();
+}
+
+// scripts/native_embeddings_avx512.c:97-125
+int triposplat_timestep_embedding_f32_avx512(const float* timesteps, const float* frequencies,
+                                             float* output, int batch, int half_dim,
+                                             int output_dim, int threads) {
+  (void)threads;
+  if (!timesteps || !frequencies || !output) return kNullPointer;
+  if (batch <= 0 || half_dim <= 0 || output_dim < half_dim * 2) return kBadDims;
+  TSB_PREAMBLE();
+  { LaunchScope _scope(kKElementwise, current_stream());
+    timestep_embed_k<<<batch, 256, 0, current_stream()>>>(timesteps, frequencies, output, batch,
+                                                        half_dim, output_dim); }
+  return launch_status();
+}
+
+// No reference counterpart: the selected-query post-process without RoPE and without
+// an index list (every query row kept): per-head 8/max(||x||,1e-12)*gamma on q and k,
+// q -> [B,H,Lq,64], k/v -> packed [B,H,64,Lk_padded].  Used for cross-attention, whose
+// condition tokens carry no position.
+int triposplat_b200_q_kv_rmsnorm_pack_f32(const float* q, const float* kv, const float* q_gamma,
+                                          const float* k_gamma, float* q_bhld, float* packed_k,
+                                          float* packed_v, int B, int Lq, int Lk, int H,
+                                          int Lk_padded) {
+  if (!q || !kv || !q_gamma || !k_gamma || !q_bhld || !packed_k || !packed_v) return kNullPointer;
+  if (B <= 0 || Lq <= 0 || Lk <= 0 || H <= 0 || Lk_padded < Lk || (Lk_padded & 15) != 0)
+    return kBadDims;
+  TSB_PREAMBLE();
+  const int kv_tiles = (Lk_padded + 63) / 64;
+  const int q_tiles = (Lq + 63) / 64;
+  const int tiles = kv_tiles > q_tiles ? kv_tiles : q_tiles;
+  { LaunchScope _scope(kKElementwise, current_stream());
+    qkv_post_k<true><<<dim3(tiles, B * H), 256, 0, current_stream()>>>(
+      q, kv, nullptr, nullptr, q_gamma, k_gamma, q_bhld, packed_k, packed_v, H, Lq, Lk,
+      Lk_padded, 1, kv_tiles); }
   return launch_status();
 }
 

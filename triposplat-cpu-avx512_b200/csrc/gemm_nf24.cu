@@ -367,6 +367,7 @@ static int gemm_launch(const float* x, const int16_t* c01, const int8_t* q2, con
   const bool tc = allow_tc && (N % 16 == 0) && (start % 16 == 0) && aligned;
   if (!tc) {
     dim3 grid((count + 127) / 128, M);
+    LaunchScope scope(kKGemmSimt, stream);
     nf24_gemm_simt<<<grid, 128, 0, stream>>>(x, c01, q2, scale, bias, out, M, K, N, start, count,
                                              stride_x, stride_out);
     return launch_status();
@@ -378,7 +379,10 @@ static int gemm_launch(const float* x, const int16_t* c01, const int8_t* q2, con
   __half* hi = reinterpret_cast<__half*>(ws);
   __half* lo = reinterpret_cast<__half*>(ws + plane);
   float* rscale = reinterpret_cast<float*>(ws + 2 * plane);
-  nf24_split_rows<<<(M + 7) / 8, 256, 0, stream>>>(x, M, K, Kp, stride_x, hi, lo, rscale);
+  {
+    LaunchScope scope(kKGemmSplit, stream);
+    nf24_split_rows<<<(M + 7) / 8, 256, 0, stream>>>(x, M, K, Kp, stride_x, hi, lo, rscale);
+  }
   if ((st = launch_status()) != kOk) return st;
 
   CUtensorMap m_hi, m_lo, m_c16, m_c8;
@@ -414,7 +418,10 @@ static int gemm_launch(const float* x, const int16_t* c01, const int8_t* q2, con
   }
   Params prm{rscale, scale, bias, out, M, K, N, start, count, stride_out, device_status()};
   dim3 grid((count + BN - 1) / BN, (M + BM - 1) / BM);
-  nf24_gemm_tc<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(m_hi, m_lo, m_c16, m_c8, prm);
+  {
+    LaunchScope scope(kKGemmTc, stream);
+    nf24_gemm_tc<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(m_hi, m_lo, m_c16, m_c8, prm);
+  }
   return launch_status();
 }
 

@@ -1,9 +1,11 @@
 // Library runtime: stream selection, device status word, workspaces, TMA maps.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <utility>
+#include <vector>
 
 #include "runtime.h"
 
@@ -53,7 +55,36 @@ DeviceState* state_for_current_device() {
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
 
+std::atomic<uint64_t> g_launches{0};
+std::atomic<int> g_profiling{0};
+struct TimedLaunch {
+  int id;
+  cudaEvent_t start, stop;
+};
+std::mutex g_prof_mutex;
+std::vector<TimedLaunch> g_timed;
+
 }  // namespace
+
+LaunchScope::LaunchScope(int kernel_id, cudaStream_t stream) : id_(kernel_id), stream_(stream) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  if (g_profiling.load(std::memory_order_relaxed)) {
+    if (cudaEventCreate(&start_) == cudaSuccess) cudaEventRecord(start_, stream_);
+    else start_ = nullptr;
+  }
+}
+
+LaunchScope::~LaunchScope() {
+  if (start_ == nullptr) return;
+  cudaEvent_t stop = nullptr;
+  if (cudaEventCreate(&stop) != cudaSuccess) {
+    cudaEventDestroy(start_);
+    return;
+  }
+  cudaEventRecord(stop, stream_);
+  std::lock_guard<std::mutex> lock(g_prof_mutex);
+  g_timed.push_back({id_, start_, stop});
+}
 
 cudaStream_t current_stream() { return t_stream; }
 
@@ -191,5 +222,38 @@ void triposplat_b200_workspace_release(void) {
 }
 
 int triposplat_b200_abi_version(void) { return 1; }
+
+uint64_t triposplat_b200_launch_count(void) {
+  return tsb::g_launches.load(std::memory_order_relaxed);
+}
+
+void triposplat_b200_profile_enable(int on) { tsb::g_profiling.store(on ? 1 : 0); }
+
+// Waits for every bracketed launch recorded so far, then returns per kernel family
+// (index = KernelId, n entries) the launch count and the summed device time in ms,
+// and forgets them.
+int triposplat_b200_profile_collect(uint64_t* launches, double* total_ms, int n) {
+  if (!launches || !total_ms || n <= 0) return tsb::kNullPointer;
+  for (int i = 0; i < n; ++i) { launches[i] = 0; total_ms[i] = 0.0; }
+  std::vector<tsb::TimedLaunch> items;
+  {
+    std::lock_guard<std::mutex> lock(tsb::g_prof_mutex);
+    items.swap(tsb::g_timed);
+  }
+  int st = 0;
+  for (auto& it : items) {
+    float ms = 0.0f;
+    if (cudaEventSynchronize(it.stop) == cudaSuccess &&
+        cudaEventElapsedTime(&ms, it.start, it.stop) == cudaSuccess) {
+      if (it.id >= 0 && it.id < n) { launches[it.id] += 1; total_ms[it.id] += ms; }
+    } else {
+      cudaGetLastError();
+      st = tsb::kLaunchFailed;
+    }
+    cudaEventDestroy(it.start);
+    cudaEventDestroy(it.stop);
+  }
+  return st;
+}
 
 }  // extern "C"

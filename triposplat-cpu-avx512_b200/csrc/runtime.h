@@ -51,4 +51,27 @@ bool encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, voi
 
 int sm_count();
 
+// Kernel families counted / timed by LaunchScope (ids are part of the C ABI).
+enum KernelId : int {
+  kKGemmTc = 0,      // nf24_gemm_tc
+  kKGemmSplit = 1,   // nf24_split_rows
+  kKGemmSimt = 2,    // nf24_gemm_simt
+  kKSdpaAttn = 3,    // sdpa_fwd_tc
+  kKSdpaSplit = 4,   // sdpa_split_q + sdpa_split_kv
+  kKElementwise = 5, // norms, activations, residuals, sampler updates, post-process
+  kKNum = 6,
+};
+
+// Wrap one kernel launch: counts it and, while profiling is enabled, brackets it with
+// CUDA events on `stream` (read back by triposplat_b200_profile_collect).
+class LaunchScope {
+ public:
+  LaunchScope(int kernel_id, cudaStream_t stream);
+  ~LaunchScope();
+ private:
+  int id_;
+  cudaStream_t stream_;
+  cudaEvent_t start_ = nullptr;
+};
+
 }  // namespace tsb

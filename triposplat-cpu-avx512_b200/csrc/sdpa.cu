@@ -498,9 +498,15 @@ static int sdpa_launch(const float* q, const float* k, const float* v, int64_t b
   float* vinv = reinterpret_cast<float*>(ws + off_vinv);
 
   const int64_t qrows = BH * Lq;
-  sdpa_split_q<<<(unsigned)((qrows + 7) / 8), 256, 0, stream>>>(q, qrows, qhi, qlo, qinv);
-  sdpa_split_kv<<<dim3(T, (unsigned)BH), 256, 0, stream>>>(k, v, bh_stride, j_stride, d_stride, Lk,
-                                                           Lkt, khi, klo, vhi, vlo, kinv, vinv);
+  {
+    LaunchScope scope(kKSdpaSplit, stream);
+    sdpa_split_q<<<(unsigned)((qrows + 7) / 8), 256, 0, stream>>>(q, qrows, qhi, qlo, qinv);
+  }
+  {
+    LaunchScope scope(kKSdpaSplit, stream);
+    sdpa_split_kv<<<dim3(T, (unsigned)BH), 256, 0, stream>>>(k, v, bh_stride, j_stride, d_stride,
+                                                             Lk, Lkt, khi, klo, vhi, vlo, kinv, vinv);
+  }
   if ((st = launch_status()) != kOk) return st;
   const uint64_t t1 = now_ns();
 
@@ -539,7 +545,10 @@ static int sdpa_launch(const float* q, const float* k, const float* v, int64_t b
   }
   Params prm{qinv, kinv, vinv, bias, (long long)bias_bh_stride, out, H, Lq, Lk, T, out_blhd, device_status()};
   dim3 grid((Lq + BQ - 1) / BQ, (unsigned)BH);
-  sdpa_fwd_tc<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(m_qhi, m_qlo, m_khi, m_klo, m_vhi, m_vlo, prm);
+  {
+    LaunchScope scope(kKSdpaAttn, stream);
+    sdpa_fwd_tc<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(m_qhi, m_qlo, m_khi, m_klo, m_vhi, m_vlo, prm);
+  }
   st = launch_status();
   const uint64_t t2 = now_ns();
   g_sdpa.calls += 1;

@@ -44,6 +44,8 @@ def nf24_linear(x, code01_t, q2_t, scale, bias, *, out=None, start: int = 0,
     count = N - start if count is None else int(count)
     if out is None:
         out = torch.empty((M, count), dtype=torch.float32, device=x.device)
+    elif not out.is_contiguous() or out.numel() != M * count or out.dtype != torch.float32:
+        raise ValueError("out must be a contiguous float32 tensor of M x count elements")
     cb = _codebook(x.device)
     _native.use_current_stream(lib)
     ptrs = (x2.data_ptr(), code01_t.data_ptr(), q2_t.data_ptr(), q2_t.data_ptr(),

@@ -57,11 +57,25 @@ def quantize_nf24_i16_per_output_channel(weight, codebook=None):
 
     if weight.device.type != "cpu" or weight.dtype != torch.float32 or weight.ndim != 2:
         raise ValueError("NF24 packing requires a CPU float32 2D weight")
+    return quantize_nf24_i16_any_device(weight, codebook)
+
+
+def quantize_nf24_i16_any_device(weight, codebook=None, stats: bool = True):
+    """Same packing on any device.  Every step is an exactly rounded elementwise op, a
+    comparison or a sort, so CUDA and CPU produce bit-identical codes (checked by
+    tests/test_model_gpu.py); used to pack synthetic weights where they are generated."""
+    import torch
+
+    if weight.dtype != torch.float32 or weight.ndim != 2:
+        raise ValueError("NF24 packing requires a float32 2D weight")
     if codebook is None:
         codebook = make_nf8_codebook(torch)
+    codebook = codebook.to(weight.device)
     w = weight.detach().contiguous()
     tiny = torch.finfo(torch.float32).tiny
-    step0 = (w.abs().amax(dim=1).clamp_min(tiny) / 127.0).contiguous()
+    # the per-row step is divided on the host: CUDA tensor-by-scalar division is not
+    # always correctly rounded, and every code depends on this value
+    step0 = (w.abs().amax(dim=1).clamp_min(tiny).cpu() / 127.0).to(w.device).contiguous()
 
     alphabet = torch.unique(torch.round(codebook * 127.0).clamp_(-127, 127)).to(torch.float32)
     mids = ((alphabet[:-1] + alphabet[1:]) * 0.5).contiguous()
@@ -78,6 +92,10 @@ def quantize_nf24_i16_per_output_channel(weight, codebook=None):
     q2 = q2_raw.clamp(-128, 127).to(torch.int8)
     r3 = r2 - q2.to(torch.float32) * scale[:, None]
 
+    code01_t = (q0.t().to(torch.int16) * 4 + q1.t().to(torch.int16)).contiguous()
+    q2_t = q2.t().contiguous()
+    if not stats:
+        return [code01_t, q2_t, q2_t], [scale, scale, scale], None
     stages = []
     for idx, (rem, name, raw) in enumerate(
         ((r1, "nf8_derived_int8_alphabet", None),
@@ -95,8 +113,6 @@ def quantize_nf24_i16_per_output_channel(weight, codebook=None):
         "nf8_derived_alphabet_size": int(alphabet.numel()),
         "stages": stages,
     }
-    code01_t = (q0.t().to(torch.int16) * 4 + q1.t().to(torch.int16)).contiguous()
-    q2_t = q2.t().contiguous()
     return [code01_t, q2_t, q2_t], [scale, scale, scale], error
 
 
