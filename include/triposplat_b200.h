@@ -17,7 +17,7 @@
  *
  * Status codes: 0 ok; -1 null pointer; -2 bad dimension / stages; -3 bad range / bias
  * length; -4 alignment (range start/count not a multiple of 16, or an unaligned q/out
- * pointer for SDPA); -5 workspace allocation failed; -9 pointer not device-accessible;
+ * pointer for SDPA); -5 workspace allocation failed; -6 problem larger than a fixed scratch; -9 pointer not device-accessible;
  * -10 kernel launch failed; -11 an earlier kernel of this library gave up on a bounded
  * wait (see triposplat_b200_status); -12 no usable CUDA device.
  */
@@ -85,6 +85,24 @@ int triposplat_gemm_rnf8_avx512_tail(const float* x, const uint8_t* codes0_t,
                                      const float* scales2, const float* codebook,
                                      const float* bias, float* out, int M, int K, int N,
                                      int stride_x, int stride_out, int threads, int stages);
+
+/* No counterpart in the reference.  Same arguments and result as
+ * triposplat_gemm_rnf8_avx512, for callers that must not let a library allocate device
+ * memory (work being captured into a CUDA graph, hosts whose device memory is owned by
+ * their own allocator or a fixed memory plan, loops that cannot absorb cudaMalloc's
+ * device-wide synchronisation).  It calls no allocator: its scratch is a fixed 32 MiB
+ * __device__ array per device, so it serves 2*M*Kp*2 + 4*M + 512 <= 32 MiB
+ * (Kp = K rounded up to 8; e.g. M <= 8183 at K = 1024) and returns -6 beyond that, and
+ * -4 unless N % 16 == 0 with 16-byte aligned code planes.  All calls on a device share
+ * the scratch: calls whose kernels may overlap on the GPU race, so order them on one
+ * stream.  Nothing in the scratch needs to start at zero.  The first call on a device
+ * resolves the scratch address; make it before capturing any stream. */
+int triposplat_gemm_nf24_noalloc(const float* x, const uint8_t* codes0_t, const uint8_t* codes1_t,
+                                 const uint8_t* codes2_t, const float* scales0,
+                                 const float* scales1, const float* scales2,
+                                 const float* codebook, const float* bias, float* out, int M,
+                                 int K, int N, int stride_x, int stride_out, int threads,
+                                 int stages);
 
 /* replaces scripts/gemm_nf24_i16_avx512.c:222-224 (rows per CTA tile here) */
 int triposplat_gemm_rnf8_avx512_row_tile(void);

@@ -40,6 +40,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "triposplat_gemm_rnf8_avx512_tail": ([VP] * 10 + [I] * 7, I),
     "triposplat_gemm_rnf8_avx512_row_tile": ([], I),
     "triposplat_gemm_rnf8_avx512_residual_mode": ([], I),
+    "triposplat_gemm_nf24_noalloc": ([VP] * 10 + [I] * 7, I),
     # exact SDPA
     "triposplat_sdpa_f32_avx512_exact_q8t512": ([VP] * 5 + [I] * 8, I),
     "triposplat_sdpa_f32_avx512_exact_q8": ([VP] * 5 + [I] * 8, I),

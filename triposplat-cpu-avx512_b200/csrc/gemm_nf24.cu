@@ -35,6 +35,8 @@
 // (scripts/gemm_nf24_i16_avx512_tail.c:32-47) operation for operation.
 #include <cuda_fp16.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "runtime.h"
 
@@ -494,5 +496,138 @@ int triposplat_gemm_rnf8_avx512_row_tile(void) { return tsb::gemm::BM; }
 
 // scripts/gemm_nf24_i16_avx512.c:226-228: 4 = nf24_i16
 int triposplat_gemm_rnf8_avx512_residual_mode(void) { return 4; }
+
+}  // extern "C"
+
+// ===========================================================================
+// Allocation-free NF24 GEMM.
+//
+// Some callers cannot let a library call cudaMalloc: code recorded into a CUDA graph
+// (allocation is not a capturable stream operation), hosts whose device memory is owned
+// by their own allocator or a fixed memory plan (an inference server, a framework's
+// caching allocator), and latency-critical loops that cannot absorb cudaMalloc's
+// implicit device-wide synchronisation.  For them this entry point computes exactly
+// what triposplat_gemm_rnf8_avx512 computes, but takes its scratch (the fp16 hi/lo
+// activation planes and the per-row scales) from the fixed array below instead of the
+// library workspace, and never allocates.
+//
+// Limits and sharing: the scratch is 32 MiB per device and holds 2*M*Kp fp16 values plus
+// M floats (Kp = K rounded up to 8); larger problems are rejected with -6.  Every call on
+// a device uses the same array, so two calls whose kernels overlap on the GPU (different
+// streams, no ordering between them) race on it: order them on one stream or with
+// events.  The split kernel writes every byte the GEMM later reads, so nothing has to
+// start at zero and nothing carries over from the previous call.
+// ===========================================================================
+namespace tsb {
+namespace gemm {
+
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scratch for each device, resolved once with that device
+// current (the host-side name of a __device__ array is not a device address).
+static void* g_noalloc_addr[64] = {};
+static std::mutex g_noalloc_mutex;
+
+static int noalloc_scratch(uint8_t** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return kNoDevice;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      return kLaunchFailed;
+    }
+    g_noalloc_addr[dev] = p;
+  }
+  *out = static_cast<uint8_t*>(g_noalloc_addr[dev]);
+  return kOk;
+}
+
+}  // namespace gemm
+}  // namespace tsb
+
+extern "C" {
+
+// No counterpart in the reference.  Same arguments and results as
+// triposplat_gemm_rnf8_avx512; allocates no memory (see the block comment above).
+// Additional status: -6 when 2*M*Kp*2 + 4*M + 512 bytes exceed the 32 MiB scratch;
+// -4 when N % 16 != 0 or a code pointer is not 16-byte aligned (this entry has only the
+// tensor-core path).  The first call on each device resolves the scratch address; make
+// that first call before capturing any stream.
+int triposplat_gemm_nf24_noalloc(const float* x, const uint8_t* codes0_t, const uint8_t* codes1_t,
+                                 const uint8_t* codes2_t, const float* scales0,
+                                 const float* scales1, const float* scales2,
+                                 const float* codebook, const float* bias, float* out, int M,
+                                 int K, int N, int stride_x, int stride_out, int threads,
+                                 int stages) {
+  using namespace tsb;
+  using namespace tsb::gemm;
+  (void)threads;
+  if (!x || !codes0_t || !codes1_t || !codes2_t || !scales0 || !scales1 || !scales2 ||
+      !codebook || !bias || !out)
+    return kNullPointer;
+  if (M <= 0 || K <= 0 || N <= 0 || stages != 3) return kBadDims;
+  if (stride_x < K || stride_out < N) return kBadRange;
+  const int16_t* c01 = reinterpret_cast<const int16_t*>(codes0_t);
+  const int8_t* q2 = reinterpret_cast<const int8_t*>(codes1_t);
+  if ((N % 16) != 0 ||
+      ((reinterpret_cast<uintptr_t>(c01) | reinterpret_cast<uintptr_t>(q2)) & 15) != 0)
+    return kBadAlignment;
+  const int Kp = (K + 7) & ~7;
+  const size_t plane = (size_t)M * Kp * 2;
+  if (2 * plane + (size_t)M * 4 + 512 > kNoAllocScratchBytes) return -6;
+  int st = entry_check_no_alloc();
+  if (st != kOk) return st;
+  if (!is_device_pointer(x) || !is_device_pointer(c01) || !is_device_pointer(q2) ||
+      !is_device_pointer(scales0) || !is_device_pointer(bias) || !is_device_pointer(out))
+    return kNotDevicePointer;
+  uint8_t* ws = nullptr;
+  if ((st = noalloc_scratch(&ws)) != kOk) return st;
+  cudaStream_t stream = current_stream();
+  __half* hi = reinterpret_cast<__half*>(ws);
+  __half* lo = reinterpret_cast<__half*>(ws + ((plane + 255) & ~size_t(255)));
+  float* rscale = reinterpret_cast<float*>(ws + 2 * ((plane + 255) & ~size_t(255)));
+  {
+    LaunchScope scope(kKGemmSplit, stream);
+    nf24_split_rows<<<(M + 7) / 8, 256, 0, stream>>>(x, M, K, Kp, stride_x, hi, lo, rscale);
+  }
+  if ((st = launch_status()) != kOk) return st;
+  CUtensorMap m_hi, m_lo, m_c16, m_c8;
+  {
+    const uint64_t dims[2] = {(uint64_t)Kp, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)Kp * 2};
+    const uint32_t box[2] = {BK, BM};
+    if (!encode_tmap(&m_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, hi, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tmap(&m_lo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, lo, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B))
+      return kLaunchFailed;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)K};
+    const uint64_t s16[1] = {(uint64_t)N * 2};
+    const uint64_t s8[1] = {(uint64_t)N};
+    const uint32_t box[2] = {BN, BK};
+    if (!encode_tmap(&m_c16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<int16_t*>(c01), dims,
+                     s16, box, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode_tmap(&m_c8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(q2), dims, s8,
+                     box, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return kLaunchFailed;
+  }
+  cudaFuncSetAttribute(nf24_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  Params prm{rscale, scales0, bias, out, M, K, N, 0, N, stride_out, device_status_no_alloc()};
+  dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
+  {
+    LaunchScope scope(kKGemmTc, stream);
+    nf24_gemm_tc<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(m_hi, m_lo, m_c16, m_c8, prm);
+  }
+  return launch_status();
+}
 
 }  // extern "C"

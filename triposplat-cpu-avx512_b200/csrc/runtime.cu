@@ -147,6 +147,33 @@ int entry_check() {
   return kOk;
 }
 
+static DeviceState* existing_state() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_mutex);
+  auto it = g_devices.find(dev);
+  return (it == g_devices.end() || it->second.host_status == nullptr) ? nullptr : &it->second;
+}
+
+int entry_check_no_alloc() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return kNoDevice;
+  }
+  DeviceState* st = existing_state();
+  if (st && *reinterpret_cast<volatile int*>(st->host_status) != 0) return kDeviceFault;
+  return kOk;
+}
+
+int* device_status_no_alloc() {
+  DeviceState* st = existing_state();
+  return st ? st->device_status : nullptr;
+}
+
 int launch_status() {
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? kOk : kLaunchFailed;

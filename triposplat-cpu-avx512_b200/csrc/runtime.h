@@ -43,6 +43,12 @@ bool is_device_pointer(const void* p);
 // Entry checks shared by all kernels: a usable device and a clean status word.
 int entry_check();
 
+// Variants that never allocate: they use this device's status word only if an earlier
+// call already created it (otherwise kernels get a null status pointer and a timeout is
+// reported through their exit path alone).
+int entry_check_no_alloc();
+int* device_status_no_alloc();
+
 int launch_status();  // maps cudaGetLastError() to kLaunchFailed / kOk
 
 bool encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, void* base,
