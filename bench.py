@@ -43,7 +43,110 @@ def parse():
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--case", default="model",
+                    choices=("model", "gemm1", "sdpa2a", "sdpa2b", "sdpa2c", "mlp3", "block4"),
+                    help="model = BASELINE config 5 (the headline); the others time one "
+                         "BASELINE config on one GPU and print its own line")
     return ap.parse_args()
+
+
+def run_case(args):
+    """One BASELINE config on cuda:0: gemm1 = config 1, sdpa2a/b/c = config 2 (a)/(b)/(c),
+    mlp3 = config 3 (LN -> fc1 -> GELU -> fc2 -> residual), block4 = config 4 (one block)."""
+    import torch
+
+    import _native
+    import native_ops as ops
+    from native_sdpa_ctypes import native_sdpa_f32
+    from nf24_linear import nf24_linear
+    from nf24_pack import quantize_nf24_i16_any_device
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    lib = _native.load()
+
+    def packed(n, k):
+        c, s_, _ = quantize_nf24_i16_any_device(torch.randn(n, k, device=dev, generator=g) * 0.02,
+                                               stats=False)
+        return c[0], c[1], s_[0], torch.randn(n, device=dev, generator=g) * 0.01
+
+    if args.case == "gemm1":
+        M, K, N = 4096, 1024, 3072
+        x = torch.randn(M, K, device=dev, generator=g)
+        c01, q2, sc, b = packed(N, K)
+        out = torch.empty(M, N, device=dev)
+        fn = lambda: nf24_linear(x, c01, q2, sc, b, out=out, lib=lib)  # noqa: E731
+        flops, passes, what = 2.0 * M * N * K, 4, "NF24 Linear 4096x1024x3072 (config 1)"
+    elif args.case.startswith("sdpa"):
+        B, H, Lq = 2, 16, 8192
+        Lk = 1374 if args.case == "sdpa2c" else 8192
+        q = torch.randn(B, H, Lq, 64, device=dev, generator=g)
+        k = torch.randn(B, H, Lk, 64, device=dev, generator=g)
+        v = torch.randn(B, H, Lk, 64, device=dev, generator=g)
+        kb = torch.randn(B, H, Lk, device=dev, generator=g) if args.case == "sdpa2b" else None
+        fn = lambda: native_sdpa_f32(q, k, v, key_bias=kb)  # noqa: E731
+        flops, passes = 4.0 * B * H * Lq * Lk * 64, 3
+        what = {"sdpa2a": "exact SDPA self 2x16x8192^2 (config 2a)",
+                "sdpa2b": "exact SDPA + key bias [2,16,8192] (config 2b)",
+                "sdpa2c": "exact SDPA cross 8192x1374 (config 2c)"}[args.case]
+    elif args.case == "mlp3":
+        M, C, F = 8192, 1024, 4096
+        x = torch.randn(1, M, C, device=dev, generator=g)
+        gam = 1.0 + torch.randn(C, device=dev, generator=g) * 0.02
+        beta = torch.zeros(C, device=dev)
+        w1, w2 = packed(F, C), packed(C, F)
+        a = torch.empty_like(x)
+        hid = torch.empty(M, F, device=dev)
+        y = torch.empty(1, M, C, device=dev)
+
+        def fn():
+            ops.layernorm(x, gam, beta, eps=1e-6, out=a)
+            nf24_linear(a, *w1, out=hid, lib=lib)
+            ops.gelu_tanh(hid, out=hid)
+            nf24_linear(hid, *w2, out=y, lib=lib)
+            ops.add_inplace(y, x)
+        flops, passes, what = 2.0 * 2 * M * C * F, 4, "MLP sub-block M=8192 1024-4096-1024 (config 3)"
+    else:  # block4
+        from flow_model import FlowModelB200, FlowSpec, make_weights
+
+        spec = FlowSpec(blocks=1)
+        model = FlowModelB200(make_weights(spec, seed=0, device=str(dev)), device=str(dev))
+        b = model.buf
+        b["x"].normal_(generator=g)
+        b["c"].normal_(generator=g)
+        b["mod"].normal_(generator=g)
+        b["mod"].mul_(0.02)
+        fn = lambda: model._block(0)  # noqa: E731
+        fl = spec.flops_per_forward(batch=2)
+        L, Mc = spec.seq, spec.cond_tokens
+        flops = 2.0 * 2 * (L * 1024 * 3072 + 3 * L * 1024 * 1024 + Mc * 1024 * 2048 + 2 * L * 1024 * 4096) \
+            + 4.0 * 2 * 16 * L * (L + Mc) * 64
+        passes, what = None, "one flow block, B=2 CFG pair, L=8193, 1374 cond tokens (config 4)"
+        del fl
+    _native.use_current_stream(lib)
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st.record()
+    for _ in range(args.steps):
+        fn()
+    en.record()
+    torch.cuda.synchronize()
+    _native.check_status(lib)
+    ms = st.elapsed_time(en) / args.steps
+    tf = flops / (ms / 1e3) / 1e12
+    peaks, src = load_peaks()
+    line = {"metric": f"{what} TFLOP/s (algorithmic flops)", "value": round(tf, 1),
+            "unit": "TFLOP/s", "case": args.case, "ms_per_step": round(ms, 4),
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "n_gpus": 1,
+            "dtype": "f32", "data": "synthetic",
+            "frac_of_bf16_burst": round(tf / float(peaks["bf16_tflops"]), 4),
+            "tensor_passes": passes,
+            "tensor_pipe_frac": None if passes is None else round(passes * tf / float(peaks["bf16_tflops"]), 4),
+            "peak_source": src}
+    print(json.dumps(line), flush=True)
+    return 0
 
 
 def load_peaks():
@@ -175,6 +278,8 @@ def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.case != "model":
+        return run_case(args)
 
     import torch
     import torch.distributed as dist
