@@ -101,6 +101,22 @@ def test_sdpa_scale_robustness(oracle):
     assert rel < 2e-6
 
 
+def test_sdpa_rescale_on_some_rows_only(oracle):
+    """Even query rows meet a much larger score in the third key tile while odd rows do not,
+    so the running-max rescale of O happens for some rows of a warp and not for others."""
+    from native_sdpa_ctypes import native_sdpa_f32
+
+    g = torch.Generator().manual_seed(21)
+    k = torch.randn(1, 2, 700, 64, generator=g)
+    v = torch.randn(1, 2, 700, 64, generator=g)
+    q = torch.randn(1, 2, 256, 64, generator=g)
+    q[:, :, 0::2] = 6.0 * k[:, :, 300:301] / k[:, :, 300:301].norm(dim=-1, keepdim=True) * 8.0
+    ref = oracle.sdpa(q.numpy(), k.numpy(), v.numpy())
+    out = native_sdpa_f32(q.cuda(), k.cuda(), v.cuda())
+    torch.cuda.synchronize()
+    _check(out.cpu().numpy(), ref)
+
+
 def test_sdpa_full_config_a_spot_check():
     """BASELINE config 2(a) at full size (B=2, H=16, L=8192): 256 query rows per head vs fp64."""
     from native_sdpa_ctypes import native_sdpa_f32

@@ -183,6 +183,16 @@ __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// tcgen05.ld writes its destination registers asynchronously: they are valid only after
+// tcgen05.wait::ld.  The wait carries no register dependency, so after it every loaded
+// register is passed through an empty asm that "modifies" it, which keeps the compiler
+// from scheduling any use of the register above the wait.
+template <int N>
+__device__ __forceinline__ void reg_fence(uint32_t (&r)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
+
 // 32 lanes x 32 consecutive 32-bit columns; thread t of the warp gets lane t.
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(

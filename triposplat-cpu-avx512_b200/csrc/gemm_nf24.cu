@@ -267,6 +267,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint32_t r[16];
         tmem_ld16(col + q * 16, r);
         tmem_wait_ld();
+        reg_fence(r);
 #pragma unroll
         for (int j = 0; j < 16; ++j) sum[q * 16 + j] += __uint_as_float(r[j]);
       }

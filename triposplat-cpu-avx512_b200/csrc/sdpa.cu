@@ -11,19 +11,24 @@
 //   O_t = Ph Vh + Ph Vl + Pl Vh                     (tcgen05, P from tensor memory)
 // The pre-scales fold into constants the softmax already multiplies by, so they are free.
 //
-// Exact online softmax.  Keys are processed in tiles of 128; per tile the softmax warps
-// take the running max m, rescale factor alpha = 2^(m_old - m_new), p = 2^(s*log2e - m),
-// the fp32 row sum, and merge the tile's fp32 output O_t (read back from TMEM) into
-// register accumulators: O = O*alpha + O_t * vscale_t.  No Lq x Lk matrix is ever
-// materialised and no score is skipped.
+// Exact online softmax.  Keys are processed in tiles of 128.  Per tile the softmax warps
+// read the score row once into registers, take the tile max, and form p = 2^(s*log2e - m)
+// against a running reference max m that is raised (and O, l rescaled by 2^(m_old-m_new))
+// only when the tile max exceeds it by more than 8: the result is the same exact softmax
+// (the common factor cancels in O/l), p stays <= 2^8, and the rescale of O is rare.  P is
+// split into fp16 hi/lo in registers and written over S in tensor memory; the P.V MMA
+// accumulates O across all tiles in TMEM.  The V tiles' power-of-two pre-scales are made
+// relative to the largest one of the head and folded into the exponent of p, and the row
+// sum l is kept in fp32.  No Lq x Lk matrix is ever materialised and no score is skipped.
 //
 // CTA: one (b, h) and 128 query rows, 192 threads, two CTAs per SM.
 //   warp 0      TMA producer (Q once, K and V^T tiles)
 //   warp 1      TMEM allocator + MMA issuer
-//   warps 2..5  softmax / merge / epilogue, thread = query row = TMEM lane
+//   warps 2..5  softmax / rescale / epilogue, thread = query row = TMEM lane
 // TMEM (256 columns): S / P tile at 0..127 (P overwrites S in place: for every 16-key
-// chunk, P_hi goes to its first 8 columns and P_lo to the next 8), O_t double buffer at
-// 128..191 and 192..255.
+// chunk, P_hi goes to its first 8 columns and P_lo to the next 8), O at 128..191.
+// Ordering: QK(t) is issued only after P.V(t-1) retired (it overwrites P), so when the
+// softmax warps see S(t) the O accumulator is quiescent and may be rescaled in place.
 #include <cuda_fp16.h>
 
 #include "common.cuh"
@@ -39,6 +44,7 @@ constexpr int NUM_THREADS = 192;
 constexpr int TMEM_COLS = 256;
 constexpr int S_COL = 0;
 constexpr int O_COL = 128;
+constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
 constexpr int PLANE = 128 * D * 2;  // 16 KB: one 128 x 64 fp16 tile
 constexpr int SMEM_BYTES = 1024 + 6 * PLANE + 4 * BKV * 4 + 32 * 8 + 16;
 constexpr float LOG2E = 1.4426950408889634f;
@@ -54,6 +60,24 @@ struct Params {
   int out_blhd;
   int* status;
 };
+
+// 32 consecutive TMEM columns of this thread's lane into s[OFF .. OFF+31]
+template <int OFF>
+__device__ __forceinline__ void tmem_ld32_at(uint32_t taddr, uint32_t (&s)[128]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(s[OFF + 0]), "=r"(s[OFF + 1]), "=r"(s[OFF + 2]), "=r"(s[OFF + 3]),
+        "=r"(s[OFF + 4]), "=r"(s[OFF + 5]), "=r"(s[OFF + 6]), "=r"(s[OFF + 7]),
+        "=r"(s[OFF + 8]), "=r"(s[OFF + 9]), "=r"(s[OFF + 10]), "=r"(s[OFF + 11]),
+        "=r"(s[OFF + 12]), "=r"(s[OFF + 13]), "=r"(s[OFF + 14]), "=r"(s[OFF + 15]),
+        "=r"(s[OFF + 16]), "=r"(s[OFF + 17]), "=r"(s[OFF + 18]), "=r"(s[OFF + 19]),
+        "=r"(s[OFF + 20]), "=r"(s[OFF + 21]), "=r"(s[OFF + 22]), "=r"(s[OFF + 23]),
+        "=r"(s[OFF + 24]), "=r"(s[OFF + 25]), "=r"(s[OFF + 26]), "=r"(s[OFF + 27]),
+        "=r"(s[OFF + 28]), "=r"(s[OFF + 29]), "=r"(s[OFF + 30]), "=r"(s[OFF + 31])
+      : "r"(taddr));
+}
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -84,9 +108,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
   uint64_t* v_empty = bars + 4;
   uint64_t* s_full = bars + 5;
   uint64_t* p_full = bars + 6;
-  uint64_t* o_full = bars + 7;  // [2]
-  uint64_t* o_free = bars + 9;  // [2]
-  uint64_t* mma_done = bars + 11;
+  uint64_t* o_done = bars + 7;  // P.V(t) retired
+  uint64_t* mma_done = bars + 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -99,10 +122,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
   if (threadIdx.x == 0) {
     for (int i = 0; i < 6; ++i) mbar_init(&bars[i], 1);  // q/k/v full+empty, s_full
     mbar_init(p_full, 4);                                 // one arrival per softmax warp
-    mbar_init(&o_full[0], 1);
-    mbar_init(&o_full[1], 1);
-    mbar_init(&o_free[0], 4);
-    mbar_init(&o_free[1], 4);
+    mbar_init(o_done, 1);
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -159,7 +179,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       const uint32_t vh = smem_u32(v_hi), vl = smem_u32(v_lo);
       for (int t = 0; t < T && ok; ++t) {
         ok = mbar_wait(k_full, t & 1, p.status, kDevTimeoutMma, abort_flag) &&
-             (t == 0 || mbar_wait(&o_full[(t - 1) & 1], ((t - 1) >> 1) & 1, p.status, kDevTimeoutMma, abort_flag));
+             (t == 0 || mbar_wait(o_done, (t - 1) & 1, p.status, kDevTimeoutMma, abort_flag));
         if (!ok) break;
         tc_fence_after();
 #pragma unroll
@@ -175,11 +195,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         mma_commit(k_empty);
         mma_commit(s_full);
         ok = mbar_wait(p_full, t & 1, p.status, kDevTimeoutMma, abort_flag) &&
-             mbar_wait(v_full, t & 1, p.status, kDevTimeoutMma, abort_flag) &&
-             (t < 2 || mbar_wait(&o_free[t & 1], ((t >> 1) & 1) ^ 1, p.status, kDevTimeoutMma, abort_flag));
+             mbar_wait(v_full, t & 1, p.status, kDevTimeoutMma, abort_flag);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t o = tmem + O_COL + (t & 1) * D;
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk) {
           const uint32_t ph = tmem + S_COL + kk * 16;  // P_hi for keys 16kk..16kk+15
@@ -187,18 +205,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
           const uint32_t voff = (kk >> 2) * (PLANE / 2) + (kk & 3) * 32;
           const uint64_t b_h = sw128_kmajor_desc(vh + voff);
           const uint64_t b_l = sw128_kmajor_desc(vl + voff);
-          mma_f16_ts(o, ph, b_h, idesc_o, kk != 0);
-          mma_f16_ts(o, ph, b_l, idesc_o, 1);
-          mma_f16_ts(o, pl, b_h, idesc_o, 1);
+          mma_f16_ts(tmem + O_COL, ph, b_h, idesc_o, (t | kk) != 0);
+          mma_f16_ts(tmem + O_COL, ph, b_l, idesc_o, 1);
+          mma_f16_ts(tmem + O_COL, pl, b_h, idesc_o, 1);
         }
         mma_commit(v_empty);
-        mma_commit(&o_full[t & 1]);
+        mma_commit(o_done);
       }
       mma_commit(mma_done);
       mbar_wait(mma_done, 0, p.status, kDevTimeoutMma, nullptr);
     }
   } else {
-    // ---------------- softmax, merge, epilogue ----------------
+    // ---------------- softmax, rescale, epilogue ----------------
     const uint32_t sub = warp & 3;
     const int r = sub * 32 + lane;  // query row within the tile == TMEM lane
     const uint32_t lane_base = (sub * 32) << 16;
@@ -206,125 +224,132 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     const bool row_valid = qrow < p.Lq;
     const float cq = 0.125f * LOG2E * (row_valid ? p.qinv[(int64_t)bh * p.Lq + qrow] : 0.0f);
     const float* bias_row = p.bias ? p.bias + (int64_t)bh * p.bias_bh_stride : nullptr;
-    float o_acc[D];
-#pragma unroll
-    for (int d = 0; d < D; ++d) o_acc[d] = 0.0f;
-    float m_run = -INFINITY, l_run = 0.0f, alpha_prev = 0.0f;
+    // reference V scale of the head: the largest per-tile inverse pre-scale
+    float vref = 0.0f;
+    for (int t = 0; t < T; ++t) vref = fmaxf(vref, p.vinv[(int64_t)bh * T + t]);
+    const int vref_exp = __float_as_int(vref) >> 23;
+    float* bt = bias_s + sub * BKV;
+    float m_run = -INFINITY, l_run = 0.0f;
     bool ok = true;
     for (int t = 0; t < T; ++t) {
-      // key bias (+ -inf past Lk) for this tile, staged in a warp-private buffer so no
-      // cross-warp barrier is needed (a warp may leave the loop early on an error)
-      float* bt = bias_s + sub * BKV;
-      __syncwarp();
+      const bool plain = bias_row == nullptr && (t + 1) * BKV <= p.Lk;  // no bias, no masking
+      if (!plain) {
+        // key bias (+ -inf past Lk) for this tile, staged in a warp-private buffer so no
+        // cross-warp barrier is needed (a warp may leave the loop early on an error)
+        __syncwarp();
 #pragma unroll
-      for (int i = 0; i < BKV / 32; ++i) {
-        const int jl = i * 32 + lane;
-        const int j = t * BKV + jl;
-        float b = -INFINITY;
-        if (j < p.Lk) b = bias_row ? bias_row[j] * LOG2E : 0.0f;
-        bt[jl] = b;
+        for (int i = 0; i < BKV / 32; ++i) {
+          const int jl = i * 32 + lane;
+          const int j = t * BKV + jl;
+          float b = -INFINITY;
+          if (j < p.Lk) b = bias_row ? bias_row[j] * LOG2E : 0.0f;
+          bt[jl] = b;
+        }
+        __syncwarp();
       }
-      __syncwarp();
+      const float c2 = cq * p.kinv[(int64_t)bh * T + t];
+      // exponent offset folding this V tile's pre-scale relative to the head reference
+      const float vshift = (float)((__float_as_int(p.vinv[(int64_t)bh * T + t]) >> 23) - vref_exp);
       ok = mbar_wait(s_full, t & 1, p.status, kDevTimeoutConsumer, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
-      const float c2 = cq * p.kinv[(int64_t)bh * T + t];
-      // pass 1: tile max
+      uint32_t s[BKV];
+      tmem_ld32_at<0>(tmem + lane_base + S_COL + 0, s);
+      tmem_ld32_at<32>(tmem + lane_base + S_COL + 32, s);
+      tmem_ld32_at<64>(tmem + lane_base + S_COL + 64, s);
+      tmem_ld32_at<96>(tmem + lane_base + S_COL + 96, s);
+      tmem_wait_ld();
+      reg_fence(s);
+      // scores in log2 units: x = s*c2 (+ bias); tile max
       float mx = -INFINITY;
-#pragma unroll 1
-      for (int ch = 0; ch < BKV / 32; ++ch) {
-        uint32_t s[32];
-        tmem_ld32(tmem + lane_base + S_COL + ch * 32, s);
-        tmem_wait_ld();
+      if (plain) {
+        float rmx = -INFINITY;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) mx = fmaxf(mx, fmaf(__uint_as_float(s[j]), c2, bt[ch * 32 + j]));
+        for (int j = 0; j < BKV; ++j) rmx = fmaxf(rmx, __uint_as_float(s[j]));
+        mx = rmx * c2;  // c2 >= 0
+      } else {
+#pragma unroll
+        for (int j = 0; j < BKV; ++j) {
+          const float x = fmaf(__uint_as_float(s[j]), c2, bt[j]);
+          s[j] = __float_as_uint(x);
+          mx = fmaxf(mx, x);
+        }
       }
-      const float m_new = fmaxf(m_run, mx);
-      const float m_use = (m_new == -INFINITY) ? 0.0f : m_new;
-      const float alpha = ex2(m_run - m_use);
-      // pass 2: p = 2^(s - m), row sum, fp16 hi/lo split written over S as the PV A operand
+      // The O rescale uses warp-collective tcgen05.ld/st, so the decision is taken per warp:
+      // if any row of the warp needs a higher reference max, every row raises its own to
+      // max(m_run, mx) (a no-op factor of 1 where it is unchanged) — still exact.
+      if (__any_sync(0xffffffffu, mx > m_run + RESCALE_THRESHOLD)) {
+        const float m_new = fmaxf(m_run, mx);
+        const float alpha = (m_new == -INFINITY) ? 1.0f : ex2(m_run - m_new);  // 0 on the first tile
+        if (t > 0) {
+#pragma unroll
+          for (int hh = 0; hh < D / 16; ++hh) {
+            uint32_t o[16];
+            tmem_ld16(tmem + lane_base + O_COL + hh * 16, o);
+            tmem_wait_ld();
+            reg_fence(o);
+#pragma unroll
+            for (int d = 0; d < 16; ++d) o[d] = __float_as_uint(__uint_as_float(o[d]) * alpha);
+            tmem_st16(tmem + lane_base + O_COL + hh * 16, o);
+          }
+        }
+        l_run *= alpha;
+        m_run = m_new;
+      }
+      // p' = 2^(x - m - vshift_t): relative to the running max and the head's V reference
+      const float msub = (m_run == -INFINITY ? 0.0f : m_run) + (-vshift);
+      const float c2p = plain ? c2 : 1.0f;
       float psum = 0.0f;
-#pragma unroll 1
+#pragma unroll
       for (int ch = 0; ch < BKV / 16; ++ch) {
-        uint32_t s[16], ph[8], pl[8];
-        tmem_ld16(tmem + lane_base + S_COL + ch * 16, s);
-        tmem_wait_ld();
+        uint32_t pk[16];
 #pragma unroll
         for (int j = 0; j < 16; j += 2) {
-          const float p0 = ex2(fmaf(__uint_as_float(s[j]), c2, bt[ch * 16 + j]) - m_use);
-          const float p1 = ex2(fmaf(__uint_as_float(s[j + 1]), c2, bt[ch * 16 + j + 1]) - m_use);
+          const float p0 = ex2(fmaf(__uint_as_float(s[ch * 16 + j]), c2p, -msub));
+          const float p1 = ex2(fmaf(__uint_as_float(s[ch * 16 + j + 1]), c2p, -msub));
           psum += p0 + p1;
-          const __half2 h = __floats2half2_rn(p0, p1);
-          const float2 hf = __half22float2(h);
-          const __half2 lo = __floats2half2_rn(p0 - hf.x, p1 - hf.y);
-          ph[j >> 1] = *reinterpret_cast<const uint32_t*>(&h);
-          pl[j >> 1] = *reinterpret_cast<const uint32_t*>(&lo);
+          // hi: p with the 13 low mantissa bits cleared (exact in fp16 for p >= 2^-14),
+          // lo: the exact fp32 remainder
+          const float h0 = __uint_as_float(__float_as_uint(p0) & 0xFFFFE000u);
+          const float h1 = __uint_as_float(__float_as_uint(p1) & 0xFFFFE000u);
+          const __half2 hh = __floats2half2_rn(h0, h1);
+          const __half2 ll = __floats2half2_rn(p0 - h0, p1 - h1);
+          pk[j >> 1] = *reinterpret_cast<const uint32_t*>(&hh);
+          pk[8 + (j >> 1)] = *reinterpret_cast<const uint32_t*>(&ll);
         }
-        const uint32_t dst = tmem + lane_base + S_COL + ch * 16;
-        asm volatile(
-            "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(dst),
-            "r"(ph[0]), "r"(ph[1]), "r"(ph[2]), "r"(ph[3]), "r"(ph[4]), "r"(ph[5]), "r"(ph[6]),
-            "r"(ph[7])
-            : "memory");
-        asm volatile(
-            "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(dst + 8),
-            "r"(pl[0]), "r"(pl[1]), "r"(pl[2]), "r"(pl[3]), "r"(pl[4]), "r"(pl[5]), "r"(pl[6]),
-            "r"(pl[7])
-            : "memory");
+        tmem_st16(tmem + lane_base + S_COL + ch * 16, pk);
       }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
-      l_run = l_run * alpha + psum;
-      m_run = m_use;
-      // merge the previous tile's P.V while the tensor core works on this one
-      if (t >= 1) {
-        const int pb = (t - 1) & 1;
-        ok = mbar_wait(&o_full[pb], ((t - 1) >> 1) & 1, p.status, kDevTimeoutConsumer, abort_flag);
-        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-        tc_fence_after();
-        const float vs = p.vinv[(int64_t)bh * T + t - 1];
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          uint32_t o[32];
-          tmem_ld32(tmem + lane_base + O_COL + pb * D + hh * 32, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int d = 0; d < 32; ++d)
-            o_acc[hh * 32 + d] = fmaf(__uint_as_float(o[d]), vs, o_acc[hh * 32 + d] * alpha_prev);
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&o_free[pb]);
-      }
-      alpha_prev = alpha;
+      l_run = fmaf(psum, ex2(-vshift), l_run);  // the row sum of the unshifted p
     }
     if (ok) {
-      const int pb = (T - 1) & 1;
-      ok = mbar_wait(&o_full[pb], ((T - 1) >> 1) & 1, p.status, kDevTimeoutEpilogue, abort_flag);
+      ok = mbar_wait(o_done, (T - 1) & 1, p.status, kDevTimeoutEpilogue, abort_flag);
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         tc_fence_after();
-        const float vs = p.vinv[(int64_t)bh * T + T - 1];
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          uint32_t o[32];
-          tmem_ld32(tmem + lane_base + O_COL + pb * D + hh * 32, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int d = 0; d < 32; ++d)
-            o_acc[hh * 32 + d] = fmaf(__uint_as_float(o[d]), vs, o_acc[hh * 32 + d] * alpha_prev);
-        }
+        uint32_t o0[32], o1[32];
+        tmem_ld32(tmem + lane_base + O_COL, o0);
+        tmem_ld32(tmem + lane_base + O_COL + 32, o1);
+        tmem_wait_ld();
+        reg_fence(o0);
+        reg_fence(o1);
         if (row_valid) {
-          const float inv = 1.0f / l_run;
+          const float f = vref / l_run;
           const int b = bh / p.H, h = bh % p.H;
           float* dst = p.out_blhd ? p.out + (((int64_t)b * p.Lq + qrow) * p.H + h) * D
                                   : p.out + ((int64_t)bh * p.Lq + qrow) * D;
 #pragma unroll
-          for (int d = 0; d < D; d += 4)
+          for (int d = 0; d < 32; d += 4) {
             *reinterpret_cast<float4*>(dst + d) =
-                make_float4(o_acc[d] * inv, o_acc[d + 1] * inv, o_acc[d + 2] * inv, o_acc[d + 3] * inv);
+                make_float4(__uint_as_float(o0[d]) * f, __uint_as_float(o0[d + 1]) * f,
+                            __uint_as_float(o0[d + 2]) * f, __uint_as_float(o0[d + 3]) * f);
+            *reinterpret_cast<float4*>(dst + 32 + d) =
+                make_float4(__uint_as_float(o1[d]) * f, __uint_as_float(o1[d + 1]) * f,
+                            __uint_as_float(o1[d + 2]) * f, __uint_as_float(o1[d + 3]) * f);
+          }
         }
       }
     }
