@@ -46,6 +46,8 @@ int triposplat_b200_workspace_reserve(uint64_t bytes);
 int triposplat_b200_workspace_stats(uint64_t* allocations, uint64_t* capacity_bytes);
 void triposplat_b200_workspace_release(void);
 int triposplat_b200_abi_version(void);
+/* Text of the last CUDA launch / tensor-map error seen by this thread's calls. */
+const char* triposplat_b200_last_error(void);
 /* Number of kernels this library has launched in this process (all devices). */
 uint64_t triposplat_b200_launch_count(void);
 /* While enabled, every launch is bracketed by CUDA events on its stream. */
@@ -54,6 +56,9 @@ void triposplat_b200_profile_enable(int on);
  * (0 GEMM tensor-core, 1 GEMM activation split, 2 GEMM scalar tail, 3 SDPA attention,
  * 4 SDPA split, 5 elementwise; n entries), the launch count and summed device ms. */
 int triposplat_b200_profile_collect(uint64_t* launches, double* total_ms, int n);
+/* Same; keep != 0 leaves the events registered (a captured CUDA graph records into them on
+ * every replay, so each read reflects the latest replay). */
+int triposplat_b200_profile_collect2(uint64_t* launches, double* total_ms, int n, int keep);
 
 /* ---------------------------------------------------------------- NF24 GEMM ----------
  * Y[M, N] = X[M, K] . W + bias,  W[k, n] = scale[n] * (256*q01[k, n] + q2[k, n]).
@@ -91,8 +96,8 @@ int triposplat_gemm_rnf8_avx512_tail(const float* x, const uint8_t* codes0_t,
  * memory (work being captured into a CUDA graph, hosts whose device memory is owned by
  * their own allocator or a fixed memory plan, loops that cannot absorb cudaMalloc's
  * device-wide synchronisation).  It calls no allocator: its scratch is a fixed 32 MiB
- * __device__ array per device, so it serves 2*M*Kp*2 + 4*M + 512 <= 32 MiB
- * (Kp = K rounded up to 8; e.g. M <= 8183 at K = 1024) and returns -6 beyond that, and
+ * __device__ array per device, so it serves split activations of up to 32 MiB
+ * (triposplat_b200_split_bytes(M, K); e.g. M <= 8184 at K = 1024), returns -6 beyond, and
  * -4 unless N % 16 == 0 with 16-byte aligned code planes.  All calls on a device share
  * the scratch: calls whose kernels may overlap on the GPU race, so order them on one
  * stream.  Nothing in the scratch needs to start at zero.  The first call on a device
@@ -103,6 +108,25 @@ int triposplat_gemm_nf24_noalloc(const float* x, const uint8_t* codes0_t, const 
                                  const float* codebook, const float* bias, float* out, int M,
                                  int K, int N, int stride_x, int stride_out, int threads,
                                  int stages);
+
+/* No reference counterpart: fused B200 entry points.  Activations pass between kernels in
+ * the GEMM's split format — fp16 hi/lo planes [M, Kp] plus one power-of-two scale per
+ * row — in a caller buffer of triposplat_b200_split_bytes(M, K) bytes
+ * (256-byte aligned), so LayerNorm / modulation / GELU / residual passes fold into the
+ * kernels that produce or consume the activations. */
+uint64_t triposplat_b200_split_bytes(int M, int K);
+int triposplat_b200_split_f32(const float* x, int M, int K, int stride_x, void* split);
+/* LayerNorm without affine, then (if shift and scale are non-null, [B, mod_ld] with
+ * b = row / rows_per_batch) h*(1+scale[b])+shift[b], written as a split buffer. */
+int triposplat_b200_ln_modulate_split(const float* x, int M, int C, float eps, const float* shift,
+                                      const float* scale, int mod_ld, int rows_per_batch,
+                                      void* split);
+/* NF24 GEMM over a split buffer; mode 0 store, 1 GELU(tanh) store, 2 out += gate[b]*y
+ * (gate [B, gate_ld], b = row / rows_per_batch), 3 out += y.  N % 16 == 0. */
+int triposplat_b200_gemm_nf24_split(const void* split, int M, int K, const int16_t* code01_t,
+                                    const int8_t* q2_t, const float* scale, const float* bias,
+                                    float* out, int N, int stride_out, int mode,
+                                    const float* gate, int gate_ld, int rows_per_batch);
 
 /* replaces scripts/gemm_nf24_i16_avx512.c:222-224 (rows per CTA tile here) */
 int triposplat_gemm_rnf8_avx512_row_tile(void);

@@ -128,3 +128,67 @@ def test_gemm_error_codes():
     assert f(hp, p, p, p, p, p, p, p, p, p, 2, 16, 16, 16, 16, 0, 3) == -9
     assert lib.triposplat_gemm_rnf8_avx512_residual_mode() == 4
     assert lib.triposplat_b200_status() == 0
+
+
+def _split_buf(lib, M, K):
+    n = int(lib.triposplat_b200_split_bytes(M, K))
+    t = torch.empty(n + 256, dtype=torch.uint8, device="cuda")
+    return t, (t.data_ptr() + 255) & ~255
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2, 3])
+def test_gemm_split_epilogues(oracle, mode):
+    """Split buffer + fused epilogues: store, GELU, gated residual, residual."""
+    import _native
+
+    lib = _native.load()
+    _native.use_current_stream(lib)
+    g = torch.Generator().manual_seed(40 + mode)
+    B, L, K, N = 2, 150, 1024, 384
+    M = B * L
+    x = torch.randn(M, K, generator=g).numpy()
+    c01, q2, sc = _pack(torch.randn(N, K, generator=g) * 0.02)
+    b = (torch.randn(N, generator=g) * 0.01).numpy()
+    base = torch.randn(M, N, generator=g).numpy()
+    gate = torch.randn(B, N, generator=g).numpy()
+    y = oracle.gemm_nf24(x, c01, q2, sc, b)
+    ref = {0: y, 1: oracle.gelu_tanh(y), 2: base + np.repeat(gate, L, axis=0) * y, 3: base + y}[mode]
+    keep, sp = _split_buf(lib, M, K)
+    xc = _cuda(x)
+    assert lib.triposplat_b200_split_f32(xc.data_ptr(), M, K, K, sp) == 0
+    out = _cuda(base.copy())
+    gc = _cuda(gate)
+    w = [_cuda(a) for a in (c01, q2, sc, b)]  # keep the device copies alive
+    st = lib.triposplat_b200_gemm_nf24_split(sp, M, K, w[0].data_ptr(), w[1].data_ptr(),
+                                             w[2].data_ptr(), w[3].data_ptr(), out.data_ptr(),
+                                             N, N, mode, gc.data_ptr(), N, L)
+    assert st == 0
+    torch.cuda.synchronize()
+    _assert_close(out.cpu().numpy(), ref)
+
+
+def test_ln_modulate_split_then_gemm(oracle):
+    import _native
+
+    lib = _native.load()
+    _native.use_current_stream(lib)
+    g = torch.Generator().manual_seed(77)
+    B, L, C, N = 2, 97, 1024, 256
+    x = (torch.randn(B, L, C, generator=g) * 2 + 0.5).numpy()
+    shift = (torch.randn(B, C, generator=g) * 0.1).numpy()
+    scale = (torch.randn(B, C, generator=g) * 0.1).numpy()
+    c01, q2, sc = _pack(torch.randn(N, C, generator=g) * 0.02)
+    b = np.zeros(N, np.float32)
+    a = oracle.modulate(oracle.layernorm(x, eps=1e-6), scale, shift).reshape(B * L, C)
+    ref = oracle.gemm_nf24(a, c01, q2, sc, b)
+    keep, sp = _split_buf(lib, B * L, C)
+    xc, shc, scc = _cuda(x), _cuda(shift), _cuda(scale)
+    assert lib.triposplat_b200_ln_modulate_split(xc.data_ptr(), B * L, C, 1e-6, shc.data_ptr(),
+                                                 scc.data_ptr(), C, L, sp) == 0
+    out = torch.empty(B * L, N, device="cuda")
+    w = [_cuda(a) for a in (c01, q2, sc, b)]  # keep the device copies alive
+    assert lib.triposplat_b200_gemm_nf24_split(sp, B * L, C, w[0].data_ptr(), w[1].data_ptr(),
+                                               w[2].data_ptr(), w[3].data_ptr(), out.data_ptr(),
+                                               N, N, 0, None, 0, 1) == 0
+    torch.cuda.synchronize()
+    _assert_close(out.cpu().numpy(), ref)

@@ -10,7 +10,7 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def _setup(spec, seed=0):
+def _setup(spec, seed=0, fused=True):
     from flow_model import FlowModelB200, make_weights, rope_freqs, timestep_frequencies
     from flow_ref import FlowOracle, weights_to_numpy
     from oracle import Oracle
@@ -18,7 +18,7 @@ def _setup(spec, seed=0):
     w = make_weights(spec, seed=seed, device="cuda")
     W, P = weights_to_numpy(w)
     orc = FlowOracle(Oracle(), spec, W, P, rope_freqs(spec), timestep_frequencies(spec))
-    return FlowModelB200(w), orc
+    return FlowModelB200(w, fused=fused), orc
 
 
 def _inputs(spec, seed=1, B=2):
@@ -46,11 +46,12 @@ def test_gpu_packer_matches_cpu_packer():
     assert torch.equal(s_cpu[0], s_gpu[0].cpu())
 
 
-def test_small_model_forward_vs_oracle():
+@pytest.mark.parametrize("fused", [True, False])
+def test_small_model_forward_vs_oracle(fused):
     from flow_model import FlowSpec
 
     spec = FlowSpec.small(blocks=2)
-    model, orc = _setup(spec)
+    model, orc = _setup(spec, fused=fused)
     x, cam, cond = _inputs(spec)
     t = np.array([730.0, 730.0], np.float32)
     vl, vc = model.forward(torch.from_numpy(x).cuda(), torch.from_numpy(cam).cuda(),
@@ -99,3 +100,24 @@ def test_full_model_step_is_finite():
     smp.step(0)
     torch.cuda.synchronize()
     assert bool(torch.isfinite(smp.x_lat[0]).all()) and bool(torch.isfinite(smp.x_cam[0]).all())
+
+
+def test_graph_replay_matches_eager_steps():
+    """A sampler step recorded as a CUDA graph gives exactly the eager step's result."""
+    from flow_model import CfgEulerSampler, FlowModelB200, FlowSpec, make_weights
+
+    spec = FlowSpec.small(blocks=2)
+    w = make_weights(spec, seed=5, device="cuda")
+    x, cam, cond = _inputs(spec, seed=6, B=1)
+    ins = [torch.from_numpy(a).cuda() for a in (x, cam, cond, np.zeros_like(cond))]
+    eager = CfgEulerSampler(FlowModelB200(w), steps=3)
+    eager.load(*ins)
+    el, ec = (t.clone() for t in eager.run())
+    graphed = CfgEulerSampler(FlowModelB200(w), steps=3)
+    graphed.load(*ins)
+    graphed.prepare_capture()
+    graphed.load(*ins)  # prepare_capture ran one eager step; start again from the inputs
+    graphed.record_graph()
+    gl, gc = graphed.run()
+    torch.cuda.synchronize()
+    assert torch.equal(el, gl) and torch.equal(ec, gc)

@@ -32,8 +32,10 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "triposplat_b200_workspace_release": ([], None),
     "triposplat_b200_abi_version": ([], I),
     "triposplat_b200_launch_count": ([], ctypes.c_uint64),
+    "triposplat_b200_last_error": ([], ctypes.c_char_p),
     "triposplat_b200_profile_enable": ([I], None),
     "triposplat_b200_profile_collect": ([U64P, ctypes.POINTER(ctypes.c_double), I], I),
+    "triposplat_b200_profile_collect2": ([U64P, ctypes.POINTER(ctypes.c_double), I, I], I),
     # NF24 GEMM
     "triposplat_gemm_rnf8_avx512": ([VP] * 10 + [I] * 7, I),
     "triposplat_gemm_rnf8_avx512_range": ([VP] * 10 + [I] * 9, I),
@@ -41,6 +43,10 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "triposplat_gemm_rnf8_avx512_row_tile": ([], I),
     "triposplat_gemm_rnf8_avx512_residual_mode": ([], I),
     "triposplat_gemm_nf24_noalloc": ([VP] * 10 + [I] * 7, I),
+    "triposplat_b200_split_bytes": ([I, I], ctypes.c_uint64),
+    "triposplat_b200_split_f32": ([VP, I, I, I, VP], I),
+    "triposplat_b200_ln_modulate_split": ([VP, I, I, F, VP, VP, I, I, VP], I),
+    "triposplat_b200_gemm_nf24_split": ([VP, I, I] + [VP] * 5 + [I, I, I, VP, I, I], I),
     # exact SDPA
     "triposplat_sdpa_f32_avx512_exact_q8t512": ([VP] * 5 + [I] * 8, I),
     "triposplat_sdpa_f32_avx512_exact_q8": ([VP] * 5 + [I] * 8, I),
@@ -133,11 +139,11 @@ def require_cuda(*tensors, what: str = "tensor") -> None:
 KERNEL_FAMILIES = ("gemm_tc", "gemm_split", "gemm_simt", "sdpa_attn", "sdpa_split", "elementwise")
 
 
-def profile_collect(lib) -> dict:
+def profile_collect(lib, keep: bool = False) -> dict:
     n = len(KERNEL_FAMILIES)
     launches = (ctypes.c_uint64 * n)()
     ms = (ctypes.c_double * n)()
-    st = lib.triposplat_b200_profile_collect(launches, ms, n)
+    st = lib.triposplat_b200_profile_collect2(launches, ms, n, int(keep))
     if st != 0:
         raise RuntimeError(f"profile_collect returned {st}")
     return {k: {"launches": int(launches[i]), "ms": float(ms[i])} for i, k in enumerate(KERNEL_FAMILIES)}

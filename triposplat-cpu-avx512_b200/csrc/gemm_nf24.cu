@@ -4,9 +4,10 @@
 //   W[k, n] = scale[n] * (256 * q01[k, n] + q2[k, n]),   q01 int16 [K, N], q2 int8 [K, N]
 //
 // Design.
-//  * X (fp32) is split once per call by `nf24_split_rows` into two exact-sum fp16 planes
-//    X' = hi + lo after an exact per-row power-of-two pre-scale (undone in the epilogue),
-//    so fp16's range never clips and hi + lo carries ~22 significant bits.
+//  * X (fp32) is split by `nf24_split_rows` (or a producer such as the fused LayerNorm)
+//    into two exact-sum fp16 planes X' = hi + lo after an exact per-row power-of-two
+//    pre-scale (undone in the epilogue), so fp16's range never clips and hi + lo carries
+//    ~22 significant bits.
 //  * W/256 = q01 + q2/256 is split into two fp16 operands that are EXACT for every code
 //    |q01| <= 1023 (the packer emits |q01| <= 636):
 //        A1 = 2*floor(q01/2)          (even integer)
@@ -22,7 +23,8 @@
 //    (64 k) is therefore accumulated into a FRESH TMEM partial (double-buffered) and
 //    promoted into round-to-nearest fp32 running sums held in the epilogue warps'
 //    registers, which keeps the error at the level of a 64-long dot product.
-//    Epilogue: y = sum * rowscale[m] * 256*scale[n] + bias[n].
+//    Epilogue: y = sum * rowscale[m] * 256*scale[n] + bias[n], then one of: store,
+//    GELU(tanh) + store, gated residual out += gate[b] * y, residual out += y.
 //
 // Warp roles (448 threads, one CTA per SM):
 //   warp 0       TMA producer (codes and X planes)
@@ -65,18 +67,31 @@ constexpr int NUM_BARS = 2 * XS + 2 * CS + 2 * AS + 5;
 constexpr int SMEM_BYTES = 1024 /*align slack*/ + XS * X_STAGE + CS * C_STAGE + BM * 4 +
                            NUM_BARS * 8 + 16;
 
+enum Epilogue : int { kStore = 0, kGelu = 1, kGatedResidual = 2, kResidual = 3 };
+
 struct Params {
-  const float* rscale;  // [M] inverse row pre-scale of the split X
+  const float* rscale;  // [Mp] inverse row pre-scale of the split X
   const float* scale;   // [N]
   const float* bias;    // [N]
-  float* out;           // [M, stride_out]
+  float* out;           // [M, stride_out]; read-modify-write for the residual modes
   int M, K, N, start, count, stride_out;
+  int mode;             // Epilogue
+  const float* gate;    // kGatedResidual: gate[(m / rows_per_batch) * gate_ld + n]
+  int gate_ld, rows_per_batch;
   int* status;
 };
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float inner = 0.7978845608028654f * (x + 0.044715f * (x * x * x));
+  return 0.5f * x * (1.0f + tanhf(inner));
+}
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 
+// 14 warps put four warps on some SM sub-partitions (16K registers each): 128 registers
+// per thread is the most that can launch.
+template <int MODE>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     nf24_gemm_tc(const __grid_constant__ CUtensorMap tm_xhi,
                  const __grid_constant__ CUtensorMap tm_xlo,
@@ -87,7 +102,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* xs = smem;
   uint8_t* cs = xs + XS * X_STAGE;
-  float* rs_s = reinterpret_cast<float*>(cs + CS * C_STAGE);
+  float* rs_s = reinterpret_cast<float*>(cs + CS * C_STAGE);  // [BM] row scales
   uint64_t* bars = reinterpret_cast<uint64_t*>(rs_s + BM);
   uint64_t* x_full = bars;
   uint64_t* x_empty = x_full + XS;
@@ -264,12 +279,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t col = tmem + lane_base + ACC_COL + b * BM + half * EPI_COLS;
 #pragma unroll
       for (int q = 0; q < EPI_COLS / 16; ++q) {
-        uint32_t r[16];
-        tmem_ld16(col + q * 16, r);
+        uint32_t v[16];
+        tmem_ld16(col + q * 16, v);
         tmem_wait_ld();
-        reg_fence(r);
+        reg_fence(v);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) sum[q * 16 + j] += __uint_as_float(r[j]);
+        for (int j = 0; j < 16; ++j) sum[q * 16 + j] += __uint_as_float(v[j]);
       }
       tc_fence_before();
       __syncwarp();
@@ -278,15 +293,51 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (ok) {
       const int nloc = n0 + nl;
       if (nloc < p.count) {
-        const float sc = p.scale[p.start + nloc] * 256.0f;
-        const float bi = p.bias[p.start + nloc];
+        const int n = p.start + nloc;
+        const float sc = p.scale[n] * 256.0f;
+        const float bi = p.bias[n];
         float* out_col = p.out + nloc;
         const int mbase = m0 + half * EPI_COLS;
+        const int rows = p.M - mbase;  // rows of this half that exist
+        // fold the row pre-scale into the sums, then one fully unrolled loop per mode so
+        // sum[] stays in registers
+        const float* rsh = rs_s + half * EPI_COLS;
 #pragma unroll
-        for (int j = 0; j < EPI_COLS; ++j) {
-          const int m = mbase + j;
-          if (m < p.M)
-            out_col[(int64_t)m * p.stride_out] = fmaf(sum[j] * rs_s[half * EPI_COLS + j], sc, bi);
+        for (int j = 0; j < EPI_COLS; ++j) sum[j] *= rsh[j];
+        if constexpr (MODE == kStore) {
+#pragma unroll
+          for (int j = 0; j < EPI_COLS; ++j)
+            if (j < rows) out_col[(int64_t)(mbase + j) * p.stride_out] = fmaf(sum[j], sc, bi);
+        } else if constexpr (MODE == kGelu) {
+#pragma unroll
+          for (int j = 0; j < EPI_COLS; ++j)
+            if (j < rows) out_col[(int64_t)(mbase + j) * p.stride_out] = gelu_tanh(fmaf(sum[j], sc, bi));
+        } else {
+          // residual modes: batch 8 independent loads of the old values before the
+          // dependent stores so the read latency is paid once per batch, not per row
+          float g0 = 1.0f, g1 = 1.0f;
+          int jb = EPI_COLS;
+          if constexpr (MODE == kGatedResidual) {
+            // at most one batch boundary falls inside these 96 rows
+            const int b0 = mbase / p.rows_per_batch;
+            jb = (b0 + 1) * p.rows_per_batch - mbase;
+            g0 = p.gate[(int64_t)b0 * p.gate_ld + n];
+            g1 = jb < rows ? p.gate[(int64_t)(b0 + 1) * p.gate_ld + n] : 0.0f;
+          }
+#pragma unroll
+          for (int j0 = 0; j0 < EPI_COLS; j0 += 8) {
+            float prev[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              prev[u] = (j0 + u < rows) ? out_col[(int64_t)(mbase + j0 + u) * p.stride_out] : 0.0f;
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const int j = j0 + u;
+              if (j < rows)
+                out_col[(int64_t)(mbase + j) * p.stride_out] =
+                    fmaf(j < jb ? g0 : g1, fmaf(sum[j], sc, bi), prev[u]);
+            }
+          }
         }
       }
     }
@@ -301,36 +352,100 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
-// X fp32 [M, K] (row stride stride_x) -> hi, lo fp16 [M, Kp] and rscale [M].
-// One warp per row; the row is pre-scaled by 2^s so its max lands in [2^14, 2^15).
-__global__ void nf24_split_rows(const float* __restrict__ x, int M, int K, int Kp, int stride_x,
-                                __half* __restrict__ hi, __half* __restrict__ lo,
-                                float* __restrict__ rscale) {
+// X fp32 [M, K] (row stride stride_x) -> hi, lo fp16 [M, Kp] and inverse row scales rs [Mp].
+// One warp per row; the row is pre-scaled by 2^s so its max lands in [2^14, 2^15) (s clamped
+// to [-60, 60]).  Rows M..Mp-1 only get rs = 0 so every scale the GEMM reads is defined.
+__device__ __forceinline__ int split_shift(float mx) {
+  if (!(mx > 0.0f) || !(mx <= 3.402823466e38f)) return 0;
+  const int s = 14 - ilogbf(mx);
+  return s < -60 ? -60 : (s > 60 ? 60 : s);
+}
+
+__global__ void nf24_split_rows(const float* __restrict__ x, int M, int Mp, int K, int Kp,
+                                int stride_x, __half* __restrict__ hi, __half* __restrict__ lo,
+                                float* __restrict__ rs) {
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (row >= M) return;
+  if (row >= Mp) return;
+  if (row >= M) {
+    if (lane == 0) rs[row] = 0.0f;
+    return;
+  }
   const float* xr = x + (int64_t)row * stride_x;
   float mx = 0.0f;
   for (int k = lane; k < K; k += 32) mx = fmaxf(mx, fabsf(xr[k]));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  int shift = 0;
-  if (mx > 0.0f && mx <= 3.402823466e38f) {
-    shift = 14 - ilogbf(mx);
-    shift = shift < -60 ? -60 : (shift > 60 ? 60 : shift);
-  }
+  const int shift = split_shift(mx);
   __half* hr = hi + (int64_t)row * Kp;
   __half* lr = lo + (int64_t)row * Kp;
   for (int k = lane * 2; k < Kp; k += 64) {
-    float a = (k < K) ? ldexpf(xr[k], shift) : 0.0f;
-    float b = (k + 1 < K) ? ldexpf(xr[k + 1], shift) : 0.0f;
+    const float a = k < K ? ldexpf(xr[k], shift) : 0.0f;
+    const float b = k + 1 < K ? ldexpf(xr[k + 1], shift) : 0.0f;
     const __half2 h = __floats2half2_rn(a, b);
     const float2 hf = __half22float2(h);
-    const __half2 l = __floats2half2_rn(a - hf.x, b - hf.y);
     *reinterpret_cast<__half2*>(hr + k) = h;
-    *reinterpret_cast<__half2*>(lr + k) = l;
+    *reinterpret_cast<__half2*>(lr + k) = __floats2half2_rn(a - hf.x, b - hf.y);
   }
-  if (lane == 0) rscale[row] = ldexpf(1.0f, -shift);
+  if (lane == 0) rs[row] = ldexpf(1.0f, -shift);
+}
+
+// LayerNorm (no affine; the reference's two-pass mean / biased variance / 1/sqrtf(var+eps),
+// scripts/native_norm_rope_avx512.c:26-41), optional adaLN modulation h*(1+scale[b])+shift[b]
+// (scripts/native_block_elementwise_avx512.c:9-22), written straight to the GEMM's split
+// format (per-row scale as nf24_split_rows).  One warp per row.
+__device__ __forceinline__ float ln_mod_value(const float* xr, int c, float mean, float inv,
+                                              const float* sh, const float* sc) {
+  float a = (xr[c] - mean) * inv;
+  if (sc) a = a * (1.0f + sc[c]) + sh[c];
+  return a;
+}
+
+__global__ void ln_modulate_split(const float* __restrict__ x, int M, int Mp, int C, int Kp,
+                                  float eps, const float* __restrict__ shift,
+                                  const float* __restrict__ scale, int mod_ld, int rows_per_batch,
+                                  __half* __restrict__ hi, __half* __restrict__ lo,
+                                  float* __restrict__ rs) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= Mp) return;
+  if (row >= M) {
+    if (lane == 0) rs[row] = 0.0f;
+    return;
+  }
+  const float* xr = x + (int64_t)row * C;
+  float s = 0.0f;
+  for (int c = lane; c < C; c += 32) s += xr[c];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s / (float)C;
+  float v = 0.0f;
+  for (int c = lane; c < C; c += 32) {
+    const float d = xr[c] - mean;
+    v = fmaf(d, d, v);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const float inv = 1.0f / sqrtf(v / (float)C + eps);
+  const int b = row / rows_per_batch;
+  const float* sh = shift ? shift + (int64_t)b * mod_ld : nullptr;
+  const float* sc = scale ? scale + (int64_t)b * mod_ld : nullptr;
+  float mx = 0.0f;
+  for (int c = lane; c < C; c += 32) mx = fmaxf(mx, fabsf(ln_mod_value(xr, c, mean, inv, sh, sc)));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const int shf = split_shift(mx);
+  __half* hr = hi + (int64_t)row * Kp;
+  __half* lr = lo + (int64_t)row * Kp;
+  for (int k = lane * 2; k < Kp; k += 64) {
+    const float a = k < C ? ldexpf(ln_mod_value(xr, k, mean, inv, sh, sc), shf) : 0.0f;
+    const float bb = k + 1 < C ? ldexpf(ln_mod_value(xr, k + 1, mean, inv, sh, sc), shf) : 0.0f;
+    const __half2 h = __floats2half2_rn(a, bb);
+    const float2 hf = __half22float2(h);
+    *reinterpret_cast<__half2*>(hr + k) = h;
+    *reinterpret_cast<__half2*>(lr + k) = __floats2half2_rn(a - hf.x, bb - hf.y);
+  }
+  if (lane == 0) rs[row] = ldexpf(1.0f, -shf);
 }
 
 // Reference-order scalar kernel: one thread per output, acc = bias, then an in-order
@@ -355,6 +470,102 @@ __global__ void nf24_gemm_simt(const float* __restrict__ x, const int16_t* __res
 
 }  // namespace gemm
 
+// Split activations: planes [M, Kp] (Kp = K rounded to 8) and row scales [Mp] (Mp = M
+// rounded to 4), laid out back to back in one buffer of split_bytes(M, K).
+struct SplitPlanes {
+  const __half* hi;
+  const __half* lo;
+  const float* rs;
+  int M, K, Kp, Mp;
+};
+
+static inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+static size_t split_bytes(int M, int K) {
+  const size_t Kp = (size_t)((K + 7) & ~7), Mp = (size_t)((M + 3) & ~3);
+  return 2 * align256((size_t)M * Kp * 2) + align256(Mp * 4);
+}
+
+static SplitPlanes split_layout(uint8_t* base, int M, int K) {
+  SplitPlanes sp;
+  sp.M = M;
+  sp.K = K;
+  sp.Kp = (K + 7) & ~7;
+  sp.Mp = (M + 3) & ~3;
+  const size_t plane = align256((size_t)M * sp.Kp * 2);
+  sp.hi = reinterpret_cast<const __half*>(base);
+  sp.lo = reinterpret_cast<const __half*>(base + plane);
+  sp.rs = reinterpret_cast<const float*>(base + 2 * plane);
+  return sp;
+}
+
+static int launch_split(const float* x, int stride_x, const SplitPlanes& sp, cudaStream_t stream) {
+  using namespace gemm;
+  LaunchScope scope(kKGemmSplit, stream);
+  nf24_split_rows<<<(sp.Mp + 7) / 8, 256, 0, stream>>>(
+      x, sp.M, sp.Mp, sp.K, sp.Kp, stride_x, const_cast<__half*>(sp.hi), const_cast<__half*>(sp.lo),
+      const_cast<float*>(sp.rs));
+  return launch_status();
+}
+
+struct EpilogueArgs {
+  int mode = gemm::kStore;
+  const float* gate = nullptr;
+  int gate_ld = 0, rows_per_batch = 1;
+};
+
+// Tensor-core GEMM on already split activations.
+static int launch_tc(const SplitPlanes& sp, const int16_t* c01, const int8_t* q2,
+                     const float* scale, const float* bias, float* out, int N, int start,
+                     int count, int stride_out, const EpilogueArgs& ep, int* status,
+                     cudaStream_t stream) {
+  using namespace gemm;
+  const int M = sp.M, K = sp.K;
+  CUtensorMap m_hi, m_lo, m_c16, m_c8;
+  {
+    const uint64_t dims[2] = {(uint64_t)sp.Kp, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)sp.Kp * 2};
+    const uint32_t box[2] = {BK, BM};
+    if (!encode_tmap(&m_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(sp.hi), dims,
+                     strides, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tmap(&m_lo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(sp.lo), dims,
+                     strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return kLaunchFailed;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)K};
+    const uint64_t s16[1] = {(uint64_t)N * 2};
+    const uint64_t s8[1] = {(uint64_t)N};
+    const uint32_t box[2] = {BN, BK};
+    if (!encode_tmap(&m_c16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<int16_t*>(c01), dims,
+                     s16, box, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode_tmap(&m_c8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(q2), dims, s8,
+                     box, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return kLaunchFailed;
+  }
+  Params prm{sp.rs, scale, bias, out, M, K, N, start, count, stride_out,
+             ep.mode, ep.gate, ep.gate_ld, ep.rows_per_batch, status};
+  dim3 grid((count + BN - 1) / BN, (M + BM - 1) / BM);
+  static uint64_t attr_done[4] = {0, 0, 0, 0};  // per mode: one bit per device ordinal
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto run = [&](auto kernel, int mode) {
+    if (!(attr_done[mode] >> (dev & 63) & 1)) {
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+      attr_done[mode] |= 1ull << (dev & 63);
+    }
+    LaunchScope scope(kKGemmTc, stream);
+    kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(m_hi, m_lo, m_c16, m_c8, prm);
+  };
+  switch (ep.mode) {
+    case kGelu: run(nf24_gemm_tc<kGelu>, kGelu); break;
+    case kGatedResidual: run(nf24_gemm_tc<kGatedResidual>, kGatedResidual); break;
+    case kResidual: run(nf24_gemm_tc<kResidual>, kResidual); break;
+    default: run(nf24_gemm_tc<kStore>, kStore); break;
+  }
+  return launch_status();
+}
+
 // Host launcher shared by the full / range / tail entry points.
 static int gemm_launch(const float* x, const int16_t* c01, const int8_t* q2, const float* scale,
                        const float* bias, float* out, int M, int K, int N, int start, int count,
@@ -375,57 +586,12 @@ static int gemm_launch(const float* x, const int16_t* c01, const int8_t* q2, con
                                              stride_x, stride_out);
     return launch_status();
   }
-  const int Kp = (K + 7) & ~7;
-  const size_t plane = (size_t)M * Kp * 2;
-  uint8_t* ws = static_cast<uint8_t*>(workspace(2 * plane + (size_t)M * 4 + 256, stream));
+  uint8_t* ws = static_cast<uint8_t*>(workspace(split_bytes(M, K), stream));
   if (!ws) return kWorkspace;
-  __half* hi = reinterpret_cast<__half*>(ws);
-  __half* lo = reinterpret_cast<__half*>(ws + plane);
-  float* rscale = reinterpret_cast<float*>(ws + 2 * plane);
-  {
-    LaunchScope scope(kKGemmSplit, stream);
-    nf24_split_rows<<<(M + 7) / 8, 256, 0, stream>>>(x, M, K, Kp, stride_x, hi, lo, rscale);
-  }
-  if ((st = launch_status()) != kOk) return st;
-
-  CUtensorMap m_hi, m_lo, m_c16, m_c8;
-  {
-    const uint64_t dims[2] = {(uint64_t)Kp, (uint64_t)M};
-    const uint64_t strides[1] = {(uint64_t)Kp * 2};
-    const uint32_t box[2] = {BK, BM};
-    if (!encode_tmap(&m_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, hi, dims, strides, box,
-                     CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_tmap(&m_lo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, lo, dims, strides, box,
-                     CU_TENSOR_MAP_SWIZZLE_128B))
-      return kLaunchFailed;
-  }
-  {
-    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)K};
-    const uint64_t s16[1] = {(uint64_t)N * 2};
-    const uint64_t s8[1] = {(uint64_t)N};
-    const uint32_t box[2] = {BN, BK};
-    if (!encode_tmap(&m_c16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<int16_t*>(c01), dims,
-                     s16, box, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode_tmap(&m_c8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(q2), dims, s8,
-                     box, CU_TENSOR_MAP_SWIZZLE_NONE))
-      return kLaunchFailed;
-  }
-  {
-    static uint64_t attr_done = 0;  // one bit per device ordinal
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!(attr_done >> dev & 1)) {
-      cudaFuncSetAttribute(nf24_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-      attr_done |= 1ull << dev;
-    }
-  }
-  Params prm{rscale, scale, bias, out, M, K, N, start, count, stride_out, device_status()};
-  dim3 grid((count + BN - 1) / BN, (M + BM - 1) / BM);
-  {
-    LaunchScope scope(kKGemmTc, stream);
-    nf24_gemm_tc<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(m_hi, m_lo, m_c16, m_c8, prm);
-  }
-  return launch_status();
+  const SplitPlanes sp = split_layout(ws, M, K);
+  if ((st = launch_split(x, stride_x, sp, stream)) != kOk) return st;
+  return launch_tc(sp, c01, q2, scale, bias, out, N, start, count, stride_out, EpilogueArgs(),
+                   device_status(), stream);
 }
 
 }  // namespace tsb
@@ -500,6 +666,86 @@ int triposplat_gemm_rnf8_avx512_residual_mode(void) { return 4; }
 
 }  // extern "C"
 
+// ---------------------------------------------------------------------------
+// Fused entry points for B200 (no reference counterpart).  They pass activations
+// between kernels in the GEMM's split format — fp16 hi/lo planes plus one power-of-two
+// scale per row — so the LayerNorm, modulation, GELU and residual
+// passes of the block are folded into the kernels that produce or consume them.
+// A split buffer holds triposplat_b200_split_bytes(M, K) bytes.
+// ---------------------------------------------------------------------------
+extern "C" {
+
+uint64_t triposplat_b200_split_bytes(int M, int K) {
+  if (M <= 0 || K <= 0) return 0;
+  return tsb::split_bytes(M, K);
+}
+
+// X fp32 [M, K] (row stride stride_x) -> split buffer.
+int triposplat_b200_split_f32(const float* x, int M, int K, int stride_x, void* split) {
+  using namespace tsb;
+  if (!x || !split) return kNullPointer;
+  if (M <= 0 || K <= 0 || stride_x < K) return kBadDims;
+  if (reinterpret_cast<uintptr_t>(split) & 255) return kBadAlignment;
+  int st = entry_check();
+  if (st != kOk) return st;
+  return launch_split(x, stride_x, split_layout(static_cast<uint8_t*>(split), M, K),
+                      current_stream());
+}
+
+// LayerNorm without affine (eps) over rows of x [M, C], then, if shift and scale are
+// given ([B, mod_ld], batch b = row / rows_per_batch), h*(1+scale[b]) + shift[b]; the
+// result goes straight to a split buffer.
+int triposplat_b200_ln_modulate_split(const float* x, int M, int C, float eps, const float* shift,
+                                      const float* scale, int mod_ld, int rows_per_batch,
+                                      void* split) {
+  using namespace tsb;
+  if (!x || !split || (!shift) != (!scale)) return kNullPointer;
+  if (M <= 0 || C <= 0 || eps < 0.0f || rows_per_batch <= 0 || (scale && mod_ld < C))
+    return kBadDims;
+  if (reinterpret_cast<uintptr_t>(split) & 255) return kBadAlignment;
+  int st = entry_check();
+  if (st != kOk) return st;
+  const SplitPlanes sp = split_layout(static_cast<uint8_t*>(split), M, C);
+  cudaStream_t stream = current_stream();
+  {
+    LaunchScope scope(kKElementwise, stream);
+    gemm::ln_modulate_split<<<(sp.Mp + 7) / 8, 256, 0, stream>>>(
+        x, M, sp.Mp, C, sp.Kp, eps, shift, scale, mod_ld, rows_per_batch,
+        const_cast<__half*>(sp.hi), const_cast<__half*>(sp.lo), const_cast<float*>(sp.rs));
+  }
+  return launch_status();
+}
+
+// NF24 GEMM on a split buffer (M x K) with one of the epilogues
+//   mode 0: out = y;  1: out = GELU_tanh(y);  2: out += gate[row / rows_per_batch] * y
+//   (gate row stride gate_ld, column n);  3: out += y,
+// y = X . W + bias over all N columns (N % 16 == 0), out row stride stride_out.
+int triposplat_b200_gemm_nf24_split(const void* split, int M, int K, const int16_t* code01_t,
+                                    const int8_t* q2_t, const float* scale, const float* bias,
+                                    float* out, int N, int stride_out, int mode,
+                                    const float* gate, int gate_ld, int rows_per_batch) {
+  using namespace tsb;
+  if (!split || !code01_t || !q2_t || !scale || !bias || !out) return kNullPointer;
+  if (M <= 0 || K <= 0 || N <= 0 || stride_out < N || mode < 0 || mode > 3) return kBadDims;
+  if (mode == gemm::kGatedResidual && (!gate || gate_ld < N || rows_per_batch <= 0))
+    return kBadRange;
+  if ((N % 16) != 0 || ((reinterpret_cast<uintptr_t>(code01_t) | reinterpret_cast<uintptr_t>(q2_t) |
+                         reinterpret_cast<uintptr_t>(split)) & 15) != 0)
+    return kBadAlignment;
+  int st = entry_check();
+  if (st != kOk) return st;
+  EpilogueArgs ep;
+  ep.mode = mode;
+  ep.gate = gate;
+  ep.gate_ld = gate_ld;
+  ep.rows_per_batch = rows_per_batch > 0 ? rows_per_batch : 1;
+  return launch_tc(split_layout(static_cast<uint8_t*>(const_cast<void*>(split)), M, K), code01_t,
+                   q2_t, scale, bias, out, N, 0, N, stride_out, ep, device_status(),
+                   current_stream());
+}
+
+}  // extern "C"
+
 // ===========================================================================
 // Allocation-free NF24 GEMM.
 //
@@ -509,11 +755,12 @@ int triposplat_gemm_rnf8_avx512_residual_mode(void) { return 4; }
 // caching allocator), and latency-critical loops that cannot absorb cudaMalloc's
 // implicit device-wide synchronisation.  For them this entry point computes exactly
 // what triposplat_gemm_rnf8_avx512 computes, but takes its scratch (the fp16 hi/lo
-// activation planes and the per-row scales) from the fixed array below instead of the
+// activation planes and their row scales) from the fixed array below instead of the
 // library workspace, and never allocates.
 //
 // Limits and sharing: the scratch is 32 MiB per device and holds 2*M*Kp fp16 values plus
-// M floats (Kp = K rounded up to 8); larger problems are rejected with -6.  Every call on
+// Mp floats (Kp = K rounded up to 8, Mp = M rounded up to 4, each part padded to 256
+// bytes); larger problems are rejected with -6.  Every call on
 // a device uses the same array, so two calls whose kernels overlap on the GPU (different
 // streams, no ordering between them) race on it: order them on one stream or with
 // events.  The split kernel writes every byte the GEMM later reads, so nothing has to
@@ -557,7 +804,7 @@ extern "C" {
 
 // No counterpart in the reference.  Same arguments and results as
 // triposplat_gemm_rnf8_avx512; allocates no memory (see the block comment above).
-// Additional status: -6 when 2*M*Kp*2 + 4*M + 512 bytes exceed the 32 MiB scratch;
+// Additional status: -6 when the split activations (see above) exceed the 32 MiB scratch;
 // -4 when N % 16 != 0 or a code pointer is not 16-byte aligned (this entry has only the
 // tensor-core path).  The first call on each device resolves the scratch address; make
 // that first call before capturing any stream.
@@ -580,9 +827,7 @@ int triposplat_gemm_nf24_noalloc(const float* x, const uint8_t* codes0_t, const 
   if ((N % 16) != 0 ||
       ((reinterpret_cast<uintptr_t>(c01) | reinterpret_cast<uintptr_t>(q2)) & 15) != 0)
     return kBadAlignment;
-  const int Kp = (K + 7) & ~7;
-  const size_t plane = (size_t)M * Kp * 2;
-  if (2 * plane + (size_t)M * 4 + 512 > kNoAllocScratchBytes) return -6;
+  if (split_bytes(M, K) > kNoAllocScratchBytes) return -6;
   int st = entry_check_no_alloc();
   if (st != kOk) return st;
   if (!is_device_pointer(x) || !is_device_pointer(c01) || !is_device_pointer(q2) ||
@@ -591,44 +836,10 @@ int triposplat_gemm_nf24_noalloc(const float* x, const uint8_t* codes0_t, const 
   uint8_t* ws = nullptr;
   if ((st = noalloc_scratch(&ws)) != kOk) return st;
   cudaStream_t stream = current_stream();
-  __half* hi = reinterpret_cast<__half*>(ws);
-  __half* lo = reinterpret_cast<__half*>(ws + ((plane + 255) & ~size_t(255)));
-  float* rscale = reinterpret_cast<float*>(ws + 2 * ((plane + 255) & ~size_t(255)));
-  {
-    LaunchScope scope(kKGemmSplit, stream);
-    nf24_split_rows<<<(M + 7) / 8, 256, 0, stream>>>(x, M, K, Kp, stride_x, hi, lo, rscale);
-  }
-  if ((st = launch_status()) != kOk) return st;
-  CUtensorMap m_hi, m_lo, m_c16, m_c8;
-  {
-    const uint64_t dims[2] = {(uint64_t)Kp, (uint64_t)M};
-    const uint64_t strides[1] = {(uint64_t)Kp * 2};
-    const uint32_t box[2] = {BK, BM};
-    if (!encode_tmap(&m_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, hi, dims, strides, box,
-                     CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_tmap(&m_lo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, lo, dims, strides, box,
-                     CU_TENSOR_MAP_SWIZZLE_128B))
-      return kLaunchFailed;
-  }
-  {
-    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)K};
-    const uint64_t s16[1] = {(uint64_t)N * 2};
-    const uint64_t s8[1] = {(uint64_t)N};
-    const uint32_t box[2] = {BN, BK};
-    if (!encode_tmap(&m_c16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<int16_t*>(c01), dims,
-                     s16, box, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode_tmap(&m_c8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(q2), dims, s8,
-                     box, CU_TENSOR_MAP_SWIZZLE_NONE))
-      return kLaunchFailed;
-  }
-  cudaFuncSetAttribute(nf24_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  Params prm{rscale, scales0, bias, out, M, K, N, 0, N, stride_out, device_status_no_alloc()};
-  dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
-  {
-    LaunchScope scope(kKGemmTc, stream);
-    nf24_gemm_tc<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(m_hi, m_lo, m_c16, m_c8, prm);
-  }
-  return launch_status();
+  const SplitPlanes sp = split_layout(ws, M, K);
+  if ((st = launch_split(x, stride_x, sp, stream)) != kOk) return st;
+  return launch_tc(sp, c01, q2, scales0, bias, out, N, 0, N, stride_out, EpilogueArgs(),
+                   device_status_no_alloc(), stream);
 }
 
 }  // extern "C"

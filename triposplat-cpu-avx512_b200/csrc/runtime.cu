@@ -7,6 +7,8 @@
 #include <utility>
 #include <vector>
 
+#include <cstdio>
+
 #include "runtime.h"
 
 namespace tsb {
@@ -66,10 +68,20 @@ std::vector<TimedLaunch> g_timed;
 
 }  // namespace
 
+// While a stream is being captured into a CUDA graph a plain event record only marks a
+// dependency; cudaEventRecordExternal makes it a real record node, replayed every launch.
+static void record_event(cudaEvent_t ev, cudaStream_t stream) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusActive)
+    cudaEventRecordWithFlags(ev, stream, cudaEventRecordExternal);
+  else
+    cudaEventRecord(ev, stream);
+}
+
 LaunchScope::LaunchScope(int kernel_id, cudaStream_t stream) : id_(kernel_id), stream_(stream) {
   g_launches.fetch_add(1, std::memory_order_relaxed);
   if (g_profiling.load(std::memory_order_relaxed)) {
-    if (cudaEventCreate(&start_) == cudaSuccess) cudaEventRecord(start_, stream_);
+    if (cudaEventCreate(&start_) == cudaSuccess) record_event(start_, stream_);
     else start_ = nullptr;
   }
 }
@@ -81,7 +93,7 @@ LaunchScope::~LaunchScope() {
     cudaEventDestroy(start_);
     return;
   }
-  cudaEventRecord(stop, stream_);
+  record_event(stop, stream_);
   std::lock_guard<std::mutex> lock(g_prof_mutex);
   g_timed.push_back({id_, start_, stop});
 }
@@ -174,9 +186,17 @@ int* device_status_no_alloc() {
   return st ? st->device_status : nullptr;
 }
 
+thread_local char t_last_error[256] = "";
+
+void set_last_error(const char* msg) {
+  snprintf(t_last_error, sizeof(t_last_error), "%s", msg);
+}
+
 int launch_status() {
   cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? kOk : kLaunchFailed;
+  if (e == cudaSuccess) return kOk;
+  set_last_error(cudaGetErrorString(e));
+  return kLaunchFailed;
 }
 
 bool encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, void* base,
@@ -191,14 +211,26 @@ bool encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, voi
       g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     }
   });
-  if (!g_encode) return false;
+  if (!g_encode) {
+    set_last_error("cuTensorMapEncodeTiled unavailable");
+    return false;
+  }
   cuuint32_t elem_strides[5] = {1, 1, 1, 1, 1};
   CUresult r = g_encode(map, dtype, rank, base, reinterpret_cast<const cuuint64_t*>(dims),
                         reinterpret_cast<const cuuint64_t*>(strides_bytes),
                         reinterpret_cast<const cuuint32_t*>(box), elem_strides,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
+  if (r != CUDA_SUCCESS) {
+    char msg[256];
+    snprintf(msg, sizeof(msg),
+             "tensor map encode failed (%d): rank %u dims %llu,%llu box %u,%u dtype %d swizzle %d",
+             (int)r, rank, (unsigned long long)dims[0], (unsigned long long)(rank > 1 ? dims[1] : 0),
+             box[0], rank > 1 ? box[1] : 0, (int)dtype, (int)swizzle);
+    set_last_error(msg);
+    return false;
+  }
+  return true;
 }
 
 }  // namespace tsb
@@ -250,6 +282,9 @@ void triposplat_b200_workspace_release(void) {
 
 int triposplat_b200_abi_version(void) { return 1; }
 
+// Text of the last CUDA / tensor-map error seen by this thread's calls ("" if none).
+const char* triposplat_b200_last_error(void) { return tsb::t_last_error; }
+
 uint64_t triposplat_b200_launch_count(void) {
   return tsb::g_launches.load(std::memory_order_relaxed);
 }
@@ -259,13 +294,16 @@ void triposplat_b200_profile_enable(int on) { tsb::g_profiling.store(on ? 1 : 0)
 // Waits for every bracketed launch recorded so far, then returns per kernel family
 // (index = KernelId, n entries) the launch count and the summed device time in ms,
 // and forgets them.
-int triposplat_b200_profile_collect(uint64_t* launches, double* total_ms, int n) {
+// With keep != 0 the events stay registered (e.g. because a captured CUDA graph still
+// records into them on every replay); each read then reflects their latest recording.
+int triposplat_b200_profile_collect2(uint64_t* launches, double* total_ms, int n, int keep) {
   if (!launches || !total_ms || n <= 0) return tsb::kNullPointer;
   for (int i = 0; i < n; ++i) { launches[i] = 0; total_ms[i] = 0.0; }
   std::vector<tsb::TimedLaunch> items;
   {
     std::lock_guard<std::mutex> lock(tsb::g_prof_mutex);
-    items.swap(tsb::g_timed);
+    if (keep) items = tsb::g_timed;
+    else items.swap(tsb::g_timed);
   }
   int st = 0;
   for (auto& it : items) {
@@ -274,13 +312,19 @@ int triposplat_b200_profile_collect(uint64_t* launches, double* total_ms, int n)
         cudaEventElapsedTime(&ms, it.start, it.stop) == cudaSuccess) {
       if (it.id >= 0 && it.id < n) { launches[it.id] += 1; total_ms[it.id] += ms; }
     } else {
-      cudaGetLastError();
+      tsb::set_last_error(cudaGetErrorString(cudaGetLastError()));
       st = tsb::kLaunchFailed;
     }
-    cudaEventDestroy(it.start);
-    cudaEventDestroy(it.stop);
+    if (!keep) {
+      cudaEventDestroy(it.start);
+      cudaEventDestroy(it.stop);
+    }
   }
   return st;
+}
+
+int triposplat_b200_profile_collect(uint64_t* launches, double* total_ms, int n) {
+  return triposplat_b200_profile_collect2(launches, total_ms, n, 0);
 }
 
 }  // extern "C"

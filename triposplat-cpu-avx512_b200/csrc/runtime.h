@@ -49,7 +49,8 @@ int entry_check();
 int entry_check_no_alloc();
 int* device_status_no_alloc();
 
-int launch_status();  // maps cudaGetLastError() to kLaunchFailed / kOk
+int launch_status();  // maps cudaGetLastError() to kLaunchFailed / kOk (and records the text)
+void set_last_error(const char* msg);
 
 bool encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, void* base,
                  const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,

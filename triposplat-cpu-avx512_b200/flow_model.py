@@ -176,9 +176,11 @@ def make_weights(spec: FlowSpec, seed: int = 0, device: str = "cuda") -> FlowWei
 class FlowModelB200:
     """Forward of the synthetic flow model on preallocated device buffers (batch = CFG pair)."""
 
-    def __init__(self, weights: FlowWeights, batch: int = 2, device: str = "cuda"):
+    def __init__(self, weights: FlowWeights, batch: int = 2, device: str = "cuda",
+                 fused: bool = True):
         import torch
 
+        self.fused = fused
         self.spec = s = weights.spec
         self.w = weights
         self.B = batch
@@ -204,6 +206,12 @@ class FlowModelB200:
             "hid": e(B, L, s.mlp, **f32),
             "v_lat": e(B, s.latent_tokens, s.latent_dim, **f32), "v_cam": e(B, 1, s.camera_dim, **f32),
         }
+        # split-format activation buffers for the fused path (LN/GELU/residual folded into
+        # the GEMMs); 256-byte aligned as the library requires
+        rows = B * L
+        for name, k in (("sp_h", h), ("sp_hid", s.mlp)):
+            nbytes = int(self.lib.triposplat_b200_split_bytes(rows, k))
+            self.buf[name] = torch.empty(nbytes + 256, dtype=torch.uint8, device=device)
         # per-block adaLN tables, expanded over the batch so they add elementwise
         self.tables = {i: weights.params[f"blocks.{i}.table"][:, None, :].expand(6, B, h).contiguous()
                        for i in range(s.blocks)}
@@ -278,7 +286,83 @@ class FlowModelB200:
             self._lin("camera_head", a[bb, Nl:], b["v_cam"][bb])
         return b["v_lat"], b["v_cam"]
 
+    def _split_ptr(self, name):
+        t = self.buf[name]
+        return (t.data_ptr() + 255) & ~255
+
+    def _lin_split(self, name, split, rows, out, mode=0, gate=None, gate_ld=0, rows_per_batch=1):
+        p = self.w.linears[name]
+        K, N = int(p.code01.shape[0]), int(p.code01.shape[1])
+        st = self.lib.triposplat_b200_gemm_nf24_split(
+            split, rows, K, p.code01.data_ptr(), p.q2.data_ptr(), p.scale.data_ptr(),
+            p.bias.data_ptr(), out.data_ptr(), N, N, mode,
+            None if gate is None else gate.data_ptr(), gate_ld, rows_per_batch)
+        self._ok(st, f"gemm_split {name}")
+
+    def _ln_split(self, x, split, shift=None, scale=None):
+        s = self.spec
+        rows = x.numel() // s.hidden
+        self._ok(self.lib.triposplat_b200_ln_modulate_split(
+            x.data_ptr(), rows, s.hidden, s.eps, None if shift is None else shift.data_ptr(),
+            None if scale is None else scale.data_ptr(), s.hidden, s.seq, split), "ln_split")
+
+    def _split(self, x, split):
+        K = int(x.shape[-1])
+        rows = x.numel() // K
+        self._ok(self.lib.triposplat_b200_split_f32(x.data_ptr(), rows, K, K, split), "split")
+
     def _block(self, i):
+        if self.fused:
+            return self._block_fused(i)
+        return self._block_reference_ops(i)
+
+    def _block_fused(self, i):
+        """Same block, with LN/modulation fused into the activation split, GELU into the fc1
+        epilogue and the (gated) residual adds into the out / cross_out / fc2 epilogues."""
+        s, b, lib = self.spec, self.buf, self.lib
+        B, L, h, H, Mc = self.B, s.seq, s.hidden, s.heads, s.cond_tokens
+        rows = B * L
+        p = f"blocks.{i}."
+        prm = self.w.params
+        m = b["mod_i"]
+        m.copy_(b["mod"])
+        self._add(m, self.tables[i])
+        shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = (m[j] for j in range(6))
+        x, y = b["x"], b["y"]
+        sph, sphid = self._split_ptr("sp_h"), self._split_ptr("sp_hid")
+        # self-attention
+        self._ln_split(x, sph, shift_msa, scale_msa)
+        self._lin_split(p + "qkv", sph, rows, b["qkv"])
+        self._ok(lib.triposplat_qkv_rope_rmsnorm_pack_f32_avx512_v2(
+            b["qkv"].data_ptr(), self.freqs.data_ptr(), prm[p + "q_gamma"].data_ptr(),
+            prm[p + "k_gamma"].data_ptr(), b["q"].data_ptr(), b["pk"].data_ptr(), b["pv"].data_ptr(),
+            B, L, H, 64, self.Lp, 1, 0), "qkv_post")
+        self._ok(lib.triposplat_sdpa_f32_avx512_exact_q8t512_packed_blhd(
+            b["q"].data_ptr(), b["pk"].data_ptr(), b["pv"].data_ptr(), None, b["o"].data_ptr(),
+            B, H, L, L, 64, self.Lp, 0, 0, 0), "self_sdpa")
+        self._split(b["o"], sph)
+        self._lin_split(p + "out", sph, rows, x, mode=2, gate=gate_msa, gate_ld=h, rows_per_batch=L)
+        # cross-attention
+        self._ln_split(x, sph)
+        self._lin_split(p + "cross_q", sph, rows, y)
+        self._lin(p + "cross_kv", b["c"], b["ckv"])
+        self._ok(lib.triposplat_b200_q_kv_rmsnorm_pack_f32(
+            y.data_ptr(), b["ckv"].data_ptr(), prm[p + "cq_gamma"].data_ptr(),
+            prm[p + "ck_gamma"].data_ptr(), b["q"].data_ptr(), b["cpk"].data_ptr(),
+            b["cpv"].data_ptr(), B, L, Mc, H, self.Mcp), "cross_post")
+        self._ok(lib.triposplat_sdpa_f32_avx512_exact_q8t512_packed_blhd(
+            b["q"].data_ptr(), b["cpk"].data_ptr(), b["cpv"].data_ptr(), None, b["o"].data_ptr(),
+            B, H, L, Mc, 64, self.Mcp, 0, 0, 0), "cross_sdpa")
+        self._split(b["o"], sph)
+        self._lin_split(p + "cross_out", sph, rows, x, mode=3)
+        # MLP
+        self._ln_split(x, sph, shift_mlp, scale_mlp)
+        self._lin_split(p + "fc1", sph, rows, b["hid"], mode=1)
+        self._split(b["hid"], sphid)
+        self._lin_split(p + "fc2", sphid, rows, x, mode=2, gate=gate_mlp, gate_ld=h, rows_per_batch=L)
+
+    def _block_reference_ops(self, i):
+        """The block as the reference's patched modules chain their kernels (one C-ABI call per op)."""
         s, b, lib = self.spec, self.buf, self.lib
         B, L, h, H, Mc = self.B, s.seq, s.hidden, s.heads, s.cond_tokens
         p = f"blocks.{i}."
@@ -342,6 +426,10 @@ class CfgEulerSampler:
         self.x_lat = torch.empty(2, s.latent_tokens, s.latent_dim, **f32)
         self.x_cam = torch.empty(2, 1, s.camera_dim, **f32)
         self.cond_pair = torch.empty(2, s.cond_tokens, s.cond_dim, **f32)
+        self.t_cur = torch.empty(2, **f32)   # the step's timestep pair, read by the body
+        self.dt_cur = torch.empty(1, **f32)  # the step's Euler step
+        self.graph = None
+        self.graph_stream = None
 
     def load(self, noise_lat, noise_cam, cond, neg_cond):
         self.x_lat[0].copy_(noise_lat.reshape(self.x_lat[0].shape), non_blocking=True)
@@ -349,19 +437,54 @@ class CfgEulerSampler:
         self.cond_pair[0].copy_(cond.reshape(self.cond_pair[0].shape), non_blocking=True)
         self.cond_pair[1].copy_(neg_cond.reshape(self.cond_pair[1].shape), non_blocking=True)
 
-    def step(self, i: int):
+    def _body(self):
+        """One sampler step reading t_cur / dt_cur: everything a CUDA graph captures."""
         m, lib = self.model, self.model.lib
         self.x_lat[1].copy_(self.x_lat[0])
         self.x_cam[1].copy_(self.x_cam[0])
-        v_lat, v_cam = m.forward(self.x_lat, self.x_cam, self.t_pair[i], self.cond_pair)
+        v_lat, v_cam = m.forward(self.x_lat, self.x_cam, self.t_cur, self.cond_pair)
         for x, v in ((self.x_lat, v_lat), (self.x_cam, v_cam)):
             n = v[0].numel()
             st = lib.triposplat_cfg_combine_inplace_f32_avx512(v[0].data_ptr(), v[1].data_ptr(),
                                                               self.g.data_ptr(), 1, n, 0)
             st = st or lib.triposplat_euler_update_inplace_f32_avx512(
-                x[0].data_ptr(), v[0].data_ptr(), self.dt[i:i + 1].data_ptr(), 1, n, 0)
+                x[0].data_ptr(), v[0].data_ptr(), self.dt_cur.data_ptr(), 1, n, 0)
             if st:
                 raise RuntimeError(f"sampler update returned status {st}")
+
+    def step(self, i: int):
+        self.t_cur.copy_(self.t_pair[i])
+        self.dt_cur.copy_(self.dt[i:i + 1])
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._body()
+
+    def prepare_capture(self):
+        """Run one eager step on the capture stream so the library's workspace for that
+        stream is sized before capture (nothing is allocated while capturing)."""
+        import torch
+
+        self.graph_stream = torch.cuda.Stream(device=self.model.dev)
+        self.graph_stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(self.graph_stream):
+            self._body()
+        self.graph_stream.synchronize()
+
+    def record_graph(self):
+        """Record one sampler step into a CUDA graph, replayed by step()."""
+        import torch
+
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=self.graph_stream, capture_error_mode="relaxed"):
+            self._body()
+        torch.cuda.current_stream().wait_stream(self.graph_stream)
+        self.graph = graph
+        return graph
+
+    def capture(self):
+        self.prepare_capture()
+        return self.record_graph()
 
     def run(self):
         for i in range(self.steps):

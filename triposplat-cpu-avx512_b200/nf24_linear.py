@@ -58,5 +58,6 @@ def nf24_linear(x, code01_t, q2_t, scale, bias, *, out=None, start: int = 0,
     else:
         st = lib.triposplat_gemm_rnf8_avx512(*ptrs, M, K, N, K, N, 0, 3)
     if st != 0:
-        raise RuntimeError(f"NF24 GEMM returned status {st} for M={M} K={K} N={N}")
+        raise RuntimeError(f"NF24 GEMM returned status {st} for M={M} K={K} N={N}: "
+                           f"{lib.triposplat_b200_last_error().decode()}")
     return out.view(*x.shape[:-1], count)
