@@ -7,7 +7,7 @@
 // bits) after an exact power-of-two pre-scale (per query row for Q; per 128-key tile for
 // K and V), and each product is formed with three tensor-core passes
 // (hi.hi + hi.lo + lo.hi; the lo.lo term is ~2^-22 relative and dropped):
-//   S = Qh Kh^T + Qh Kl^T + Ql Kh^T                (tcgen05, A/B from shared memory)
+//   S = Qh Kh^T + Qh Kl^T + Ql Kh^T                (tcgen05, Q from tensor memory)
 //   O_t = Ph Vh + Ph Vl + Pl Vh                     (tcgen05, P from tensor memory)
 // The pre-scales fold into constants the softmax already multiplies by, so they are free.
 //
@@ -22,11 +22,13 @@
 // sum l is kept in fp32.  No Lq x Lk matrix is ever materialised and no score is skipped.
 //
 // CTA: one (b, h) and 128 query rows, 192 threads, two CTAs per SM.
-//   warp 0      TMA producer (Q once, K and V^T tiles)
+//   warp 0      TMA producer (K and V^T tiles)
 //   warp 1      TMEM allocator + MMA issuer
-//   warps 2..5  softmax / rescale / epilogue, thread = query row = TMEM lane
+//   warps 2..5  Q loader, softmax / rescale / epilogue; thread = query row = TMEM lane
 // TMEM (256 columns): S / P tile at 0..127 (P overwrites S in place: for every 16-key
-// chunk, P_hi goes to its first 8 columns and P_lo to the next 8), O at 128..191.
+// chunk, P_hi goes to its first 8 columns and P_lo to the next 8), O at 128..191, Q_hi at
+// 192..223 and Q_lo at 224..255.  Q lives in tensor memory so the QK^T MMAs read only the
+// K tile from shared memory (half the shared-memory traffic of an SS MMA).
 // Ordering: QK(t) is issued only after P.V(t-1) retired (it overwrites P), so when the
 // softmax warps see S(t) the O accumulator is quiescent and may be rescaled in place.
 #include <cuda_fp16.h>
@@ -44,9 +46,10 @@ constexpr int NUM_THREADS = 192;
 constexpr int TMEM_COLS = 256;
 constexpr int S_COL = 0;
 constexpr int O_COL = 128;
+constexpr int Q_COL = 192;  // Q_hi (32 columns) then Q_lo (32 columns)
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
 constexpr int PLANE = 128 * D * 2;  // 16 KB: one 128 x 64 fp16 tile
-constexpr int SMEM_BYTES = 1024 + 6 * PLANE + 4 * BKV * 4 + 32 * 8 + 16;
+constexpr int SMEM_BYTES = 1024 + 4 * PLANE + 4 * BKV * 4 + 32 * 8 + 16;
 constexpr float LOG2E = 1.4426950408889634f;
 
 struct Params {
@@ -86,22 +89,20 @@ __device__ __forceinline__ float ex2(float x) {
 }
 
 __global__ void __launch_bounds__(NUM_THREADS, 2)
-    sdpa_fwd_tc(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant__ CUtensorMap tm_qlo,
+    sdpa_fwd_tc(const __half* __restrict__ qhi_g, const __half* __restrict__ qlo_g,
                 const __grid_constant__ CUtensorMap tm_khi, const __grid_constant__ CUtensorMap tm_klo,
                 const __grid_constant__ CUtensorMap tm_vhi, const __grid_constant__ CUtensorMap tm_vlo,
                 const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* q_hi = smem;
-  uint8_t* q_lo = q_hi + PLANE;
-  uint8_t* k_hi = q_lo + PLANE;
+  uint8_t* k_hi = smem;
   uint8_t* k_lo = k_hi + PLANE;
   uint8_t* v_hi = k_lo + PLANE;  // two [64 dims x 64 keys] swizzled blocks
   uint8_t* v_lo = v_hi + PLANE;
   float* bias_s = reinterpret_cast<float*>(v_lo + PLANE);  // [4 warps][BKV], log2 units
   uint64_t* bars = reinterpret_cast<uint64_t*>(bias_s + 4 * BKV);
-  uint64_t* q_full = bars + 0;
+  uint64_t* q_full = bars + 0;  // Q rows stored into TMEM (4 softmax-warp arrivals)
   uint64_t* k_full = bars + 1;
   uint64_t* k_empty = bars + 2;
   uint64_t* v_full = bars + 3;
@@ -120,7 +121,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
   const int T = p.T;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 6; ++i) mbar_init(&bars[i], 1);  // q/k/v full+empty, s_full
+    mbar_init(q_full, 4);
+    for (int i = 1; i < 6; ++i) mbar_init(&bars[i], 1);  // k/v full+empty, s_full
     mbar_init(p_full, 4);                                 // one arrival per softmax warp
     mbar_init(o_done, 1);
     mbar_init(mma_done, 1);
@@ -128,7 +130,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tm_qhi); tma_prefetch_desc(&tm_qlo);
     tma_prefetch_desc(&tm_khi); tma_prefetch_desc(&tm_klo);
     tma_prefetch_desc(&tm_vhi); tma_prefetch_desc(&tm_vlo);
   }
@@ -145,9 +146,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     // ---------------- TMA producer ----------------
     if (elect_one()) {
       int issued_k = -1, issued_v = -1;
-      mbar_arrive_expect_tx(q_full, 2 * PLANE);
-      tma_load_3d(q_hi, &tm_qhi, q_full, 0, q0, bh);
-      tma_load_3d(q_lo, &tm_qlo, q_full, 0, q0, bh);
       for (int t = 0; t < T; ++t) {
         if (t >= 1 && !mbar_wait(k_empty, (t - 1) & 1, p.status, kDevTimeoutProducer, abort_flag)) break;
         mbar_arrive_expect_tx(k_full, 2 * PLANE);
@@ -163,7 +161,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         issued_v = t;
       }
       if (*abort_flag) {
-        mbar_wait(q_full, 0, p.status, kDevTimeoutProducer, nullptr);
         if (issued_k >= 0) mbar_wait(k_full, issued_k & 1, p.status, kDevTimeoutProducer, nullptr);
         if (issued_v >= 0) mbar_wait(v_full, issued_v & 1, p.status, kDevTimeoutProducer, nullptr);
       }
@@ -174,7 +171,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       constexpr uint32_t idesc_s = idesc_f16_f32(BQ, BKV);
       constexpr uint32_t idesc_o = idesc_f16_f32(BQ, D);
       bool ok = mbar_wait(q_full, 0, p.status, kDevTimeoutMma, abort_flag);
-      const uint32_t qh = smem_u32(q_hi), ql = smem_u32(q_lo);
       const uint32_t kh = smem_u32(k_hi), kl = smem_u32(k_lo);
       const uint32_t vh = smem_u32(v_hi), vl = smem_u32(v_lo);
       for (int t = 0; t < T && ok; ++t) {
@@ -184,13 +180,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t a_h = sw128_kmajor_desc(qh + kk * 32);
-          const uint64_t a_l = sw128_kmajor_desc(ql + kk * 32);
+          const uint32_t a_h = tmem + Q_COL + kk * 8;
+          const uint32_t a_l = tmem + Q_COL + 32 + kk * 8;
           const uint64_t b_h = sw128_kmajor_desc(kh + kk * 32);
           const uint64_t b_l = sw128_kmajor_desc(kl + kk * 32);
-          mma_f16_ss(tmem + S_COL, a_h, b_h, idesc_s, kk != 0);
-          mma_f16_ss(tmem + S_COL, a_h, b_l, idesc_s, 1);
-          mma_f16_ss(tmem + S_COL, a_l, b_h, idesc_s, 1);
+          mma_f16_ts(tmem + S_COL, a_h, b_h, idesc_s, kk != 0);
+          mma_f16_ts(tmem + S_COL, a_h, b_l, idesc_s, 1);
+          mma_f16_ts(tmem + S_COL, a_l, b_h, idesc_s, 1);
         }
         mma_commit(k_empty);
         mma_commit(s_full);
@@ -229,6 +225,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     for (int t = 0; t < T; ++t) vref = fmaxf(vref, p.vinv[(int64_t)bh * T + t]);
     const int vref_exp = __float_as_int(vref) >> 23;
     float* bt = bias_s + sub * BKV;
+    {
+      // this row's Q hi/lo (64 fp16 each) into TMEM as the A operand of QK^T, one plane at
+      // a time to keep register pressure low
+#pragma unroll 1
+      for (int plane = 0; plane < 2; ++plane) {
+        uint32_t qv[32];
+        const __half* src = plane == 0 ? qhi_g : qlo_g;
+        if (row_valid) {
+          const uint4* g4 = reinterpret_cast<const uint4*>(src + ((int64_t)bh * p.Lq + qrow) * D);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const uint4 a = g4[i];
+            qv[4 * i] = a.x; qv[4 * i + 1] = a.y; qv[4 * i + 2] = a.z; qv[4 * i + 3] = a.w;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) qv[i] = 0u;
+        }
+        tmem_st32(tmem + lane_base + Q_COL + plane * 32, qv);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_full);
+    }
     float m_run = -INFINITY, l_run = 0.0f;
     bool ok = true;
     for (int t = 0; t < T; ++t) {
@@ -535,16 +556,9 @@ static int sdpa_launch(const float* q, const float* k, const float* v, int64_t b
   if ((st = launch_status()) != kOk) return st;
   const uint64_t t1 = now_ns();
 
-  CUtensorMap m_qhi, m_qlo, m_khi, m_klo, m_vhi, m_vlo;
+  CUtensorMap m_khi, m_klo, m_vhi, m_vlo;
   const uint32_t box_rows[3] = {64, 128, 1};
   const uint32_t box_vt[3] = {64, 64, 1};
-  {
-    const uint64_t dims[3] = {D, (uint64_t)Lq, (uint64_t)BH};
-    const uint64_t strides[2] = {D * 2, (uint64_t)Lq * D * 2};
-    if (!encode_tmap(&m_qhi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, qhi, dims, strides, box_rows, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_tmap(&m_qlo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, qlo, dims, strides, box_rows, CU_TENSOR_MAP_SWIZZLE_128B))
-      return kLaunchFailed;
-  }
   {
     const uint64_t dims[3] = {D, (uint64_t)Lkt, (uint64_t)BH};
     const uint64_t strides[2] = {D * 2, (uint64_t)Lkt * D * 2};
@@ -572,7 +586,7 @@ static int sdpa_launch(const float* q, const float* k, const float* v, int64_t b
   dim3 grid((Lq + BQ - 1) / BQ, (unsigned)BH);
   {
     LaunchScope scope(kKSdpaAttn, stream);
-    sdpa_fwd_tc<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(m_qhi, m_qlo, m_khi, m_klo, m_vhi, m_vlo, prm);
+    sdpa_fwd_tc<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(qhi, qlo, m_khi, m_klo, m_vhi, m_vlo, prm);
   }
   st = launch_status();
   const uint64_t t2 = now_ns();
