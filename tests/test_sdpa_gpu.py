@@ -12,6 +12,7 @@ pytestmark = pytest.mark.gpu
 
 MAX_ABS = 2e-5
 RMSE = 2e-6
+REL_RMSE_LONG = 2e-6  # rmse / rms(o) vs fp64 at 8K-32K keys
 
 CASES = ["sdpa_self256", "sdpa_masked256", "sdpa_cross193x256", "sdpa_cross5x17_bias",
          "sdpa_q3_k1", "sdpa_q70_k700_bias"]
@@ -132,8 +133,32 @@ def test_sdpa_full_config_a_spot_check():
     ref = torch.softmax(s, dim=-1) @ v.double()
     err = (out[:, :, rows].double() - ref).abs()
     assert float(err.max()) <= MAX_ABS
-    assert float(err.pow(2).mean().sqrt()) <= RMSE
+    # relative to the output's rms (|o| shrinks like 1/sqrt(L)): the fp32 reference sits
+    # near 5e-7 here; a tensor-core accumulator carried across key tiles drifts to 3e-5
+    rel = float(err.pow(2).mean().sqrt() / ref.pow(2).mean().sqrt())
+    assert rel <= REL_RMSE_LONG, f"relative rmse {rel:.3e}"
     assert bool(torch.isfinite(out).all())
+
+
+@pytest.mark.parametrize("Lk,bias", [(32768, False), (20000, True)])
+def test_sdpa_long_keys_relative_error(Lk, bias):
+    """Error must not grow with the number of key tiles (256 / 157 tiles of 128 keys)."""
+    from native_sdpa_ctypes import native_sdpa_f32
+
+    g = torch.Generator(device="cuda").manual_seed(Lk)
+    Lq = 256
+    q = torch.randn(1, 2, Lq, 64, device="cuda", generator=g)
+    k = torch.randn(1, 2, Lk, 64, device="cuda", generator=g)
+    v = torch.randn(1, 2, Lk, 64, device="cuda", generator=g)
+    b = torch.randn(1, Lk, device="cuda", generator=g) * 3 - 2 if bias else None
+    out = native_sdpa_f32(q, k, v, key_bias=b)
+    s = (q.double() @ k.double().transpose(-1, -2)) * 0.125
+    if bias:
+        s = s + b.double()
+    ref = torch.softmax(s, dim=-1) @ v.double()
+    err = out.double() - ref
+    rel = float(err.pow(2).mean().sqrt() / ref.pow(2).mean().sqrt())
+    assert rel <= REL_RMSE_LONG, f"relative rmse {rel:.3e}"
 
 
 def test_sdpa_error_codes():
