@@ -269,6 +269,18 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
 __device__ __forceinline__ uint32_t warp_id() { return threadIdx.x >> 5; }
 __device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31; }
 
+// Per-warpgroup register budget changes (all four warps of a warpgroup execute the same
+// one).  The sum over the block's warpgroups must stay within the launch allocation
+// (threads x registers per thread at launch), or an increase would wait for ever.
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
   asm volatile(

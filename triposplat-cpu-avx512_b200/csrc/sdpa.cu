@@ -11,12 +11,15 @@
 //   O_t = Ph Vh + Ph Vl + Pl Vh                     (tcgen05, P from tensor memory)
 // The pre-scales fold into constants the softmax already multiplies by, so they are free.
 //
-// Exact online softmax.  Keys are processed in tiles of 128.  Per tile the softmax warps
-// read the score row once into registers, take the tile max, and form p = 2^(s*log2e - m)
-// against a running reference max m that is raised (and O, l rescaled by 2^(m_old-m_new))
-// only when the tile max exceeds it by more than 8: the result is the same exact softmax
-// (the common factor cancels in O/l) and p stays <= 2^8.  P is split into fp16 hi/lo in
-// registers and written over S in tensor memory.  Each tile's P.V goes into a FRESH TMEM
+// Exact online softmax.  Keys are processed in tiles of 128, each read once from tensor
+// memory in four 32-key chunks.  Every chunk's max is checked against a running reference
+// max m before its p = 2^(s*log2e - m) are formed; m is raised (to an integer, so the
+// factor applied to what was accumulated is an exact power of two) only when a chunk
+// exceeds it by more than 8, which after the first chunk of a row is rare: the result is
+// the same exact softmax (the common factor cancels in O/l) and p stays <= 2^8.  P is
+// formed as p * 2^7 (<= 2^15, inside fp16 range, and small terms stay out of fp16's
+// subnormal range), split into fp16 hi/lo in registers and written over S in tensor
+// memory.  Each tile's P.V goes into a FRESH TMEM
 // accumulator O_t that the softmax warps add into fp32 registers before the next P.V: the
 // tensor core's fp32 accumulation truncates, and one accumulator carried over all tiles
 // drifts linearly with the key count (measured: 3e-5 relative rmse at 8192 keys, 60x the
@@ -25,10 +28,11 @@
 // and folded into the exponent of p; the row sum l is kept in fp32.  No Lq x Lk matrix is
 // ever materialised and no score is skipped.
 //
-// CTA: one (b, h) and 128 query rows, 192 threads, two CTAs per SM.
+// CTA: one (b, h) and 128 query rows, 256 threads, two CTAs per SM.
 //   warp 0      TMA producer (K and V^T tiles)
 //   warp 1      TMEM allocator + MMA issuer
-//   warps 2..5  Q loader, softmax / rescale / epilogue; thread = query row = TMEM lane
+//   warps 2..3  idle (they complete warpgroup 0, whose register budget is cut to 56)
+//   warps 4..7  Q loader, softmax / rescale / epilogue; thread = query row = TMEM lane
 // TMEM (256 columns): S / P tile at 0..127 (P overwrites S in place: for every 16-key
 // chunk, P_hi goes to its first 8 columns and P_lo to the next 8), O at 128..191, Q_hi at
 // 192..223 and Q_lo at 224..255.  Q lives in tensor memory so the QK^T MMAs read only the
@@ -47,12 +51,19 @@ namespace sdpa {
 constexpr int D = 64;
 constexpr int BQ = 128;
 constexpr int BKV = 128;
-constexpr int NUM_THREADS = 192;
+constexpr int NUM_THREADS = 256;
+// Register budget: 256 threads x 128 registers at launch (two CTAs per SM).  Warpgroup 0
+// (TMA, MMA, two idle warps) drops to 56 and the softmax warpgroup rises to 200:
+// (56 + 200) x 128 = 32768 = the launch allocation.
+constexpr uint32_t REGS_CONTROL = 56;
+constexpr uint32_t REGS_SOFTMAX = 200;
+static_assert((REGS_CONTROL + REGS_SOFTMAX) * 128 <= 128 * NUM_THREADS, "register split");
 constexpr int TMEM_COLS = 256;
 constexpr int S_COL = 0;
 constexpr int O_COL = 128;
 constexpr int Q_COL = 192;  // Q_hi (32 columns) then Q_lo (32 columns)
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
+constexpr float P_LIFT = 7.0f;  // p' = p * 2^7 <= 2^15 < fp16 max
 constexpr int PLANE = 128 * D * 2;  // 16 KB: one 128 x 64 fp16 tile
 constexpr int SMEM_BYTES = 1024 + 4 * PLANE + 4 * BKV * 4 + 32 * 8 + 16;
 constexpr float LOG2E = 1.4426950408889634f;
@@ -69,28 +80,198 @@ struct Params {
   int* status;
 };
 
-// 32 consecutive TMEM columns of this thread's lane into s[OFF .. OFF+31]
-template <int OFF>
-__device__ __forceinline__ void tmem_ld32_at(uint32_t taddr, uint32_t (&s)[128]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(s[OFF + 0]), "=r"(s[OFF + 1]), "=r"(s[OFF + 2]), "=r"(s[OFF + 3]),
-        "=r"(s[OFF + 4]), "=r"(s[OFF + 5]), "=r"(s[OFF + 6]), "=r"(s[OFF + 7]),
-        "=r"(s[OFF + 8]), "=r"(s[OFF + 9]), "=r"(s[OFF + 10]), "=r"(s[OFF + 11]),
-        "=r"(s[OFF + 12]), "=r"(s[OFF + 13]), "=r"(s[OFF + 14]), "=r"(s[OFF + 15]),
-        "=r"(s[OFF + 16]), "=r"(s[OFF + 17]), "=r"(s[OFF + 18]), "=r"(s[OFF + 19]),
-        "=r"(s[OFF + 20]), "=r"(s[OFF + 21]), "=r"(s[OFF + 22]), "=r"(s[OFF + 23]),
-        "=r"(s[OFF + 24]), "=r"(s[OFF + 25]), "=r"(s[OFF + 26]), "=r"(s[OFF + 27]),
-        "=r"(s[OFF + 28]), "=r"(s[OFF + 29]), "=r"(s[OFF + 30]), "=r"(s[OFF + 31])
-      : "r"(taddr));
-}
-
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// max over 32 values (16 three-input max instructions)
+__device__ __forceinline__ float max32(const float (&v)[32]) {
+  float a[11];
+#pragma unroll
+  for (int i = 0; i < 10; ++i) a[i] = max3(v[3 * i], v[3 * i + 1], v[3 * i + 2]);
+  a[10] = fmaxf(v[30], v[31]);
+  const float b0 = max3(a[0], a[1], a[2]), b1 = max3(a[3], a[4], a[5]), b2 = max3(a[6], a[7], a[8]);
+  return max3(max3(b0, b1, b2), a[9], a[10]);
+}
+
+// Max over one 32-key chunk, in log2 units (x = s*c2 (+ bias)).
+template <bool PLAIN>
+__device__ __forceinline__ float chunk_max(const uint32_t (&s)[32], const float* bt, float c2) {
+  float x[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    x[j] = PLAIN ? __uint_as_float(s[j]) : fmaf(__uint_as_float(s[j]), c2, bt[j]);
+  const float m = max32(x);
+  return PLAIN ? m * c2 : m;  // c2 >= 0
+}
+
+// Packed fp32x2 arithmetic (one instruction for two lanes of fp32 work).
+__device__ __forceinline__ uint64_t f2pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// p = 2^(s*c2 (+ bias) + nm) for one 16-key chunk (s[0..15]): two packed partial row sums,
+// fp16 hi/lo split, written over the chunk's scores in tensor memory (8 columns P_hi,
+// 8 columns P_lo).
+template <bool PLAIN>
+__device__ __forceinline__ void chunk_exp_store(const uint32_t* s, const float* bt, uint64_t c2x2,
+                                                uint64_t nmx2, uint64_t (&ps)[2], uint32_t taddr) {
+  uint32_t pk[16];
+#pragma unroll
+  for (int j = 0; j < 16; j += 2) {
+    const uint64_t sx = f2pack(__uint_as_float(s[j]), __uint_as_float(s[j + 1]));
+    const uint64_t off = PLAIN ? nmx2 : f2add(f2pack(bt[j], bt[j + 1]), nmx2);
+    float x0, x1;
+    f2unpack(f2fma(sx, c2x2, off), x0, x1);
+    const float p0 = ex2(x0), p1 = ex2(x1);
+    const uint64_t px = f2pack(p0, p1);
+    ps[(j >> 1) & 1] = f2add(ps[(j >> 1) & 1], px);
+    // hi: p with the 13 low mantissa bits cleared (exact in fp16 for p >= 2^-14),
+    // lo: the exact fp32 remainder
+    const float h0 = __uint_as_float(__float_as_uint(p0) & 0xFFFFE000u);
+    const float h1 = __uint_as_float(__float_as_uint(p1) & 0xFFFFE000u);
+    float l0, l1;
+    f2unpack(f2sub(px, f2pack(h0, h1)), l0, l1);
+    const __half2 hh = __floats2half2_rn(h0, h1);
+    const __half2 ll = __floats2half2_rn(l0, l1);
+    pk[j >> 1] = *reinterpret_cast<const uint32_t*>(&hh);
+    pk[8 + (j >> 1)] = *reinterpret_cast<const uint32_t*>(&ll);
+  }
+  tmem_st16(taddr, pk);
+}
+
+// Raise this row's reference max where the 32-key chunk C exceeds it by more than the
+// threshold (warp-uniform: the caller votes).  The new reference is an integer, so the
+// factor alpha = 2^(m_old - m_new) is an exact power of two and the accumulators, the
+// partial row sums and the P chunks already written for this tile (fp16 hi/lo, rescaled
+// in tensor memory) all keep exactly the values they would have had with m_new from the
+// start, up to fp16 rounding of terms that fall below 2^-14 (subnormal).
+template <int C>
+__device__ __forceinline__ void raise_reference(uint32_t trow, float cm, float& m_run, float& l_run,
+                                                uint64_t (&ps)[2], float (&o_acc)[D]) {
+  const float m_new = cm > m_run + RESCALE_THRESHOLD ? ceilf(cm) : m_run;
+  const float alpha = m_new == m_run ? 1.0f : ex2(m_run - m_new);  // 0 when m_run = -inf
+#pragma unroll
+  for (int d = 0; d < D; ++d) o_acc[d] *= alpha;
+  l_run *= alpha;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    float a, b;
+    f2unpack(ps[i], a, b);
+    ps[i] = f2pack(a * alpha, b * alpha);
+  }
+  if (C > 0) {
+    const __half2 a2 = __float2half2_rn(alpha);
+    tmem_wait_st();  // the chunks below were stored asynchronously
+#pragma unroll 1
+    for (int c = 0; c < 2 * C; ++c) {
+      uint32_t pv[16];
+      tmem_ld16(trow + S_COL + c * 16, pv);
+      tmem_wait_ld();
+      reg_fence(pv);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const __half2 h = __hmul2(*reinterpret_cast<const __half2*>(&pv[j]), a2);
+        pv[j] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      tmem_st16(trow + S_COL + c * 16, pv);
+    }
+  }
+  m_run = m_new;
+}
+
+// One 32-key chunk: issue the next chunk's load, check the chunk max against the
+// reference, form p and P.  `cur` holds this chunk's scores; `nxt` receives chunk C+1.
+template <bool PLAIN, int C>
+__device__ __forceinline__ void softmax_chunk(uint32_t trow, const uint32_t (&cur)[32],
+                                              uint32_t (&nxt)[32], const float* bt, float c2,
+                                              float vshift, float& m_run, float& l_run,
+                                              uint64_t (&ps)[2], float (&o_acc)[D]) {
+  if (C < 3) tmem_ld32(trow + S_COL + (C + 1) * 32, nxt);
+  const float cm = chunk_max<PLAIN>(cur, bt + C * 32, c2);
+  if (__any_sync(0xffffffffu, cm > m_run + RESCALE_THRESHOLD))
+    raise_reference<C>(trow, cm, m_run, l_run, ps, o_acc);
+  // p' = 2^(x - m + 7 + vshift): p' <= 2^15 keeps P in fp16's range while lifting small
+  // terms out of fp16's subnormal range (the 2^7 cancels in O / l)
+  const float nm = vshift + P_LIFT - (m_run == -INFINITY ? 0.0f : m_run);
+  const uint64_t c2x2 = f2pack(c2, c2), nmx2 = f2pack(nm, nm);
+  chunk_exp_store<PLAIN>(cur, bt + C * 32, c2x2, nmx2, ps, trow + S_COL + C * 32);
+  chunk_exp_store<PLAIN>(cur + 16, bt + C * 32 + 16, c2x2, nmx2, ps, trow + S_COL + C * 32 + 16);
+  if (C < 3) {
+    tmem_wait_ld();
+    reg_fence(nxt);
+  }
+}
+
+// One key tile of the softmax warps, after S(t) is in tensor memory and O_{t-1} complete.
+// Single pass over the scores: each 32-key chunk is checked against the running
+// reference max before its p are formed (the reference is raised, rarely, by
+// raise_reference), and each chunk's tensor-memory load is issued before the previous
+// chunk is processed, so one load latency is exposed per tile.
+template <bool PLAIN>
+__device__ __forceinline__ void softmax_tile(uint32_t trow, bool merge_o, const float* bt, float c2,
+                                             float vshift, float& m_run, float& l_run,
+                                             float (&o_acc)[D]) {
+  uint32_t sa[32], sb[32];
+  if (merge_o) {
+    // O_{t-1} (relative to the current reference max) into the fp32 accumulators, loaded
+    // together with the first score chunk
+    uint32_t o0[32], o1[32];
+    tmem_ld32(trow + O_COL, o0);
+    tmem_ld32(trow + O_COL + 32, o1);
+    tmem_ld32(trow + S_COL, sa);
+    tmem_wait_ld();
+    reg_fence(o0);
+    reg_fence(o1);
+#pragma unroll
+    for (int d = 0; d < 32; d += 2) {
+      f2unpack(f2add(f2pack(o_acc[d], o_acc[d + 1]), f2pack(__uint_as_float(o0[d]), __uint_as_float(o0[d + 1]))),
+               o_acc[d], o_acc[d + 1]);
+      f2unpack(f2add(f2pack(o_acc[32 + d], o_acc[33 + d]), f2pack(__uint_as_float(o1[d]), __uint_as_float(o1[d + 1]))),
+               o_acc[32 + d], o_acc[33 + d]);
+    }
+  } else {
+    tmem_ld32(trow + S_COL, sa);
+    tmem_wait_ld();
+  }
+  reg_fence(sa);
+  uint64_t ps[2] = {0ull, 0ull};  // packed (+0.0f, +0.0f)
+  softmax_chunk<PLAIN, 0>(trow, sa, sb, bt, c2, vshift, m_run, l_run, ps, o_acc);
+  softmax_chunk<PLAIN, 1>(trow, sb, sa, bt, c2, vshift, m_run, l_run, ps, o_acc);
+  softmax_chunk<PLAIN, 2>(trow, sa, sb, bt, c2, vshift, m_run, l_run, ps, o_acc);
+  softmax_chunk<PLAIN, 3>(trow, sb, sa, bt, c2, vshift, m_run, l_run, ps, o_acc);
+  float s0, s1, s2, s3;
+  f2unpack(ps[0], s0, s1);
+  f2unpack(ps[1], s2, s3);
+  l_run = fmaf((s0 + s1) + (s2 + s3), ex2(-vshift), l_run);  // sum of unshifted p
 }
 
 __global__ void __launch_bounds__(NUM_THREADS, 2)
@@ -147,6 +328,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  if (warp < 4) {
+    setmaxnreg_dec<REGS_CONTROL>();
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (elect_one()) {
@@ -183,7 +366,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
              (t == 0 || mbar_wait(o_done, (t - 1) & 1, p.status, kDevTimeoutMma, abort_flag));
         if (!ok) break;
         tc_fence_after();
-#pragma unroll
+        // rolled loops: fully unrolled, the 24 loop-invariant descriptors would be hoisted
+        // out of the tile loop and overflow this warpgroup's 56-register budget
+#pragma unroll 1
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t a_h = tmem + Q_COL + kk * 8;
           const uint32_t a_l = tmem + Q_COL + 32 + kk * 8;
@@ -199,7 +384,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
              mbar_wait(v_full, t & 1, p.status, kDevTimeoutMma, abort_flag);
         if (!ok) break;
         tc_fence_after();
-#pragma unroll
+#pragma unroll 1
         for (int kk = 0; kk < BKV / 16; ++kk) {
           const uint32_t ph = tmem + S_COL + kk * 16;  // P_hi for keys 16kk..16kk+15
           const uint32_t pl = ph + 8;                  // P_lo
@@ -216,7 +401,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       mma_commit(mma_done);
       mbar_wait(mma_done, 0, p.status, kDevTimeoutMma, nullptr);
     }
+  }
   } else {
+    setmaxnreg_inc<REGS_SOFTMAX>();
     // ---------------- softmax, rescale, epilogue ----------------
     const uint32_t sub = warp & 3;
     const int r = sub * 32 + lane;  // query row within the tile == TMEM lane
@@ -282,90 +469,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       ok = mbar_wait(s_full, t & 1, p.status, kDevTimeoutConsumer, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
-      // O_{t-1} (relative to the current reference max) into the fp32 accumulators
-      if (t > 0) {
-#pragma unroll
-        for (int hh = 0; hh < D / 16; ++hh) {
-          uint32_t o[16];
-          tmem_ld16(tmem + lane_base + O_COL + hh * 16, o);
-          tmem_wait_ld();
-          reg_fence(o);
-#pragma unroll
-          for (int d = 0; d < 16; ++d) o_acc[hh * 16 + d] += __uint_as_float(o[d]);
-        }
-      }
-      // pass 1: tile max (scores in log2 units: x = s*c2 (+ bias)), two 64-column halves
-      float mx = -INFINITY;
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        uint32_t sv[32], sw[32];
-        tmem_ld32(tmem + lane_base + S_COL + hf * 64, sv);
-        tmem_ld32(tmem + lane_base + S_COL + hf * 64 + 32, sw);
-        tmem_wait_ld();
-        reg_fence(sv);
-        reg_fence(sw);
-        if (plain) {
-          float rmx = -INFINITY;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) rmx = fmaxf(rmx, fmaxf(__uint_as_float(sv[j]), __uint_as_float(sw[j])));
-          mx = fmaxf(mx, rmx * c2);  // c2 >= 0
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            mx = fmaxf(mx, fmaf(__uint_as_float(sv[j]), c2, bt[hf * 64 + j]));
-            mx = fmaxf(mx, fmaf(__uint_as_float(sw[j]), c2, bt[hf * 64 + 32 + j]));
-          }
-        }
-      }
-      // warp-uniform decision (tcgen05 collectives follow): raise the reference max where
-      // a tile max exceeds it by more than the threshold; rescale accumulators in registers
-      if (__any_sync(0xffffffffu, mx > m_run + RESCALE_THRESHOLD)) {
-        const float m_new = fmaxf(m_run, mx);
-        const float alpha = (m_new == -INFINITY) ? 1.0f : ex2(m_run - m_new);  // 0 on the first tile
-#pragma unroll
-        for (int d = 0; d < D; ++d) o_acc[d] *= alpha;
-        l_run *= alpha;
-        m_run = m_new;
-      }
-      // pass 2: p' = 2^(x - m - vshift_t), row sum, fp16 hi/lo split written over S
-      const float msub = (m_run == -INFINITY ? 0.0f : m_run) + (-vshift);
-      float psum = 0.0f;
-#pragma unroll
-      for (int hf = 0; hf < 4; ++hf) {
-        uint32_t sv[32];
-        tmem_ld32(tmem + lane_base + S_COL + hf * 32, sv);
-        tmem_wait_ld();
-        reg_fence(sv);
-#pragma unroll
-        for (int ch = 0; ch < 2; ++ch) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int j = 0; j < 16; j += 2) {
-            const int c = hf * 32 + ch * 16 + j;
-            const float x0 = plain ? __uint_as_float(sv[ch * 16 + j]) * c2
-                                   : fmaf(__uint_as_float(sv[ch * 16 + j]), c2, bt[c]);
-            const float x1 = plain ? __uint_as_float(sv[ch * 16 + j + 1]) * c2
-                                   : fmaf(__uint_as_float(sv[ch * 16 + j + 1]), c2, bt[c + 1]);
-            const float p0 = ex2(x0 - msub);
-            const float p1 = ex2(x1 - msub);
-            psum += p0 + p1;
-            // hi: p with the 13 low mantissa bits cleared (exact in fp16 for p >= 2^-14),
-            // lo: the exact fp32 remainder
-            const float h0 = __uint_as_float(__float_as_uint(p0) & 0xFFFFE000u);
-            const float h1 = __uint_as_float(__float_as_uint(p1) & 0xFFFFE000u);
-            const __half2 hh = __floats2half2_rn(h0, h1);
-            const __half2 ll = __floats2half2_rn(p0 - h0, p1 - h1);
-            pk[j >> 1] = *reinterpret_cast<const uint32_t*>(&hh);
-            pk[8 + (j >> 1)] = *reinterpret_cast<const uint32_t*>(&ll);
-          }
-          tmem_st16(tmem + lane_base + S_COL + hf * 32 + ch * 16, pk);
-        }
-      }
+      if (plain)
+        softmax_tile<true>(tmem + lane_base, t > 0, bt, c2, vshift, m_run, l_run, o_acc);
+      else
+        softmax_tile<false>(tmem + lane_base, t > 0, bt, c2, vshift, m_run, l_run, o_acc);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
-      l_run = fmaf(psum, ex2(-vshift), l_run);  // the row sum of the unshifted p
     }
     if (ok) {
       ok = mbar_wait(o_done, (T - 1) & 1, p.status, kDevTimeoutEpilogue, abort_flag);
@@ -373,13 +484,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       if (ok) {
         tc_fence_after();
 #pragma unroll
-        for (int hh = 0; hh < D / 16; ++hh) {
-          uint32_t o[16];
-          tmem_ld16(tmem + lane_base + O_COL + hh * 16, o);
+        for (int hh = 0; hh < D / 32; ++hh) {
+          uint32_t o[32];
+          tmem_ld32(tmem + lane_base + O_COL + hh * 32, o);
           tmem_wait_ld();
           reg_fence(o);
 #pragma unroll
-          for (int d = 0; d < 16; ++d) o_acc[hh * 16 + d] += __uint_as_float(o[d]);
+          for (int d = 0; d < 32; ++d) o_acc[hh * 32 + d] += __uint_as_float(o[d]);
         }
         if (row_valid) {
           const float f = vref / l_run;
