@@ -29,8 +29,12 @@
 // Warp roles (448 threads, one CTA per SM):
 //   warp 0       TMA producer (codes and X planes)
 //   warp 1       TMEM allocator + single-thread MMA issuer
-//   warps 2..5   weight decoders (raw codes smem -> registers -> TMEM)
-//   warps 6..13  promotion + epilogue; two warps per TMEM lane quarter, 96 tokens each
+//   warps 2..5   weight decoders (raw codes smem -> registers -> TMEM), k pairs 0..19 of
+//                every 64-k block
+//   warps 6..13  promotion + epilogue; two warps per TMEM lane quarter, 96 tokens each.
+//                They also decode k pairs 20..25 / 26..31 of block kb+2 as soon as the
+//                MMAs of block kb retire (their promotion work leaves them idle most of a
+//                k-block; the dedicated decoders alone could not keep up with the MMAs)
 //
 // Columns whose layout TMA cannot address (N % 16 != 0, unaligned pointers) go to
 // `nf24_gemm_simt`, which reproduces the reference's scalar tail kernel
@@ -59,6 +63,12 @@ constexpr int C_STAGE = C16_BYTES + C8_BYTES;
 constexpr int NUM_EPI_WARPS = 8;
 constexpr int EPI_COLS = BM / 2;  // tokens per epilogue warp
 constexpr int NUM_THREADS = 32 * (6 + NUM_EPI_WARPS);
+constexpr int DEC_ARRIVALS = 4 + NUM_EPI_WARPS;  // warps decoding a share of every stage
+// k pairs (of 32 per 64-k block) decoded by each of warps 2..5 and by each epilogue warp,
+// balanced so the epilogue warps' promotion plus decode share fits in one k-block
+constexpr int DEC_PAIRS = 20;
+constexpr int EPI_PAIRS = 6;
+static_assert(DEC_PAIRS + 2 * EPI_PAIRS == BK / 2, "decode shares cover the block");
 constexpr int TMEM_COLS = 512;
 constexpr int ACC_COL = 0;        // 2 partial buffers x BM fp32 columns
 constexpr int A_COL = 2 * BM;     // AS stages x (32 cols A1 + 32 cols A2)
@@ -88,6 +98,51 @@ __device__ __forceinline__ float gelu_tanh(float x) {
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+// Decode NP k pairs (k = 2*pair0 .. 2*(pair0+NP)-1) of weight column nl from a raw-code
+// stage into the exact fp16 operands A1 / A2 and store them to this warp's TMEM lanes
+// (A1 at column pair0, A2 at column 32 + pair0 of the stage).
+template <int NP>
+__device__ __forceinline__ void decode_pairs(const uint8_t* cstage, int nl, int pair0, uint32_t ta) {
+  // explicit shared-memory loads, all issued before the arithmetic (the stage pointer is
+  // generic after the kernel's alignment arithmetic, and generic loads are slower)
+  const uint32_t a16 = smem_u32(cstage) + (2 * pair0 * BN + nl) * 2;
+  const uint32_t a8 = smem_u32(cstage) + C16_BYTES + 2 * pair0 * BN + nl;
+  uint32_t v[2 * NP], bb[2 * NP];
+#pragma unroll
+  for (int i = 0; i < 2 * NP; ++i) {
+    asm volatile("ld.shared.u16 %0, [%1];" : "=r"(v[i]) : "r"(a16 + i * BN * 2));
+    asm volatile("ld.shared.u8 %0, [%1];" : "=r"(bb[i]) : "r"(a8 + i * BN));
+  }
+  const __half2 two = __floats2half2_rn(2.0f, 2.0f);
+  const __half2 m3072 = __floats2half2_rn(-3072.0f, -3072.0f);
+  const __half2 inv256 = __floats2half2_rn(1.0f / 256.0f, 1.0f / 256.0f);
+  const __half2 m4p5 = __floats2half2_rn(-4.5f, -4.5f);
+  uint32_t r1[NP], r2[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const uint32_t pq = __byte_perm(v[2 * i], v[2 * i + 1], 0x5410);
+    const uint32_t pc = __byte_perm(bb[2 * i], bb[2 * i + 1], 0x5410);
+    const uint32_t f1 = ((pq >> 1) & 0x03FF03FFu) ^ 0x66006600u;
+    const uint32_t f2 = (((pq << 8) & 0x01000100u) | pc) ^ 0x64806480u;
+    r1[i] = h2_bits(__hfma2(bits_h2(f1), two, m3072));
+    r2[i] = h2_bits(__hfma2(bits_h2(f2), inv256, m4p5));
+  }
+  // NP columns of A1 and of A2 (NP = 20 or 6: x16 + x4 or x4 + x2 stores)
+  static_assert(NP == 20 || NP == 6, "decode share");
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const uint32_t* r = half ? r2 : r1;
+    const uint32_t t = ta + half * 32 + pair0;
+    if constexpr (NP == 20) {
+      tmem_st16(t, *reinterpret_cast<const uint32_t(*)[16]>(r));
+      tmem_st4(t + 16, r[16], r[17], r[18], r[19]);
+    } else {
+      tmem_st4(t, r[0], r[1], r[2], r[3]);
+      tmem_st2(t + 4, r[4], r[5]);
+    }
+  }
+}
 
 // 14 warps put four warps on some SM sub-partitions (16K registers each): 128 registers
 // per thread is the most that can launch.
@@ -124,8 +179,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < XS; ++i) { mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], 1); }
-    for (int i = 0; i < CS; ++i) { mbar_init(&c_full[i], 1); mbar_init(&c_empty[i], 4); }
-    for (int i = 0; i < AS; ++i) { mbar_init(&a_full[i], 4); mbar_init(&a_empty[i], 1); }
+    for (int i = 0; i < CS; ++i) { mbar_init(&c_full[i], 1); mbar_init(&c_empty[i], DEC_ARRIVALS); }
+    for (int i = 0; i < AS; ++i) { mbar_init(&a_full[i], DEC_ARRIVALS); mbar_init(&a_empty[i], 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_free[i], NUM_EPI_WARPS); }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -223,10 +278,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t sub = warp & 3;  // TMEM lane quarter this warp may touch
     const int nl = sub * 32 + lane;
     const uint32_t lane_base = (sub * 32) << 16;
-    const __half2 two = __floats2half2_rn(2.0f, 2.0f);
-    const __half2 m3072 = __floats2half2_rn(-3072.0f, -3072.0f);
-    const __half2 inv256 = __floats2half2_rn(1.0f / 256.0f, 1.0f / 256.0f);
-    const __half2 m4p5 = __floats2half2_rn(-4.5f, -4.5f);
     for (int kb = 0; kb < kblocks; ++kb) {
       const int c = kb % CS, a = kb % AS;
       bool ok = mbar_wait(&c_full[c], (kb / CS) & 1, p.status, kDevTimeoutConsumer, abort_flag);
@@ -235,27 +286,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // the tcgen05 st below is warp-collective: leave the loop as a whole warp
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      const uint16_t* c16 = reinterpret_cast<const uint16_t*>(cs + c * C_STAGE);
-      const uint8_t* c8 = cs + c * C_STAGE + C16_BYTES;
-      uint32_t r1[32], r2[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const uint32_t v0 = c16[(2 * i) * BN + nl];
-        const uint32_t v1 = c16[(2 * i + 1) * BN + nl];
-        const uint32_t b0 = c8[(2 * i) * BN + nl];
-        const uint32_t b1 = c8[(2 * i + 1) * BN + nl];
-        const uint32_t pq = v0 | (v1 << 16);
-        const uint32_t pc = b0 | (b1 << 16);
-        const uint32_t f1 = ((pq >> 1) & 0x03FF03FFu) ^ 0x66006600u;
-        const uint32_t f2 = (((pq << 8) & 0x01000100u) | pc) ^ 0x64806480u;
-        r1[i] = h2_bits(__hfma2(bits_h2(f1), two, m3072));
-        r2[i] = h2_bits(__hfma2(bits_h2(f2), inv256, m4p5));
-      }
+      decode_pairs<DEC_PAIRS>(cs + c * C_STAGE, nl, 0, tmem + lane_base + A_COL + a * 64);
       __syncwarp();
       if (lane == 0) mbar_arrive(&c_empty[c]);
-      const uint32_t taddr = tmem + lane_base + A_COL + a * 64;
-      tmem_st32(taddr, r1);
-      tmem_st32(taddr + 32, r2);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -267,15 +300,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int half = (warp - 6) >> 2;  // which 96-token half of the tile
     const int nl = sub * 32 + lane;
     const uint32_t lane_base = (sub * 32) << 16;
+    const int pair0 = DEC_PAIRS + half * EPI_PAIRS;
+    // this warp's decode share of k-block kbd into A stage kbd % AS (free: either never
+    // used, or the MMAs of block kbd - AS retired, which acc_full of that block tells)
+    auto decode_share = [&](int kbd) -> bool {
+      const int c = kbd % CS;
+      const bool got = mbar_wait(&c_full[c], (kbd / CS) & 1, p.status, kDevTimeoutEpilogue, abort_flag);
+      if (!__all_sync(0xffffffffu, got)) return false;
+      decode_pairs<EPI_PAIRS>(cs + c * C_STAGE, nl, pair0, tmem + lane_base + A_COL + (kbd % AS) * 64);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&c_empty[c]);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&a_full[kbd % AS]);
+      return true;
+    };
     float sum[EPI_COLS];
 #pragma unroll
     for (int j = 0; j < EPI_COLS; ++j) sum[j] = 0.0f;
     bool ok = true;
-    for (int kb = 0; kb < kblocks; ++kb) {
+    for (int kbd = 0; kbd < AS && kbd < kblocks && ok; ++kbd) ok = decode_share(kbd);
+    for (int kb = 0; kb < kblocks && ok; ++kb) {
       const int b = kb & 1;
       ok = mbar_wait(&acc_full[b], (kb >> 1) & 1, p.status, kDevTimeoutEpilogue, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
+      if (kb + AS < kblocks && !decode_share(kb + AS)) { ok = false; break; }
       const uint32_t col = tmem + lane_base + ACC_COL + b * BM + half * EPI_COLS;
 #pragma unroll
       for (int q = 0; q < EPI_COLS / 16; ++q) {
@@ -284,7 +335,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tmem_wait_ld();
         reg_fence(v);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) sum[q * 16 + j] += __uint_as_float(v[j]);
+        for (int j = 0; j < 16; j += 2) {
+          float2 a = make_float2(sum[q * 16 + j], sum[q * 16 + j + 1]);
+          asm("add.rn.f32x2 %0, %0, %1;" : "+l"(*reinterpret_cast<uint64_t*>(&a))
+              : "l"((uint64_t)v[j] | ((uint64_t)v[j + 1] << 32)));
+          sum[q * 16 + j] = a.x;
+          sum[q * 16 + j + 1] = a.y;
+        }
       }
       tc_fence_before();
       __syncwarp();
