@@ -74,8 +74,8 @@ constexpr int ACC_COL = 0;        // 2 partial buffers x BM fp32 columns
 constexpr int A_COL = 2 * BM;     // AS stages x (32 cols A1 + 32 cols A2)
 static_assert(A_COL + AS * 64 <= TMEM_COLS, "TMEM budget");
 constexpr int NUM_BARS = 2 * XS + 2 * CS + 2 * AS + 5;
-constexpr int SMEM_BYTES = 1024 /*align slack*/ + XS * X_STAGE + CS * C_STAGE + BM * 4 +
-                           NUM_BARS * 8 + 16;
+constexpr int SMEM_BYTES = 1024 /*align slack*/ + XS * X_STAGE + CS * C_STAGE +
+                           NUM_EPI_WARPS * EPI_COLS * 4 + NUM_BARS * 8 + 16;
 
 enum Epilogue : int { kStore = 0, kGelu = 1, kGatedResidual = 2, kResidual = 3 };
 
@@ -157,8 +157,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* xs = smem;
   uint8_t* cs = xs + XS * X_STAGE;
-  float* rs_s = reinterpret_cast<float*>(cs + CS * C_STAGE);  // [BM] row scales
-  uint64_t* bars = reinterpret_cast<uint64_t*>(rs_s + BM);
+  float* rs_s = reinterpret_cast<float*>(cs + CS * C_STAGE);  // [8 epilogue warps][96] row scales
+  uint64_t* bars = reinterpret_cast<uint64_t*>(rs_s + NUM_EPI_WARPS * EPI_COLS);
   uint64_t* x_full = bars;
   uint64_t* x_empty = x_full + XS;
   uint64_t* c_full = x_empty + XS;
@@ -173,9 +173,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
-  const int n0 = blockIdx.x * BN;  // local column (within [0, count))
-  const int m0 = blockIdx.y * BM;
+  // persistent CTAs: tile t = blockIdx.x + i * gridDim.x, weight tiles fastest (CTAs
+  // running together share the token tile); every role walks the same tile sequence, and
+  // pipeline stages / barrier phases run on one k-block counter g across tiles
   const int kblocks = (p.K + BK - 1) / BK;
+  const int n_tiles = (p.count + BN - 1) / BN;
+  const int num_tiles = n_tiles * ((p.M + BM - 1) / BM);
+  const int my_tiles = blockIdx.x < num_tiles ? (num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int total_g = my_tiles * kblocks;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < XS; ++i) { mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], 1); }
@@ -196,10 +201,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
   }
-  if (warp >= 6) {
-    for (int i = threadIdx.x - 192; i < BM; i += 32 * NUM_EPI_WARPS)
-      rs_s[i] = (m0 + i < p.M) ? p.rscale[m0 + i] : 0.0f;
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -211,24 +212,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int last_c[CS], last_x[XS];
       for (int i = 0; i < CS; ++i) last_c[i] = -1;
       for (int i = 0; i < XS; ++i) last_x[i] = -1;
-      for (int kb = 0; kb < kblocks; ++kb) {
-        const int c = kb % CS, x = kb % XS;
-        if (kb >= CS &&
-            !mbar_wait(&c_empty[c], ((kb / CS) & 1) ^ 1, p.status, kDevTimeoutProducer, abort_flag))
+      bool ok = true;
+      for (int g = 0; g < total_g && ok; ++g) {
+        const int kb = g % kblocks, t = blockIdx.x + (g / kblocks) * gridDim.x;
+        const int n0 = (t % n_tiles) * BN, m0 = (t / n_tiles) * BM;
+        const int c = g % CS, x = g % XS;
+        if (g >= CS &&
+            !mbar_wait(&c_empty[c], ((g / CS) & 1) ^ 1, p.status, kDevTimeoutProducer, abort_flag)) {
+          ok = false;
           break;
+        }
         uint8_t* cdst = cs + c * C_STAGE;
         mbar_arrive_expect_tx(&c_full[c], C_STAGE);
         tma_load_2d(cdst, &tm_c16, &c_full[c], p.start + n0, kb * BK);
         tma_load_2d(cdst + C16_BYTES, &tm_c8, &c_full[c], p.start + n0, kb * BK);
-        last_c[c] = kb;
-        if (kb >= XS &&
-            !mbar_wait(&x_empty[x], ((kb / XS) & 1) ^ 1, p.status, kDevTimeoutProducer, abort_flag))
+        last_c[c] = g;
+        if (g >= XS &&
+            !mbar_wait(&x_empty[x], ((g / XS) & 1) ^ 1, p.status, kDevTimeoutProducer, abort_flag)) {
+          ok = false;
           break;
+        }
         uint8_t* xdst = xs + x * X_STAGE;
         mbar_arrive_expect_tx(&x_full[x], X_STAGE);
         tma_load_2d(xdst, &tm_xhi, &x_full[x], kb * BK, m0);
         tma_load_2d(xdst + X_PLANE, &tm_xlo, &x_full[x], kb * BK, m0);
-        last_x[x] = kb;
+        last_x[x] = g;
       }
       if (*abort_flag) {
         // never leave the CTA while a bulk copy may still write its shared memory
@@ -243,11 +251,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (elect_one()) {
       constexpr uint32_t idesc = idesc_f16_f32(BN, BM);
       bool ok = true;
-      for (int kb = 0; kb < kblocks && ok; ++kb) {
-        const int x = kb % XS, a = kb % AS, b = kb & 1;
-        ok = mbar_wait(&x_full[x], (kb / XS) & 1, p.status, kDevTimeoutMma, abort_flag) &&
-             mbar_wait(&a_full[a], (kb / AS) & 1, p.status, kDevTimeoutMma, abort_flag) &&
-             (kb < 2 || mbar_wait(&acc_free[b], ((kb >> 1) & 1) ^ 1, p.status, kDevTimeoutMma, abort_flag));
+      for (int g = 0; g < total_g && ok; ++g) {
+        const int x = g % XS, a = g % AS, b = g & 1;
+        ok = mbar_wait(&x_full[x], (g / XS) & 1, p.status, kDevTimeoutMma, abort_flag) &&
+             mbar_wait(&a_full[a], (g / AS) & 1, p.status, kDevTimeoutMma, abort_flag) &&
+             (g < 2 || mbar_wait(&acc_free[b], ((g >> 1) & 1) ^ 1, p.status, kDevTimeoutMma, abort_flag));
         if (!ok) break;
         tc_fence_after();
         const uint32_t hi = smem_u32(xs + x * X_STAGE);
@@ -278,11 +286,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t sub = warp & 3;  // TMEM lane quarter this warp may touch
     const int nl = sub * 32 + lane;
     const uint32_t lane_base = (sub * 32) << 16;
-    for (int kb = 0; kb < kblocks; ++kb) {
-      const int c = kb % CS, a = kb % AS;
-      bool ok = mbar_wait(&c_full[c], (kb / CS) & 1, p.status, kDevTimeoutConsumer, abort_flag);
-      if (ok && kb >= AS)
-        ok = mbar_wait(&a_empty[a], ((kb / AS) & 1) ^ 1, p.status, kDevTimeoutConsumer, abort_flag);
+    for (int g = 0; g < total_g; ++g) {
+      const int c = g % CS, a = g % AS;
+      bool ok = mbar_wait(&c_full[c], (g / CS) & 1, p.status, kDevTimeoutConsumer, abort_flag);
+      if (ok && g >= AS)
+        ok = mbar_wait(&a_empty[a], ((g / AS) & 1) ^ 1, p.status, kDevTimeoutConsumer, abort_flag);
       // the tcgen05 st below is warp-collective: leave the loop as a whole warp
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
@@ -316,17 +324,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (lane == 0) mbar_arrive(&a_full[kbd % AS]);
       return true;
     };
+    bool ok = true;
+    for (int gd = 0; gd < AS && gd < total_g && ok; ++gd) ok = decode_share(gd);
+    for (int i = 0; i < my_tiles && ok; ++i) {
+    const int t = blockIdx.x + i * gridDim.x;
+    const int n0 = (t % n_tiles) * BN, m0 = (t / n_tiles) * BM;
+    // this tile's row pre-scales into the warp's private slice of shared memory (read
+    // back at the store; the loads complete while the k-blocks run)
+    float* rsw = rs_s + (warp - 6) * EPI_COLS;
+    __syncwarp();
+    for (int j = lane; j < EPI_COLS; j += 32) {
+      const int m = m0 + half * EPI_COLS + j;
+      rsw[j] = m < p.M ? p.rscale[m] : 0.0f;
+    }
+    __syncwarp();
     float sum[EPI_COLS];
 #pragma unroll
     for (int j = 0; j < EPI_COLS; ++j) sum[j] = 0.0f;
-    bool ok = true;
-    for (int kbd = 0; kbd < AS && kbd < kblocks && ok; ++kbd) ok = decode_share(kbd);
     for (int kb = 0; kb < kblocks && ok; ++kb) {
-      const int b = kb & 1;
-      ok = mbar_wait(&acc_full[b], (kb >> 1) & 1, p.status, kDevTimeoutEpilogue, abort_flag);
+      const int g = i * kblocks + kb, b = g & 1;
+      ok = mbar_wait(&acc_full[b], (g >> 1) & 1, p.status, kDevTimeoutEpilogue, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
-      if (kb + AS < kblocks && !decode_share(kb + AS)) { ok = false; break; }
+      if (g + AS < total_g && !decode_share(g + AS)) { ok = false; break; }
       const uint32_t col = tmem + lane_base + ACC_COL + b * BM + half * EPI_COLS;
 #pragma unroll
       for (int q = 0; q < EPI_COLS / 16; ++q) {
@@ -358,9 +378,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int rows = p.M - mbase;  // rows of this half that exist
         // fold the row pre-scale into the sums, then one fully unrolled loop per mode so
         // sum[] stays in registers
-        const float* rsh = rs_s + half * EPI_COLS;
 #pragma unroll
-        for (int j = 0; j < EPI_COLS; ++j) sum[j] *= rsh[j];
+        for (int j = 0; j < EPI_COLS; ++j) sum[j] *= rsw[j];
         if constexpr (MODE == kStore) {
 #pragma unroll
           for (int j = 0; j < EPI_COLS; ++j)
@@ -398,6 +417,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
+    }  // tile loop
   }
 
   tc_fence_before();
@@ -602,10 +622,18 @@ static int launch_tc(const SplitPlanes& sp, const int16_t* c01, const int8_t* q2
   }
   Params prm{sp.rs, scale, bias, out, M, K, N, start, count, stride_out,
              ep.mode, ep.gate, ep.gate_ld, ep.rows_per_batch, status};
-  dim3 grid((count + BN - 1) / BN, (M + BM - 1) / BM);
   static uint64_t attr_done[4] = {0, 0, 0, 0};  // per mode: one bit per device ordinal
+  static int sm_count[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
+  if (sm_count[dev & 63] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    sm_count[dev & 63] = n > 0 ? n : 148;
+  }
+  // one persistent CTA per SM (or one per tile when there are fewer tiles)
+  const long long tiles = (long long)((count + BN - 1) / BN) * ((M + BM - 1) / BM);
+  const dim3 grid((unsigned)(tiles < sm_count[dev & 63] ? tiles : sm_count[dev & 63]));
   auto run = [&](auto kernel, int mode) {
     if (!(attr_done[mode] >> (dev & 63) & 1)) {
       cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
