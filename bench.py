@@ -2,17 +2,21 @@
 """Benchmark: s20 CFG flow sampling of the synthetic 28-block NF24 flow model on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--parallel replicas|cfg] [--case model|gemm1|sdpa2a|sdpa2b|sdpa2c|mlp3|block4]
 
 A step is one CFG sampler step (one forward of the batch-2 [cond, uncond] pair through
-28 blocks and 206 NF24 Linears, then CFG combine + Euler update) for one image per GPU.
-Multi-GPU (torchrun, one process per GPU): every rank samples its own image (weak
-scaling, replicas; no collective on the data path); timing is the max over ranks.
+28 blocks and 206 NF24 Linears, then CFG combine + Euler update) for one image.
+Multi-GPU (torchrun, one process per GPU), timing is the max over ranks:
+  --parallel replicas (default): every rank samples its own image (weak scaling, no
+      collective on the data path); value = (time of K steps) / K * 20 / N.
+  --parallel cfg: each image's CFG pair is split over two GPUs (conditional branch on the
+      even rank, unconditional on the odd one; one NCCL all-gather of the velocity per
+      step); value = (time of K steps) / K * 20 / (N / 2).
 
-Reported metric: seconds per image for 20-step sampling (lower is better), whole job:
-value = (max-over-ranks time of K steps) / K * 20 / N.  Also reported: the end-to-end
-number through the public sampler API with host buffers (H2D of each step's inputs, D2H
-of its result), the roofline of the dominant kernel (the attention kernel), per-kernel
-device time, and, on rank 0 at N=1, the reference CPU path timed on this host.
+Reported metric: seconds per image for 20-step sampling (lower is better), whole job.
+Also reported: the end-to-end number through the public sampler API with host buffers
+(H2D of each step's inputs, D2H of its result), the roofline of the dominant kernel,
+per-kernel device time, and, on rank 0 at N=1, the reference CPU path timed on this host.
 """
 from __future__ import annotations
 
@@ -43,6 +47,10 @@ def parse():
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--parallel", choices=("replicas", "cfg"), default="replicas",
+                    help="replicas: one image per GPU (default); cfg: each image's CFG pair split "
+                         "over two GPUs (conditional / unconditional branch), one NCCL all-gather "
+                         "of the velocity per step")
     ap.add_argument("--no-graph", action="store_true",
                     help="issue every kernel from the host each step instead of replaying "
                          "the step's CUDA graph")
@@ -160,13 +168,13 @@ def load_peaks():
     return FALLBACK_PEAKS, "fallback"
 
 
-def profiled_traffic():
-    """DRAM bytes per attention launch from the committed ncu summary, if present."""
-    f = REPO / "profiles" / "sdpa_fwd_tc_config2a.md"
+def profiled_traffic(profile: str, key: str):
+    """DRAM bytes per launch (`key:` line) from a committed ncu summary, if present."""
+    f = REPO / "profiles" / profile
     if not f.is_file():
         return None
     for line in f.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_full_launch:"):
+        if line.startswith(key + ":"):
             try:
                 return float(line.split(":", 1)[1].strip())
             except ValueError:
@@ -303,11 +311,27 @@ def main():
     spec = FlowSpec()
     lib = _native.load()
     weights = make_weights(spec, seed=0, device=str(dev))
-    model = FlowModelB200(weights, device=str(dev))
-    sampler = CfgEulerSampler(model, steps=SAMPLER_STEPS, guidance=3.0, shift=3.0)
+    split = args.parallel == "cfg"
+    if split:
+        # pairs of ranks (2p, 2p+1) share one image: rank 2p the conditional branch
+        if world % 2:
+            raise SystemExit("--parallel cfg needs an even number of GPUs")
+        if world == 1:
+            raise SystemExit("--parallel cfg needs --gpus >= 2")
+        from cfg_split import CfgSplitSampler
 
-    # per-rank image: seeded inputs in pinned host memory (also the e2e source buffers)
-    g = torch.Generator().manual_seed(1000 + rank)
+        groups = [dist.new_group([2 * p, 2 * p + 1]) for p in range(world // 2)]
+        model = FlowModelB200(weights, batch=1, device=str(dev))
+        sampler = CfgSplitSampler(model, branch=rank % 2, group=groups[rank // 2],
+                                  steps=SAMPLER_STEPS, guidance=3.0, shift=3.0)
+        images, image = world // 2, rank // 2
+    else:
+        model = FlowModelB200(weights, device=str(dev))
+        sampler = CfgEulerSampler(model, steps=SAMPLER_STEPS, guidance=3.0, shift=3.0)
+        images, image = world, rank
+
+    # per-image seeded inputs in pinned host memory (also the e2e source buffers)
+    g = torch.Generator().manual_seed(1000 + image)
     h_lat = torch.randn(1, spec.latent_tokens, spec.latent_dim, generator=g).pin_memory()
     h_cam = torch.randn(1, 1, spec.camera_dim, generator=g).pin_memory()
     h_cond = torch.randn(1, spec.cond_tokens, spec.cond_dim, generator=g).pin_memory()
@@ -343,6 +367,7 @@ def main():
         launches0 = int(lib.triposplat_b200_launch_count())
         sampler.record_graph()
         launches_per_step = int(lib.triposplat_b200_launch_count()) - launches0
+        launches_per_step += getattr(sampler, "eager_launches_per_step", 0)
         lib.triposplat_b200_profile_enable(0)
     else:
         lib.triposplat_b200_profile_enable(1)
@@ -394,24 +419,49 @@ def main():
 
     # ---- report
     ms_step = ms_total / args.steps
-    value = ms_step / 1e3 * SAMPLER_STEPS / world
-    e2e_value = e2e_ms / args.steps / 1e3 * SAMPLER_STEPS / world
-    flops = spec.flops_per_forward(batch=2)
+    value = ms_step / 1e3 * SAMPLER_STEPS / images
+    e2e_value = e2e_ms / args.steps / 1e3 * SAMPLER_STEPS / images
+    flops = spec.flops_per_forward(batch=model.B)  # this GPU's share: the pair, or one branch
     peaks, peak_src = load_peaks()
     attn = prof["sdpa_attn"]
-    L, Mc, BH = spec.seq, spec.cond_tokens, 2 * spec.heads
+    L, Mc, BH = spec.seq, spec.cond_tokens, model.B * spec.heads
     attn_flops_per_step = spec.blocks * 4.0 * BH * L * (L + Mc) * spec.head_dim
     achieved = None
     if attn["launches"]:
         launches_per_step = attn["launches"] / args.steps
         achieved = attn_flops_per_step / launches_per_step / (attn["ms"] / attn["launches"] / 1e3) / 1e12
     peak = float(peaks.get("bf16_tflops_sustained") or peaks["bf16_tflops"])
-    traffic_full = profiled_traffic()
     kernels = {k: {"launches_per_step": round(v["launches"] / args.steps, 2),
                    "ms_per_step": round(v["ms"] / args.steps, 3),
                    "share": round(v["ms"] / max(1e-9, sum(x["ms"] for x in prof.values())), 4)}
                for k, v in prof.items()}
     gemm = prof["gemm_tc"]
+    g_achieved = None
+    if gemm["ms"]:
+        g_achieved = flops["gemm"] / (gemm["ms"] / args.steps / 1e3) / 1e12
+    # the dominant kernel (larger share of the step) first
+    roof_attn = {"kernel": "sdpa_fwd_tc (exact SDPA, self + cross)", "bound": "tensor",
+                 "achieved": None if achieved is None else round(achieved, 1),
+                 "peak": peak, "unit": "TFLOP/s",
+                 "frac": None if achieved is None else round(achieved / peak, 4),
+                 "peak_source": f"bf16_tflops_sustained, {peak_src} (of measured)",
+                 "flops": "algorithmic 4*B*H*Lq*Lk*64 per launch (3 split-fp16 tensor passes each)",
+                 "tensor_pipe_frac": None if achieved is None else round(3 * achieved / peak, 4),
+                 "ms_per_step": round(attn["ms"] / args.steps, 3),
+                 "traffic": profiled_traffic("sdpa_fwd_tc_config2a.md", "traffic_bytes_per_full_launch")}
+    roof_gemm = {"kernel": "nf24_gemm_tc (NF24 GEMM, all tensor-core Linears of the step)",
+                 "bound": "tensor",
+                 "achieved": None if g_achieved is None else round(g_achieved, 1),
+                 "peak": peak, "unit": "TFLOP/s",
+                 "frac": None if g_achieved is None else round(g_achieved / peak, 4),
+                 "peak_source": f"bf16_tflops_sustained, {peak_src} (of measured)",
+                 "flops": "algorithmic 2*M*N*K per launch, summed over the step's Linears "
+                          "(4 fp16 tensor passes each)",
+                 "tensor_pipe_frac": None if g_achieved is None else round(4 * g_achieved / peak, 4),
+                 "ms_per_step": round(gemm["ms"] / args.steps, 3),
+                 "traffic": profiled_traffic("model_s20_step_launches.md",
+                                             "nf24_gemm_tc_traffic_bytes_per_launch")}
+    roofs = [roof_gemm, roof_attn] if gemm["ms"] >= attn["ms"] else [roof_attn, roof_gemm]
     line = {
         "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
@@ -421,24 +471,16 @@ def main():
                    "blocks": spec.blocks, "linears": len(spec.linears()), "hidden": spec.hidden,
                    "heads": spec.heads, "mlp": spec.mlp, "latent_tokens": spec.latent_tokens,
                    "seq": spec.seq, "cond_tokens": Mc, "sampler_steps": SAMPLER_STEPS,
-                   "guidance": 3.0, "shift": 3.0, "global_batch": f"{world} image(s) x CFG pair",
-                   "parallelism": f"replicas x{world} (one image per GPU, no data-path collective)",
+                   "guidance": 3.0, "shift": 3.0, "global_batch": f"{images} image(s) x CFG pair",
+                   "parallelism": (f"cfg-split x{images} (each image's CFG pair on 2 GPUs, one NCCL "
+                                   "all-gather of the velocity per step)") if split else
+                                  f"replicas x{world} (one image per GPU, no data-path collective)",
                    "launch": "host-issued kernels" if args.no_graph else "one CUDA graph per sampler step",
                    "l2": "no flush: every step streams 1.4 GB of NF24 weights and ~1 GB of "
                          "activations, far above the 126 MB L2"},
         "tflops_logical_per_gpu": round(flops["total"] / (ms_step / 1e3) / 1e12, 1),
-        "roofline": {"kernel": "sdpa_fwd_tc (exact SDPA, self + cross)", "bound": "tensor",
-                     "achieved": None if achieved is None else round(achieved, 1),
-                     "peak": peak, "unit": "TFLOP/s",
-                     "frac": None if achieved is None else round(achieved / peak, 4),
-                     "peak_source": f"bf16_tflops_sustained, {peak_src}",
-                     "flops": "algorithmic 4*B*H*Lq*Lk*64 per launch (3 split-fp16 tensor passes each)",
-                     "tensor_pipe_frac": None if achieved is None else round(3 * achieved / peak, 4),
-                     "traffic": traffic_full},
-        "gemm": {"kernel": "nf24_gemm_tc", "launches_per_step": round(gemm["launches"] / args.steps, 1),
-                 "ms_per_step": round(gemm["ms"] / args.steps, 3),
-                 "achieved_tflops_logical": round(flops["gemm"] / (gemm["ms"] / args.steps / 1e3) / 1e12, 1)
-                 if gemm["ms"] else None},
+        "roofline": roofs[0],
+        "roofline_second": roofs[1],
         "kernels": kernels,
         "gpu_launches": launches,
         "clocks": clk.summary(),
@@ -451,6 +493,7 @@ def main():
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
+        sampler.graph = None  # release graphs before the process group goes
         dist.destroy_process_group()
     return 0
 
