@@ -7,7 +7,7 @@
 // bits) after an exact power-of-two pre-scale (per query row for Q; per 128-key tile for
 // K and V), and each product is formed with three tensor-core passes
 // (hi.hi + hi.lo + lo.hi; the lo.lo term is ~2^-22 relative and dropped):
-//   S = Qh Kh^T + Qh Kl^T + Ql Kh^T                (tcgen05, Q from tensor memory)
+//   S = Qh Kh^T + Qh Kl^T + Ql Kh^T                (tcgen05, Q and K from shared memory)
 //   O_t = Ph Vh + Ph Vl + Pl Vh                     (tcgen05, P from tensor memory)
 // The pre-scales fold into constants the softmax already multiplies by, so they are free.
 //
@@ -28,18 +28,23 @@
 // and folded into the exponent of p; the row sum l is kept in fp32.  No Lq x Lk matrix is
 // ever materialised and no score is skipped.
 //
-// CTA: one (b, h) and 128 query rows, 256 threads, two CTAs per SM.
-//   warp 0      TMA producer (K and V^T tiles)
-//   warp 1      TMEM allocator + MMA issuer
-//   warps 2..3  idle (they complete warpgroup 0, whose register budget is cut to 56)
-//   warps 4..7  Q loader, softmax / rescale / epilogue; thread = query row = TMEM lane
-// TMEM (256 columns): S / P tile at 0..127 (P overwrites S in place: for every 16-key
-// chunk, P_hi goes to its first 8 columns and P_lo to the next 8), O at 128..191, Q_hi at
-// 192..223 and Q_lo at 224..255.  Q lives in tensor memory so the QK^T MMAs read only the
-// K tile from shared memory (half the shared-memory traffic of an SS MMA).
-// Ordering: QK(t) is issued only after P.V(t-1) retired (it overwrites P), so when the
-// softmax warps see S(t), O_{t-1} is complete; they fold it into their registers before
-// releasing P(t), and only then may P.V(t) overwrite it.
+// Two softmax teams split the key tiles of a row (split-K): team 0 takes the even tiles,
+// team 1 the odd ones, each with its own reference max, row sum and fp32 O accumulators;
+// at the end the two partial softmaxes are merged with exact power-of-two factors (both
+// references are integers).  The teams' phases interleave on the SM's pipes, and the
+// scores of a team's next tile are computed while it works on the current one.
+//
+// CTA: one (b, h) and 128 query rows, 384 threads, one CTA per SM.
+//   warp 0 / 2  TMA producers of the K / V^T tiles (two stages each)
+//   warp 1      TMEM allocator + QK^T issuer;  warp 3  P.V issuer (separate threads, so a
+//               team's next QK never waits behind the other team's P)
+//   warps 4..7  softmax team 0, warps 8..11 team 1; thread = query row = TMEM lane.  The
+//               teams also write the Q tile (hi / lo plane) into shared memory.
+// TMEM (512 columns): three S / P buffers (tile t uses buffer t % 3; P overwrites S in
+// place: for every 16-key chunk, P_hi goes to its first 8 columns and P_lo to the next 8),
+// then O of team 0 and O of team 1 (64 columns each).
+// Ordering: QK(t) waits only for P.V(t-3), the last reader of its buffer; P.V(t) writes
+// team (t & 1)'s O only after that team folded its previous O into registers (p_full).
 #include <cuda_fp16.h>
 
 #include "common.cuh"
@@ -51,21 +56,27 @@ namespace sdpa {
 constexpr int D = 64;
 constexpr int BQ = 128;
 constexpr int BKV = 128;
-constexpr int NUM_THREADS = 256;
-// Register budget: 256 threads x 128 registers at launch (two CTAs per SM).  Warpgroup 0
-// (TMA, MMA, two idle warps) drops to 56 and the softmax warpgroup rises to 200:
-// (56 + 200) x 128 = 32768 = the launch allocation.
+constexpr int NUM_THREADS = 384;
+// Register budget: 384 threads x 168 registers at launch (one CTA per SM; the host checks
+// the compiled count).  Warpgroup 0 (TMA producers, MMA issuers) drops to 56 and each
+// softmax team rises to 224: 56 + 2 x 224 = 504 = 3 x 168.
+constexpr uint32_t REGS_LAUNCH = 168;
 constexpr uint32_t REGS_CONTROL = 56;
-constexpr uint32_t REGS_SOFTMAX = 200;
-static_assert((REGS_CONTROL + REGS_SOFTMAX) * 128 <= 128 * NUM_THREADS, "register split");
-constexpr int TMEM_COLS = 256;
+constexpr uint32_t REGS_SOFTMAX = 224;
+static_assert(REGS_LAUNCH * NUM_THREADS <= 65536, "launch allocation");
+static_assert((REGS_CONTROL + 2 * REGS_SOFTMAX) * 128 <= REGS_LAUNCH * NUM_THREADS, "register split");
+constexpr int TMEM_COLS = 512;
+constexpr int NSB = 3;                  // score / P buffers: tile t uses S_COL + (t % 3) * BKV
 constexpr int S_COL = 0;
-constexpr int O_COL = 128;
-constexpr int Q_COL = 192;  // Q_hi (32 columns) then Q_lo (32 columns)
+constexpr int O_COL = NSB * BKV;        // 384: O of team 0, then O of team 1 (64 columns each)
+static_assert(O_COL + 2 * D <= TMEM_COLS, "TMEM budget");
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
 constexpr float P_LIFT = 7.0f;  // p' = p * 2^7 <= 2^15 < fp16 max
-constexpr int PLANE = 128 * D * 2;  // 16 KB: one 128 x 64 fp16 tile
-constexpr int SMEM_BYTES = 1024 + 4 * PLANE + 4 * BKV * 4 + 32 * 8 + 16;
+constexpr int PLANE = 128 * D * 2;      // 16 KB: one 128 x 64 fp16 tile
+constexpr int STAGE = 2 * PLANE;        // hi + lo planes of one Q, K or V^T tile
+// Q, 2 K stages, 2 V stages, per-warp bias [8][BKV], team maxima / sums [2][BQ] each,
+// output halves [2 teams][BQ][32], barriers
+constexpr int SMEM_BYTES = 1024 + 5 * STAGE + 8 * BKV * 4 + 4 * BQ * 4 + 2 * BQ * 32 * 4 + 32 * 8 + 16;
 constexpr float LOG2E = 1.4426950408889634f;
 
 struct Params {
@@ -175,7 +186,7 @@ __device__ __forceinline__ void chunk_exp_store(const uint32_t* s, const float* 
 // in tensor memory) all keep exactly the values they would have had with m_new from the
 // start, up to fp16 rounding of terms that fall below 2^-14 (subnormal).
 template <int C>
-__device__ __forceinline__ void raise_reference(uint32_t trow, float cm, float& m_run, float& l_run,
+__device__ __forceinline__ void raise_reference(uint32_t srow, float cm, float& m_run, float& l_run,
                                                 uint64_t (&ps)[2], float (&o_acc)[D]) {
   const float m_new = cm > m_run + RESCALE_THRESHOLD ? ceilf(cm) : m_run;
   const float alpha = m_new == m_run ? 1.0f : ex2(m_run - m_new);  // 0 when m_run = -inf
@@ -194,7 +205,7 @@ __device__ __forceinline__ void raise_reference(uint32_t trow, float cm, float& 
 #pragma unroll 1
     for (int c = 0; c < 2 * C; ++c) {
       uint32_t pv[16];
-      tmem_ld16(trow + S_COL + c * 16, pv);
+      tmem_ld16(srow + c * 16, pv);
       tmem_wait_ld();
       reg_fence(pv);
 #pragma unroll
@@ -202,7 +213,7 @@ __device__ __forceinline__ void raise_reference(uint32_t trow, float cm, float& 
         const __half2 h = __hmul2(*reinterpret_cast<const __half2*>(&pv[j]), a2);
         pv[j] = *reinterpret_cast<const uint32_t*>(&h);
       }
-      tmem_st16(trow + S_COL + c * 16, pv);
+      tmem_st16(srow + c * 16, pv);
     }
   }
   m_run = m_new;
@@ -211,20 +222,20 @@ __device__ __forceinline__ void raise_reference(uint32_t trow, float cm, float& 
 // One 32-key chunk: issue the next chunk's load, check the chunk max against the
 // reference, form p and P.  `cur` holds this chunk's scores; `nxt` receives chunk C+1.
 template <bool PLAIN, int C>
-__device__ __forceinline__ void softmax_chunk(uint32_t trow, const uint32_t (&cur)[32],
+__device__ __forceinline__ void softmax_chunk(uint32_t srow, const uint32_t (&cur)[32],
                                               uint32_t (&nxt)[32], const float* bt, float c2,
                                               float vshift, float& m_run, float& l_run,
                                               uint64_t (&ps)[2], float (&o_acc)[D]) {
-  if (C < 3) tmem_ld32(trow + S_COL + (C + 1) * 32, nxt);
+  if (C < 3) tmem_ld32(srow + (C + 1) * 32, nxt);
   const float cm = chunk_max<PLAIN>(cur, bt + C * 32, c2);
   if (__any_sync(0xffffffffu, cm > m_run + RESCALE_THRESHOLD))
-    raise_reference<C>(trow, cm, m_run, l_run, ps, o_acc);
+    raise_reference<C>(srow, cm, m_run, l_run, ps, o_acc);
   // p' = 2^(x - m + 7 + vshift): p' <= 2^15 keeps P in fp16's range while lifting small
   // terms out of fp16's subnormal range (the 2^7 cancels in O / l)
   const float nm = vshift + P_LIFT - (m_run == -INFINITY ? 0.0f : m_run);
   const uint64_t c2x2 = f2pack(c2, c2), nmx2 = f2pack(nm, nm);
-  chunk_exp_store<PLAIN>(cur, bt + C * 32, c2x2, nmx2, ps, trow + S_COL + C * 32);
-  chunk_exp_store<PLAIN>(cur + 16, bt + C * 32 + 16, c2x2, nmx2, ps, trow + S_COL + C * 32 + 16);
+  chunk_exp_store<PLAIN>(cur, bt + C * 32, c2x2, nmx2, ps, srow + C * 32);
+  chunk_exp_store<PLAIN>(cur + 16, bt + C * 32 + 16, c2x2, nmx2, ps, srow + C * 32 + 16);
   if (C < 3) {
     tmem_wait_ld();
     reg_fence(nxt);
@@ -237,7 +248,7 @@ __device__ __forceinline__ void softmax_chunk(uint32_t trow, const uint32_t (&cu
 // raise_reference), and each chunk's tensor-memory load is issued before the previous
 // chunk is processed, so one load latency is exposed per tile.
 template <bool PLAIN>
-__device__ __forceinline__ void softmax_tile(uint32_t trow, bool merge_o, const float* bt, float c2,
+__device__ __forceinline__ void softmax_tile(uint32_t srow, uint32_t orow, bool merge_o, const float* bt, float c2,
                                              float vshift, float& m_run, float& l_run,
                                              float (&o_acc)[D]) {
   uint32_t sa[32], sb[32];
@@ -245,9 +256,9 @@ __device__ __forceinline__ void softmax_tile(uint32_t trow, bool merge_o, const 
     // O_{t-1} (relative to the current reference max) into the fp32 accumulators, loaded
     // together with the first score chunk
     uint32_t o0[32], o1[32];
-    tmem_ld32(trow + O_COL, o0);
-    tmem_ld32(trow + O_COL + 32, o1);
-    tmem_ld32(trow + S_COL, sa);
+    tmem_ld32(orow, o0);
+    tmem_ld32(orow + 32, o1);
+    tmem_ld32(srow, sa);
     tmem_wait_ld();
     reg_fence(o0);
     reg_fence(o1);
@@ -259,22 +270,22 @@ __device__ __forceinline__ void softmax_tile(uint32_t trow, bool merge_o, const 
                o_acc[32 + d], o_acc[33 + d]);
     }
   } else {
-    tmem_ld32(trow + S_COL, sa);
+    tmem_ld32(srow, sa);
     tmem_wait_ld();
   }
   reg_fence(sa);
   uint64_t ps[2] = {0ull, 0ull};  // packed (+0.0f, +0.0f)
-  softmax_chunk<PLAIN, 0>(trow, sa, sb, bt, c2, vshift, m_run, l_run, ps, o_acc);
-  softmax_chunk<PLAIN, 1>(trow, sb, sa, bt, c2, vshift, m_run, l_run, ps, o_acc);
-  softmax_chunk<PLAIN, 2>(trow, sa, sb, bt, c2, vshift, m_run, l_run, ps, o_acc);
-  softmax_chunk<PLAIN, 3>(trow, sb, sa, bt, c2, vshift, m_run, l_run, ps, o_acc);
+  softmax_chunk<PLAIN, 0>(srow, sa, sb, bt, c2, vshift, m_run, l_run, ps, o_acc);
+  softmax_chunk<PLAIN, 1>(srow, sb, sa, bt, c2, vshift, m_run, l_run, ps, o_acc);
+  softmax_chunk<PLAIN, 2>(srow, sa, sb, bt, c2, vshift, m_run, l_run, ps, o_acc);
+  softmax_chunk<PLAIN, 3>(srow, sb, sa, bt, c2, vshift, m_run, l_run, ps, o_acc);
   float s0, s1, s2, s3;
   f2unpack(ps[0], s0, s1);
   f2unpack(ps[1], s2, s3);
   l_run = fmaf((s0 + s1) + (s2 + s3), ex2(-vshift), l_run);  // sum of unshifted p
 }
 
-__global__ void __launch_bounds__(NUM_THREADS, 2)
+__global__ void __launch_bounds__(NUM_THREADS, 1)
     sdpa_fwd_tc(const __half* __restrict__ qhi_g, const __half* __restrict__ qlo_g,
                 const __grid_constant__ CUtensorMap tm_khi, const __grid_constant__ CUtensorMap tm_klo,
                 const __grid_constant__ CUtensorMap tm_vhi, const __grid_constant__ CUtensorMap tm_vlo,
@@ -282,22 +293,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* k_hi = smem;
-  uint8_t* k_lo = k_hi + PLANE;
-  uint8_t* v_hi = k_lo + PLANE;  // two [64 dims x 64 keys] swizzled blocks
-  uint8_t* v_lo = v_hi + PLANE;
-  float* bias_s = reinterpret_cast<float*>(v_lo + PLANE);  // [4 warps][BKV], log2 units
-  uint64_t* bars = reinterpret_cast<uint64_t*>(bias_s + 4 * BKV);
-  uint64_t* q_full = bars + 0;  // Q rows stored into TMEM (4 softmax-warp arrivals)
-  uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = bars + 2;
-  uint64_t* v_full = bars + 3;
-  uint64_t* v_empty = bars + 4;
-  uint64_t* s_full = bars + 5;
-  uint64_t* p_full = bars + 6;
-  uint64_t* o_done = bars + 7;  // P.V(t) retired
-  uint64_t* mma_done = bars + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint8_t* q_s = smem;                 // [hi, lo] Q tile (128 rows x 64, 128-byte swizzle)
+  uint8_t* k_st = q_s + STAGE;         // [2][hi, lo] K tiles
+  uint8_t* v_st = k_st + 2 * STAGE;    // [2][hi, lo] V^T tiles, each two [64 x 64] blocks
+  float* bias_s = reinterpret_cast<float*>(v_st + 2 * STAGE);  // [8 warps][BKV], log2 units
+  float* xm = bias_s + 8 * BKV;        // [2 teams][BQ] final reference maxima
+  float* xl = xm + 2 * BQ;             // [2 teams][BQ] final row sums
+  float* xo = xl + 2 * BQ;             // [2 teams][BQ][32] output halves for the other team
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xo + 2 * BQ * 32);
+  uint64_t* q_full = bars + 0;   // Q rows written to shared memory (8 softmax-warp arrivals)
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2]
+  uint64_t* v_full = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;  // [2]
+  uint64_t* s_full = bars + 9;   // [3] QK(t) retired into S buffer t % 3
+  uint64_t* pv_done = bars + 12; // [3] P.V(t) retired (read buffer t % 3; wrote team t&1's O)
+  uint64_t* p_full = bars + 15;  // [2] per team: P(t) written, its previous O merged
+  uint64_t* qk_done = bars + 17; // QK issuer's MMAs retired (teardown)
+  uint64_t* pv_all = bars + 18;  // P.V issuer's MMAs retired (teardown)
+  uint64_t* xbar = bars + 19;    // end-of-row exchange between the teams (8 arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const uint32_t warp = warp_id();
@@ -307,11 +322,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
   const int T = p.T;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 4);
-    for (int i = 1; i < 6; ++i) mbar_init(&bars[i], 1);  // k/v full+empty, s_full
-    mbar_init(p_full, 4);                                 // one arrival per softmax warp
-    mbar_init(o_done, 1);
-    mbar_init(mma_done, 1);
+    mbar_init(q_full, 8);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1); mbar_init(&v_empty[i], 1);
+      mbar_init(&p_full[i], 4);
+    }
+    for (int i = 0; i < NSB; ++i) { mbar_init(&s_full[i], 1); mbar_init(&pv_done[i], 1); }
+    mbar_init(qk_done, 1);
+    mbar_init(pv_all, 1);
+    mbar_init(xbar, 8);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -330,84 +350,110 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
 
   if (warp < 4) {
     setmaxnreg_dec<REGS_CONTROL>();
-  if (warp == 0) {
-    // ---------------- TMA producer ----------------
+  if (warp == 0 || warp == 2) {
+    // ---------------- TMA producers: warp 0 the K tiles, warp 2 the V^T tiles --------
     if (elect_one()) {
-      int issued_k = -1, issued_v = -1;
+      const bool is_k = warp == 0;
+      uint64_t* full = is_k ? k_full : v_full;
+      uint64_t* empty = is_k ? k_empty : v_empty;
+      uint8_t* base = is_k ? k_st : v_st;
+      int issued[2] = {-1, -1};
       for (int t = 0; t < T; ++t) {
-        if (t >= 1 && !mbar_wait(k_empty, (t - 1) & 1, p.status, kDevTimeoutProducer, abort_flag)) break;
-        mbar_arrive_expect_tx(k_full, 2 * PLANE);
-        tma_load_3d(k_hi, &tm_khi, k_full, 0, t * BKV, bh);
-        tma_load_3d(k_lo, &tm_klo, k_full, 0, t * BKV, bh);
-        issued_k = t;
-        if (t >= 1 && !mbar_wait(v_empty, (t - 1) & 1, p.status, kDevTimeoutProducer, abort_flag)) break;
-        mbar_arrive_expect_tx(v_full, 2 * PLANE);
-        tma_load_3d(v_hi, &tm_vhi, v_full, t * BKV, 0, bh);
-        tma_load_3d(v_hi + PLANE / 2, &tm_vhi, v_full, t * BKV + 64, 0, bh);
-        tma_load_3d(v_lo, &tm_vlo, v_full, t * BKV, 0, bh);
-        tma_load_3d(v_lo + PLANE / 2, &tm_vlo, v_full, t * BKV + 64, 0, bh);
-        issued_v = t;
+        const int st = t & 1;
+        if (t >= 2 && !mbar_wait(&empty[st], ((t >> 1) & 1) ^ 1, p.status, kDevTimeoutProducer, abort_flag)) break;
+        uint8_t* d = base + st * STAGE;
+        mbar_arrive_expect_tx(&full[st], STAGE);
+        if (is_k) {
+          tma_load_3d(d, &tm_khi, &full[st], 0, t * BKV, bh);
+          tma_load_3d(d + PLANE, &tm_klo, &full[st], 0, t * BKV, bh);
+        } else {
+          tma_load_3d(d, &tm_vhi, &full[st], t * BKV, 0, bh);
+          tma_load_3d(d + PLANE / 2, &tm_vhi, &full[st], t * BKV + 64, 0, bh);
+          tma_load_3d(d + PLANE, &tm_vlo, &full[st], t * BKV, 0, bh);
+          tma_load_3d(d + PLANE + PLANE / 2, &tm_vlo, &full[st], t * BKV + 64, 0, bh);
+        }
+        issued[st] = t;
       }
       if (*abort_flag) {
-        if (issued_k >= 0) mbar_wait(k_full, issued_k & 1, p.status, kDevTimeoutProducer, nullptr);
-        if (issued_v >= 0) mbar_wait(v_full, issued_v & 1, p.status, kDevTimeoutProducer, nullptr);
+        // never leave the CTA while a bulk copy may still write its shared memory
+        for (int i = 0; i < 2; ++i)
+          if (issued[i] >= 0) mbar_wait(&full[i], (issued[i] >> 1) & 1, p.status, kDevTimeoutProducer, nullptr);
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
+    // ---------------- QK^T issuer ----------------
+    // QK(t) goes into S buffer t % 3 as soon as its K tile is in and P.V(t-3), the last
+    // reader of that buffer, has retired; P.V is issued by warp 3, so the scores of a
+    // team's next tile never wait behind the other team's P.
     if (elect_one()) {
       constexpr uint32_t idesc_s = idesc_f16_f32(BQ, BKV);
-      constexpr uint32_t idesc_o = idesc_f16_f32(BQ, D);
       bool ok = mbar_wait(q_full, 0, p.status, kDevTimeoutMma, abort_flag);
-      const uint32_t kh = smem_u32(k_hi), kl = smem_u32(k_lo);
-      const uint32_t vh = smem_u32(v_hi), vl = smem_u32(v_lo);
+      const uint32_t qh = smem_u32(q_s), ql = qh + PLANE;
       for (int t = 0; t < T && ok; ++t) {
-        ok = mbar_wait(k_full, t & 1, p.status, kDevTimeoutMma, abort_flag) &&
-             (t == 0 || mbar_wait(o_done, (t - 1) & 1, p.status, kDevTimeoutMma, abort_flag));
+        const int st = t & 1, sb = t % NSB;
+        ok = mbar_wait(&k_full[st], (t >> 1) & 1, p.status, kDevTimeoutMma, abort_flag) &&
+             (t < NSB || mbar_wait(&pv_done[sb], ((t - NSB) / NSB) & 1, p.status, kDevTimeoutMma, abort_flag));
         if (!ok) break;
         tc_fence_after();
-        // rolled loops: fully unrolled, the 24 loop-invariant descriptors would be hoisted
-        // out of the tile loop and overflow this warpgroup's 56-register budget
+        const uint32_t kh = smem_u32(k_st + st * STAGE), kl = kh + PLANE;
+        const uint32_t sd = tmem + S_COL + sb * BKV;
+        // rolled loop: fully unrolled, the loop-invariant descriptors would be hoisted out
+        // of the tile loop and overflow this warpgroup's register budget
 #pragma unroll 1
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t a_h = tmem + Q_COL + kk * 8;
-          const uint32_t a_l = tmem + Q_COL + 32 + kk * 8;
+          const uint64_t a_h = sw128_kmajor_desc(qh + kk * 32);
+          const uint64_t a_l = sw128_kmajor_desc(ql + kk * 32);
           const uint64_t b_h = sw128_kmajor_desc(kh + kk * 32);
           const uint64_t b_l = sw128_kmajor_desc(kl + kk * 32);
-          mma_f16_ts(tmem + S_COL, a_h, b_h, idesc_s, kk != 0);
-          mma_f16_ts(tmem + S_COL, a_h, b_l, idesc_s, 1);
-          mma_f16_ts(tmem + S_COL, a_l, b_h, idesc_s, 1);
+          mma_f16_ss(sd, a_h, b_h, idesc_s, kk != 0);
+          mma_f16_ss(sd, a_h, b_l, idesc_s, 1);
+          mma_f16_ss(sd, a_l, b_h, idesc_s, 1);
         }
-        mma_commit(k_empty);
-        mma_commit(s_full);
-        ok = mbar_wait(p_full, t & 1, p.status, kDevTimeoutMma, abort_flag) &&
-             mbar_wait(v_full, t & 1, p.status, kDevTimeoutMma, abort_flag);
+        mma_commit(&k_empty[st]);
+        mma_commit(&s_full[sb]);
+      }
+      mma_commit(qk_done);
+      mbar_wait(qk_done, 0, p.status, kDevTimeoutMma, nullptr);
+    }
+  } else {
+    // ---------------- P.V issuer (warp 3) ----------------
+    if (elect_one()) {
+      constexpr uint32_t idesc_o = idesc_f16_f32(BQ, D);
+      bool ok = true;
+      for (int t = 0; t < T && ok; ++t) {
+        const int st = t & 1, team = t & 1;
+        ok = mbar_wait(&p_full[team], (t >> 1) & 1, p.status, kDevTimeoutMma, abort_flag) &&
+             mbar_wait(&v_full[st], (t >> 1) & 1, p.status, kDevTimeoutMma, abort_flag);
         if (!ok) break;
         tc_fence_after();
+        const uint32_t vh = smem_u32(v_st + st * STAGE), vl = vh + PLANE;
+        const uint32_t ps = tmem + S_COL + (t % NSB) * BKV;
+        const uint32_t od = tmem + O_COL + team * D;
 #pragma unroll 1
         for (int kk = 0; kk < BKV / 16; ++kk) {
-          const uint32_t ph = tmem + S_COL + kk * 16;  // P_hi for keys 16kk..16kk+15
-          const uint32_t pl = ph + 8;                  // P_lo
+          const uint32_t ph = ps + kk * 16;  // P_hi for keys 16kk..16kk+15
+          const uint32_t pl = ph + 8;        // P_lo
           const uint32_t voff = (kk >> 2) * (PLANE / 2) + (kk & 3) * 32;
           const uint64_t b_h = sw128_kmajor_desc(vh + voff);
           const uint64_t b_l = sw128_kmajor_desc(vl + voff);
-          mma_f16_ts(tmem + O_COL, ph, b_h, idesc_o, kk != 0);  // fresh O_t per key tile
-          mma_f16_ts(tmem + O_COL, ph, b_l, idesc_o, 1);
-          mma_f16_ts(tmem + O_COL, pl, b_h, idesc_o, 1);
+          mma_f16_ts(od, ph, b_h, idesc_o, kk != 0);  // fresh O_t per key tile
+          mma_f16_ts(od, ph, b_l, idesc_o, 1);
+          mma_f16_ts(od, pl, b_h, idesc_o, 1);
         }
-        mma_commit(v_empty);
-        mma_commit(o_done);
+        mma_commit(&v_empty[st]);
+        mma_commit(&pv_done[t % NSB]);
       }
-      mma_commit(mma_done);
-      mbar_wait(mma_done, 0, p.status, kDevTimeoutMma, nullptr);
+      mma_commit(pv_all);
+      mbar_wait(pv_all, 0, p.status, kDevTimeoutMma, nullptr);
     }
   }
   } else {
     setmaxnreg_inc<REGS_SOFTMAX>();
-    // ---------------- softmax, rescale, epilogue ----------------
+    // ---------------- softmax: team 0 takes even tiles, team 1 odd tiles ---------------
+    const int team = (warp - 4) >> 2;
     const uint32_t sub = warp & 3;
     const int r = sub * 32 + lane;  // query row within the tile == TMEM lane
-    const uint32_t lane_base = (sub * 32) << 16;
+    const uint32_t trow = tmem + ((sub * 32) << 16);
     const int qrow = q0 + r;
     const bool row_valid = qrow < p.Lq;
     const float cq = 0.125f * LOG2E * (row_valid ? p.qinv[(int64_t)bh * p.Lq + qrow] : 0.0f);
@@ -416,29 +462,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     float vref = 0.0f;
     for (int t = 0; t < T; ++t) vref = fmaxf(vref, p.vinv[(int64_t)bh * T + t]);
     const int vref_exp = __float_as_int(vref) >> 23;
-    float* bt = bias_s + sub * BKV;
+    float* bt = bias_s + (warp - 4) * BKV;
     {
-      // this row's Q hi/lo (64 fp16 each) into TMEM as the A operand of QK^T, one plane at
-      // a time to keep register pressure low
-#pragma unroll 1
-      for (int plane = 0; plane < 2; ++plane) {
-        uint32_t qv[32];
-        const __half* src = plane == 0 ? qhi_g : qlo_g;
-        if (row_valid) {
-          const uint4* g4 = reinterpret_cast<const uint4*>(src + ((int64_t)bh * p.Lq + qrow) * D);
+      // this row's Q plane (team 0: hi, team 1: lo) into shared memory in the MMA's
+      // 128-byte-swizzled K-major layout (16-byte chunk c of row r at chunk c ^ (r & 7))
+      uint8_t* rowp = q_s + team * PLANE + (r >> 3) * 1024 + (r & 7) * 128;
+      const uint4* src = reinterpret_cast<const uint4*>((team == 0 ? qhi_g : qlo_g) + ((int64_t)bh * p.Lq + qrow) * D);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const uint4 a = g4[i];
-            qv[4 * i] = a.x; qv[4 * i + 1] = a.y; qv[4 * i + 2] = a.z; qv[4 * i + 3] = a.w;
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) qv[i] = 0u;
-        }
-        tmem_st32(tmem + lane_base + Q_COL + plane * 32, qv);
+      for (int c = 0; c < 8; ++c) {
+        const uint4 v = row_valid ? src[c] : make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(rowp + ((c ^ (r & 7)) << 4)) = v;
       }
-      tmem_wait_st();
-      tc_fence_before();
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor core
       __syncwarp();
       if (lane == 0) mbar_arrive(q_full);
     }
@@ -447,60 +482,104 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
 #pragma unroll
     for (int d = 0; d < D; ++d) o_acc[d] = 0.0f;
     bool ok = true;
-    for (int t = 0; t < T; ++t) {
+    const uint32_t orow = trow + O_COL + team * D;
+    int n = 0;  // tiles this team has processed
+    for (int t = team; t < T; t += 2, ++n) {
+      const int sb = t % NSB;
       const bool plain = bias_row == nullptr && (t + 1) * BKV <= p.Lk;  // no bias, no masking
       if (!plain) {
-        // key bias (+ -inf past Lk) for this tile, staged in a warp-private buffer so no
-        // cross-warp barrier is needed (a warp may leave the loop early on an error)
+        // key bias (+ -inf past Lk) for this tile, staged in a warp-private buffer
         __syncwarp();
 #pragma unroll
         for (int i = 0; i < BKV / 32; ++i) {
           const int jl = i * 32 + lane;
           const int j = t * BKV + jl;
-          float b = -INFINITY;
-          if (j < p.Lk) b = bias_row ? bias_row[j] * LOG2E : 0.0f;
-          bt[jl] = b;
+          bt[jl] = j < p.Lk ? (bias_row ? bias_row[j] * LOG2E : 0.0f) : -INFINITY;
         }
         __syncwarp();
       }
       const float c2 = cq * p.kinv[(int64_t)bh * T + t];
       // exponent offset folding this V tile's pre-scale relative to the head reference
       const float vshift = (float)((__float_as_int(p.vinv[(int64_t)bh * T + t]) >> 23) - vref_exp);
-      ok = mbar_wait(s_full, t & 1, p.status, kDevTimeoutConsumer, abort_flag);
+      ok = mbar_wait(&s_full[sb], (t / NSB) & 1, p.status, kDevTimeoutConsumer, abort_flag);
+      // this team's previous O, P.V(t-2), retired long ago; it is folded in with the scores
+      if (ok && n > 0) {
+        const int tp = t - 2;
+        ok = mbar_wait(&pv_done[tp % NSB], (tp / NSB) & 1, p.status, kDevTimeoutConsumer, abort_flag);
+      }
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
+      const uint32_t srow = trow + S_COL + sb * BKV;
       if (plain)
-        softmax_tile<true>(tmem + lane_base, t > 0, bt, c2, vshift, m_run, l_run, o_acc);
+        softmax_tile<true>(srow, orow, n > 0, bt, c2, vshift, m_run, l_run, o_acc);
       else
-        softmax_tile<false>(tmem + lane_base, t > 0, bt, c2, vshift, m_run, l_run, o_acc);
+        softmax_tile<false>(srow, orow, n > 0, bt, c2, vshift, m_run, l_run, o_acc);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(&p_full[team]);
     }
-    if (ok) {
-      ok = mbar_wait(o_done, (T - 1) & 1, p.status, kDevTimeoutEpilogue, abort_flag);
-      ok = __all_sync(0xffffffffu, ok);
+    if (ok && n > 0) {
+      // the team's last O
+      const int tl = team + 2 * (n - 1);
+      ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[tl % NSB], (tl / NSB) & 1, p.status,
+                                             kDevTimeoutEpilogue, abort_flag));
       if (ok) {
         tc_fence_after();
 #pragma unroll
-        for (int hh = 0; hh < D / 32; ++hh) {
+        for (int hh = 0; hh < 2; ++hh) {
           uint32_t o[32];
-          tmem_ld32(tmem + lane_base + O_COL + hh * 32, o);
+          tmem_ld32(orow + hh * 32, o);
           tmem_wait_ld();
           reg_fence(o);
 #pragma unroll
           for (int d = 0; d < 32; ++d) o_acc[hh * 32 + d] += __uint_as_float(o[d]);
         }
-        if (row_valid) {
-          const float f = vref / l_run;
-          const int b = bh / p.H, h = bh % p.H;
-          float* dst = p.out_blhd ? p.out + (((int64_t)b * p.Lq + qrow) * p.H + h) * D
-                                  : p.out + ((int64_t)bh * p.Lq + qrow) * D;
+      }
+    }
+    if (ok) {
+      // merge the two teams' partial softmaxes of this row (split-K over the key tiles):
+      // common reference m, factors 2^(m_team - m), exact since both references are
+      // integers (or -inf for a team without tiles)
+      xm[team * BQ + r] = m_run;
+      xl[team * BQ + r] = l_run;
+      float* mine = xo + ((1 - team) * BQ + r) * 32;  // the half the other team writes out
+      if (team == 0) {
 #pragma unroll
-          for (int d = 0; d < D; d += 4)
-            *reinterpret_cast<float4*>(dst + d) =
-                make_float4(o_acc[d] * f, o_acc[d + 1] * f, o_acc[d + 2] * f, o_acc[d + 3] * f);
+        for (int d = 0; d < 32; d += 4)
+          *reinterpret_cast<float4*>(mine + d) = make_float4(o_acc[32 + d], o_acc[33 + d], o_acc[34 + d], o_acc[35 + d]);
+      } else {
+#pragma unroll
+        for (int d = 0; d < 32; d += 4)
+          *reinterpret_cast<float4*>(mine + d) = make_float4(o_acc[d], o_acc[d + 1], o_acc[d + 2], o_acc[d + 3]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(xbar);
+      ok = __all_sync(0xffffffffu, mbar_wait(xbar, 0, p.status, kDevTimeoutEpilogue, abort_flag));
+      if (ok && row_valid) {
+        const float m_o = xm[(1 - team) * BQ + r], l_o = xl[(1 - team) * BQ + r];
+        const float m = fmaxf(m_run, m_o);
+        const float f_me = m_run == m ? 1.0f : ex2(m_run - m);  // 0 for a team with no tiles
+        const float f_o = m_o == m ? 1.0f : ex2(m_o - m);
+        const float f = vref / (l_run * f_me + l_o * f_o);
+        const float* other = xo + (team * BQ + r) * 32;  // the other team's half of my dims
+        const int b = bh / p.H, hh = bh % p.H;
+        float* dst = (p.out_blhd ? p.out + (((int64_t)b * p.Lq + qrow) * p.H + hh) * D
+                                 : p.out + ((int64_t)bh * p.Lq + qrow) * D) + team * 32;
+        float res[32];
+        if (team == 0) {
+#pragma unroll
+          for (int d = 0; d < 32; ++d) res[d] = o_acc[d];
+        } else {
+#pragma unroll
+          for (int d = 0; d < 32; ++d) res[d] = o_acc[32 + d];
+        }
+#pragma unroll
+        for (int d = 0; d < 32; d += 4) {
+          const float4 ov = *reinterpret_cast<const float4*>(other + d);
+          *reinterpret_cast<float4*>(dst + d) =
+              make_float4((res[d] * f_me + ov.x * f_o) * f, (res[d + 1] * f_me + ov.y * f_o) * f,
+                          (res[d + 2] * f_me + ov.z * f_o) * f, (res[d + 3] * f_me + ov.w * f_o) * f);
         }
       }
     }
@@ -708,6 +787,14 @@ static int sdpa_launch(const float* q, const float* k, const float* v, int64_t b
     int dev = 0;
     cudaGetDevice(&dev);
     if (!(attr_done >> dev & 1)) {
+      // the warpgroups' setmaxnreg budgets add up to the launch allocation of a kernel
+      // compiled with REGS_LAUNCH registers per thread; with fewer, an increase would wait
+      // for ever, so refuse to launch instead
+      cudaFuncAttributes fa{};
+      if (cudaFuncGetAttributes(&fa, sdpa_fwd_tc) != cudaSuccess || fa.numRegs < (int)REGS_LAUNCH) {
+        set_last_error("sdpa_fwd_tc was compiled with fewer registers than its warpgroup budget needs");
+        return kLaunchFailed;
+      }
       cudaFuncSetAttribute(sdpa_fwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
       attr_done |= 1ull << dev;
     }
