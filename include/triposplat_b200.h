@@ -233,6 +233,21 @@ int triposplat_b200_q_kv_rmsnorm_pack_f32(const float* q, const float* kv, const
                                           float* packed_v, int B, int Lq, int Lk, int H,
                                           int Lk_padded);
 
+/* No reference counterpart: triposplat_qkv_rope_rmsnorm_pack_f32_avx512_v2 followed by
+ * triposplat_sdpa_f32_avx512_exact_q8t512_packed_blhd in one call.  qkv [B,L,3,H,64],
+ * frequencies [frequency_batches, L, H, 64] (interleaved cos/sin) -> out_blhd [B,L,H,64];
+ * q / k / v go straight to the attention's split format (same results bit for bit as the
+ * two calls).  D must be 64. */
+int triposplat_b200_qkv_rope_rmsnorm_sdpa_f32(const float* qkv, const float* frequencies,
+                                              const float* q_gamma, const float* k_gamma,
+                                              float* out_blhd, int B, int L, int H, int D,
+                                              int frequency_batches);
+/* No reference counterpart: triposplat_b200_q_kv_rmsnorm_pack_f32 followed by the packed
+ * SDPA in one call (cross-attention).  q [B,Lq,H,64], kv [B,Lk,2,H,64] -> out_blhd [B,Lq,H,64]. */
+int triposplat_b200_q_kv_rmsnorm_sdpa_f32(const float* q, const float* kv, const float* q_gamma,
+                                          const float* k_gamma, float* out_blhd, int B, int Lq,
+                                          int Lk, int H);
+
 #ifdef __cplusplus
 }
 #endif

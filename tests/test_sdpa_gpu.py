@@ -178,3 +178,44 @@ def test_sdpa_error_codes():
     assert f(host.ctypes.data, p, p, None, p, 1, 1, 4, 4, 64, 0, 0, 0) == -9
     assert lib.triposplat_sdpa_packed_output_is_blhd() == 1
     assert lib.triposplat_b200_status() == 0
+
+
+@pytest.mark.parametrize("case", ["pos_self_12294", "neg_compressed_8194_logM", "final_8193x12294",
+                                  "final_packed_blhd_8193x12294"])
+def test_sdpa_reference_real_shapes(case):
+    """The shapes the reference's attention patch produces at its real resolution
+    (triposplat_attention_patch.py): positive branch self-attention over 12294 tokens,
+    negative branch compressed to 8194 keys whose key bias is log(multiplicity), and the
+    selected-query final block (8193 queries against 12294 keys), also through the packed
+    K/V + BLHD entry.  fp64 spot check on 96 query rows per head, relative to the rms of O."""
+    from native_sdpa_ctypes import native_sdpa_f32, native_sdpa_packed_blhd
+
+    Lq, Lk = {"pos_self_12294": (12294, 12294), "neg_compressed_8194_logM": (8194, 8194),
+              "final_8193x12294": (8193, 12294), "final_packed_blhd_8193x12294": (8193, 12294)}[case]
+    g = torch.Generator(device="cuda").manual_seed(Lq + Lk)
+    B, H = 1, 2
+    q = torch.randn(B, H, Lq, 64, device="cuda", generator=g)
+    k = torch.randn(B, H, Lk, 64, device="cuda", generator=g)
+    v = torch.randn(B, H, Lk, 64, device="cuda", generator=g)
+    bias = None
+    if case.startswith("neg"):
+        mult = torch.randint(1, 65, (Lk,), device="cuda", generator=g).float()
+        bias = torch.log(mult)
+    if case.endswith("packed_blhd_8193x12294"):
+        Lkp = (Lk + 15) // 16 * 16
+        pk = torch.zeros(B, H, 64, Lkp, device="cuda")
+        pv = torch.zeros(B, H, 64, Lkp, device="cuda")
+        pk[..., :Lk] = k.transpose(-1, -2)
+        pv[..., :Lk] = v.transpose(-1, -2)
+        out = native_sdpa_packed_blhd(q, pk, pv, Lk).permute(0, 2, 1, 3)
+    else:
+        out = native_sdpa_f32(q, k, v, key_bias=bias)
+    rows = torch.randperm(Lq, generator=torch.Generator().manual_seed(5))[:96].cuda()
+    s = (q[:, :, rows].double() @ k.double().transpose(-1, -2)) * 0.125
+    if bias is not None:
+        s = s + bias.double()
+    ref = torch.softmax(s, dim=-1) @ v.double()
+    err = out[:, :, rows].double() - ref
+    rel = float(err.pow(2).mean().sqrt() / ref.pow(2).mean().sqrt())
+    assert bool(torch.isfinite(out).all())
+    assert rel <= REL_RMSE_LONG, f"relative rmse {rel:.3e}"

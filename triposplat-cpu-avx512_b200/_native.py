@@ -74,6 +74,8 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "triposplat_qkv_rope_rmsnorm_pack_f32_avx512_v2": ([VP] * 7 + [I] * 7, I),
     "triposplat_q_kv_selected_rope_rmsnorm_pack_f32_avx512_v2": ([VP] * 9 + [I] * 8, I),
     "triposplat_b200_q_kv_rmsnorm_pack_f32": ([VP] * 7 + [I] * 5, I),
+    "triposplat_b200_qkv_rope_rmsnorm_sdpa_f32": ([VP] * 5 + [I] * 5, I),
+    "triposplat_b200_q_kv_rmsnorm_sdpa_f32": ([VP] * 5 + [I] * 4, I),
     "triposplat_timestep_embedding_f32_avx512": ([VP] * 3 + [I] * 4, I),
 }
 

@@ -297,6 +297,24 @@ __device__ __forceinline__ void setmaxnreg_dec() {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// RoPE (interleaved complex) then 8/max(||.||, 1e-12) * gamma on one 64-vector held as
+// one complex pair per lane (scripts/native_qkv_postprocess_v2_avx512.c:3-24).  The
+// products are contracted explicitly, so every kernel that includes this computes the
+// same bits (the fused QKV -> attention-split path is checked bit for bit against the
+// separate post-process + split).
+__device__ __forceinline__ float2 rope_rms64(float2 x, float2 f, float2 g) {
+  const float2 r = make_float2(fmaf(x.x, f.x, -(x.y * f.y)), fmaf(x.x, f.y, x.y * f.x));
+  const float ss = warp_sum(fmaf(r.x, r.x, r.y * r.y));
+  const float fac = 8.0f / fmaxf(sqrtf(ss), 1.0e-12f);
+  return make_float2(r.x * fac * g.x, r.y * fac * g.y);
+}
+
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
   asm volatile(

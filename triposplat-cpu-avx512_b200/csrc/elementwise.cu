@@ -16,11 +16,6 @@
 namespace tsb {
 namespace ew {
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
 
 inline unsigned grid_for(int64_t work, int per_block) {
   const int64_t blocks = (work + per_block - 1) / per_block;
@@ -146,15 +141,6 @@ __global__ void euler_k(float* __restrict__ x, const float* __restrict__ v,
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
     x[i] = x[i] - dt[i / per_batch] * v[i];
-}
-
-// RoPE (interleaved complex) then 8/max(||.||, 1e-12) * gamma on one 64-vector held as
-// one complex pair per lane.  scripts/native_qkv_postprocess_v2_avx512.c:3-24
-__device__ __forceinline__ float2 rope_rms64(float2 x, float2 f, float2 g) {
-  const float2 r = make_float2(x.x * f.x - x.y * f.y, x.x * f.y + x.y * f.x);
-  const float ss = warp_sum(fmaf(r.x, r.x, r.y * r.y));
-  const float fac = 8.0f / fmaxf(sqrtf(ss), 1.0e-12f);
-  return make_float2(r.x * fac * g.x, r.y * fac * g.y);
 }
 
 // One CTA per (bh, 64-token tile).  Q rows go straight to [B,H,L,64]; K and V are

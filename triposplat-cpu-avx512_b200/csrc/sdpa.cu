@@ -701,6 +701,155 @@ __global__ void __launch_bounds__(256) sdpa_split_kv(
   }
 }
 
+
+// Fused QKV post-process -> attention split format (no reference counterpart; the
+// composition of scripts/native_qkv_postprocess_v2_avx512.c:45-191 with the split above).
+// One CTA per (bh, 128-token tile): RoPE + 8/max(||.||,1e-12)*gamma on q and k
+// (rope_rms64), then q rows straight to the Q planes (per-row pre-scale, as
+// sdpa_split_q) and the tile's k / v through shared memory to the K and V^T planes (per-tile
+// pre-scales, as sdpa_split_kv): the same bits as the two-kernel path, with q / k / v never
+// written to HBM in fp32.  Source layouts: kSelected = false: qkv [B, L, 3, H, 64]
+// (q, k and v of token t); kSelected = true: q [B, Lq, H, 64] and kv [B, Lk, 2, H, 64], RoPE
+// frequency row of query i = sel[i] (no frequencies: no rotation).
+template <bool kSelected>
+__global__ void __launch_bounds__(256) qkv_split_k(
+    const float* __restrict__ qsrc, const float* __restrict__ kvsrc, const float* __restrict__ freqs,
+    const int64_t* __restrict__ sel, const float* __restrict__ qg, const float* __restrict__ kg,
+    int H, int Lq, int Lk, int Lkt, int fb, __half* __restrict__ qhi, __half* __restrict__ qlo,
+    float* __restrict__ qinv, __half* __restrict__ khi, __half* __restrict__ klo,
+    __half* __restrict__ vhi, __half* __restrict__ vlo, float* __restrict__ kinv,
+    float* __restrict__ vinv) {
+  extern __shared__ float sm_kv[];
+  float(*kt)[D + 1] = reinterpret_cast<float(*)[D + 1]>(sm_kv);            // [BKV][65]
+  float(*vt)[D + 1] = reinterpret_cast<float(*)[D + 1]>(sm_kv + BKV * (D + 1));
+  __shared__ float red[2][8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y, b = bh / H, h = bh % H;
+  const int fbb = fb == 1 ? 0 : b;
+  const int tile = blockIdx.x, T = Lkt / BKV;
+  const float2 gq = reinterpret_cast<const float2*>(qg + (int64_t)h * 64)[lane];
+  const float2 gk = reinterpret_cast<const float2*>(kg + (int64_t)h * 64)[lane];
+  // one q row (rope_rms64 output held as one complex pair per lane) into the Q planes
+  auto emit_q = [&](int64_t row, float2 qy) {
+    float mx = fmaxf(fabsf(qy.x), fabsf(qy.y));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const int sq = pow2_shift(mx);
+    const float a = ldexpf(qy.x, sq), c = ldexpf(qy.y, sq);
+    const __half2 hh = __floats2half2_rn(a, c);
+    const float2 hf = __half22float2(hh);
+    *reinterpret_cast<__half2*>(qhi + row * D + lane * 2) = hh;
+    *reinterpret_cast<__half2*>(qlo + row * D + lane * 2) = __floats2half2_rn(a - hf.x, c - hf.y);
+    if (lane == 0) qinv[row] = ldexpf(1.0f, -sq);
+  };
+  if (tile < T) {
+    const int t0 = tile * BKV;
+    float kmx = 0.0f, vmx = 0.0f;
+    // 16 tokens per warp, four at a time with all their loads issued first (the loop is
+    // latency-bound otherwise: one token's loads and warp reductions at a time)
+    for (int j0 = 0; j0 < BKV / 8; j0 += 4) {
+      float2 qx[4], kx[4], vx[4], fr[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int t = t0 + warp + 8 * (j0 + u);
+        qx[u] = kx[u] = vx[u] = make_float2(0.0f, 0.0f);
+        fr[u] = make_float2(1.0f, 0.0f);
+        if (t < Lk) {
+          if (freqs) fr[u] = reinterpret_cast<const float2*>(freqs + (((int64_t)fbb * Lk + t) * H + h) * 64)[lane];
+          const float* ks = kSelected ? kvsrc + (((int64_t)b * Lk + t) * 2 * H + h) * 64
+                                      : kvsrc + (((int64_t)b * Lk + t) * 3 * H + H + h) * 64;
+          if (!kSelected) qx[u] = reinterpret_cast<const float2*>(ks - (int64_t)H * 64)[lane];
+          kx[u] = reinterpret_cast<const float2*>(ks)[lane];
+          vx[u] = reinterpret_cast<const float2*>(ks + (int64_t)H * 64)[lane];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = warp + 8 * (j0 + u);
+        const int t = t0 + i;
+        float2 ky = make_float2(0.0f, 0.0f), vy = make_float2(0.0f, 0.0f);
+        if (t < Lk) {  // warp-uniform: t depends on the warp only
+          if (!kSelected) emit_q((int64_t)bh * Lq + t, rope_rms64(qx[u], fr[u], gq));
+          ky = rope_rms64(kx[u], fr[u], gk);
+          vy = vx[u];
+        }
+        kt[i][2 * lane] = ky.x;
+        kt[i][2 * lane + 1] = ky.y;
+        vt[i][2 * lane] = vy.x;
+        vt[i][2 * lane + 1] = vy.y;
+        kmx = fmaxf(kmx, fmaxf(fabsf(ky.x), fabsf(ky.y)));
+        vmx = fmaxf(vmx, fmaxf(fabsf(vy.x), fabsf(vy.y)));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      kmx = fmaxf(kmx, __shfl_xor_sync(0xffffffffu, kmx, o));
+      vmx = fmaxf(vmx, __shfl_xor_sync(0xffffffffu, vmx, o));
+    }
+    if (lane == 0) { red[0][warp] = kmx; red[1][warp] = vmx; }
+    __syncthreads();
+    kmx = red[0][0]; vmx = red[1][0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) { kmx = fmaxf(kmx, red[0][w]); vmx = fmaxf(vmx, red[1][w]); }
+    const int sk = pow2_shift(kmx), sv = pow2_shift(vmx);
+    for (int e = threadIdx.x; e < BKV * (D / 8); e += 256) {
+      const int j = e / (D / 8), d0 = (e % (D / 8)) * 8;
+      __align__(16) __half h8[8];
+      __align__(16) __half l8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float x = ldexpf(kt[j][d0 + i], sk);
+        const __half hh = __float2half_rn(x);
+        h8[i] = hh;
+        l8[i] = __float2half_rn(x - __half2float(hh));
+      }
+      const int64_t off = ((int64_t)bh * Lkt + t0 + j) * D + d0;
+      *reinterpret_cast<uint4*>(khi + off) = *reinterpret_cast<uint4*>(h8);
+      *reinterpret_cast<uint4*>(klo + off) = *reinterpret_cast<uint4*>(l8);
+    }
+    for (int e = threadIdx.x; e < D * (BKV / 8); e += 256) {
+      const int d = e / (BKV / 8), jb = (e % (BKV / 8)) * 8;
+      __align__(16) __half h8[8];
+      __align__(16) __half l8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float x = ldexpf(vt[jb + i][d], sv);
+        const __half hh = __float2half_rn(x);
+        h8[i] = hh;
+        l8[i] = __float2half_rn(x - __half2float(hh));
+      }
+      const int64_t off = ((int64_t)bh * D + d) * Lkt + t0 + jb;
+      *reinterpret_cast<uint4*>(vhi + off) = *reinterpret_cast<uint4*>(h8);
+      *reinterpret_cast<uint4*>(vlo + off) = *reinterpret_cast<uint4*>(l8);
+    }
+    if (threadIdx.x == 0) {
+      kinv[(int64_t)bh * T + tile] = ldexpf(1.0f, -sk);
+      vinv[(int64_t)bh * T + tile] = ldexpf(1.0f, -sv);
+    }
+  }
+  if (kSelected) {
+    for (int j0 = 0; j0 < BKV / 8; j0 += 4) {
+      float2 qx[4], fr[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int qi = tile * BKV + warp + 8 * (j0 + u);
+        qx[u] = make_float2(0.0f, 0.0f);
+        fr[u] = make_float2(1.0f, 0.0f);  // no frequencies: identity rotation
+        if (qi < Lq) {
+          if (freqs) fr[u] = reinterpret_cast<const float2*>(freqs + (((int64_t)fbb * Lk + sel[qi]) * H + h) * 64)[lane];
+          qx[u] = reinterpret_cast<const float2*>(qsrc + (((int64_t)b * Lq + qi) * H + h) * 64)[lane];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int qi = tile * BKV + warp + 8 * (j0 + u);
+        if (qi < Lq) emit_q((int64_t)bh * Lq + qi, rope_rms64(qx[u], fr[u], gq));  // warp-uniform
+      }
+    }
+  }
+}
+constexpr int QKV_SPLIT_SMEM = 2 * BKV * (D + 1) * 4;
+
 }  // namespace sdpa
 
 struct SdpaCounters {
@@ -712,6 +861,91 @@ static uint64_t now_ns() {
   timespec ts;
   clock_gettime(CLOCK_MONOTONIC, &ts);
   return (uint64_t)ts.tv_sec * 1000000000ull + ts.tv_nsec;
+}
+
+// Attention inputs in the split format, in the library workspace of the current stream.
+struct SplitPlanesSdpa {
+  __half *qhi, *qlo, *khi, *klo, *vhi, *vlo;
+  float *qinv, *kinv, *vinv;
+  int T, Lkt;
+};
+
+static int sdpa_planes(int64_t BH, int Lq, int Lk, cudaStream_t stream, SplitPlanesSdpa& sp) {
+  using namespace sdpa;
+  sp.T = (Lk + BKV - 1) / BKV;
+  sp.Lkt = sp.T * BKV;
+  const size_t qplane = (size_t)BH * Lq * D * 2;
+  const size_t kplane = (size_t)BH * sp.Lkt * D * 2;
+  auto al = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+  const size_t off_qlo = al(qplane), off_qinv = off_qlo + al(qplane);
+  const size_t off_khi = off_qinv + al((size_t)BH * Lq * 4);
+  const size_t off_klo = off_khi + al(kplane), off_vhi = off_klo + al(kplane);
+  const size_t off_vlo = off_vhi + al(kplane), off_kinv = off_vlo + al(kplane);
+  const size_t off_vinv = off_kinv + al((size_t)BH * sp.T * 4);
+  const size_t total = off_vinv + al((size_t)BH * sp.T * 4);
+  uint8_t* ws = static_cast<uint8_t*>(workspace(total, stream));
+  if (!ws) return kWorkspace;
+  sp.qhi = reinterpret_cast<__half*>(ws);
+  sp.qlo = reinterpret_cast<__half*>(ws + off_qlo);
+  sp.qinv = reinterpret_cast<float*>(ws + off_qinv);
+  sp.khi = reinterpret_cast<__half*>(ws + off_khi);
+  sp.klo = reinterpret_cast<__half*>(ws + off_klo);
+  sp.vhi = reinterpret_cast<__half*>(ws + off_vhi);
+  sp.vlo = reinterpret_cast<__half*>(ws + off_vlo);
+  sp.kinv = reinterpret_cast<float*>(ws + off_kinv);
+  sp.vinv = reinterpret_cast<float*>(ws + off_vinv);
+  return kOk;
+}
+
+// The attention kernel on split planes.
+static int sdpa_attend(const SplitPlanesSdpa& sp, const float* bias, int64_t bias_bh_stride,
+                       float* out, int64_t BH, int H, int Lq, int Lk, int out_blhd,
+                       cudaStream_t stream) {
+  using namespace sdpa;
+  CUtensorMap m_khi, m_klo, m_vhi, m_vlo;
+  const uint32_t box_rows[3] = {64, 128, 1};
+  const uint32_t box_vt[3] = {64, 64, 1};
+  {
+    const uint64_t dims[3] = {D, (uint64_t)sp.Lkt, (uint64_t)BH};
+    const uint64_t strides[2] = {D * 2, (uint64_t)sp.Lkt * D * 2};
+    if (!encode_tmap(&m_khi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, sp.khi, dims, strides, box_rows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tmap(&m_klo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, sp.klo, dims, strides, box_rows, CU_TENSOR_MAP_SWIZZLE_128B))
+      return kLaunchFailed;
+  }
+  {
+    const uint64_t dims[3] = {(uint64_t)sp.Lkt, D, (uint64_t)BH};
+    const uint64_t strides[2] = {(uint64_t)sp.Lkt * 2, (uint64_t)sp.Lkt * D * 2};
+    if (!encode_tmap(&m_vhi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, sp.vhi, dims, strides, box_vt, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tmap(&m_vlo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, sp.vlo, dims, strides, box_vt, CU_TENSOR_MAP_SWIZZLE_128B))
+      return kLaunchFailed;
+  }
+  {
+    static uint64_t attr_done = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(attr_done >> dev & 1)) {
+      // the warpgroups' setmaxnreg budgets add up to the launch allocation of a kernel
+      // compiled with REGS_LAUNCH registers per thread; with fewer, an increase would wait
+      // for ever, so refuse to launch instead
+      cudaFuncAttributes fa{};
+      if (cudaFuncGetAttributes(&fa, sdpa_fwd_tc) != cudaSuccess || fa.numRegs < (int)REGS_LAUNCH) {
+        set_last_error("sdpa_fwd_tc was compiled with fewer registers than its warpgroup budget needs");
+        return kLaunchFailed;
+      }
+      cudaFuncSetAttribute(sdpa_fwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+      cudaFuncSetAttribute(qkv_split_k<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, QKV_SPLIT_SMEM);
+      cudaFuncSetAttribute(qkv_split_k<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, QKV_SPLIT_SMEM);
+      attr_done |= 1ull << dev;
+    }
+  }
+  Params prm{sp.qinv, sp.kinv, sp.vinv, bias, (long long)bias_bh_stride, out, H, Lq, Lk, sp.T, out_blhd,
+             device_status()};
+  dim3 grid((Lq + BQ - 1) / BQ, (unsigned)BH);
+  {
+    LaunchScope scope(kKSdpaAttn, stream);
+    sdpa_fwd_tc<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(sp.qhi, sp.qlo, m_khi, m_klo, m_vhi, m_vlo, prm);
+  }
+  return launch_status();
 }
 
 // k/v element (bh, j, d) at base + bh*bh_stride + j*j_stride + d*d_stride
@@ -729,88 +963,72 @@ static int sdpa_launch(const float* q, const float* k, const float* v, int64_t b
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15) return kBadAlignment;
   cudaStream_t stream = current_stream();
   const int64_t BH = (int64_t)B * H;
-  const int T = (Lk + BKV - 1) / BKV;
-  const int Lkt = T * BKV;
-  const size_t qplane = (size_t)BH * Lq * D * 2;
-  const size_t kplane = (size_t)BH * Lkt * D * 2;
-  auto al = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
-  const size_t off_qlo = al(qplane), off_qinv = off_qlo + al(qplane);
-  const size_t off_khi = off_qinv + al((size_t)BH * Lq * 4);
-  const size_t off_klo = off_khi + al(kplane), off_vhi = off_klo + al(kplane);
-  const size_t off_vlo = off_vhi + al(kplane), off_kinv = off_vlo + al(kplane);
-  const size_t off_vinv = off_kinv + al((size_t)BH * T * 4);
-  const size_t total = off_vinv + al((size_t)BH * T * 4);
-  uint8_t* ws = static_cast<uint8_t*>(workspace(total, stream));
-  if (!ws) return kWorkspace;
-  __half* qhi = reinterpret_cast<__half*>(ws);
-  __half* qlo = reinterpret_cast<__half*>(ws + off_qlo);
-  float* qinv = reinterpret_cast<float*>(ws + off_qinv);
-  __half* khi = reinterpret_cast<__half*>(ws + off_khi);
-  __half* klo = reinterpret_cast<__half*>(ws + off_klo);
-  __half* vhi = reinterpret_cast<__half*>(ws + off_vhi);
-  __half* vlo = reinterpret_cast<__half*>(ws + off_vlo);
-  float* kinv = reinterpret_cast<float*>(ws + off_kinv);
-  float* vinv = reinterpret_cast<float*>(ws + off_vinv);
-
+  SplitPlanesSdpa sp;
+  if ((st = sdpa_planes(BH, Lq, Lk, stream, sp)) != kOk) return st;
   const int64_t qrows = BH * Lq;
   {
     LaunchScope scope(kKSdpaSplit, stream);
-    sdpa_split_q<<<(unsigned)((qrows + 7) / 8), 256, 0, stream>>>(q, qrows, qhi, qlo, qinv);
+    sdpa_split_q<<<(unsigned)((qrows + 7) / 8), 256, 0, stream>>>(q, qrows, sp.qhi, sp.qlo, sp.qinv);
   }
   {
     LaunchScope scope(kKSdpaSplit, stream);
-    sdpa_split_kv<<<dim3(T, (unsigned)BH), 256, 0, stream>>>(k, v, bh_stride, j_stride, d_stride,
-                                                             Lk, Lkt, khi, klo, vhi, vlo, kinv, vinv);
+    sdpa_split_kv<<<dim3(sp.T, (unsigned)BH), 256, 0, stream>>>(k, v, bh_stride, j_stride, d_stride, Lk,
+                                                                sp.Lkt, sp.khi, sp.klo, sp.vhi, sp.vlo,
+                                                                sp.kinv, sp.vinv);
   }
   if ((st = launch_status()) != kOk) return st;
   const uint64_t t1 = now_ns();
-
-  CUtensorMap m_khi, m_klo, m_vhi, m_vlo;
-  const uint32_t box_rows[3] = {64, 128, 1};
-  const uint32_t box_vt[3] = {64, 64, 1};
-  {
-    const uint64_t dims[3] = {D, (uint64_t)Lkt, (uint64_t)BH};
-    const uint64_t strides[2] = {D * 2, (uint64_t)Lkt * D * 2};
-    if (!encode_tmap(&m_khi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, khi, dims, strides, box_rows, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_tmap(&m_klo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, klo, dims, strides, box_rows, CU_TENSOR_MAP_SWIZZLE_128B))
-      return kLaunchFailed;
-  }
-  {
-    const uint64_t dims[3] = {(uint64_t)Lkt, D, (uint64_t)BH};
-    const uint64_t strides[2] = {(uint64_t)Lkt * 2, (uint64_t)Lkt * D * 2};
-    if (!encode_tmap(&m_vhi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, vhi, dims, strides, box_vt, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_tmap(&m_vlo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, vlo, dims, strides, box_vt, CU_TENSOR_MAP_SWIZZLE_128B))
-      return kLaunchFailed;
-  }
-  {
-    static uint64_t attr_done = 0;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!(attr_done >> dev & 1)) {
-      // the warpgroups' setmaxnreg budgets add up to the launch allocation of a kernel
-      // compiled with REGS_LAUNCH registers per thread; with fewer, an increase would wait
-      // for ever, so refuse to launch instead
-      cudaFuncAttributes fa{};
-      if (cudaFuncGetAttributes(&fa, sdpa_fwd_tc) != cudaSuccess || fa.numRegs < (int)REGS_LAUNCH) {
-        set_last_error("sdpa_fwd_tc was compiled with fewer registers than its warpgroup budget needs");
-        return kLaunchFailed;
-      }
-      cudaFuncSetAttribute(sdpa_fwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-      attr_done |= 1ull << dev;
-    }
-  }
-  Params prm{qinv, kinv, vinv, bias, (long long)bias_bh_stride, out, H, Lq, Lk, T, out_blhd, device_status()};
-  dim3 grid((Lq + BQ - 1) / BQ, (unsigned)BH);
-  {
-    LaunchScope scope(kKSdpaAttn, stream);
-    sdpa_fwd_tc<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(qhi, qlo, m_khi, m_klo, m_vhi, m_vlo, prm);
-  }
-  st = launch_status();
+  st = sdpa_attend(sp, bias, bias_bh_stride, out, BH, H, Lq, Lk, out_blhd, stream);
   const uint64_t t2 = now_ns();
   g_sdpa.calls += 1;
   g_sdpa.split_ns += t1 - t0;
   g_sdpa.attn_ns += t2 - t1;
   return st;
+}
+
+// Fused post-process + split, then the attention (BLHD output).  qsrc / kvsrc / freqs /
+// sel as qkv_split_k; frequency rows: fb batches of [Lk, H, 64].
+template <bool kSelected>
+static int qkv_sdpa_launch(const float* qsrc, const float* kvsrc, const float* freqs,
+                           const int64_t* sel, const float* qg, const float* kg, float* out_blhd,
+                           int B, int H, int Lq, int Lk, int fb) {
+  using namespace sdpa;
+  int st = entry_check();
+  if (st != kOk) return st;
+  if (!is_device_pointer(kvsrc) || !is_device_pointer(qg) || !is_device_pointer(kg) ||
+      !is_device_pointer(out_blhd) || (qsrc && !is_device_pointer(qsrc)) ||
+      (freqs && !is_device_pointer(freqs)))
+    return kNotDevicePointer;
+  if ((reinterpret_cast<uintptr_t>(kvsrc) | reinterpret_cast<uintptr_t>(out_blhd) |
+       reinterpret_cast<uintptr_t>(qsrc) | reinterpret_cast<uintptr_t>(freqs) |
+       reinterpret_cast<uintptr_t>(qg) | reinterpret_cast<uintptr_t>(kg)) & 15)
+    return kBadAlignment;
+  cudaStream_t stream = current_stream();
+  const int64_t BH = (int64_t)B * H;
+  SplitPlanesSdpa sp;
+  if ((st = sdpa_planes(BH, Lq, Lk, stream, sp)) != kOk) return st;
+  // make sure the attention kernel's attributes (and the fused kernel's shared memory
+  // opt-in) are set before the fused kernel's first launch on this device
+  {
+    static uint64_t attr_done = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(attr_done >> dev & 1)) {
+      cudaFuncSetAttribute(qkv_split_k<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, QKV_SPLIT_SMEM);
+      cudaFuncSetAttribute(qkv_split_k<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, QKV_SPLIT_SMEM);
+      attr_done |= 1ull << dev;
+    }
+  }
+  const int q_tiles = (Lq + BKV - 1) / BKV;
+  const int tiles = kSelected ? (sp.T > q_tiles ? sp.T : q_tiles) : sp.T;
+  {
+    LaunchScope scope(kKSdpaSplit, stream);
+    qkv_split_k<kSelected><<<dim3(tiles, (unsigned)BH), 256, QKV_SPLIT_SMEM, stream>>>(
+        qsrc, kvsrc, freqs, sel, qg, kg, H, Lq, Lk, sp.Lkt, fb, sp.qhi, sp.qlo, sp.qinv, sp.khi, sp.klo,
+        sp.vhi, sp.vlo, sp.kinv, sp.vinv);
+  }
+  if ((st = launch_status()) != kOk) return st;
+  return sdpa_attend(sp, nullptr, 0, out_blhd, BH, H, Lq, Lk, 1, stream);
 }
 
 }  // namespace tsb
@@ -879,6 +1097,33 @@ int triposplat_sdpa_f32_cuda_bias_bh(const float* q, const float* k, const float
   if (bias && bias_bh_stride != 0 && bias_bh_stride < Lk) return tsb::kBadRange;
   return tsb::sdpa_launch(q, k, v, (int64_t)Lk * 64, 64, 1, bias, bias_bh_stride, out, B, H, Lq,
                           Lk, out_blhd ? 1 : 0);
+}
+
+// No reference counterpart: the reference's QKV post-process followed by its packed SDPA
+// (scripts/native_qkv_postprocess_v2_avx512.c:45-105, then
+// scripts/native_sdpa_avx512_exact_q8t512_packed.c:3-158) in one call: qkv [B, L, 3, H, 64]
+// -> attention output [B, L, H, 64], with q / k / v going straight to the attention's split
+// format (same results bit for bit as the two calls, without their fp32 intermediates).
+int triposplat_b200_qkv_rope_rmsnorm_sdpa_f32(const float* qkv, const float* frequencies,
+                                              const float* q_gamma, const float* k_gamma,
+                                              float* out_blhd, int B, int L, int H, int D,
+                                              int frequency_batches) {
+  if (!qkv || !frequencies || !q_gamma || !k_gamma || !out_blhd) return tsb::kNullPointer;
+  if (B <= 0 || L <= 0 || H <= 0 || D != 64 || (frequency_batches != 1 && frequency_batches != B))
+    return tsb::kBadDims;
+  return tsb::qkv_sdpa_launch<false>(nullptr, qkv, frequencies, nullptr, q_gamma, k_gamma, out_blhd,
+                                     B, H, L, L, frequency_batches);
+}
+
+// No reference counterpart: triposplat_b200_q_kv_rmsnorm_pack_f32 (per-head RMSNorm of q
+// [B, Lq, H, 64] and of the keys of kv [B, Lk, 2, H, 64], no RoPE) followed by the packed
+// SDPA, in one call with the split format written directly (cross-attention).
+int triposplat_b200_q_kv_rmsnorm_sdpa_f32(const float* q, const float* kv, const float* q_gamma,
+                                          const float* k_gamma, float* out_blhd, int B, int Lq,
+                                          int Lk, int H) {
+  if (!q || !kv || !q_gamma || !k_gamma || !out_blhd) return tsb::kNullPointer;
+  if (B <= 0 || Lq <= 0 || Lk <= 0 || H <= 0) return tsb::kBadDims;
+  return tsb::qkv_sdpa_launch<true>(q, kv, nullptr, nullptr, q_gamma, k_gamma, out_blhd, B, H, Lq, Lk, 1);
 }
 
 // scripts/native_sdpa_avx512_exact_q8t512.c:64-70: tile sizes of this implementation

@@ -333,26 +333,19 @@ class FlowModelB200:
         # self-attention
         self._ln_split(x, sph, shift_msa, scale_msa)
         self._lin_split(p + "qkv", sph, rows, b["qkv"])
-        self._ok(lib.triposplat_qkv_rope_rmsnorm_pack_f32_avx512_v2(
+        # RoPE + RMSNorm straight into the attention's split format, then the attention
+        self._ok(lib.triposplat_b200_qkv_rope_rmsnorm_sdpa_f32(
             b["qkv"].data_ptr(), self.freqs.data_ptr(), prm[p + "q_gamma"].data_ptr(),
-            prm[p + "k_gamma"].data_ptr(), b["q"].data_ptr(), b["pk"].data_ptr(), b["pv"].data_ptr(),
-            B, L, H, 64, self.Lp, 1, 0), "qkv_post")
-        self._ok(lib.triposplat_sdpa_f32_avx512_exact_q8t512_packed_blhd(
-            b["q"].data_ptr(), b["pk"].data_ptr(), b["pv"].data_ptr(), None, b["o"].data_ptr(),
-            B, H, L, L, 64, self.Lp, 0, 0, 0), "self_sdpa")
+            prm[p + "k_gamma"].data_ptr(), b["o"].data_ptr(), B, L, H, 64, 1), "self_attention")
         self._split(b["o"], sph)
         self._lin_split(p + "out", sph, rows, x, mode=2, gate=gate_msa, gate_ld=h, rows_per_batch=L)
         # cross-attention
         self._ln_split(x, sph)
         self._lin_split(p + "cross_q", sph, rows, y)
         self._lin(p + "cross_kv", b["c"], b["ckv"])
-        self._ok(lib.triposplat_b200_q_kv_rmsnorm_pack_f32(
+        self._ok(lib.triposplat_b200_q_kv_rmsnorm_sdpa_f32(
             y.data_ptr(), b["ckv"].data_ptr(), prm[p + "cq_gamma"].data_ptr(),
-            prm[p + "ck_gamma"].data_ptr(), b["q"].data_ptr(), b["cpk"].data_ptr(),
-            b["cpv"].data_ptr(), B, L, Mc, H, self.Mcp), "cross_post")
-        self._ok(lib.triposplat_sdpa_f32_avx512_exact_q8t512_packed_blhd(
-            b["q"].data_ptr(), b["cpk"].data_ptr(), b["cpv"].data_ptr(), None, b["o"].data_ptr(),
-            B, H, L, Mc, 64, self.Mcp, 0, 0, 0), "cross_sdpa")
+            prm[p + "ck_gamma"].data_ptr(), b["o"].data_ptr(), B, L, Mc, H), "cross_attention")
         self._split(b["o"], sph)
         self._lin_split(p + "cross_out", sph, rows, x, mode=3)
         # MLP
