@@ -467,6 +467,106 @@ __global__ void nf24_split_rows(const float* __restrict__ x, int M, int Mp, int 
   if (lane == 0) rs[row] = ldexpf(1.0f, -shift);
 }
 
+// Register-resident variants for rows of NV * 128 floats (16-byte aligned rows): the row is
+// read from HBM once (the generic kernels read it two to four times), and the pre-scale is a
+// multiplication by the exact power of two (identical to ldexpf in the normal range the
+// shift keeps the values in).  One warp per row; lane i owns float4 groups i, i+32, ...
+__device__ __forceinline__ float pow2f(int s) { return __int_as_float((127 + s) << 23); }
+
+template <int NV>
+__device__ __forceinline__ void store_split_row(const float4 (&v)[NV], float mx, int lane, __half* hr,
+                                                __half* lr, float* rs_row) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const int shf = split_shift(mx);
+  const float p2 = pow2f(shf);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const float a0 = v[i].x * p2, a1 = v[i].y * p2, a2 = v[i].z * p2, a3 = v[i].w * p2;
+    const __half2 h01 = __floats2half2_rn(a0, a1), h23 = __floats2half2_rn(a2, a3);
+    const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+    const __half2 l01 = __floats2half2_rn(a0 - f01.x, a1 - f01.y), l23 = __floats2half2_rn(a2 - f23.x, a3 - f23.y);
+    const int c = (i * 32 + lane) * 4;
+    *reinterpret_cast<uint2*>(hr + c) = make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+    *reinterpret_cast<uint2*>(lr + c) = make_uint2(*reinterpret_cast<const uint32_t*>(&l01), *reinterpret_cast<const uint32_t*>(&l23));
+  }
+  if (lane == 0) *rs_row = pow2f(-shf);
+}
+
+template <int NV>
+__global__ void __launch_bounds__(256) nf24_split_rows_reg(const float* __restrict__ x, int M, int Mp,
+                                                           int stride_x, __half* __restrict__ hi,
+                                                           __half* __restrict__ lo, float* __restrict__ rs) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= Mp) return;
+  if (row >= M) {
+    if (lane == 0) rs[row] = 0.0f;
+    return;
+  }
+  const float4* xr = reinterpret_cast<const float4*>(x + (int64_t)row * stride_x);
+  float4 v[NV];
+  float mx = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    v[i] = xr[i * 32 + lane];
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+  }
+  constexpr int K = NV * 128;
+  store_split_row<NV>(v, mx, lane, hi + (int64_t)row * K, lo + (int64_t)row * K, rs + row);
+}
+
+template <int NV>
+__global__ void __launch_bounds__(256) ln_modulate_split_reg(
+    const float* __restrict__ x, int M, int Mp, float eps, const float* __restrict__ shift,
+    const float* __restrict__ scale, int mod_ld, int rows_per_batch, __half* __restrict__ hi,
+    __half* __restrict__ lo, float* __restrict__ rs) {
+  constexpr int C = NV * 128;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= Mp) return;
+  if (row >= M) {
+    if (lane == 0) rs[row] = 0.0f;
+    return;
+  }
+  const float4* xr = reinterpret_cast<const float4*>(x + (int64_t)row * C);
+  float4 v[NV];
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    v[i] = xr[i * 32 + lane];
+    s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s / (float)C;
+  float var = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const float d0 = v[i].x - mean, d1 = v[i].y - mean, d2 = v[i].z - mean, d3 = v[i].w - mean;
+    var = fmaf(d0, d0, fmaf(d1, d1, fmaf(d2, d2, fmaf(d3, d3, var))));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
+  const float inv = 1.0f / sqrtf(var / (float)C + eps);
+  const int b = row / rows_per_batch;
+  const float4* sh = shift ? reinterpret_cast<const float4*>(shift + (int64_t)b * mod_ld) : nullptr;
+  const float4* sc = scale ? reinterpret_cast<const float4*>(scale + (int64_t)b * mod_ld) : nullptr;
+  float mx = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    float4 y = make_float4((v[i].x - mean) * inv, (v[i].y - mean) * inv, (v[i].z - mean) * inv, (v[i].w - mean) * inv);
+    if (sc) {
+      const float4 a = sc[i * 32 + lane], c = sh[i * 32 + lane];
+      y = make_float4(y.x * (1.0f + a.x) + c.x, y.y * (1.0f + a.y) + c.y, y.z * (1.0f + a.z) + c.z,
+                      y.w * (1.0f + a.w) + c.w);
+    }
+    v[i] = y;
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w))));
+  }
+  store_split_row<NV>(v, mx, lane, hi + (int64_t)row * C, lo + (int64_t)row * C, rs + row);
+}
+
 // LayerNorm (no affine; the reference's two-pass mean / biased variance / 1/sqrtf(var+eps),
 // scripts/native_norm_rope_avx512.c:26-41), optional adaLN modulation h*(1+scale[b])+shift[b]
 // (scripts/native_block_elementwise_avx512.c:9-22), written straight to the GEMM's split
@@ -579,9 +679,19 @@ static SplitPlanes split_layout(uint8_t* base, int M, int K) {
 static int launch_split(const float* x, int stride_x, const SplitPlanes& sp, cudaStream_t stream) {
   using namespace gemm;
   LaunchScope scope(kKGemmSplit, stream);
-  nf24_split_rows<<<(sp.Mp + 7) / 8, 256, 0, stream>>>(
-      x, sp.M, sp.Mp, sp.K, sp.Kp, stride_x, const_cast<__half*>(sp.hi), const_cast<__half*>(sp.lo),
-      const_cast<float*>(sp.rs));
+  __half* hi = const_cast<__half*>(sp.hi);
+  __half* lo = const_cast<__half*>(sp.lo);
+  float* rs = const_cast<float*>(sp.rs);
+  const unsigned grid = (unsigned)((sp.Mp + 7) / 8);
+  const bool vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (stride_x & 3) == 0 && sp.Kp == sp.K;
+  if (vec && sp.K == 1024)
+    nf24_split_rows_reg<8><<<grid, 256, 0, stream>>>(x, sp.M, sp.Mp, stride_x, hi, lo, rs);
+  else if (vec && sp.K == 2048)
+    nf24_split_rows_reg<16><<<grid, 256, 0, stream>>>(x, sp.M, sp.Mp, stride_x, hi, lo, rs);
+  else if (vec && sp.K == 4096)
+    nf24_split_rows_reg<32><<<grid, 256, 0, stream>>>(x, sp.M, sp.Mp, stride_x, hi, lo, rs);
+  else
+    nf24_split_rows<<<grid, 256, 0, stream>>>(x, sp.M, sp.Mp, sp.K, sp.Kp, stride_x, hi, lo, rs);
   return launch_status();
 }
 
@@ -794,9 +904,16 @@ int triposplat_b200_ln_modulate_split(const float* x, int M, int C, float eps, c
   cudaStream_t stream = current_stream();
   {
     LaunchScope scope(kKElementwise, stream);
-    gemm::ln_modulate_split<<<(sp.Mp + 7) / 8, 256, 0, stream>>>(
-        x, M, sp.Mp, C, sp.Kp, eps, shift, scale, mod_ld, rows_per_batch,
-        const_cast<__half*>(sp.hi), const_cast<__half*>(sp.lo), const_cast<float*>(sp.rs));
+    const bool vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && C == 1024 && (mod_ld & 3) == 0 &&
+                     ((reinterpret_cast<uintptr_t>(shift) | reinterpret_cast<uintptr_t>(scale)) & 15) == 0;
+    if (vec)
+      gemm::ln_modulate_split_reg<8><<<(sp.Mp + 7) / 8, 256, 0, stream>>>(
+          x, M, sp.Mp, eps, shift, scale, mod_ld, rows_per_batch, const_cast<__half*>(sp.hi),
+          const_cast<__half*>(sp.lo), const_cast<float*>(sp.rs));
+    else
+      gemm::ln_modulate_split<<<(sp.Mp + 7) / 8, 256, 0, stream>>>(
+          x, M, sp.Mp, C, sp.Kp, eps, shift, scale, mod_ld, rows_per_batch,
+          const_cast<__half*>(sp.hi), const_cast<__half*>(sp.lo), const_cast<float*>(sp.rs));
   }
   return launch_status();
 }
