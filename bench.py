@@ -2,7 +2,7 @@
 """Benchmark: s20 CFG flow sampling of the synthetic 28-block NF24 flow model on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--parallel replicas|cfg] [--case model|gemm1|sdpa2a|sdpa2b|sdpa2c|mlp3|block4]
+                    [--parallel replicas|cfg] [--tp T] [--case model|gemm1|sdpa2a|sdpa2b|sdpa2c|mlp3|block4]
 
 A step is one CFG sampler step (one forward of the batch-2 [cond, uncond] pair through
 28 blocks and 206 NF24 Linears, then CFG combine + Euler update) for one image.
@@ -12,6 +12,8 @@ Multi-GPU (torchrun, one process per GPU), timing is the max over ranks:
   --parallel cfg: each image's CFG pair is split over two GPUs (conditional branch on the
       even rank, unconditional on the odd one; one NCCL all-gather of the velocity per
       step); value = (time of K steps) / K * 20 / (N / 2).
+  --tp T: each model runs head-sharded over T GPUs (three NCCL all-reduces per block);
+      with --parallel cfg an image spans 2T GPUs, otherwise T.
 
 Reported metric: seconds per image for 20-step sampling (lower is better), whole job.
 Also reported: the end-to-end number through the public sampler API with host buffers
@@ -51,6 +53,10 @@ def parse():
                     help="replicas: one image per GPU (default); cfg: each image's CFG pair split "
                          "over two GPUs (conditional / unconditional branch), one NCCL all-gather "
                          "of the velocity per step")
+    ap.add_argument("--tp", type=int, default=1,
+                    help="head-sharded tensor parallelism: each model (the CFG pair, or one "
+                         "branch with --parallel cfg) runs on this many GPUs, heads and MLP "
+                         "columns split, three NCCL all-reduces per block")
     ap.add_argument("--no-graph", action="store_true",
                     help="issue every kernel from the host each step instead of replaying "
                          "the step's CUDA graph")
@@ -285,6 +291,17 @@ def run_reference(args):
     return 0
 
 
+def parallelism_label(split: bool, tp: int, images: int) -> str:
+    parts = []
+    if split:
+        parts.append("CFG pair split over 2 GPU groups (one NCCL all-gather of the velocity per step)")
+    if tp > 1:
+        parts.append(f"heads and MLP columns sharded over {tp} GPUs (3 NCCL all-reduces per block)")
+    if not parts:
+        return f"replicas x{images} (one image per GPU, no data-path collective)"
+    return f"{images} image(s) in parallel; per image: " + "; ".join(parts)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -312,23 +329,40 @@ def main():
     lib = _native.load()
     weights = make_weights(spec, seed=0, device=str(dev))
     split = args.parallel == "cfg"
+    T = args.tp
+    span = T * (2 if split else 1)  # GPUs per image
+    if T < 1 or spec.heads % T or world % span or (split and world < 2):
+        raise SystemExit(f"--gpus {world} does not split into images of {span} GPU(s) "
+                         f"(--parallel {args.parallel} --tp {T}; tp must divide {spec.heads} heads)")
+    images, image = world // span, rank // span
+    branch, tp_rank = (rank // T) % 2 if split else 0, rank % T
+    # every rank creates every group, in the same order
+    tp_groups, pair_groups = {}, {}
+    if T > 1:
+        for im in range(images):
+            for br in range(2 if split else 1):
+                base = im * span + br * T
+                tp_groups[(im, br)] = dist.new_group(list(range(base, base + T)))
     if split:
-        # pairs of ranks (2p, 2p+1) share one image: rank 2p the conditional branch
-        if world % 2:
-            raise SystemExit("--parallel cfg needs an even number of GPUs")
-        if world == 1:
-            raise SystemExit("--parallel cfg needs --gpus >= 2")
+        for im in range(images):
+            for j in range(T):
+                pair_groups[(im, j)] = dist.new_group([im * span + j, im * span + T + j])
+    batch = 1 if split else 2
+    if T > 1:
+        from head_shard import HeadShardedFlowModel
+
+        model = HeadShardedFlowModel(weights, rank=tp_rank, tp=T, batch=batch, device=str(dev),
+                                     group=tp_groups[(image, branch)])
+    else:
+        model = FlowModelB200(weights, batch=batch, device=str(dev))
+    if split:
         from cfg_split import CfgSplitSampler
 
-        groups = [dist.new_group([2 * p, 2 * p + 1]) for p in range(world // 2)]
-        model = FlowModelB200(weights, batch=1, device=str(dev))
-        sampler = CfgSplitSampler(model, branch=rank % 2, group=groups[rank // 2],
+        # branch 0 (conditional) on the first T ranks of the image, branch 1 on the next T
+        sampler = CfgSplitSampler(model, branch=branch, group=pair_groups[(image, tp_rank)],
                                   steps=SAMPLER_STEPS, guidance=3.0, shift=3.0)
-        images, image = world // 2, rank // 2
     else:
-        model = FlowModelB200(weights, device=str(dev))
         sampler = CfgEulerSampler(model, steps=SAMPLER_STEPS, guidance=3.0, shift=3.0)
-        images, image = world, rank
 
     # per-image seeded inputs in pinned host memory (also the e2e source buffers)
     g = torch.Generator().manual_seed(1000 + image)
@@ -421,10 +455,11 @@ def main():
     ms_step = ms_total / args.steps
     value = ms_step / 1e3 * SAMPLER_STEPS / images
     e2e_value = e2e_ms / args.steps / 1e3 * SAMPLER_STEPS / images
-    flops = spec.flops_per_forward(batch=model.B)  # this GPU's share: the pair, or one branch
+    # this GPU's share: the pair, or one branch, and 1/T of the block work under --tp
+    flops = spec.flops_per_forward(batch=model.B, tp=T)
     peaks, peak_src = load_peaks()
     attn = prof["sdpa_attn"]
-    L, Mc, BH = spec.seq, spec.cond_tokens, model.B * spec.heads
+    L, Mc, BH = spec.seq, spec.cond_tokens, model.B * spec.heads // T
     attn_flops_per_step = spec.blocks * 4.0 * BH * L * (L + Mc) * spec.head_dim
     achieved = None
     if attn["launches"]:
@@ -472,9 +507,7 @@ def main():
                    "heads": spec.heads, "mlp": spec.mlp, "latent_tokens": spec.latent_tokens,
                    "seq": spec.seq, "cond_tokens": Mc, "sampler_steps": SAMPLER_STEPS,
                    "guidance": 3.0, "shift": 3.0, "global_batch": f"{images} image(s) x CFG pair",
-                   "parallelism": (f"cfg-split x{images} (each image's CFG pair on 2 GPUs, one NCCL "
-                                   "all-gather of the velocity per step)") if split else
-                                  f"replicas x{world} (one image per GPU, no data-path collective)",
+                   "parallelism": parallelism_label(split, T, images),
                    "launch": "host-issued kernels" if args.no_graph else "one CUDA graph per sampler step",
                    "l2": "no flush: every step streams 1.4 GB of NF24 weights and ~1 GB of "
                          "activations, far above the 126 MB L2"},

@@ -127,6 +127,14 @@ int triposplat_b200_gemm_nf24_split(const void* split, int M, int K, const int16
                                     const int8_t* q2_t, const float* scale, const float* bias,
                                     float* out, int N, int stride_out, int mode,
                                     const float* gate, int gate_ld, int rows_per_batch);
+/* No reference counterpart: triposplat_b200_gemm_nf24_split restricted to the output columns
+ * [start, start + count) of the N-column weight (out [M, count], stride_out per row): the
+ * column windows a tensor-parallel rank computes.  start, count multiples of 16. */
+int triposplat_b200_gemm_nf24_split_range(const void* split, int M, int K, const int16_t* code01_t,
+                                          const int8_t* q2_t, const float* scale, const float* bias,
+                                          float* out, int N, int start, int count, int stride_out,
+                                          int mode, const float* gate, int gate_ld,
+                                          int rows_per_batch);
 
 /* replaces scripts/gemm_nf24_i16_avx512.c:222-224 (rows per CTA tile here) */
 int triposplat_gemm_rnf8_avx512_row_tile(void);

@@ -946,6 +946,39 @@ int triposplat_b200_gemm_nf24_split(const void* split, int M, int K, const int16
                    current_stream());
 }
 
+// No reference counterpart: triposplat_b200_gemm_nf24_split restricted to the output
+// columns [start, start + count) of an N-column weight (out is [M, count], stride_out
+// elements per row) -- the column windows a tensor-parallel rank computes.  start and count
+// are multiples of 16 (the weights' TMA addressing).
+int triposplat_b200_gemm_nf24_split_range(const void* split, int M, int K, const int16_t* code01_t,
+                                          const int8_t* q2_t, const float* scale, const float* bias,
+                                          float* out, int N, int start, int count, int stride_out,
+                                          int mode, const float* gate, int gate_ld,
+                                          int rows_per_batch) {
+  using namespace tsb;
+  if (!split || !code01_t || !q2_t || !scale || !bias || !out) return kNullPointer;
+  if (M <= 0 || K <= 0 || N <= 0 || count <= 0 || start < 0 || stride_out < count || mode < 0 || mode > 3)
+    return kBadDims;
+  if (start + count > N) return kBadRange;
+  // the gate is indexed by the weight's column: each batch row holds N entries
+  if (mode == gemm::kGatedResidual && (!gate || gate_ld < N || rows_per_batch <= 0))
+    return kBadRange;
+  if ((N % 16) != 0 || (start % 16) != 0 || (count % 16) != 0 ||
+      ((reinterpret_cast<uintptr_t>(code01_t) | reinterpret_cast<uintptr_t>(q2_t) |
+        reinterpret_cast<uintptr_t>(split)) & 15) != 0)
+    return kBadAlignment;
+  int st = entry_check();
+  if (st != kOk) return st;
+  EpilogueArgs ep;
+  ep.mode = mode;
+  ep.gate = gate;
+  ep.gate_ld = gate_ld;
+  ep.rows_per_batch = rows_per_batch > 0 ? rows_per_batch : 1;
+  return launch_tc(split_layout(static_cast<uint8_t*>(const_cast<void*>(split)), M, K), code01_t,
+                   q2_t, scale, bias, out, N, start, count, stride_out, ep, device_status(),
+                   current_stream());
+}
+
 }  // extern "C"
 
 // ===========================================================================

@@ -80,18 +80,21 @@ class FlowSpec:
                     (p + "fc2", self.mlp, h)]
         return out
 
-    def flops_per_forward(self, batch: int = 2) -> dict[str, float]:
-        """Algorithmic flops of one forward (2*M*K*N per Linear, 4*Lq*Lk*64 per head)."""
+    def flops_per_forward(self, batch: int = 2, tp: int = 1) -> dict[str, float]:
+        """Algorithmic flops of one forward (2*M*K*N per Linear, 4*Lq*Lk*64 per head); with
+        tp > 1 one head-sharded rank's share (1/tp of the blocks, all of the rest)."""
         L, Mc = self.seq, self.cond_tokens
         gemm = 0.0
         for name, k, n in self.linears():
             rows = {"x_embedder": self.latent_tokens, "camera_embedder": 1, "t_fc1": 1, "t_fc2": 1,
                     "adaLN": 1, "final_adaLN": 1, "final_linear": self.latent_tokens,
                     "camera_head": 1, "cond_embedder": Mc, "cond_refiner": Mc}.get(name)
+            share = 1.0
             if rows is None:
                 rows = Mc if name.endswith("cross_kv") else L
-            gemm += 2.0 * batch * rows * k * n
-        sdpa = self.blocks * 4.0 * batch * self.heads * L * (L + Mc) * self.head_dim
+                share = 1.0 / tp
+            gemm += 2.0 * batch * rows * k * n * share
+        sdpa = self.blocks * 4.0 * batch * self.heads * L * (L + Mc) * self.head_dim / tp
         return {"gemm": gemm, "sdpa": sdpa, "total": gemm + sdpa}
 
 
@@ -209,8 +212,8 @@ class FlowModelB200:
         # split-format activation buffers for the fused path (LN/GELU/residual folded into
         # the GEMMs); 256-byte aligned as the library requires
         rows = B * L
-        for name, k in (("sp_h", h), ("sp_hid", s.mlp)):
-            nbytes = int(self.lib.triposplat_b200_split_bytes(rows, k))
+        for name, r, k in (("sp_h", rows, h), ("sp_hid", rows, s.mlp), ("sp_c", B * Mc, h)):
+            nbytes = int(self.lib.triposplat_b200_split_bytes(r, k))
             self.buf[name] = torch.empty(nbytes + 256, dtype=torch.uint8, device=device)
         # per-block adaLN tables, expanded over the batch so they add elementwise
         self.tables = {i: weights.params[f"blocks.{i}.table"][:, None, :].expand(6, B, h).contiguous()
@@ -251,8 +254,15 @@ class FlowModelB200:
     # -- forward -------------------------------------------------------------------------
     def forward(self, x_lat, cam, t1000, cond):
         """x_lat [B,Nl,Cl], cam [B,1,Cc], t1000 [B] (already x1000), cond [B,Mc,Dc]."""
+        self._embed(x_lat, cam, t1000, cond)
+        for i in range(self.spec.blocks):
+            self._block(i)
+        return self._final_layer()
+
+    def _embed(self, x_lat, cam, t1000, cond):
+        """Timestep / adaLN / condition / token embeddings into the block inputs."""
         s, b, lib = self.spec, self.buf, self.lib
-        B, L, h, H, Mc, Nl = self.B, s.seq, s.hidden, s.heads, s.cond_tokens, s.latent_tokens
+        B, h, Nl = self.B, s.hidden, s.latent_tokens
         _native.use_current_stream(lib)
         # timestep embedding -> temb -> adaLN modulation (shared) and final modulation
         self._ok(lib.triposplat_timestep_embedding_f32_avx512(
@@ -270,15 +280,18 @@ class FlowModelB200:
         self._lin("cond_embedder", cond, b["c0"])
         self._silu(b["c0"], b["c0"])
         self._lin("cond_refiner", b["c0"], b["c"])
+        if self.fused:  # every block's cross_kv GEMM reads the same split condition tokens
+            self._split(b["c"], self._split_ptr("sp_c"))
         # token embedding: [latent | camera]
         x = b["x"]
         for bb in range(B):  # per batch: the camera row sits between the batches' latents
             self._lin("x_embedder", x_lat[bb], x[bb, :Nl])
             self._lin("camera_embedder", cam[bb], x[bb, Nl:])
-        for i in range(s.blocks):
-            self._block(i)
-        # final layer
-        a = b["a"]
+
+    def _final_layer(self):
+        s, b = self.spec, self.buf
+        B, Nl = self.B, s.latent_tokens
+        x, a = b["x"], b["a"]
         self._ln(x, a)
         self._modulate(a, b["fmod"][1], b["fmod"][0])
         for bb in range(B):
@@ -342,7 +355,7 @@ class FlowModelB200:
         # cross-attention
         self._ln_split(x, sph)
         self._lin_split(p + "cross_q", sph, rows, y)
-        self._lin(p + "cross_kv", b["c"], b["ckv"])
+        self._lin_split(p + "cross_kv", self._split_ptr("sp_c"), B * Mc, b["ckv"])
         self._ok(lib.triposplat_b200_q_kv_rmsnorm_sdpa_f32(
             y.data_ptr(), b["ckv"].data_ptr(), prm[p + "cq_gamma"].data_ptr(),
             prm[p + "ck_gamma"].data_ptr(), b["o"].data_ptr(), B, L, Mc, H), "cross_attention")
