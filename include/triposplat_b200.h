@@ -136,6 +136,22 @@ int triposplat_b200_gemm_nf24_split_range(const void* split, int M, int K, const
                                           int mode, const float* gate, int gate_ld,
                                           int rows_per_batch);
 
+/* No reference counterpart: copies a weight's reference-layout code planes (code01_t int16
+ * [K, N], q2_t int8 [K, N]) into k-contiguous planes code01_nk int16 [N, K], q2_nk int8
+ * [N, K] for triposplat_b200_gemm_nf24_split_nk (once, at load). */
+int triposplat_b200_nf24_codes_to_nk(const int16_t* code01_t, const int8_t* q2_t, int K, int N,
+                                     int16_t* code01_nk, int8_t* q2_nk);
+
+/* No reference counterpart: triposplat_b200_gemm_nf24_split_range on k-contiguous planes.
+ * Row n holds output column n's K codes, rows ldk elements apart (ldk >= K; an offset
+ * pointer with ldk > K selects a window of input features).  16-byte aligned planes,
+ * ldk % 16 == 0.  Same modes and status codes as the split entry. */
+int triposplat_b200_gemm_nf24_split_nk(const void* split, int M, int K, const int16_t* code01_nk,
+                                       const int8_t* q2_nk, int ldk, const float* scale,
+                                       const float* bias, float* out, int N, int start, int count,
+                                       int stride_out, int mode, const float* gate, int gate_ld,
+                                       int rows_per_batch);
+
 /* replaces scripts/gemm_nf24_i16_avx512.c:222-224 (rows per CTA tile here) */
 int triposplat_gemm_rnf8_avx512_row_tile(void);
 /* replaces scripts/gemm_nf24_i16_avx512.c:226-228; returns 4 (= nf24_i16) */

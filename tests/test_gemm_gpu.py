@@ -192,3 +192,90 @@ def test_ln_modulate_split_then_gemm(oracle):
                                                N, N, 0, None, 0, 1) == 0
     torch.cuda.synchronize()
     _assert_close(out.cpu().numpy(), ref)
+
+
+def _to_nk(lib, c01_dev, q2_dev):
+    K, N = int(c01_dev.shape[0]), int(c01_dev.shape[1])
+    c_nk = torch.empty(N, K, dtype=torch.int16, device="cuda")
+    q_nk = torch.empty(N, K, dtype=torch.int8, device="cuda")
+    assert lib.triposplat_b200_nf24_codes_to_nk(c01_dev.data_ptr(), q2_dev.data_ptr(), K, N,
+                                                c_nk.data_ptr(), q_nk.data_ptr()) == 0
+    return c_nk, q_nk
+
+
+def test_codes_to_nk_is_a_transpose():
+    import _native
+
+    lib = _native.load()
+    _native.use_current_stream(lib)
+    g = torch.Generator().manual_seed(5)
+    K, N = 200, 72  # ragged against the 32 x 32 tiles
+    c01 = torch.randint(-636, 637, (K, N), generator=g, dtype=torch.int16)
+    q2 = torch.randint(-128, 128, (K, N), generator=g, dtype=torch.int8)
+    c_nk, q_nk = _to_nk(lib, c01.cuda(), q2.cuda())
+    torch.cuda.synchronize()
+    assert torch.equal(c_nk.cpu(), c01.T.contiguous()) and torch.equal(q_nk.cpu(), q2.T.contiguous())
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2, 3])
+def test_gemm_split_nk_bitwise_equals_reference_layout(mode):
+    """The k-contiguous code layout decodes the same operands in the same MMA order: the
+    result is bit-identical to the reference-layout kernel, for full weights, column
+    windows and input-feature windows (ldk > K).  Only the gated residual rounds once more
+    (its TMA reduce-add adds the rounded gate * y, where the other kernel fuses one FMA)."""
+    import _native
+
+    lib = _native.load()
+    _native.use_current_stream(lib)
+    g = torch.Generator().manual_seed(60 + mode)
+    B, L, K, N = 2, 300, 1024, 640
+    M = B * L
+    x = torch.randn(M, K, generator=g)
+    c01, q2, sc = _pack(torch.randn(N, K, generator=g) * 0.02)
+    w = [_cuda(a) for a in (c01, q2, sc, (torch.randn(N, generator=g) * 0.01).numpy())]
+    c_nk, q_nk = _to_nk(lib, w[0], w[1])
+    gate = torch.randn(B, N, generator=g).cuda()
+    base = torch.randn(M, N, generator=g).cuda()
+    for k0, kw, start, count in ((0, K, 0, N), (0, K, 128, 384), (256, 512, 0, N), (512, 256, 64, 320)):
+        keep, sp = _split_buf(lib, M, kw)
+        xc = x[:, k0:k0 + kw].contiguous().cuda()
+        assert lib.triposplat_b200_split_f32(xc.data_ptr(), M, kw, kw, sp) == 0
+        outs = []
+        for nk in (False, True):
+            out = base[:, start:start + count].contiguous()
+            if nk:
+                st = lib.triposplat_b200_gemm_nf24_split_nk(
+                    sp, M, kw, c_nk.data_ptr() + 2 * k0, q_nk.data_ptr() + k0, K,
+                    w[2].data_ptr(), w[3].data_ptr(), out.data_ptr(), N, start, count, count,
+                    mode, gate.data_ptr(), N, L)
+            else:
+                st = lib.triposplat_b200_gemm_nf24_split_range(
+                    sp, M, kw, w[0][k0:].data_ptr(), w[1][k0:].data_ptr(), w[2].data_ptr(),
+                    w[3].data_ptr(), out.data_ptr(), N, start, count, count, mode,
+                    gate.data_ptr(), N, L)
+            assert st == 0, (k0, kw, start, count, st)
+            outs.append(out)
+        torch.cuda.synchronize()
+        if mode == 2:
+            ref = base[:, start:start + count]
+            tol = 2.0 ** -23 * (ref.abs() + (outs[0] - ref).abs()) * 2
+            assert ((outs[0] - outs[1]).abs() <= tol).all(), (k0, kw, start, count)
+        else:
+            assert torch.equal(outs[0], outs[1]), (k0, kw, start, count,
+                                                   float((outs[0] - outs[1]).abs().max()))
+
+
+def test_gemm_split_nk_rejects_bad_arguments():
+    import _native
+
+    lib = _native.load()
+    t = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+    p = t.data_ptr()
+    f = lib.triposplat_b200_gemm_nf24_split_nk
+    assert f(None, 16, 64, p, p, 64, p, p, p, 64, 0, 64, 64, 0, None, 0, 1) == -1
+    assert f(p, 16, 64, p, p, 32, p, p, p, 64, 0, 64, 64, 0, None, 0, 1) == -3   # ldk < K
+    assert f(p, 16, 64, p, p, 64, p, p, p, 64, 16, 64, 64, 0, None, 0, 1) == -3  # past N
+    assert f(p, 16, 64, p, p, 72, p, p, p, 64, 0, 64, 64, 0, None, 0, 1) == -4   # ldk % 16
+    assert f(p, 16, 64, p + 8, p, 64, p, p, p, 64, 0, 64, 64, 0, None, 0, 1) == -4
+    assert f(p, 16, 64, p, p, 64, p, p, p + 4, 64, 0, 64, 64, 0, None, 0, 1) == -4  # out
+    assert f(p, 16, 64, p, p, 64, p, p, p, 64, 0, 62, 62, 0, None, 0, 1) == -4       # stride

@@ -48,6 +48,8 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "triposplat_b200_ln_modulate_split": ([VP, I, I, F, VP, VP, I, I, VP], I),
     "triposplat_b200_gemm_nf24_split": ([VP, I, I] + [VP] * 5 + [I, I, I, VP, I, I], I),
     "triposplat_b200_gemm_nf24_split_range": ([VP, I, I] + [VP] * 5 + [I] * 5 + [VP, I, I], I),
+    "triposplat_b200_nf24_codes_to_nk": ([VP, VP, I, I, VP, VP], I),
+    "triposplat_b200_gemm_nf24_split_nk": ([VP, I, I, VP, VP, I] + [VP] * 3 + [I] * 5 + [VP, I, I], I),
     # exact SDPA
     "triposplat_sdpa_f32_avx512_exact_q8t512": ([VP] * 5 + [I] * 8, I),
     "triposplat_sdpa_f32_avx512_exact_q8": ([VP] * 5 + [I] * 8, I),

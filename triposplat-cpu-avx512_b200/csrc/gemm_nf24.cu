@@ -8,15 +8,20 @@
 //    into two exact-sum fp16 planes X' = hi + lo after an exact per-row power-of-two
 //    pre-scale (undone in the epilogue), so fp16's range never clips and hi + lo carries
 //    ~22 significant bits.
-//  * W/256 = q01 + q2/256 is split into two fp16 operands that are EXACT for every code
-//    |q01| <= 1023 (the packer emits |q01| <= 636):
+//  * W/256 = q01 + q2/256 is first written as two exact fp16 values (any |q01| <= 1023;
+//    the packer emits |q01| <= 636):
 //        A1 = 2*floor(q01/2)          (even integer)
 //        A2 = (q01 & 1) + q2/256      (multiple of 1/256 in [-0.5, 1.5))
-//    Both are built from the raw codes with integer/bit operations and one HFMA2 each
-//    (magic-exponent construction), in registers, and written straight into tensor memory.
+//    built from the raw codes with integer/bit operations and one HFMA2 each (magic-
+//    exponent construction), then renormalised by Fast2Sum (Dekker 1971) in fp16 into
+//        S = fp16_rn(W/256),  T = W/256 - S  (exact, |T| <= 2^-11 |S|),
+//    in registers, and written straight into tensor memory.
 //  * The tcgen05 MMA computes the TRANSPOSED product D[n, m] = sum_k A[n, k] * X'[m, k]
 //    with A (weights) read from TMEM and X' (hi or lo plane, TMA-loaded with 128-B
-//    swizzle) from shared memory:  4 MMAs per k-step (A1.hi, A1.lo, A2.hi, A2.lo).
+//    swizzle) from shared memory:  3 MMAs per k-step (S.hi, S.lo, T.hi).  The omitted
+//    T.lo term is at most 2^-11 * 2^-11 = 2^-22 of |x w| per product: the same order as
+//    the hi + lo representation error of X itself (~2^-22), well under the reference's
+//    fp32 accumulation error over K.
 //  * Accuracy: the tensor core's fp32 accumulation truncates, so an error that grows
 //    linearly with the number of accumulation steps builds up in a long-lived accumulator
 //    (measured: rmse 1.8e-5 relative at K = 4096, 16x the fp32 reference).  Each k-block
@@ -69,6 +74,15 @@ constexpr int DEC_ARRIVALS = 4 + NUM_EPI_WARPS;  // warps decoding a share of ev
 constexpr int DEC_PAIRS = 20;
 constexpr int EPI_PAIRS = 6;
 static_assert(DEC_PAIRS + 2 * EPI_PAIRS == BK / 2, "decode shares cover the block");
+// the same split for the k-contiguous code layout, whose decode is cheaper
+#ifndef TSB_NK_DEC_PAIRS
+#define TSB_NK_DEC_PAIRS 32
+#endif
+constexpr int NK_DEC_PAIRS = TSB_NK_DEC_PAIRS;
+constexpr int NK_EPI_PAIRS = (BK / 2 - NK_DEC_PAIRS) / 2;
+static_assert(NK_DEC_PAIRS % 2 == 0 && NK_EPI_PAIRS % 2 == 0 &&
+              NK_DEC_PAIRS + 2 * NK_EPI_PAIRS == BK / 2, "k-contiguous decode shares");
+constexpr int NK_DEC_ARRIVALS = 4 + (NK_EPI_PAIRS ? NUM_EPI_WARPS : 0);
 constexpr int TMEM_COLS = 512;
 constexpr int ACC_COL = 0;        // 2 partial buffers x BM fp32 columns
 constexpr int A_COL = 2 * BM;     // AS stages x (32 cols A1 + 32 cols A2)
@@ -76,6 +90,18 @@ static_assert(A_COL + AS * 64 <= TMEM_COLS, "TMEM budget");
 constexpr int NUM_BARS = 2 * XS + 2 * CS + 2 * AS + 5;
 constexpr int SMEM_BYTES = 1024 /*align slack*/ + XS * X_STAGE + CS * C_STAGE +
                            NUM_EPI_WARPS * EPI_COLS * 4 + NUM_BARS * 8 + 16;
+// The k-contiguous kernel stores its outputs asynchronously: each epilogue warp writes
+// 12-row x 32-column chunks into a double-buffered shared-memory slot and one lane hands
+// them to the TMA (store, or reduce-add for the residual modes), so the tile-end store
+// overlaps the next tile's k-blocks.  Its two code stages leave room for the slots.
+constexpr int CS_NK = 2;
+constexpr int OUT_ROWS = 12;
+constexpr int OUT_CHUNK = OUT_ROWS * 32;                        // floats
+constexpr int OUT_STAGE_BYTES = NUM_EPI_WARPS * 2 * OUT_CHUNK * 4;  // 24 KB
+static_assert(EPI_COLS % OUT_ROWS == 0, "whole chunks per epilogue warp");
+constexpr int SMEM_BYTES_NK = 1024 + XS * X_STAGE + CS_NK * C_STAGE + OUT_STAGE_BYTES +
+                              NUM_EPI_WARPS * EPI_COLS * 4 + NUM_BARS * 8 + 16;
+static_assert(SMEM_BYTES_NK <= 232448, "shared memory per block");
 
 enum Epilogue : int { kStore = 0, kGelu = 1, kGatedResidual = 2, kResidual = 3 };
 
@@ -99,9 +125,21 @@ __device__ __forceinline__ float gelu_tanh(float x) {
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 
+// Round-to-nearest fp16x2 add / subtract (explicit .rn: never contracted with a multiply)
+__device__ __forceinline__ uint32_t hadd2_rn(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t hsub2_rn(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
 // Decode NP k pairs (k = 2*pair0 .. 2*(pair0+NP)-1) of weight column nl from a raw-code
-// stage into the exact fp16 operands A1 / A2 and store them to this warp's TMEM lanes
-// (A1 at column pair0, A2 at column 32 + pair0 of the stage).
+// stage into the fp16 operands S / T (S + T = W/256 exactly) and store them to this
+// warp's TMEM lanes (S at column pair0, T at column 32 + pair0 of the stage).
 template <int NP>
 __device__ __forceinline__ void decode_pairs(const uint8_t* cstage, int nl, int pair0, uint32_t ta) {
   // explicit shared-memory loads, all issued before the arithmetic (the stage pointer is
@@ -125,8 +163,12 @@ __device__ __forceinline__ void decode_pairs(const uint8_t* cstage, int nl, int 
     const uint32_t pc = __byte_perm(bb[2 * i], bb[2 * i + 1], 0x5410);
     const uint32_t f1 = ((pq >> 1) & 0x03FF03FFu) ^ 0x66006600u;
     const uint32_t f2 = (((pq << 8) & 0x01000100u) | pc) ^ 0x64806480u;
-    r1[i] = h2_bits(__hfma2(bits_h2(f1), two, m3072));
-    r2[i] = h2_bits(__hfma2(bits_h2(f2), inv256, m4p5));
+    const uint32_t a1 = h2_bits(__hfma2(bits_h2(f1), two, m3072));
+    const uint32_t a2 = h2_bits(__hfma2(bits_h2(f2), inv256, m4p5));
+    // Fast2Sum in fp16 (valid: a1 == 0 or |a1| >= 2 > |a2|): S = fp16_rn(W/256) and the
+    // exact remainder T = W/256 - S, |T| <= 2^-11 |S|
+    r1[i] = hadd2_rn(a1, a2);
+    r2[i] = hsub2_rn(a2, hsub2_rn(r1[i], a1));
   }
   // NP columns of A1 and of A2 (NP = 20 or 6: x16 + x4 or x4 + x2 stores)
   static_assert(NP == 20 || NP == 6, "decode share");
@@ -144,20 +186,104 @@ __device__ __forceinline__ void decode_pairs(const uint8_t* cstage, int nl, int 
   }
 }
 
+// Shared-memory loads of 1, 2 or 4 consecutive 32-bit words.
+template <int W>
+__device__ __forceinline__ void lds_words(uint32_t addr, uint32_t* d) {
+  if constexpr (W == 4)
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3]) : "r"(addr));
+  else if constexpr (W == 2)
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(d[0]), "=r"(d[1]) : "r"(addr));
+  else
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(d[0]) : "r"(addr));
+}
+
+// Words [W0, W0 + NW) of a swizzled row (row_addr: the row's first byte; 16-byte chunk c
+// of the row lives at chunk c ^ sw), loaded with the widest aligned accesses (unrolled at
+// compile time, so d stays in registers).
+template <int W0, int NW, int I = 0>
+__device__ __forceinline__ void lds_row_words(uint32_t row_addr, uint32_t sw, uint32_t* d) {
+  if constexpr (I < NW) {
+    constexpr int byte = 4 * (W0 + I);
+    constexpr int left = NW - I;
+    constexpr int in_chunk = (16 - (byte & 15)) / 4;
+    constexpr int W = ((byte & 15) == 0 && left >= 4) ? 4
+                      : (((byte & 7) == 0 && left >= 2 && in_chunk >= 2) ? 2 : 1);
+    const uint32_t addr = row_addr + (((uint32_t)(byte >> 4) ^ sw) << 4) + (byte & 15);
+    lds_words<W>(addr, d + I);
+    lds_row_words<W0, NW, I + W>(row_addr, sw, d);
+  }
+}
+
+// Words r[0, NW) to consecutive TMEM columns from t (this warp's lanes), in 16/8/4/2-wide
+// stores.
+template <int NW, int I = 0>
+__device__ __forceinline__ void tmem_st_run(uint32_t t, const uint32_t* r) {
+  if constexpr (NW - I >= 16) {
+    tmem_st16(t + I, *reinterpret_cast<const uint32_t(*)[16]>(r + I));
+    tmem_st_run<NW, I + 16>(t, r);
+  } else if constexpr (NW - I >= 8) {
+    tmem_st8(t + I, *reinterpret_cast<const uint32_t(*)[8]>(r + I));
+    tmem_st_run<NW, I + 8>(t, r);
+  } else if constexpr (NW - I >= 4) {
+    tmem_st4(t + I, r[I], r[I + 1], r[I + 2], r[I + 3]);
+    tmem_st_run<NW, I + 4>(t, r);
+  } else if constexpr (NW - I >= 2) {
+    tmem_st2(t + I, r[I], r[I + 1]);
+    tmem_st_run<NW, I + 2>(t, r);
+  }
+}
+
+// decode_pairs for the k-contiguous code layout ([N][K] planes, see nf24_codes_to_nk):
+// the stage holds row nl of the q01 tile as 128 B (64 k, TMA 128-B swizzle: chunk c at
+// c ^ (nl & 7)) and of the q2 tile as 64 B (64-B swizzle: chunk c at c ^ ((nl >> 1) & 3)),
+// so a thread reads its own column with 16-byte loads and a warp's load instruction covers
+// whole 128-byte bank rows.  Pairs [P0, P0 + NP) of the 64-k block.
+template <int P0, int NP>
+__device__ __forceinline__ void decode_pairs_nk(const uint8_t* cstage, int nl, uint32_t ta) {
+  static_assert(P0 % 2 == 0 && NP % 2 == 0, "q2 words hold two k pairs");
+  const uint32_t row16 = smem_u32(cstage) + nl * 128;
+  const uint32_t row8 = smem_u32(cstage) + C16_BYTES + nl * 64;
+  uint32_t pq[NP], pb[NP / 2];
+  lds_row_words<P0, NP>(row16, nl & 7, pq);            // q01: one word per k pair
+  lds_row_words<P0 / 2, NP / 2>(row8, (nl >> 1) & 3, pb);  // q2: one word per 4 k
+  const __half2 two = __floats2half2_rn(2.0f, 2.0f);
+  const __half2 m3072 = __floats2half2_rn(-3072.0f, -3072.0f);
+  const __half2 inv256 = __floats2half2_rn(1.0f / 256.0f, 1.0f / 256.0f);
+  const __half2 m4p5 = __floats2half2_rn(-4.5f, -4.5f);
+  uint32_t r1[NP], r2[NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const uint32_t pc = __byte_perm(pb[i >> 1], 0u, (i & 1) ? 0x4342 : 0x4140);
+    const uint32_t f1 = ((pq[i] >> 1) & 0x03FF03FFu) ^ 0x66006600u;
+    const uint32_t f2 = (((pq[i] << 8) & 0x01000100u) | pc) ^ 0x64806480u;
+    const uint32_t a1 = h2_bits(__hfma2(bits_h2(f1), two, m3072));
+    const uint32_t a2 = h2_bits(__hfma2(bits_h2(f2), inv256, m4p5));
+    r1[i] = hadd2_rn(a1, a2);
+    r2[i] = hsub2_rn(a2, hsub2_rn(r1[i], a1));
+  }
+  tmem_st_run<NP>(ta + P0, r1);
+  tmem_st_run<NP>(ta + 32 + P0, r2);
+}
+
 // 14 warps put four warps on some SM sub-partitions (16K registers each): 128 registers
 // per thread is the most that can launch.
-template <int MODE>
+template <int MODE, bool NK>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     nf24_gemm_tc(const __grid_constant__ CUtensorMap tm_xhi,
                  const __grid_constant__ CUtensorMap tm_xlo,
                  const __grid_constant__ CUtensorMap tm_c16,
-                 const __grid_constant__ CUtensorMap tm_c8, const Params p) {
+                 const __grid_constant__ CUtensorMap tm_c8,
+                 const __grid_constant__ CUtensorMap tm_out, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* xs = smem;
+  constexpr int kCS = NK ? CS_NK : CS;  // code stages
   uint8_t* cs = xs + XS * X_STAGE;
-  float* rs_s = reinterpret_cast<float*>(cs + CS * C_STAGE);  // [8 epilogue warps][96] row scales
+  float* ostage = reinterpret_cast<float*>(cs + kCS * C_STAGE);  // k-contiguous kernel only
+  // [8 epilogue warps][96] row scales
+  float* rs_s = reinterpret_cast<float*>(cs + kCS * C_STAGE + (NK ? OUT_STAGE_BYTES : 0));
   uint64_t* bars = reinterpret_cast<uint64_t*>(rs_s + NUM_EPI_WARPS * EPI_COLS);
   uint64_t* x_full = bars;
   uint64_t* x_empty = x_full + XS;
@@ -184,8 +310,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < XS; ++i) { mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], 1); }
-    for (int i = 0; i < CS; ++i) { mbar_init(&c_full[i], 1); mbar_init(&c_empty[i], DEC_ARRIVALS); }
-    for (int i = 0; i < AS; ++i) { mbar_init(&a_full[i], DEC_ARRIVALS); mbar_init(&a_empty[i], 1); }
+    constexpr int arrivals = NK ? NK_DEC_ARRIVALS : DEC_ARRIVALS;
+    for (int i = 0; i < kCS; ++i) { mbar_init(&c_full[i], 1); mbar_init(&c_empty[i], arrivals); }
+    for (int i = 0; i < AS; ++i) { mbar_init(&a_full[i], arrivals); mbar_init(&a_empty[i], 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_free[i], NUM_EPI_WARPS); }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -209,23 +336,28 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (elect_one()) {
-      int last_c[CS], last_x[XS];
-      for (int i = 0; i < CS; ++i) last_c[i] = -1;
+      int last_c[kCS], last_x[XS];
+      for (int i = 0; i < kCS; ++i) last_c[i] = -1;
       for (int i = 0; i < XS; ++i) last_x[i] = -1;
       bool ok = true;
       for (int g = 0; g < total_g && ok; ++g) {
         const int kb = g % kblocks, t = blockIdx.x + (g / kblocks) * gridDim.x;
         const int n0 = (t % n_tiles) * BN, m0 = (t / n_tiles) * BM;
-        const int c = g % CS, x = g % XS;
-        if (g >= CS &&
-            !mbar_wait(&c_empty[c], ((g / CS) & 1) ^ 1, p.status, kDevTimeoutProducer, abort_flag)) {
+        const int c = g % kCS, x = g % XS;
+        if (g >= kCS &&
+            !mbar_wait(&c_empty[c], ((g / kCS) & 1) ^ 1, p.status, kDevTimeoutProducer, abort_flag)) {
           ok = false;
           break;
         }
         uint8_t* cdst = cs + c * C_STAGE;
         mbar_arrive_expect_tx(&c_full[c], C_STAGE);
-        tma_load_2d(cdst, &tm_c16, &c_full[c], p.start + n0, kb * BK);
-        tma_load_2d(cdst + C16_BYTES, &tm_c8, &c_full[c], p.start + n0, kb * BK);
+        if constexpr (NK) {  // [N][K] planes: x = k
+          tma_load_2d(cdst, &tm_c16, &c_full[c], kb * BK, p.start + n0);
+          tma_load_2d(cdst + C16_BYTES, &tm_c8, &c_full[c], kb * BK, p.start + n0);
+        } else {             // [K][N] planes: x = n
+          tma_load_2d(cdst, &tm_c16, &c_full[c], p.start + n0, kb * BK);
+          tma_load_2d(cdst + C16_BYTES, &tm_c8, &c_full[c], p.start + n0, kb * BK);
+        }
         last_c[c] = g;
         if (g >= XS &&
             !mbar_wait(&x_empty[x], ((g / XS) & 1) ^ 1, p.status, kDevTimeoutProducer, abort_flag)) {
@@ -240,8 +372,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       if (*abort_flag) {
         // never leave the CTA while a bulk copy may still write its shared memory
-        for (int i = 0; i < CS; ++i)
-          if (last_c[i] >= 0) mbar_wait(&c_full[i], (last_c[i] / CS) & 1, p.status, kDevTimeoutProducer, nullptr);
+        for (int i = 0; i < kCS; ++i)
+          if (last_c[i] >= 0) mbar_wait(&c_full[i], (last_c[i] / kCS) & 1, p.status, kDevTimeoutProducer, nullptr);
         for (int i = 0; i < XS; ++i)
           if (last_x[i] >= 0) mbar_wait(&x_full[i], (last_x[i] / XS) & 1, p.status, kDevTimeoutProducer, nullptr);
       }
@@ -268,10 +400,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint64_t dlo = sw128_kmajor_desc(lo + kk * 32);
           const uint32_t a1 = a_col + kk * 8;
           const uint32_t a2 = a_col + 32 + kk * 8;
+          // S.hi + S.lo + T.hi; the dropped T.lo is below 2^-22 of |x w| per product
           mma_f16_ts(d, a1, dhi, idesc, kk != 0);  // fresh partial per k-block
           mma_f16_ts(d, a1, dlo, idesc, 1);
           mma_f16_ts(d, a2, dhi, idesc, 1);
-          mma_f16_ts(d, a2, dlo, idesc, 1);
         }
         mma_commit(&x_empty[x]);
         mma_commit(&a_empty[a]);
@@ -287,14 +419,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int nl = sub * 32 + lane;
     const uint32_t lane_base = (sub * 32) << 16;
     for (int g = 0; g < total_g; ++g) {
-      const int c = g % CS, a = g % AS;
-      bool ok = mbar_wait(&c_full[c], (g / CS) & 1, p.status, kDevTimeoutConsumer, abort_flag);
+      const int c = g % kCS, a = g % AS;
+      bool ok = mbar_wait(&c_full[c], (g / kCS) & 1, p.status, kDevTimeoutConsumer, abort_flag);
       if (ok && g >= AS)
         ok = mbar_wait(&a_empty[a], ((g / AS) & 1) ^ 1, p.status, kDevTimeoutConsumer, abort_flag);
       // the tcgen05 st below is warp-collective: leave the loop as a whole warp
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      decode_pairs<DEC_PAIRS>(cs + c * C_STAGE, nl, 0, tmem + lane_base + A_COL + a * 64);
+      if constexpr (NK)
+        decode_pairs_nk<0, NK_DEC_PAIRS>(cs + c * C_STAGE, nl, tmem + lane_base + A_COL + a * 64);
+      else
+        decode_pairs<DEC_PAIRS>(cs + c * C_STAGE, nl, 0, tmem + lane_base + A_COL + a * 64);
       __syncwarp();
       if (lane == 0) mbar_arrive(&c_empty[c]);
       tmem_wait_st();
@@ -312,10 +447,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // this warp's decode share of k-block kbd into A stage kbd % AS (free: either never
     // used, or the MMAs of block kbd - AS retired, which acc_full of that block tells)
     auto decode_share = [&](int kbd) -> bool {
-      const int c = kbd % CS;
-      const bool got = mbar_wait(&c_full[c], (kbd / CS) & 1, p.status, kDevTimeoutEpilogue, abort_flag);
+      if constexpr (NK && NK_EPI_PAIRS == 0) return true;  // the decoder warps do it all
+      const int c = kbd % kCS;
+      const bool got = mbar_wait(&c_full[c], (kbd / kCS) & 1, p.status, kDevTimeoutEpilogue, abort_flag);
       if (!__all_sync(0xffffffffu, got)) return false;
-      decode_pairs<EPI_PAIRS>(cs + c * C_STAGE, nl, pair0, tmem + lane_base + A_COL + (kbd % AS) * 64);
+      const uint32_t ta = tmem + lane_base + A_COL + (kbd % AS) * 64;
+      if constexpr (NK) {
+        if constexpr (NK_EPI_PAIRS > 0) {
+          if (half == 0)
+            decode_pairs_nk<NK_DEC_PAIRS, NK_EPI_PAIRS>(cs + c * C_STAGE, nl, ta);
+          else
+            decode_pairs_nk<NK_DEC_PAIRS + NK_EPI_PAIRS, NK_EPI_PAIRS>(cs + c * C_STAGE, nl, ta);
+        }
+      } else {
+        decode_pairs<EPI_PAIRS>(cs + c * C_STAGE, nl, pair0, ta);
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&c_empty[c]);
       tmem_wait_st();
@@ -367,7 +513,57 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_free[b]);
     }
-    if (ok) {
+    if constexpr (NK) {
+      if (ok) {
+        // asynchronous store: 12-row chunks through this warp's two shared-memory slots
+        const int nw0 = n0 + sub * 32;  // this warp's first column (relative to start)
+        const int nloc = n0 + nl;
+        const bool col_ok = nloc < p.count;
+        const int n = p.start + (col_ok ? nloc : 0);
+        const float sc = col_ok ? p.scale[n] * 256.0f : 0.0f;
+        const float bi = col_ok ? p.bias[n] : 0.0f;
+        const int mbase = m0 + half * EPI_COLS;
+#pragma unroll
+        for (int j = 0; j < EPI_COLS; ++j) sum[j] *= rsw[j];
+        float g0 = 1.0f, g1 = 1.0f;
+        int jb = EPI_COLS;
+        if constexpr (MODE == kGatedResidual) {
+          const int b0 = mbase / p.rows_per_batch;
+          jb = (b0 + 1) * p.rows_per_batch - mbase;
+          g0 = col_ok ? p.gate[(int64_t)b0 * p.gate_ld + n] : 0.0f;
+          g1 = (col_ok && jb < EPI_COLS && mbase + jb < p.M) ? p.gate[(int64_t)(b0 + 1) * p.gate_ld + n] : 0.0f;
+        }
+        float* wst = ostage + (warp - 6) * 2 * OUT_CHUNK;
+        if (nw0 < p.count) {
+#pragma unroll
+          for (int c = 0; c < EPI_COLS / OUT_ROWS; ++c) {
+            if (mbase + c * OUT_ROWS >= p.M) break;  // rows past M (warp-uniform)
+            float* buf = wst + (c & 1) * OUT_CHUNK;
+            // the slot's previous store (two chunks back, possibly of the previous tile)
+            // has finished reading it
+            if (lane == 0) bulk_wait_group_read<1>();
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < OUT_ROWS; ++j) {
+              const int r = c * OUT_ROWS + j;
+              float v = fmaf(sum[r], sc, bi);
+              if constexpr (MODE == kGelu) v = gelu_tanh(v);
+              if constexpr (MODE == kGatedResidual) v *= (r < jb ? g0 : g1);
+              buf[j * 32 + lane] = v;
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              if constexpr (MODE == kStore || MODE == kGelu)
+                tma_store_2d(&tm_out, buf, nw0, mbase + c * OUT_ROWS);
+              else
+                tma_reduce_add_2d(&tm_out, buf, nw0, mbase + c * OUT_ROWS);
+              bulk_commit_group();
+            }
+          }
+        }
+      }
+    } else if (ok) {
       const int nloc = n0 + nl;
       if (nloc < p.count) {
         const int n = p.start + nloc;
@@ -418,6 +614,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
     }
     }  // tile loop
+    // every asynchronous store complete before the CTA's shared memory goes away
+    if constexpr (NK) {
+      if (lane == 0) bulk_wait_group<0>();
+      __syncwarp();
+    }
   }
 
   tc_fence_before();
@@ -701,11 +902,39 @@ struct EpilogueArgs {
   int gate_ld = 0, rows_per_batch = 1;
 };
 
-// Tensor-core GEMM on already split activations.
+// [K][N] -> [N][K] for both code planes (one-time prepack of a weight into the
+// k-contiguous layout the NK decoder reads); 32 x 32 tiles through shared memory.
+__global__ void nf24_codes_to_nk_kernel(const int16_t* __restrict__ c01, const int8_t* __restrict__ q2,
+                                        int K, int N, int16_t* __restrict__ c01_nk,
+                                        int8_t* __restrict__ q2_nk) {
+  __shared__ int16_t t16[32][33];
+  __shared__ int8_t t8[32][36];
+  const int n0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  for (int j = ty; j < 32; j += 8) {
+    const int k = k0 + j, n = n0 + tx;
+    if (k < K && n < N) {
+      t16[j][tx] = c01[(size_t)k * N + n];
+      t8[j][tx] = q2[(size_t)k * N + n];
+    }
+  }
+  __syncthreads();
+  for (int j = ty; j < 32; j += 8) {
+    const int n = n0 + j, k = k0 + tx;
+    if (n < N && k < K) {
+      c01_nk[(size_t)n * K + k] = t16[tx][j];
+      q2_nk[(size_t)n * K + k] = t8[tx][j];
+    }
+  }
+}
+
+// Tensor-core GEMM on already split activations.  ldk == 0: the reference's [K][N] code
+// planes; ldk > 0: k-contiguous [N][K] planes (nf24_codes_to_nk) with rows ldk elements
+// apart (ldk > K for a window of input features).
 static int launch_tc(const SplitPlanes& sp, const int16_t* c01, const int8_t* q2,
                      const float* scale, const float* bias, float* out, int N, int start,
                      int count, int stride_out, const EpilogueArgs& ep, int* status,
-                     cudaStream_t stream) {
+                     cudaStream_t stream, int ldk = 0) {
   using namespace gemm;
   const int M = sp.M, K = sp.K;
   CUtensorMap m_hi, m_lo, m_c16, m_c8;
@@ -719,7 +948,8 @@ static int launch_tc(const SplitPlanes& sp, const int16_t* c01, const int8_t* q2
                      strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
       return kLaunchFailed;
   }
-  {
+  const bool nk = ldk > 0;
+  if (!nk) {
     const uint64_t dims[2] = {(uint64_t)N, (uint64_t)K};
     const uint64_t s16[1] = {(uint64_t)N * 2};
     const uint64_t s8[1] = {(uint64_t)N};
@@ -729,10 +959,32 @@ static int launch_tc(const SplitPlanes& sp, const int16_t* c01, const int8_t* q2
         !encode_tmap(&m_c8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(q2), dims, s8,
                      box, CU_TENSOR_MAP_SWIZZLE_NONE))
       return kLaunchFailed;
+  } else {
+    // rows of 64 k: 128 B of q01 (128-B swizzle), 64 B of q2 (64-B swizzle)
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)N};
+    const uint64_t s16[1] = {(uint64_t)ldk * 2};
+    const uint64_t s8[1] = {(uint64_t)ldk};
+    const uint32_t box[2] = {BK, BN};
+    if (!encode_tmap(&m_c16, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<int16_t*>(c01), dims,
+                     s16, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tmap(&m_c8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(q2), dims, s8,
+                     box, CU_TENSOR_MAP_SWIZZLE_64B))
+      return kLaunchFailed;
+  }
+  CUtensorMap m_out;  // k-contiguous kernel: the [M, count] output for its TMA stores
+  if (nk) {
+    const uint64_t dims[2] = {(uint64_t)count, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)stride_out * 4};
+    const uint32_t box[2] = {32, OUT_ROWS};
+    if (!encode_tmap(&m_out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, out, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_NONE))
+      return kLaunchFailed;
+  } else {
+    m_out = m_c8;  // unused
   }
   Params prm{sp.rs, scale, bias, out, M, K, N, start, count, stride_out,
              ep.mode, ep.gate, ep.gate_ld, ep.rows_per_batch, status};
-  static uint64_t attr_done[4] = {0, 0, 0, 0};  // per mode: one bit per device ordinal
+  static uint64_t attr_done[8] = {0};  // per kernel: one bit per device ordinal
   static int sm_count[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -744,19 +996,29 @@ static int launch_tc(const SplitPlanes& sp, const int16_t* c01, const int8_t* q2
   // one persistent CTA per SM (or one per tile when there are fewer tiles)
   const long long tiles = (long long)((count + BN - 1) / BN) * ((M + BM - 1) / BM);
   const dim3 grid((unsigned)(tiles < sm_count[dev & 63] ? tiles : sm_count[dev & 63]));
+  const int smem = nk ? SMEM_BYTES_NK : SMEM_BYTES;
   auto run = [&](auto kernel, int mode) {
     if (!(attr_done[mode] >> (dev & 63) & 1)) {
-      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       attr_done[mode] |= 1ull << (dev & 63);
     }
     LaunchScope scope(kKGemmTc, stream);
-    kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(m_hi, m_lo, m_c16, m_c8, prm);
+    kernel<<<grid, NUM_THREADS, smem, stream>>>(m_hi, m_lo, m_c16, m_c8, m_out, prm);
   };
-  switch (ep.mode) {
-    case kGelu: run(nf24_gemm_tc<kGelu>, kGelu); break;
-    case kGatedResidual: run(nf24_gemm_tc<kGatedResidual>, kGatedResidual); break;
-    case kResidual: run(nf24_gemm_tc<kResidual>, kResidual); break;
-    default: run(nf24_gemm_tc<kStore>, kStore); break;
+  if (nk) {
+    switch (ep.mode) {
+      case kGelu: run(nf24_gemm_tc<kGelu, true>, 4 + kGelu); break;
+      case kGatedResidual: run(nf24_gemm_tc<kGatedResidual, true>, 4 + kGatedResidual); break;
+      case kResidual: run(nf24_gemm_tc<kResidual, true>, 4 + kResidual); break;
+      default: run(nf24_gemm_tc<kStore, true>, 4 + kStore); break;
+    }
+  } else {
+    switch (ep.mode) {
+      case kGelu: run(nf24_gemm_tc<kGelu, false>, kGelu); break;
+      case kGatedResidual: run(nf24_gemm_tc<kGatedResidual, false>, kGatedResidual); break;
+      case kResidual: run(nf24_gemm_tc<kResidual, false>, kResidual); break;
+      default: run(nf24_gemm_tc<kStore, false>, kStore); break;
+    }
   }
   return launch_status();
 }
@@ -977,6 +1239,56 @@ int triposplat_b200_gemm_nf24_split_range(const void* split, int M, int K, const
   return launch_tc(split_layout(static_cast<uint8_t*>(const_cast<void*>(split)), M, K), code01_t,
                    q2_t, scale, bias, out, N, start, count, stride_out, ep, device_status(),
                    current_stream());
+}
+
+// No reference counterpart: copies a weight's reference-layout code planes (code01_t int16
+// [K, N], q2_t int8 [K, N]) into the k-contiguous planes code01_nk int16 [N, K] and
+// q2_nk int8 [N, K] read by triposplat_b200_gemm_nf24_split_nk (done once, at load).
+int triposplat_b200_nf24_codes_to_nk(const int16_t* code01_t, const int8_t* q2_t, int K, int N,
+                                     int16_t* code01_nk, int8_t* q2_nk) {
+  using namespace tsb;
+  if (!code01_t || !q2_t || !code01_nk || !q2_nk) return kNullPointer;
+  if (K <= 0 || N <= 0 || K / 32 >= 65535) return kBadDims;
+  int st = entry_check();
+  if (st != kOk) return st;
+  cudaStream_t stream = current_stream();
+  LaunchScope scope(kKElementwise, stream);
+  nf24_codes_to_nk_kernel<<<dim3((N + 31) / 32, (K + 31) / 32), dim3(32, 8), 0, stream>>>(
+      code01_t, q2_t, K, N, code01_nk, q2_nk);
+  return launch_status();
+}
+
+// No reference counterpart: triposplat_b200_gemm_nf24_split_range on k-contiguous code planes
+// (triposplat_b200_nf24_codes_to_nk).  Row n of the planes holds the K codes of output column
+// n, rows ldk elements apart (ldk >= K; ldk > K with the planes offset by k0 selects the input
+// features [k0, k0 + K) of a wider weight).  Plane pointers 16-byte aligned, ldk % 16 == 0.
+int triposplat_b200_gemm_nf24_split_nk(const void* split, int M, int K, const int16_t* code01_nk,
+                                       const int8_t* q2_nk, int ldk, const float* scale,
+                                       const float* bias, float* out, int N, int start, int count,
+                                       int stride_out, int mode, const float* gate, int gate_ld,
+                                       int rows_per_batch) {
+  using namespace tsb;
+  if (!split || !code01_nk || !q2_nk || !scale || !bias || !out) return kNullPointer;
+  if (M <= 0 || K <= 0 || N <= 0 || count <= 0 || start < 0 || stride_out < count || mode < 0 || mode > 3)
+    return kBadDims;
+  if (start + count > N || ldk < K) return kBadRange;
+  if (mode == gemm::kGatedResidual && (!gate || gate_ld < N || rows_per_batch <= 0))
+    return kBadRange;
+  // outputs leave through TMA stores: 16-byte aligned base and row stride
+  if ((ldk % 16) != 0 || (stride_out % 4) != 0 ||
+      ((reinterpret_cast<uintptr_t>(code01_nk) | reinterpret_cast<uintptr_t>(q2_nk) |
+        reinterpret_cast<uintptr_t>(split) | reinterpret_cast<uintptr_t>(out)) & 15) != 0)
+    return kBadAlignment;
+  int st = entry_check();
+  if (st != kOk) return st;
+  EpilogueArgs ep;
+  ep.mode = mode;
+  ep.gate = gate;
+  ep.gate_ld = gate_ld;
+  ep.rows_per_batch = rows_per_batch > 0 ? rows_per_batch : 1;
+  return launch_tc(split_layout(static_cast<uint8_t*>(const_cast<void*>(split)), M, K), code01_nk,
+                   q2_nk, scale, bias, out, N, start, count, stride_out, ep, device_status(),
+                   current_stream(), ldk);
 }
 
 }  // extern "C"

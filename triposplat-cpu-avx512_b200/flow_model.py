@@ -215,6 +215,21 @@ class FlowModelB200:
         for name, r, k in (("sp_h", rows, h), ("sp_hid", rows, s.mlp), ("sp_c", B * Mc, h)):
             nbytes = int(self.lib.triposplat_b200_split_bytes(r, k))
             self.buf[name] = torch.empty(nbytes + 256, dtype=torch.uint8, device=device)
+        # k-contiguous copies of the block Linears' code planes ([N][K], one-time device
+        # transpose) for the split-activation GEMMs of the fused path
+        self.nk = {}
+        if fused:
+            _native.use_current_stream(self.lib)
+            for name, lin in weights.linears.items():
+                if not name.startswith("blocks."):
+                    continue
+                K, N = (int(d) for d in lin.code01.shape)
+                c = torch.empty(N, K, dtype=torch.int16, device=device)
+                q = torch.empty(N, K, dtype=torch.int8, device=device)
+                self._ok(self.lib.triposplat_b200_nf24_codes_to_nk(
+                    lin.code01.data_ptr(), lin.q2.data_ptr(), K, N, c.data_ptr(), q.data_ptr()),
+                    f"codes_to_nk {name}")
+                self.nk[name] = (c, q)
         # per-block adaLN tables, expanded over the batch so they add elementwise
         self.tables = {i: weights.params[f"blocks.{i}.table"][:, None, :].expand(6, B, h).contiguous()
                        for i in range(s.blocks)}
@@ -305,10 +320,11 @@ class FlowModelB200:
 
     def _lin_split(self, name, split, rows, out, mode=0, gate=None, gate_ld=0, rows_per_batch=1):
         p = self.w.linears[name]
-        K, N = int(p.code01.shape[0]), int(p.code01.shape[1])
-        st = self.lib.triposplat_b200_gemm_nf24_split(
-            split, rows, K, p.code01.data_ptr(), p.q2.data_ptr(), p.scale.data_ptr(),
-            p.bias.data_ptr(), out.data_ptr(), N, N, mode,
+        c, q = self.nk[name]
+        N, K = int(c.shape[0]), int(c.shape[1])
+        st = self.lib.triposplat_b200_gemm_nf24_split_nk(
+            split, rows, K, c.data_ptr(), q.data_ptr(), K, p.scale.data_ptr(),
+            p.bias.data_ptr(), out.data_ptr(), N, 0, N, N, mode,
             None if gate is None else gate.data_ptr(), gate_ld, rows_per_batch)
         self._ok(st, f"gemm_split {name}")
 

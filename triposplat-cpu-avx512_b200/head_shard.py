@@ -6,10 +6,10 @@ by attention head and by MLP column.  With ``tp`` ranks each rank owns ``H / tp`
 and ``mlp / tp`` hidden columns:
 
 * qkv, cross_q, cross_kv, fc1: column windows of the NF24 weight (the rank's heads' q / k /
-  v columns, its MLP columns) through ``triposplat_b200_gemm_nf24_split_range``; the
+  v columns, its MLP columns) through ``triposplat_b200_gemm_nf24_split_nk``; the
   attention (RoPE + RMSNorm fused, self and cross) runs on the rank's heads only.
-* out, cross_out, fc2: row (K) windows of the weight -- the code planes offset by
-  ``k0 * N`` -- give a partial product over the rank's features; the bias is added on rank
+* out, cross_out, fc2: input-feature windows of the weight -- the k-contiguous code planes
+  offset by ``k0`` -- give a partial product over the rank's features; the bias is added on rank
   0 only, the partials are summed over the ranks by one all-reduce, and the (gated)
   residual add follows.
 * embedders, adaLN and the final layer are replicated, so every rank holds the same
@@ -90,21 +90,23 @@ class HeadShardedFlowModel(FlowModelB200):
     # -- GEMM windows ----------------------------------------------------------------------
     def _lin_cols(self, name, split, rows, out_ptr, start, count, stride_out, mode=0):
         p = self.w.linears[name]
-        K, N = int(p.code01.shape[0]), int(p.code01.shape[1])
-        self._ok(self.lib.triposplat_b200_gemm_nf24_split_range(
-            split, rows, K, p.code01.data_ptr(), p.q2.data_ptr(), p.scale.data_ptr(),
+        c, q = self.nk[name]
+        N, K = int(c.shape[0]), int(c.shape[1])
+        self._ok(self.lib.triposplat_b200_gemm_nf24_split_nk(
+            split, rows, K, c.data_ptr(), q.data_ptr(), K, p.scale.data_ptr(),
             p.bias.data_ptr(), out_ptr, N, start, count, stride_out, mode, None, 0, 1),
-            f"gemm_split_range {name}")
+            f"gemm columns {name}")
 
     def _lin_rows(self, name, split, rows, k0, count, out):
         """Partial product over input features [k0, k0 + count) into out [rows, N]."""
         p = self.w.linears[name]
-        N = int(p.code01.shape[1])
+        c, q = self.nk[name]
+        N, K = int(c.shape[0]), int(c.shape[1])
         bias = p.bias if self.rank == 0 else self.zero_bias
-        self._ok(self.lib.triposplat_b200_gemm_nf24_split(
-            split, rows, count, p.code01[k0:k0 + count].data_ptr(),
-            p.q2[k0:k0 + count].data_ptr(), p.scale.data_ptr(), bias.data_ptr(),
-            out.data_ptr(), N, N, 0, None, 0, 1), f"gemm_split rows {name}")
+        self._ok(self.lib.triposplat_b200_gemm_nf24_split_nk(
+            split, rows, count, c.data_ptr() + 2 * k0, q.data_ptr() + k0, K,
+            p.scale.data_ptr(), bias.data_ptr(), out.data_ptr(), N, 0, N, N, 0, None, 0, 1),
+            f"gemm rows {name}")
 
     def _nccl_all_reduce(self, t):
         import torch.distributed as dist
