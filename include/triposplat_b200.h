@@ -98,7 +98,8 @@ int triposplat_gemm_rnf8_avx512_tail(const float* x, const uint8_t* codes0_t,
  * device-wide synchronisation).  It calls no allocator: its scratch is a fixed 32 MiB
  * __device__ array per device, so it serves split activations of up to 32 MiB
  * (triposplat_b200_split_bytes(M, K); e.g. M <= 8184 at K = 1024), returns -6 beyond, and
- * -4 unless N % 16 == 0 with 16-byte aligned code planes.  All calls on a device share
+ * -4 unless N % 16 == 0 with 16-byte aligned code planes and output (stride_out % 4 == 0).
+ * All calls on a device share
  * the scratch: calls whose kernels may overlap on the GPU race, so order them on one
  * stream.  Nothing in the scratch needs to start at zero.  The first call on a device
  * resolves the scratch address; make it before capturing any stream. */
@@ -122,7 +123,8 @@ int triposplat_b200_ln_modulate_split(const float* x, int M, int C, float eps, c
                                       const float* scale, int mod_ld, int rows_per_batch,
                                       void* split);
 /* NF24 GEMM over a split buffer; mode 0 store, 1 GELU(tanh) store, 2 out += gate[b]*y
- * (gate [B, gate_ld], b = row / rows_per_batch), 3 out += y.  N % 16 == 0. */
+ * (gate [B, gate_ld], b = row / rows_per_batch), 3 out += y.  N % 16 == 0; out 16-byte
+ * aligned with stride_out % 4 == 0 (the outputs leave through TMA stores). */
 int triposplat_b200_gemm_nf24_split(const void* split, int M, int K, const int16_t* code01_t,
                                     const int8_t* q2_t, const float* scale, const float* bias,
                                     float* out, int N, int stride_out, int mode,

@@ -58,7 +58,7 @@ constexpr int BN = 128;  // weight columns per CTA = TMEM lanes = MMA M
 constexpr int BM = 192;  // tokens per CTA = MMA N
 constexpr int BK = 64;   // k per stage: one 128-B swizzle row of fp16
 constexpr int XS = 3;    // X stages (hi + lo planes)
-constexpr int CS = 3;    // raw-code stages
+constexpr int CS = 2;    // raw-code stages
 constexpr int AS = 2;    // decoded-weight stages in TMEM
 constexpr int X_PLANE = BM * BK * 2;       // 24 KB
 constexpr int X_STAGE = 2 * X_PLANE;       // 48 KB
@@ -75,10 +75,8 @@ constexpr int DEC_PAIRS = 20;
 constexpr int EPI_PAIRS = 6;
 static_assert(DEC_PAIRS + 2 * EPI_PAIRS == BK / 2, "decode shares cover the block");
 // the same split for the k-contiguous code layout, whose decode is cheaper
-#ifndef TSB_NK_DEC_PAIRS
-#define TSB_NK_DEC_PAIRS 32
-#endif
-constexpr int NK_DEC_PAIRS = TSB_NK_DEC_PAIRS;
+// (measured: the decoder warps alone keep up, so the epilogue warps only promote)
+constexpr int NK_DEC_PAIRS = 32;
 constexpr int NK_EPI_PAIRS = (BK / 2 - NK_DEC_PAIRS) / 2;
 static_assert(NK_DEC_PAIRS % 2 == 0 && NK_EPI_PAIRS % 2 == 0 &&
               NK_DEC_PAIRS + 2 * NK_EPI_PAIRS == BK / 2, "k-contiguous decode shares");
@@ -87,21 +85,19 @@ constexpr int TMEM_COLS = 512;
 constexpr int ACC_COL = 0;        // 2 partial buffers x BM fp32 columns
 constexpr int A_COL = 2 * BM;     // AS stages x (32 cols A1 + 32 cols A2)
 static_assert(A_COL + AS * 64 <= TMEM_COLS, "TMEM budget");
-constexpr int NUM_BARS = 2 * XS + 2 * CS + 2 * AS + 5;
-constexpr int SMEM_BYTES = 1024 /*align slack*/ + XS * X_STAGE + CS * C_STAGE +
-                           NUM_EPI_WARPS * EPI_COLS * 4 + NUM_BARS * 8 + 16;
-// The k-contiguous kernel stores its outputs asynchronously: each epilogue warp writes
-// 12-row x 32-column chunks into a double-buffered shared-memory slot and one lane hands
-// them to the TMA (store, or reduce-add for the residual modes), so the tile-end store
-// overlaps the next tile's k-blocks.  Its two code stages leave room for the slots.
-constexpr int CS_NK = 2;
+// Outputs leave asynchronously: each epilogue warp writes 12-row x 32-column chunks into a
+// double-buffered shared-memory slot and one lane hands them to the TMA (store, or
+// reduce-add for the residual modes), so the tile-end store overlaps the next tile's
+// k-blocks.  Two code stages leave room for the slots.
 constexpr int OUT_ROWS = 12;
-constexpr int OUT_CHUNK = OUT_ROWS * 32;                        // floats
+constexpr int OUT_CHUNK = OUT_ROWS * 32;                            // floats
 constexpr int OUT_STAGE_BYTES = NUM_EPI_WARPS * 2 * OUT_CHUNK * 4;  // 24 KB
 static_assert(EPI_COLS % OUT_ROWS == 0, "whole chunks per epilogue warp");
-constexpr int SMEM_BYTES_NK = 1024 + XS * X_STAGE + CS_NK * C_STAGE + OUT_STAGE_BYTES +
-                              NUM_EPI_WARPS * EPI_COLS * 4 + NUM_BARS * 8 + 16;
-static_assert(SMEM_BYTES_NK <= 232448, "shared memory per block");
+constexpr int NUM_BARS = 2 * XS + 2 * CS + 2 * AS + 5;
+constexpr int SMEM_BYTES = 1024 /*align slack*/ + XS * X_STAGE + CS * C_STAGE + OUT_STAGE_BYTES +
+                           NUM_EPI_WARPS * EPI_COLS * 4 + NUM_BARS * 8 + 16;
+static_assert(SMEM_BYTES <= 232448, "shared memory per block");
+
 
 enum Epilogue : int { kStore = 0, kGelu = 1, kGatedResidual = 2, kResidual = 3 };
 
@@ -240,7 +236,8 @@ __device__ __forceinline__ void tmem_st_run(uint32_t t, const uint32_t* r) {
 // so a thread reads its own column with 16-byte loads and a warp's load instruction covers
 // whole 128-byte bank rows.  Pairs [P0, P0 + NP) of the 64-k block.
 template <int P0, int NP>
-__device__ __forceinline__ void decode_pairs_nk(const uint8_t* cstage, int nl, uint32_t ta) {
+__device__ __forceinline__ void decode_pairs_nk_regs(const uint8_t* cstage, int nl, uint32_t (&r1)[NP],
+                                                     uint32_t (&r2)[NP]) {
   static_assert(P0 % 2 == 0 && NP % 2 == 0, "q2 words hold two k pairs");
   const uint32_t row16 = smem_u32(cstage) + nl * 128;
   const uint32_t row8 = smem_u32(cstage) + C16_BYTES + nl * 64;
@@ -251,7 +248,6 @@ __device__ __forceinline__ void decode_pairs_nk(const uint8_t* cstage, int nl, u
   const __half2 m3072 = __floats2half2_rn(-3072.0f, -3072.0f);
   const __half2 inv256 = __floats2half2_rn(1.0f / 256.0f, 1.0f / 256.0f);
   const __half2 m4p5 = __floats2half2_rn(-4.5f, -4.5f);
-  uint32_t r1[NP], r2[NP];
 #pragma unroll
   for (int i = 0; i < NP; ++i) {
     const uint32_t pc = __byte_perm(pb[i >> 1], 0u, (i & 1) ? 0x4342 : 0x4140);
@@ -262,6 +258,12 @@ __device__ __forceinline__ void decode_pairs_nk(const uint8_t* cstage, int nl, u
     r1[i] = hadd2_rn(a1, a2);
     r2[i] = hsub2_rn(a2, hsub2_rn(r1[i], a1));
   }
+}
+
+template <int P0, int NP>
+__device__ __forceinline__ void decode_pairs_nk(const uint8_t* cstage, int nl, uint32_t ta) {
+  uint32_t r1[NP], r2[NP];
+  decode_pairs_nk_regs<P0, NP>(cstage, nl, r1, r2);
   tmem_st_run<NP>(ta + P0, r1);
   tmem_st_run<NP>(ta + 32 + P0, r2);
 }
@@ -279,11 +281,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* xs = smem;
-  constexpr int kCS = NK ? CS_NK : CS;  // code stages
+  constexpr int kCS = CS;  // code stages
   uint8_t* cs = xs + XS * X_STAGE;
-  float* ostage = reinterpret_cast<float*>(cs + kCS * C_STAGE);  // k-contiguous kernel only
+  float* ostage = reinterpret_cast<float*>(cs + kCS * C_STAGE);  // output staging slots
   // [8 epilogue warps][96] row scales
-  float* rs_s = reinterpret_cast<float*>(cs + kCS * C_STAGE + (NK ? OUT_STAGE_BYTES : 0));
+  float* rs_s = reinterpret_cast<float*>(cs + kCS * C_STAGE + OUT_STAGE_BYTES);
   uint64_t* bars = reinterpret_cast<uint64_t*>(rs_s + NUM_EPI_WARPS * EPI_COLS);
   uint64_t* x_full = bars;
   uint64_t* x_empty = x_full + XS;
@@ -421,17 +423,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int g = 0; g < total_g; ++g) {
       const int c = g % kCS, a = g % AS;
       bool ok = mbar_wait(&c_full[c], (g / kCS) & 1, p.status, kDevTimeoutConsumer, abort_flag);
-      if (ok && g >= AS)
-        ok = mbar_wait(&a_empty[a], ((g / AS) & 1) ^ 1, p.status, kDevTimeoutConsumer, abort_flag);
-      // the tcgen05 st below is warp-collective: leave the loop as a whole warp
-      if (!__all_sync(0xffffffffu, ok)) break;
-      tc_fence_after();
-      if constexpr (NK)
-        decode_pairs_nk<0, NK_DEC_PAIRS>(cs + c * C_STAGE, nl, tmem + lane_base + A_COL + a * 64);
-      else
+      if constexpr (NK) {
+        // decode into registers as soon as the codes land; only the TMEM store waits for
+        // the stage's previous MMAs, so the decode stays off the MMA's critical path
+        if (!__all_sync(0xffffffffu, ok)) break;
+        uint32_t r1[NK_DEC_PAIRS], r2[NK_DEC_PAIRS];
+        decode_pairs_nk_regs<0, NK_DEC_PAIRS>(cs + c * C_STAGE, nl, r1, r2);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&c_empty[c]);
+        if (g >= AS)
+          ok = mbar_wait(&a_empty[a], ((g / AS) & 1) ^ 1, p.status, kDevTimeoutConsumer, abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) break;
+        tc_fence_after();
+        const uint32_t ta = tmem + lane_base + A_COL + a * 64;
+        tmem_st_run<NK_DEC_PAIRS>(ta, r1);
+        tmem_st_run<NK_DEC_PAIRS>(ta + 32, r2);
+      } else {
+        if (ok && g >= AS)
+          ok = mbar_wait(&a_empty[a], ((g / AS) & 1) ^ 1, p.status, kDevTimeoutConsumer, abort_flag);
+        // the tcgen05 st below is warp-collective: leave the loop as a whole warp
+        if (!__all_sync(0xffffffffu, ok)) break;
+        tc_fence_after();
         decode_pairs<DEC_PAIRS>(cs + c * C_STAGE, nl, 0, tmem + lane_base + A_COL + a * 64);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&c_empty[c]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&c_empty[c]);
+      }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -513,8 +529,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_free[b]);
     }
-    if constexpr (NK) {
-      if (ok) {
+    if (ok) {
         // asynchronous store: 12-row chunks through this warp's two shared-memory slots
         const int nw0 = n0 + sub * 32;  // this warp's first column (relative to start)
         const int nloc = n0 + nl;
@@ -563,62 +578,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         }
       }
-    } else if (ok) {
-      const int nloc = n0 + nl;
-      if (nloc < p.count) {
-        const int n = p.start + nloc;
-        const float sc = p.scale[n] * 256.0f;
-        const float bi = p.bias[n];
-        float* out_col = p.out + nloc;
-        const int mbase = m0 + half * EPI_COLS;
-        const int rows = p.M - mbase;  // rows of this half that exist
-        // fold the row pre-scale into the sums, then one fully unrolled loop per mode so
-        // sum[] stays in registers
-#pragma unroll
-        for (int j = 0; j < EPI_COLS; ++j) sum[j] *= rsw[j];
-        if constexpr (MODE == kStore) {
-#pragma unroll
-          for (int j = 0; j < EPI_COLS; ++j)
-            if (j < rows) out_col[(int64_t)(mbase + j) * p.stride_out] = fmaf(sum[j], sc, bi);
-        } else if constexpr (MODE == kGelu) {
-#pragma unroll
-          for (int j = 0; j < EPI_COLS; ++j)
-            if (j < rows) out_col[(int64_t)(mbase + j) * p.stride_out] = gelu_tanh(fmaf(sum[j], sc, bi));
-        } else {
-          // residual modes: batch 8 independent loads of the old values before the
-          // dependent stores so the read latency is paid once per batch, not per row
-          float g0 = 1.0f, g1 = 1.0f;
-          int jb = EPI_COLS;
-          if constexpr (MODE == kGatedResidual) {
-            // at most one batch boundary falls inside these 96 rows
-            const int b0 = mbase / p.rows_per_batch;
-            jb = (b0 + 1) * p.rows_per_batch - mbase;
-            g0 = p.gate[(int64_t)b0 * p.gate_ld + n];
-            g1 = jb < rows ? p.gate[(int64_t)(b0 + 1) * p.gate_ld + n] : 0.0f;
-          }
-#pragma unroll
-          for (int j0 = 0; j0 < EPI_COLS; j0 += 8) {
-            float prev[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-              prev[u] = (j0 + u < rows) ? out_col[(int64_t)(mbase + j0 + u) * p.stride_out] : 0.0f;
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const int j = j0 + u;
-              if (j < rows)
-                out_col[(int64_t)(mbase + j) * p.stride_out] =
-                    fmaf(j < jb ? g0 : g1, fmaf(sum[j], sc, bi), prev[u]);
-            }
-          }
-        }
-      }
-    }
     }  // tile loop
     // every asynchronous store complete before the CTA's shared memory goes away
-    if constexpr (NK) {
-      if (lane == 0) bulk_wait_group<0>();
-      __syncwarp();
-    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -971,16 +934,14 @@ static int launch_tc(const SplitPlanes& sp, const int16_t* c01, const int8_t* q2
                      box, CU_TENSOR_MAP_SWIZZLE_64B))
       return kLaunchFailed;
   }
-  CUtensorMap m_out;  // k-contiguous kernel: the [M, count] output for its TMA stores
-  if (nk) {
+  CUtensorMap m_out;  // the [M, count] output, for the epilogue's TMA stores
+  {
     const uint64_t dims[2] = {(uint64_t)count, (uint64_t)M};
     const uint64_t strides[1] = {(uint64_t)stride_out * 4};
     const uint32_t box[2] = {32, OUT_ROWS};
     if (!encode_tmap(&m_out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, out, dims, strides, box,
                      CU_TENSOR_MAP_SWIZZLE_NONE))
       return kLaunchFailed;
-  } else {
-    m_out = m_c8;  // unused
   }
   Params prm{sp.rs, scale, bias, out, M, K, N, start, count, stride_out,
              ep.mode, ep.gate, ep.gate_ld, ep.rows_per_batch, status};
@@ -996,7 +957,7 @@ static int launch_tc(const SplitPlanes& sp, const int16_t* c01, const int8_t* q2
   // one persistent CTA per SM (or one per tile when there are fewer tiles)
   const long long tiles = (long long)((count + BN - 1) / BN) * ((M + BM - 1) / BM);
   const dim3 grid((unsigned)(tiles < sm_count[dev & 63] ? tiles : sm_count[dev & 63]));
-  const int smem = nk ? SMEM_BYTES_NK : SMEM_BYTES;
+  const int smem = SMEM_BYTES;
   auto run = [&](auto kernel, int mode) {
     if (!(attr_done[mode] >> (dev & 63) & 1)) {
       cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -1034,7 +995,10 @@ static int gemm_launch(const float* x, const int16_t* c01, const int8_t* q2, con
       !is_device_pointer(scale) || !is_device_pointer(bias) || !is_device_pointer(out))
     return kNotDevicePointer;
   cudaStream_t stream = current_stream();
-  const bool aligned = ((reinterpret_cast<uintptr_t>(c01) | reinterpret_cast<uintptr_t>(q2)) & 15) == 0;
+  // the tensor-core kernel reads the code planes and writes `out` through TMA: 16-byte
+  // aligned bases and row strides
+  const bool aligned = ((reinterpret_cast<uintptr_t>(c01) | reinterpret_cast<uintptr_t>(q2) |
+                         reinterpret_cast<uintptr_t>(out)) & 15) == 0 && (stride_out % 4) == 0;
   const bool tc = allow_tc && (N % 16 == 0) && (start % 16 == 0) && aligned;
   if (!tc) {
     dim3 grid((count + 127) / 128, M);
@@ -1193,8 +1157,9 @@ int triposplat_b200_gemm_nf24_split(const void* split, int M, int K, const int16
   if (M <= 0 || K <= 0 || N <= 0 || stride_out < N || mode < 0 || mode > 3) return kBadDims;
   if (mode == gemm::kGatedResidual && (!gate || gate_ld < N || rows_per_batch <= 0))
     return kBadRange;
-  if ((N % 16) != 0 || ((reinterpret_cast<uintptr_t>(code01_t) | reinterpret_cast<uintptr_t>(q2_t) |
-                         reinterpret_cast<uintptr_t>(split)) & 15) != 0)
+  if ((N % 16) != 0 || (stride_out % 4) != 0 ||
+      ((reinterpret_cast<uintptr_t>(code01_t) | reinterpret_cast<uintptr_t>(q2_t) |
+        reinterpret_cast<uintptr_t>(split) | reinterpret_cast<uintptr_t>(out)) & 15) != 0)
     return kBadAlignment;
   int st = entry_check();
   if (st != kOk) return st;
@@ -1225,9 +1190,9 @@ int triposplat_b200_gemm_nf24_split_range(const void* split, int M, int K, const
   // the gate is indexed by the weight's column: each batch row holds N entries
   if (mode == gemm::kGatedResidual && (!gate || gate_ld < N || rows_per_batch <= 0))
     return kBadRange;
-  if ((N % 16) != 0 || (start % 16) != 0 || (count % 16) != 0 ||
+  if ((N % 16) != 0 || (start % 16) != 0 || (count % 16) != 0 || (stride_out % 4) != 0 ||
       ((reinterpret_cast<uintptr_t>(code01_t) | reinterpret_cast<uintptr_t>(q2_t) |
-        reinterpret_cast<uintptr_t>(split)) & 15) != 0)
+        reinterpret_cast<uintptr_t>(split) | reinterpret_cast<uintptr_t>(out)) & 15) != 0)
     return kBadAlignment;
   int st = entry_check();
   if (st != kOk) return st;
@@ -1371,8 +1336,9 @@ int triposplat_gemm_nf24_noalloc(const float* x, const uint8_t* codes0_t, const 
   if (stride_x < K || stride_out < N) return kBadRange;
   const int16_t* c01 = reinterpret_cast<const int16_t*>(codes0_t);
   const int8_t* q2 = reinterpret_cast<const int8_t*>(codes1_t);
-  if ((N % 16) != 0 ||
-      ((reinterpret_cast<uintptr_t>(c01) | reinterpret_cast<uintptr_t>(q2)) & 15) != 0)
+  if ((N % 16) != 0 || (stride_out % 4) != 0 ||
+      ((reinterpret_cast<uintptr_t>(c01) | reinterpret_cast<uintptr_t>(q2) |
+        reinterpret_cast<uintptr_t>(out)) & 15) != 0)
     return kBadAlignment;
   if (split_bytes(M, K) > kNoAllocScratchBytes) return -6;
   int st = entry_check_no_alloc();
