@@ -234,6 +234,17 @@ int triposplat_cfg_combine_inplace_f32_avx512(float* positive, const float* nega
 int triposplat_euler_update_inplace_f32_avx512(float* sample, const float* prediction,
                                                const float* dt, int batch,
                                                int64_t elements_per_batch, int threads);
+/* scripts/native_sampler_avx512.c:91-130: Adams-Bashforth-2 step
+ * x -= dt*((1+r)*v - r*v_prev), r = 0.5*dt/max(dt_prev, 1e-12), per batch entry. */
+int triposplat_ab2_update_inplace_f32_avx512(float* sample, const float* prediction,
+                                             const float* previous_prediction, const float* dt,
+                                             const float* previous_dt, int batch,
+                                             int64_t elements_per_batch, int threads);
+/* No reference counterpart: CFG combine + Euler step in one kernel, bit-identical to the
+ * two reference calls in sequence (positive is not overwritten). */
+int triposplat_b200_cfg_euler_update_f32(float* sample, const float* positive,
+                                         const float* negative, const float* guidance,
+                                         const float* dt, int batch, int64_t elements_per_batch);
 /* replaces scripts/native_qkv_postprocess_v2_avx512.c:45-105 */
 int triposplat_qkv_rope_rmsnorm_pack_f32_avx512_v2(const float* qkv, const float* frequencies,
                                                    const float* q_gamma, const float* k_gamma,
@@ -251,6 +262,23 @@ int triposplat_q_kv_selected_rope_rmsnorm_pack_f32_avx512_v2(
 int triposplat_timestep_embedding_f32_avx512(const float* timesteps, const float* frequencies,
                                              float* output, int batch, int half_dim,
                                              int output_dim, int threads);
+/* scripts/native_embeddings_avx512.c:58-95: per row and axis [sin | cos] of x*f(*2)*pi over
+ * frequency_dim frequencies, zero padding to channels; -1 null, -2 bad sizes. */
+int triposplat_pcd_position_embedding_f32_avx512(const float* positions, const float* frequencies,
+                                                 float* output, int64_t rows, int input_dims,
+                                                 int frequency_dim, int channels, int double_pi,
+                                                 int threads);
+/* scripts/native_repo_avx512.c:69-83: lhs *= rhs; -1 null, -2 elements <= 0. */
+int triposplat_mul_inplace_f32_avx512(float* lhs, const float* rhs, int64_t elements, int threads);
+/* scripts/native_repo_avx512.c:85-129: RePo phasors, interleaved complex (cos, sin) of
+ * (x*tanh_f + x*residual_f)*pi per vector and axis; -1 delta/output null, -2 a frequency
+ * array null, -3 bad sizes. */
+int triposplat_repo_phasor_f32_avx512(const float* delta, const float* freq_tanh_0,
+                                      const float* freq_residual_0, int freq_dim_0,
+                                      const float* freq_tanh_1, const float* freq_residual_1,
+                                      int freq_dim_1, const float* freq_tanh_2,
+                                      const float* freq_residual_2, int freq_dim_2,
+                                      float* output_interleaved, int64_t vectors, int threads);
 /* No reference counterpart: the selected-query post-process without RoPE or an index list
  * (cross-attention: condition tokens carry no position).  q [B,Lq,H,64], kv [B,Lk,2,H,64]
  * -> q_bhld [B,H,Lq,64], packed k/v [B,H,64,Lk_padded]; k and q get 8/max(||x||,1e-12)*gamma. */

@@ -343,3 +343,145 @@ int oracle_qkv_rope_rmsnorm_pack(const float* qkv, const float* freqs,
     }
   return 0;
 }
+
+/* ---------------------------------------------------------------------------
+ * Position / timestep embeddings and the RePo phasor
+ * (scripts/native_embeddings_avx512.c:12-125, scripts/native_repo_avx512.c:12-129)
+ * ------------------------------------------------------------------------- */
+
+/* sin and cos of x by the reference's own method (native_embeddings_avx512.c:12-56,
+   identical in native_repo_avx512.c:12-56): q = x * 2/pi rounded to the nearest integer
+   (ties to even; out of int32 range -> INT32_MIN, the AVX-512 conversion's indefinite
+   value), r = x - q*pi/2 in two fused steps with pi/2 split into a high and a low part,
+   Taylor polynomials in z = r^2 for sin (to r^13) and cos (to r^14) by Horner with fused
+   multiply-adds, then the quadrant q & 3 selects and negates the pair. */
+static void ref_sincos(float x, float* s_out, float* c_out) {
+  const float inv_pio2 = 0.63661977236758134308f;
+  const float pio2_hi = 1.57079625129699707031f;
+  const float pio2_lo = 7.54978941586159635335e-8f;
+  const float t = x * inv_pio2;
+  const int32_t q = (fabsf(t) < 2147483648.0f) ? (int32_t)lrintf(t) : INT32_MIN;
+  const float qf = (float)q;
+  float r = fmaf(-qf, pio2_hi, x);
+  r = fmaf(-qf, pio2_lo, r);
+  const float z = r * r;
+  float sp = -1.0f / 6227020800.0f;
+  sp = fmaf(sp, z, 1.0f / 39916800.0f);
+  sp = fmaf(sp, z, -1.0f / 362880.0f);
+  sp = fmaf(sp, z, 1.0f / 5040.0f);
+  sp = fmaf(sp, z, -1.0f / 120.0f);
+  sp = fmaf(sp, z, 1.0f / 6.0f);
+  const float sin_r = r - (r * z) * sp;
+  float cp = -1.0f / 87178291200.0f;
+  cp = fmaf(cp, z, 1.0f / 479001600.0f);
+  cp = fmaf(cp, z, -1.0f / 3628800.0f);
+  cp = fmaf(cp, z, 1.0f / 40320.0f);
+  cp = fmaf(cp, z, -1.0f / 720.0f);
+  cp = fmaf(cp, z, 1.0f / 24.0f);
+  cp = fmaf(cp, z, -0.5f);
+  const float cos_r = fmaf(cp, z, 1.0f);
+  float s = sin_r, c = cos_r;
+  switch (q & 3) {
+    case 1: s = cos_r; c = -sin_r; break;
+    case 2: s = -sin_r; c = -cos_r; break;
+    case 3: s = -cos_r; c = sin_r; break;
+    default: break;
+  }
+  *s_out = s;
+  *c_out = c;
+}
+
+/* output[sample] = [cos(t f_0..f_{H-1}) | sin(t f_0..) | 0 ...]
+   (native_embeddings_avx512.c:97-125) */
+int oracle_timestep_embedding(const float* timesteps, const float* frequencies, float* output,
+                              int batch, int half_dim, int output_dim) {
+  if (!timesteps || !frequencies || !output) return -1;
+  if (batch <= 0 || half_dim <= 0 || output_dim < half_dim * 2) return -2;
+  for (int b = 0; b < batch; ++b) {
+    float* cos_dst = output + (int64_t)b * output_dim;
+    float* sin_dst = cos_dst + half_dim;
+    for (int i = 0; i < half_dim; ++i) ref_sincos(timesteps[b] * frequencies[i], sin_dst + i, cos_dst + i);
+    for (int i = 2 * half_dim; i < output_dim; ++i) cos_dst[i] = 0.0f;
+  }
+  return 0;
+}
+
+/* per row and axis: [sin(a_0..a_{F-1}) | cos(a_0..)] with a = x f (x 2 if double_pi) x pi,
+   zero padding to `channels` (native_embeddings_avx512.c:58-95) */
+int oracle_pcd_position_embedding(const float* positions, const float* frequencies, float* output,
+                                  int64_t rows, int input_dims, int frequency_dim, int channels,
+                                  int double_pi) {
+  if (!positions || !frequencies || !output) return -1;
+  if (rows <= 0 || input_dims <= 0 || frequency_dim <= 0 || channels < input_dims * frequency_dim * 2)
+    return -2;
+  const float pi = 3.14159274101257324219f;
+  for (int64_t r = 0; r < rows; ++r) {
+    float* dst = output + r * (int64_t)channels;
+    for (int a = 0; a < input_dims; ++a) {
+      const float x = positions[r * input_dims + a];
+      float* sin_dst = dst + a * (2 * frequency_dim);
+      float* cos_dst = sin_dst + frequency_dim;
+      for (int i = 0; i < frequency_dim; ++i) {
+        float angle = x * frequencies[i];
+        if (double_pi) angle = angle + angle;
+        angle = angle * pi;
+        ref_sincos(angle, sin_dst + i, cos_dst + i);
+      }
+    }
+    for (int i = input_dims * frequency_dim * 2; i < channels; ++i) dst[i] = 0.0f;
+  }
+  return 0;
+}
+
+/* lhs *= rhs elementwise (native_repo_avx512.c:69-83) */
+int oracle_mul_inplace(float* lhs, const float* rhs, int64_t n) {
+  if (!lhs || !rhs) return -1;
+  if (n <= 0) return -2;
+  for (int64_t i = 0; i < n; ++i) lhs[i] = lhs[i] * rhs[i];
+  return 0;
+}
+
+/* RePo rotary phasors: per vector v and axis a (3 axes, dims d_a), for each frequency
+   angle = (x ft + x fr) pi with x = delta[v, a], written as interleaved complex
+   (cos, sin) along the concatenated axes (native_repo_avx512.c:85-129) */
+int oracle_repo_phasor(const float* delta, const float* ft0, const float* fr0, int d0,
+                       const float* ft1, const float* fr1, int d1, const float* ft2,
+                       const float* fr2, int d2, float* out, int64_t vectors) {
+  if (!delta || !out) return -1;
+  if (!ft0 || !fr0 || !ft1 || !fr1 || !ft2 || !fr2) return -2;
+  if (vectors <= 0 || d0 <= 0 || d1 <= 0 || d2 <= 0) return -3;
+  const float* ft[3] = {ft0, ft1, ft2};
+  const float* fr[3] = {fr0, fr1, fr2};
+  const int dims[3] = {d0, d1, d2};
+  const int total = d0 + d1 + d2;
+  const float pi = 3.14159274101257324219f;
+  for (int64_t v = 0; v < vectors; ++v) {
+    float* dst = out + v * (int64_t)(2 * total);
+    int k = 0;
+    for (int a = 0; a < 3; ++a) {
+      const float x = delta[v * 3 + a];
+      for (int i = 0; i < dims[a]; ++i, ++k) {
+        const float angle = (x * ft[a][i] + x * fr[a][i]) * pi;
+        ref_sincos(angle, dst + 2 * k + 1, dst + 2 * k);
+      }
+    }
+  }
+  return 0;
+}
+
+/* Adams-Bashforth-2 sampler step (scripts/native_sampler_avx512.c:91-130):
+   x -= dt * ((1 + r) * v - r * v_prev), r = 0.5 * (dt / max(dt_prev, 1e-12)) */
+int oracle_ab2_update_inplace(float* sample, const float* pred, const float* prev, const float* dt,
+                              const float* prev_dt, int batch, int64_t per_batch) {
+  if (!sample || !pred || !prev || !dt || !prev_dt) return -1;
+  if (batch <= 0 || per_batch <= 0) return -2;
+  for (int b = 0; b < batch; ++b) {
+    const float r = 0.5f * (dt[b] / fmaxf(prev_dt[b], 1.0e-12f));
+    const float cur_scale = 1.0f + r;
+    for (int64_t i = (int64_t)b * per_batch; i < (int64_t)(b + 1) * per_batch; ++i) {
+      const float eff = cur_scale * pred[i] - r * prev[i];
+      sample[i] = sample[i] - dt[b] * eff;
+    }
+  }
+  return 0;
+}

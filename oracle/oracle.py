@@ -51,6 +51,11 @@ class Oracle:
             "oracle_cfg_combine_inplace": ([_VP] * 3 + [_I, _I64]),
             "oracle_euler_update_inplace": ([_VP] * 3 + [_I, _I64]),
             "oracle_qkv_rope_rmsnorm_pack": ([_VP] * 7 + [_I] * 5),
+            "oracle_timestep_embedding": ([_VP] * 3 + [_I] * 3),
+            "oracle_pcd_position_embedding": ([_VP] * 3 + [_I64] + [_I] * 4),
+            "oracle_mul_inplace": ([_VP] * 2 + [_I64]),
+            "oracle_ab2_update_inplace": ([_VP] * 5 + [_I, _I64]),
+            "oracle_repo_phasor": ([_VP, _VP, _VP, _I, _VP, _VP, _I, _VP, _VP, _I, _VP, _I64]),
         }
         for name, args in sig.items():
             fn = getattr(lib, name)
@@ -166,6 +171,51 @@ class Oracle:
             _p(sample), _p(_f32(pred)), _p(_f32(dt)), B, sample.size // B),
             "oracle_euler_update_inplace")
         return sample
+
+    def timestep_embedding(self, t, freqs, output_dim=None):
+        """[batch] timesteps, [half] frequencies -> [batch, output_dim] = [cos | sin | 0]."""
+        t, f = _f32(t), _f32(freqs)
+        half = f.shape[0]
+        output_dim = 2 * half if output_dim is None else output_dim
+        out = np.empty((t.shape[0], output_dim), np.float32)
+        self._check(self.lib.oracle_timestep_embedding(_p(t), _p(f), _p(out), t.shape[0], half,
+                                                       output_dim), "oracle_timestep_embedding")
+        return out
+
+    def pcd_position_embedding(self, positions, freqs, channels, double_pi=False):
+        """positions [rows, dims], freqs [F] -> [rows, channels] = per axis [sin | cos], 0 pad."""
+        x, f = _f32(positions), _f32(freqs)
+        out = np.empty((x.shape[0], channels), np.float32)
+        self._check(self.lib.oracle_pcd_position_embedding(
+            _p(x), _p(f), _p(out), x.shape[0], x.shape[1], f.shape[0], channels, int(double_pi)),
+            "oracle_pcd_position_embedding")
+        return out
+
+    def ab2_update(self, sample, pred, prev, dt, prev_dt):
+        """[batch, n] sample / predictions, dt and prev_dt [batch] -> updated sample."""
+        out = _f32(sample).copy()
+        b = out.shape[0]
+        self._check(self.lib.oracle_ab2_update_inplace(
+            _p(out), _p(_f32(pred)), _p(_f32(prev)), _p(_f32(dt)), _p(_f32(prev_dt)), b,
+            out.size // b), "oracle_ab2_update_inplace")
+        return out
+
+    def mul(self, lhs, rhs):
+        out = _f32(lhs).copy()
+        self._check(self.lib.oracle_mul_inplace(_p(out), _p(_f32(rhs)), out.size), "oracle_mul_inplace")
+        return out
+
+    def repo_phasor(self, delta, ft, fr):
+        """delta [vectors, 3]; ft / fr: three per-axis arrays -> [vectors, 2 * sum(dims)]
+        interleaved (cos, sin)."""
+        d = _f32(delta)
+        ft, fr = [_f32(a) for a in ft], [_f32(a) for a in fr]
+        dims = [a.shape[0] for a in ft]
+        out = np.empty((d.shape[0], 2 * sum(dims)), np.float32)
+        self._check(self.lib.oracle_repo_phasor(
+            _p(d), _p(ft[0]), _p(fr[0]), dims[0], _p(ft[1]), _p(fr[1]), dims[1],
+            _p(ft[2]), _p(fr[2]), dims[2], _p(out), d.shape[0]), "oracle_repo_phasor")
+        return out
 
     def qkv_rope_rmsnorm_pack(self, qkv, freqs, q_gamma, k_gamma, Lp=None):
         qkv = _f32(qkv)

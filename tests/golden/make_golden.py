@@ -213,10 +213,75 @@ def elementwise_cases(torch):
     np.savez_compressed(HERE / "elementwise.npz", **data)
 
 
+def embedding_cases(torch):
+    """Timestep / point-cloud position embeddings (scripts/native_embeddings_avx512.c:58-125),
+    the RePo phasor and feature multiply (scripts/native_repo_avx512.c:69-129).  Angles span
+    small, large (|x| ~ 1e3..1e4 rad, where the two-constant range reduction is coarse) and
+    negative values, so a restatement must follow the reference's sin/cos method exactly."""
+    emb = ctypes.CDLL(str(REF_LIBS / "libref_embeddings.so"))
+    rep = ctypes.CDLL(str(REF_LIBS / "libref_repo.so"))
+    ts = bind(emb, "triposplat_timestep_embedding_f32_avx512", [VP] * 3 + [I] * 4)
+    pcd = bind(emb, "triposplat_pcd_position_embedding_f32_avx512", [VP] * 3 + [I64] + [I] * 5)
+    mul = bind(rep, "triposplat_mul_inplace_f32_avx512", [VP] * 2 + [I64, I])
+    pha = bind(rep, "triposplat_repo_phasor_f32_avx512",
+               [VP, VP, VP, I, VP, VP, I, VP, VP, I, VP, I64, I])
+    g = torch.Generator(device="cpu").manual_seed(2)
+
+    def rn(*shape, s=1.0):
+        return (torch.randn(shape, generator=g) * s).numpy().astype(np.float32)
+
+    data = {}
+    # timestep embedding: 1000*t over the sampler's range, frequencies exp(-ln(1e4) i / half)
+    half = 128
+    t = np.array([999.0, 731.25, 0.5, 0.0, -3.0], np.float32)
+    f = torch.exp(-float(np.log(10000)) * torch.arange(0, half, dtype=torch.float32) / half).numpy()
+    out = np.full((5, 2 * half + 4), 7.0, np.float32)
+    check(ts(ptr(t), ptr(f), ptr(out), 5, half, 2 * half + 4, 2), "timestep")
+    data.update(ts_t=t, ts_f=f, ts_out=out)
+    # point-cloud positions: 3 axes, 20 frequencies (not a multiple of 16), padded channels
+    pos = rn(37, 3, s=2.0)
+    pf = (2.0 ** np.linspace(0, 9, 20)).astype(np.float32)
+    for dp in (0, 1):
+        o = np.full((37, 128), 7.0, np.float32)
+        check(pcd(ptr(pos), ptr(pf), ptr(o), 37, 3, 20, 128, dp, 2), "pcd")
+        data[f"pcd_out{dp}"] = o
+    data.update(pcd_pos=pos, pcd_f=pf)
+    # RePo: delta [vectors, 3]; per-axis frequencies split as tanh(f) + (f - tanh(f))
+    for name, dims in (("a", (10, 11, 11)), ("b", (20, 3, 17))):
+        fr = [torch.randn(d, generator=g) * 3.0 for d in dims]
+        fts = [x.tanh().contiguous() for x in fr]
+        frs = [(x - y).contiguous() for x, y in zip(fr, fts)]
+        fts = [x.numpy().astype(np.float32) for x in fts]
+        frs = [x.numpy().astype(np.float32) for x in frs]
+        delta = rn(53, 3, s=40.0)
+        o = np.full((53, 2 * sum(dims)), 7.0, np.float32)
+        check(pha(ptr(delta), ptr(fts[0]), ptr(frs[0]), dims[0], ptr(fts[1]), ptr(frs[1]), dims[1],
+                  ptr(fts[2]), ptr(frs[2]), dims[2], ptr(o), 53, 2), "phasor")
+        data.update({f"repo_{name}_delta": delta, f"repo_{name}_out": o,
+                     f"repo_{name}_dims": np.array(dims, np.int32)})
+        for a in range(3):
+            data[f"repo_{name}_ft{a}"], data[f"repo_{name}_fr{a}"] = fts[a], frs[a]
+    smp = ctypes.CDLL(str(REF_LIBS / "libref_sampler.so"))
+    ab2 = bind(smp, "triposplat_ab2_update_inplace_f32_avx512", [VP] * 5 + [I, I64, I])
+    x, v, vp = rn(2, 333), rn(2, 333), rn(2, 333)
+    dt, pdt = np.array([0.05, 0.031], np.float32), np.array([0.07, 0.0], np.float32)
+    xo = x.copy()
+    check(ab2(ptr(xo), ptr(v), ptr(vp), ptr(dt), ptr(pdt), 2, 333, 2), "ab2")
+    data.update(ab2_x=x, ab2_v=v, ab2_vp=vp, ab2_dt=dt, ab2_pdt=pdt, ab2_out=xo)
+    lhs, rhs = rn(1001), rn(1001)
+    prod = lhs.copy()
+    check(mul(ptr(prod), ptr(rhs), 1001, 2), "mul")
+    data.update(mul_lhs=lhs, mul_rhs=rhs, mul_out=prod)
+    np.savez_compressed(HERE / "embeddings.npz", **data)
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
+    ap.add_argument("--cases", default="gemm,sdpa,elementwise,embeddings",
+                    help="comma-separated subset of the fixture groups to (re)write")
     args = ap.parse_args()
+    cases = set(args.cases.split(","))
     sys.path.insert(0, str(args.reference / "scripts"))
     import torch
     from native_linear_nf8_avx512_patch import make_nf8_codebook  # reference packer
@@ -227,11 +292,16 @@ def main() -> int:
         return [codes[0], codes[1]], scales, err
 
     codebook = make_nf8_codebook(torch)
-    np.save(HERE / "nf8_codebook.npy", codebook.numpy())
-    gemm_cases(torch, pack, codebook, ctypes.CDLL(str(REF_LIBS / "libref_gemm_nf24_i16.so")))
-    sdpa_cases(torch, ctypes.CDLL(str(REF_LIBS / "libref_sdpa_q8t512.so")),
-               ctypes.CDLL(str(REF_LIBS / "libref_sdpa_q8t512_packed.so")))
-    elementwise_cases(torch)
+    if "gemm" in cases:
+        np.save(HERE / "nf8_codebook.npy", codebook.numpy())
+        gemm_cases(torch, pack, codebook, ctypes.CDLL(str(REF_LIBS / "libref_gemm_nf24_i16.so")))
+    if "sdpa" in cases:
+        sdpa_cases(torch, ctypes.CDLL(str(REF_LIBS / "libref_sdpa_q8t512.so")),
+                   ctypes.CDLL(str(REF_LIBS / "libref_sdpa_q8t512_packed.so")))
+    if "elementwise" in cases:
+        elementwise_cases(torch)
+    if "embeddings" in cases:
+        embedding_cases(torch)
     print("golden fixtures written to", HERE)
     return 0
 

@@ -59,3 +59,23 @@ def test_oracle_error_codes(oracle):
     s = np.zeros(16, np.float32)
     with pytest.raises(RuntimeError):
         oracle.gemm_nf24(x, c, q, s, s, start=8, count=16)  # range overflow -> -3
+
+
+def test_embeddings_oracle_bit_exact(oracle, golden):
+    """The oracle's restatement of the reference's sin / cos method reproduces the reference
+    kernels bit for bit (timestep and point-cloud position embeddings, RePo phasor, feature
+    multiply), including angles of 1e3..1e4 rad where the range reduction is coarse."""
+    g = golden("embeddings")
+    out = oracle.timestep_embedding(g["ts_t"], g["ts_f"], output_dim=g["ts_out"].shape[1])
+    np.testing.assert_array_equal(out, g["ts_out"])
+    for dp in (0, 1):
+        out = oracle.pcd_position_embedding(g["pcd_pos"], g["pcd_f"], g[f"pcd_out{dp}"].shape[1],
+                                            double_pi=bool(dp))
+        np.testing.assert_array_equal(out, g[f"pcd_out{dp}"])
+    for name in ("a", "b"):
+        out = oracle.repo_phasor(g[f"repo_{name}_delta"], [g[f"repo_{name}_ft{a}"] for a in range(3)],
+                                 [g[f"repo_{name}_fr{a}"] for a in range(3)])
+        np.testing.assert_array_equal(out, g[f"repo_{name}_out"])
+    np.testing.assert_array_equal(oracle.mul(g["mul_lhs"], g["mul_rhs"]), g["mul_out"])
+    np.testing.assert_array_equal(
+        oracle.ab2_update(g["ab2_x"], g["ab2_v"], g["ab2_vp"], g["ab2_dt"], g["ab2_pdt"]), g["ab2_out"])

@@ -74,12 +74,17 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "triposplat_add_inplace_f32_avx512": ([VP] * 2 + [I64, I], I),
     "triposplat_cfg_combine_inplace_f32_avx512": ([VP] * 3 + [I, I64, I], I),
     "triposplat_euler_update_inplace_f32_avx512": ([VP] * 3 + [I, I64, I], I),
+    "triposplat_ab2_update_inplace_f32_avx512": ([VP] * 5 + [I, I64, I], I),
+    "triposplat_b200_cfg_euler_update_f32": ([VP] * 5 + [I, I64], I),
     "triposplat_qkv_rope_rmsnorm_pack_f32_avx512_v2": ([VP] * 7 + [I] * 7, I),
     "triposplat_q_kv_selected_rope_rmsnorm_pack_f32_avx512_v2": ([VP] * 9 + [I] * 8, I),
     "triposplat_b200_q_kv_rmsnorm_pack_f32": ([VP] * 7 + [I] * 5, I),
     "triposplat_b200_qkv_rope_rmsnorm_sdpa_f32": ([VP] * 5 + [I] * 5, I),
     "triposplat_b200_q_kv_rmsnorm_sdpa_f32": ([VP] * 5 + [I] * 4, I),
     "triposplat_timestep_embedding_f32_avx512": ([VP] * 3 + [I] * 4, I),
+    "triposplat_pcd_position_embedding_f32_avx512": ([VP] * 3 + [I64] + [I] * 5, I),
+    "triposplat_mul_inplace_f32_avx512": ([VP, VP, I64, I], I),
+    "triposplat_repo_phasor_f32_avx512": ([VP, VP, VP, I, VP, VP, I, VP, VP, I, VP, I64, I], I),
 }
 
 

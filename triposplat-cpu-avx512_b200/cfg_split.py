@@ -89,10 +89,9 @@ class CfgSplitSampler:
     def update_phase(self):
         lib = self.model.lib
         _native.use_current_stream(lib)
-        st = lib.triposplat_cfg_combine_inplace_f32_avx512(
-            self.recv[0].data_ptr(), self.recv[1].data_ptr(), self.g.data_ptr(), 1, self.n, 0)
-        st = st or lib.triposplat_euler_update_inplace_f32_avx512(
-            self.x.data_ptr(), self.recv[0].data_ptr(), self.dt_cur.data_ptr(), 1, self.n, 0)
+        st = lib.triposplat_b200_cfg_euler_update_f32(
+            self.x.data_ptr(), self.recv[0].data_ptr(), self.recv[1].data_ptr(), self.g.data_ptr(),
+            self.dt_cur.data_ptr(), 1, self.n)
         if st:
             raise RuntimeError(f"sampler update returned status {st}")
 
@@ -132,5 +131,5 @@ class CfgSplitSampler:
         self.prepare_capture()
         return self.record_graph()
 
-    # kernels launched per step outside the graph (combine + Euler update)
-    eager_launches_per_step = 2
+    # kernels launched per step outside the graph (the fused CFG combine + Euler update)
+    eager_launches_per_step = 1

@@ -10,6 +10,8 @@
 // vector, and grids sized in multiples of the SM count.  Pointers are device pointers.
 #include <cuda_fp16.h>
 
+#include <climits>
+
 #include "common.cuh"
 #include "runtime.h"
 
@@ -132,7 +134,8 @@ __global__ void cfg_k(float* __restrict__ pos, const float* __restrict__ neg,
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const float gb = g[i / per_batch];
-    pos[i] = gb * pos[i] - (gb - 1.0f) * neg[i];
+    // g*pos - (g-1)*neg with the reference's three roundings (no contraction)
+    pos[i] = __fsub_rn(__fmul_rn(gb, pos[i]), __fmul_rn(__fsub_rn(gb, 1.0f), neg[i]));
   }
 }
 
@@ -140,7 +143,36 @@ __global__ void euler_k(float* __restrict__ x, const float* __restrict__ v,
                         const float* __restrict__ dt, int64_t per_batch, int64_t n) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
-    x[i] = x[i] - dt[i / per_batch] * v[i];
+    x[i] = __fsub_rn(x[i], __fmul_rn(dt[i / per_batch], v[i]));
+}
+
+// x -= dt * ((1 + r) * v - r * v_prev), r = 0.5 * dt / max(dt_prev, 1e-12), each product and
+// difference rounded separately (scripts/native_sampler_avx512.c:91-130)
+__global__ void ab2_k(float* __restrict__ x, const float* __restrict__ v,
+                      const float* __restrict__ v_prev, const float* __restrict__ dt,
+                      const float* __restrict__ dt_prev, int64_t per_batch, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = i / per_batch;
+    const float half_ratio = __fmul_rn(0.5f, __fdiv_rn(dt[b], fmaxf(dt_prev[b], 1.0e-12f)));
+    const float cur_scale = __fadd_rn(1.0f, half_ratio);
+    const float eff = __fsub_rn(__fmul_rn(cur_scale, v[i]), __fmul_rn(half_ratio, v_prev[i]));
+    x[i] = __fsub_rn(x[i], __fmul_rn(dt[b], eff));
+  }
+}
+
+// CFG combine then Euler step in one pass: x -= dt * (g*pos - (g-1)*neg), rounded exactly as
+// the two reference kernels in sequence; `positive` is left unchanged.
+__global__ void cfg_euler_k(float* __restrict__ x, const float* __restrict__ pos,
+                            const float* __restrict__ neg, const float* __restrict__ g,
+                            const float* __restrict__ dt, int64_t per_batch, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = i / per_batch;
+    const float gb = g[b];
+    const float v = __fsub_rn(__fmul_rn(gb, pos[i]), __fmul_rn(__fsub_rn(gb, 1.0f), neg[i]));
+    x[i] = __fsub_rn(x[i], __fmul_rn(dt[b], v));
+  }
 }
 
 // One CTA per (bh, 64-token tile).  Q rows go straight to [B,H,L,64]; K and V are
@@ -214,6 +246,43 @@ __global__ void __launch_bounds__(256) qkv_post_k(
   }
 }
 
+// sin and cos of x by the reference's own method (scripts/native_embeddings_avx512.c:12-56,
+// the same in scripts/native_repo_avx512.c:12-56), operation for operation so results are
+// bit-identical: q = x * 2/pi rounded to the nearest integer (ties to even; out of int32
+// range or NaN -> INT_MIN, the AVX-512 conversion's indefinite value), r = x - q * pi/2 in
+// two fused steps with pi/2 split into high and low parts, Taylor polynomials in z = r^2
+// for sin (to r^13) and cos (to r^14) by Horner with fused multiply-adds, and the quadrant
+// q & 3 selecting / negating the pair.  Explicit _rn intrinsics keep the compiler from
+// contracting the separate multiplies and adds.
+__device__ __forceinline__ void ref_sincos(float x, float& s_out, float& c_out) {
+  const float t = __fmul_rn(x, 0.63661977236758134308f);
+  const int q = fabsf(t) < 2147483648.0f ? __float2int_rn(t) : INT_MIN;
+  const float qf = __int2float_rn(q);
+  float r = __fmaf_rn(-qf, 1.57079625129699707031f, x);
+  r = __fmaf_rn(-qf, 7.54978941586159635335e-8f, r);
+  const float z = __fmul_rn(r, r);
+  float sp = -1.0f / 6227020800.0f;
+  sp = __fmaf_rn(sp, z, 1.0f / 39916800.0f);
+  sp = __fmaf_rn(sp, z, -1.0f / 362880.0f);
+  sp = __fmaf_rn(sp, z, 1.0f / 5040.0f);
+  sp = __fmaf_rn(sp, z, -1.0f / 120.0f);
+  sp = __fmaf_rn(sp, z, 1.0f / 6.0f);
+  const float sin_r = __fsub_rn(r, __fmul_rn(__fmul_rn(r, z), sp));
+  float cp = -1.0f / 87178291200.0f;
+  cp = __fmaf_rn(cp, z, 1.0f / 479001600.0f);
+  cp = __fmaf_rn(cp, z, -1.0f / 3628800.0f);
+  cp = __fmaf_rn(cp, z, 1.0f / 40320.0f);
+  cp = __fmaf_rn(cp, z, -1.0f / 720.0f);
+  cp = __fmaf_rn(cp, z, 1.0f / 24.0f);
+  cp = __fmaf_rn(cp, z, -0.5f);
+  const float cos_r = __fmaf_rn(cp, z, 1.0f);
+  const int quadrant = q & 3;
+  s_out = quadrant == 0 ? sin_r : quadrant == 1 ? cos_r : quadrant == 2 ? -sin_r : -cos_r;
+  c_out = quadrant == 0 ? cos_r : quadrant == 1 ? -sin_r : quadrant == 2 ? -cos_r : sin_r;
+}
+
+constexpr float kRefPi = 3.14159274101257324219f;
+
 // [cos(t*f) | sin(t*f) | 0...] per sample  (scripts/native_embeddings_avx512.c:97-125)
 __global__ void timestep_embed_k(const float* __restrict__ t, const float* __restrict__ f,
                                  float* __restrict__ out, int batch, int half, int out_dim) {
@@ -221,10 +290,70 @@ __global__ void timestep_embed_k(const float* __restrict__ t, const float* __res
   if (b >= batch) return;
   for (int i = threadIdx.x; i < out_dim; i += blockDim.x) {
     float v = 0.0f;
-    if (i < half) v = cosf(t[b] * f[i]);
-    else if (i < 2 * half) v = sinf(t[b] * f[i - half]);
+    if (i < 2 * half) {
+      float sn, cs;
+      ref_sincos(__fmul_rn(t[b], f[i < half ? i : i - half]), sn, cs);
+      v = i < half ? cs : sn;
+    }
     out[(int64_t)b * out_dim + i] = v;
   }
+}
+
+// per row and axis [sin(a_0..a_{F-1}) | cos(a_0..)], a = x*f (doubled if double_pi) * pi,
+// zero padding to `channels`  (scripts/native_embeddings_avx512.c:58-95)
+__global__ void pcd_position_k(const float* __restrict__ pos, const float* __restrict__ f,
+                               float* __restrict__ out, int64_t rows, int dims, int F,
+                               int channels, int double_pi) {
+  const int64_t n = rows * (int64_t)channels;
+  const int used = dims * F * 2;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = e / channels;
+    const int c = (int)(e - row * channels);
+    float v = 0.0f;
+    if (c < used) {
+      const int axis = c / (2 * F), j = c - axis * 2 * F;
+      const int i = j < F ? j : j - F;
+      float angle = __fmul_rn(pos[row * dims + axis], f[i]);
+      if (double_pi) angle = __fadd_rn(angle, angle);
+      float sn, cs;
+      ref_sincos(__fmul_rn(angle, kRefPi), sn, cs);
+      v = j < F ? sn : cs;
+    }
+    out[e] = v;
+  }
+}
+
+// RePo phasors: complex k of vector v on axis a: (cos, sin) of (x*ft + x*fr)*pi,
+// x = delta[v, a]  (scripts/native_repo_avx512.c:85-129)
+struct RepoFreqs {
+  const float* ft[3];
+  const float* fr[3];
+  int dims[3];
+};
+
+__global__ void repo_phasor_k(const float* __restrict__ delta, RepoFreqs fq,
+                              float2* __restrict__ out, int64_t vectors) {
+  const int total = fq.dims[0] + fq.dims[1] + fq.dims[2];
+  const int64_t n = vectors * (int64_t)total;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t v = e / total;
+    int k = (int)(e - v * total), a = 0;
+    if (k >= fq.dims[0]) { k -= fq.dims[0]; a = 1; if (k >= fq.dims[1]) { k -= fq.dims[1]; a = 2; } }
+    const float x = delta[v * 3 + a];
+    const float angle = __fmul_rn(__fadd_rn(__fmul_rn(x, fq.ft[a][k]), __fmul_rn(x, fq.fr[a][k])), kRefPi);
+    float sn, cs;
+    ref_sincos(angle, sn, cs);
+    out[e] = make_float2(cs, sn);
+  }
+}
+
+// lhs *= rhs  (scripts/native_repo_avx512.c:69-83)
+__global__ void mul_k(float* __restrict__ lhs, const float* __restrict__ rhs, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    lhs[i] = __fmul_rn(lhs[i], rhs[i]);
 }
 
 }  // namespace ew
@@ -376,6 +505,38 @@ int triposplat_euler_update_inplace_f32_avx512(float* sample, const float* predi
   return launch_status();
 }
 
+// scripts/native_sampler_avx512.c:91-130
+int triposplat_ab2_update_inplace_f32_avx512(float* sample, const float* prediction,
+                                             const float* previous_prediction, const float* dt,
+                                             const float* previous_dt, int batch,
+                                             int64_t elements_per_batch, int threads) {
+  (void)threads;
+  if (!sample || !prediction || !previous_prediction || !dt || !previous_dt) return kNullPointer;
+  if (batch <= 0 || elements_per_batch <= 0) return kBadDims;
+  TSB_PREAMBLE();
+  const int64_t n = (int64_t)batch * elements_per_batch;
+  { LaunchScope _scope(kKElementwise, current_stream());
+    ab2_k<<<grid_for(n, 256), 256, 0, current_stream()>>>(sample, prediction, previous_prediction,
+                                                        dt, previous_dt, elements_per_batch, n); }
+  return launch_status();
+}
+
+// No reference counterpart: triposplat_cfg_combine_inplace_f32_avx512 followed by
+// triposplat_euler_update_inplace_f32_avx512 in one kernel (same results bit for bit;
+// `positive` is not overwritten).  guidance and dt hold one value per batch entry.
+int triposplat_b200_cfg_euler_update_f32(float* sample, const float* positive,
+                                         const float* negative, const float* guidance,
+                                         const float* dt, int batch, int64_t elements_per_batch) {
+  if (!sample || !positive || !negative || !guidance || !dt) return kNullPointer;
+  if (batch <= 0 || elements_per_batch <= 0) return kBadDims;
+  TSB_PREAMBLE();
+  const int64_t n = (int64_t)batch * elements_per_batch;
+  { LaunchScope _scope(kKElementwise, current_stream());
+    cfg_euler_k<<<grid_for(n, 256), 256, 0, current_stream()>>>(sample, positive, negative,
+                                                              guidance, dt, elements_per_batch, n); }
+  return launch_status();
+}
+
 // scripts/native_qkv_postprocess_v2_avx512.c:45-105
 int triposplat_qkv_rope_rmsnorm_pack_f32_avx512_v2(const float* qkv, const float* frequencies,
                                                    const float* q_gamma, const float* k_gamma,
@@ -449,6 +610,59 @@ int triposplat_timestep_embedding_f32_avx512(const float* timesteps, const float
   { LaunchScope _scope(kKElementwise, current_stream());
     timestep_embed_k<<<batch, 256, 0, current_stream()>>>(timesteps, frequencies, output, batch,
                                                         half_dim, output_dim); }
+  return launch_status();
+}
+
+// scripts/native_embeddings_avx512.c:58-95
+int triposplat_pcd_position_embedding_f32_avx512(const float* positions, const float* frequencies,
+                                                 float* output, int64_t rows, int input_dims,
+                                                 int frequency_dim, int channels, int double_pi,
+                                                 int threads) {
+  (void)threads;
+  if (!positions || !frequencies || !output) return kNullPointer;
+  if (rows <= 0 || input_dims <= 0 || frequency_dim <= 0 ||
+      channels < input_dims * frequency_dim * 2)
+    return kBadDims;
+  TSB_PREAMBLE();
+  { LaunchScope _scope(kKElementwise, current_stream());
+    pcd_position_k<<<grid_for(rows * (int64_t)channels, 256), 256, 0, current_stream()>>>(
+        positions, frequencies, output, rows, input_dims, frequency_dim, channels, double_pi); }
+  return launch_status();
+}
+
+// scripts/native_repo_avx512.c:69-83
+int triposplat_mul_inplace_f32_avx512(float* lhs, const float* rhs, int64_t elements, int threads) {
+  (void)threads;
+  if (!lhs || !rhs) return kNullPointer;
+  if (elements <= 0) return kBadDims;
+  TSB_PREAMBLE();
+  { LaunchScope _scope(kKElementwise, current_stream());
+    mul_k<<<grid_for(elements, 256), 256, 0, current_stream()>>>(lhs, rhs, elements); }
+  return launch_status();
+}
+
+// scripts/native_repo_avx512.c:85-129 (status -1 delta / output null, -2 a frequency null,
+// -3 bad sizes, as the reference)
+int triposplat_repo_phasor_f32_avx512(const float* delta, const float* freq_tanh_0,
+                                      const float* freq_residual_0, int freq_dim_0,
+                                      const float* freq_tanh_1, const float* freq_residual_1,
+                                      int freq_dim_1, const float* freq_tanh_2,
+                                      const float* freq_residual_2, int freq_dim_2,
+                                      float* output_interleaved, int64_t vectors, int threads) {
+  (void)threads;
+  if (!delta || !output_interleaved) return -1;
+  if (!freq_tanh_0 || !freq_residual_0 || !freq_tanh_1 || !freq_residual_1 || !freq_tanh_2 ||
+      !freq_residual_2)
+    return -2;
+  if (vectors <= 0 || freq_dim_0 <= 0 || freq_dim_1 <= 0 || freq_dim_2 <= 0) return -3;
+  TSB_PREAMBLE();
+  RepoFreqs fq{{freq_tanh_0, freq_tanh_1, freq_tanh_2},
+               {freq_residual_0, freq_residual_1, freq_residual_2},
+               {freq_dim_0, freq_dim_1, freq_dim_2}};
+  const int64_t n = vectors * (int64_t)(freq_dim_0 + freq_dim_1 + freq_dim_2);
+  { LaunchScope _scope(kKElementwise, current_stream());
+    repo_phasor_k<<<grid_for(n, 256), 256, 0, current_stream()>>>(
+        delta, fq, reinterpret_cast<float2*>(output_interleaved), vectors); }
   return launch_status();
 }
 

@@ -466,11 +466,11 @@ class CfgEulerSampler:
         self.x_cam[1].copy_(self.x_cam[0])
         v_lat, v_cam = m.forward(self.x_lat, self.x_cam, self.t_cur, self.cond_pair)
         for x, v in ((self.x_lat, v_lat), (self.x_cam, v_cam)):
-            n = v[0].numel()
-            st = lib.triposplat_cfg_combine_inplace_f32_avx512(v[0].data_ptr(), v[1].data_ptr(),
-                                                              self.g.data_ptr(), 1, n, 0)
-            st = st or lib.triposplat_euler_update_inplace_f32_avx512(
-                x[0].data_ptr(), v[0].data_ptr(), self.dt_cur.data_ptr(), 1, n, 0)
+            # CFG combine + Euler step in one kernel (bit-identical to the reference's
+            # triposplat_cfg_combine_inplace + triposplat_euler_update_inplace pair)
+            st = lib.triposplat_b200_cfg_euler_update_f32(
+                x[0].data_ptr(), v[0].data_ptr(), v[1].data_ptr(), self.g.data_ptr(),
+                self.dt_cur.data_ptr(), 1, v[0].numel())
             if st:
                 raise RuntimeError(f"sampler update returned status {st}")
 

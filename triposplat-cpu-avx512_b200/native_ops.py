@@ -4,7 +4,8 @@ Each function mirrors the computation the reference's strict patch performs with
 its AVX-512 kernel (scripts/native_norm_rope_avx512_patch.py,
 native_gelu_avx512_patch.py, native_silu_avx512_patch.py,
 native_block_elementwise_avx512_patch.py, native_sampler_avx512_backend.py,
-native_qkv_packed_attention_patch_v3.py) and raises on any non-zero status.
+native_qkv_packed_attention_patch_v3.py, native_embeddings_avx512_patch.py,
+native_repo_avx512_patch.py) and raises on any non-zero status.
 """
 from __future__ import annotations
 
@@ -157,3 +158,68 @@ def q_kv_selected_rope_rmsnorm_pack(q, kv, freqs, selected, q_gamma, k_gamma, Lk
         selected.data_ptr(), q_gamma.data_ptr(), k_gamma.data_ptr(), qo.data_ptr(), pk.data_ptr(),
         pv.data_ptr(), B, Lq, Lk, H, D, Lp, int(freqs.shape[0]), 0), "q_kv_selected_pack")
     return qo, pk, pv
+
+
+def timestep_embedding(timesteps, frequencies, output_dim=None):
+    """[batch] timesteps, [half] frequencies -> [batch, output_dim] = [cos | sin | 0 ...]
+    (scripts/native_embeddings_avx512_patch.py:76-97)."""
+    import torch
+
+    t, f = _f32(timesteps, "timestep_embedding"), _f32(frequencies, "timestep_embedding")
+    half = int(f.numel())
+    output_dim = 2 * half if output_dim is None else int(output_dim)
+    out = torch.empty((int(t.numel()), output_dim), dtype=torch.float32, device=t.device)
+    _ok(_lib().triposplat_timestep_embedding_f32_avx512(
+        t.data_ptr(), f.data_ptr(), out.data_ptr(), int(t.numel()), half, output_dim, 0),
+        "timestep_embedding")
+    return out
+
+
+def pcd_position_embedding(positions, frequencies, channels, double_pi=False):
+    """positions [..., dims] -> [..., channels]: per axis [sin | cos] of x*f(*2)*pi, zero pad
+    (scripts/native_embeddings_avx512_patch.py, point-cloud position embedder)."""
+    import torch
+
+    x, f = _f32(positions, "pcd_position_embedding"), _f32(frequencies, "pcd_position_embedding")
+    dims = int(x.shape[-1])
+    rows = x.numel() // dims
+    out = torch.empty((*x.shape[:-1], int(channels)), dtype=torch.float32, device=x.device)
+    _ok(_lib().triposplat_pcd_position_embedding_f32_avx512(
+        x.data_ptr(), f.data_ptr(), out.data_ptr(), rows, dims, int(f.numel()), int(channels),
+        int(bool(double_pi)), 0), "pcd_position_embedding")
+    return out
+
+
+def mul_inplace(lhs, rhs):
+    """lhs *= rhs (the RePo gate * content product, scripts/native_repo_avx512_patch.py:55-66)."""
+    lhs, rhs = _f32(lhs, "mul_inplace"), _f32(rhs, "mul_inplace")
+    if lhs.shape != rhs.shape:
+        raise ValueError("mul_inplace: shapes differ")
+    _ok(_lib().triposplat_mul_inplace_f32_avx512(lhs.data_ptr(), rhs.data_ptr(), lhs.numel(), 0),
+        "mul_inplace")
+    return lhs
+
+
+def repo_phasor(delta, frequencies):
+    """RePo 3-D rotary phasors (scripts/native_repo_avx512_patch.py:68-105): delta
+    [B, L, 3 * heads] and the three per-axis frequency vectors f_a -> complex64
+    [B, L, heads, sum(dims)] with angle (x*tanh(f) + x*(f - tanh(f))) * pi per axis."""
+    import torch
+
+    d = _f32(delta, "repo_phasor")
+    if d.ndim != 3 or int(d.shape[-1]) % 3:
+        raise ValueError("repo_phasor: delta must be [B, L, 3 * heads]")
+    parts = []
+    for f in frequencies:
+        f = _f32(f.reshape(-1), "repo_phasor")
+        ft = torch.tanh(f).contiguous()
+        parts.append((ft, (f - ft).contiguous()))
+    dims = [int(p[0].numel()) for p in parts]
+    B, L, heads = int(d.shape[0]), int(d.shape[1]), int(d.shape[2]) // 3
+    out = torch.empty((B, L, heads, sum(dims)), dtype=torch.complex64, device=d.device)
+    _ok(_lib().triposplat_repo_phasor_f32_avx512(
+        d.data_ptr(), parts[0][0].data_ptr(), parts[0][1].data_ptr(), dims[0],
+        parts[1][0].data_ptr(), parts[1][1].data_ptr(), dims[1],
+        parts[2][0].data_ptr(), parts[2][1].data_ptr(), dims[2],
+        out.data_ptr(), B * L * heads, 0), "repo_phasor")
+    return out
