@@ -275,10 +275,38 @@ def embedding_cases(torch):
     np.savez_compressed(HERE / "embeddings.npz", **data)
 
 
+def shard_cases(torch):
+    """A tiny NF24 shard directory written by the reference's own packer
+    (scripts/native_linear_nf24_prepacked.py:202-335, format triposplat_nf24_i16_v1) from a
+    seeded three-Linear safetensors checkpoint (one without bias) plus two non-Linear
+    tensors; the loader here must read it, and its codes must equal this repo's packer."""
+    import shutil
+
+    from safetensors.torch import save_file
+    from native_linear_nf24_prepacked import pack_nf24_i16_checkpoint
+
+    g = torch.Generator(device="cpu").manual_seed(4)
+    src = {
+        "blocks.0.attn.qkv.weight": torch.randn(96, 64, generator=g) * 0.02,
+        "blocks.0.attn.qkv.bias": torch.randn(96, generator=g) * 0.01,
+        "blocks.0.mlp.fc1.weight": torch.randn(48, 96, generator=g) * 0.02,
+        "blocks.0.mlp.fc1.bias": torch.randn(48, generator=g) * 0.01,
+        "head.weight": torch.randn(16, 48, generator=g) * 0.02,
+        "blocks.0.norm.gamma": 1.0 + torch.randn(64, generator=g) * 0.02,
+        "pos_table": torch.randn(8, 64, generator=g),
+    }
+    src_path = HERE / "shards_src.safetensors"
+    save_file(src, src_path.as_posix())
+    out = HERE / "shards_ref"
+    if out.exists():
+        shutil.rmtree(out)
+    pack_nf24_i16_checkpoint(src_path, out, expected_linear_count=3)
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
-    ap.add_argument("--cases", default="gemm,sdpa,elementwise,embeddings",
+    ap.add_argument("--cases", default="gemm,sdpa,elementwise,embeddings,shards",
                     help="comma-separated subset of the fixture groups to (re)write")
     args = ap.parse_args()
     cases = set(args.cases.split(","))
@@ -302,6 +330,8 @@ def main() -> int:
         elementwise_cases(torch)
     if "embeddings" in cases:
         embedding_cases(torch)
+    if "shards" in cases:
+        shard_cases(torch)
     print("golden fixtures written to", HERE)
     return 0
 
