@@ -711,8 +711,25 @@ __global__ void __launch_bounds__(256) sdpa_split_kv(
 // written to HBM in fp32.  Source layouts: kSelected = false: qkv [B, L, 3, H, 64]
 // (q, k and v of token t); kSelected = true: q [B, Lq, H, 64] and kv [B, Lk, 2, H, 64], RoPE
 // frequency row of query i = sel[i] (no frequencies: no rotation).
+// One q row (the rope_rms64 output, one complex pair per lane) into the Q planes with its
+// per-row power-of-two pre-scale (as sdpa_split_q).
+__device__ __forceinline__ void emit_q_row(__half* __restrict__ qhi, __half* __restrict__ qlo,
+                                           float* __restrict__ qinv, int64_t row, float2 qy,
+                                           int lane) {
+  float mx = fmaxf(fabsf(qy.x), fabsf(qy.y));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const int sq = pow2_shift(mx);
+  const float a = ldexpf(qy.x, sq), c = ldexpf(qy.y, sq);
+  const __half2 hh = __floats2half2_rn(a, c);
+  const float2 hf = __half22float2(hh);
+  *reinterpret_cast<__half2*>(qhi + row * D + lane * 2) = hh;
+  *reinterpret_cast<__half2*>(qlo + row * D + lane * 2) = __floats2half2_rn(a - hf.x, c - hf.y);
+  if (lane == 0) qinv[row] = ldexpf(1.0f, -sq);
+}
+
 template <bool kSelected>
-__global__ void __launch_bounds__(256) qkv_split_k(
+__global__ void __launch_bounds__(256, 3) qkv_split_k(
     const float* __restrict__ qsrc, const float* __restrict__ kvsrc, const float* __restrict__ freqs,
     const int64_t* __restrict__ sel, const float* __restrict__ qg, const float* __restrict__ kg,
     int H, int Lq, int Lk, int Lkt, int fb, __half* __restrict__ qhi, __half* __restrict__ qlo,
@@ -720,8 +737,7 @@ __global__ void __launch_bounds__(256) qkv_split_k(
     __half* __restrict__ vhi, __half* __restrict__ vlo, float* __restrict__ kinv,
     float* __restrict__ vinv) {
   extern __shared__ float sm_kv[];
-  float(*kt)[D + 1] = reinterpret_cast<float(*)[D + 1]>(sm_kv);            // [BKV][65]
-  float(*vt)[D + 1] = reinterpret_cast<float(*)[D + 1]>(sm_kv + BKV * (D + 1));
+  float(*vt)[D + 1] = reinterpret_cast<float(*)[D + 1]>(sm_kv);  // [BKV][65]: V for the transpose
   __shared__ float red[2][8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.y, b = bh / H, h = bh % H;
@@ -730,23 +746,15 @@ __global__ void __launch_bounds__(256) qkv_split_k(
   const float2 gq = reinterpret_cast<const float2*>(qg + (int64_t)h * 64)[lane];
   const float2 gk = reinterpret_cast<const float2*>(kg + (int64_t)h * 64)[lane];
   // one q row (rope_rms64 output held as one complex pair per lane) into the Q planes
-  auto emit_q = [&](int64_t row, float2 qy) {
-    float mx = fmaxf(fabsf(qy.x), fabsf(qy.y));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    const int sq = pow2_shift(mx);
-    const float a = ldexpf(qy.x, sq), c = ldexpf(qy.y, sq);
-    const __half2 hh = __floats2half2_rn(a, c);
-    const float2 hf = __half22float2(hh);
-    *reinterpret_cast<__half2*>(qhi + row * D + lane * 2) = hh;
-    *reinterpret_cast<__half2*>(qlo + row * D + lane * 2) = __floats2half2_rn(a - hf.x, c - hf.y);
-    if (lane == 0) qinv[row] = ldexpf(1.0f, -sq);
-  };
+  auto emit_q = [&](int64_t row, float2 qy) { emit_q_row(qhi, qlo, qinv, row, qy, lane); };
   if (tile < T) {
     const int t0 = tile * BKV;
     float kmx = 0.0f, vmx = 0.0f;
+    float2 kreg[BKV / 8];  // this warp's 16 k rows (one complex pair per lane) until the
+                           // tile's scale is known; V goes through shared memory (transpose)
     // 16 tokens per warp, four at a time with all their loads issued first (the loop is
     // latency-bound otherwise: one token's loads and warp reductions at a time)
+#pragma unroll
     for (int j0 = 0; j0 < BKV / 8; j0 += 4) {
       float2 qx[4], kx[4], vx[4], fr[4];
 #pragma unroll
@@ -773,8 +781,7 @@ __global__ void __launch_bounds__(256) qkv_split_k(
           ky = rope_rms64(kx[u], fr[u], gk);
           vy = vx[u];
         }
-        kt[i][2 * lane] = ky.x;
-        kt[i][2 * lane + 1] = ky.y;
+        kreg[j0 + u] = ky;
         vt[i][2 * lane] = vy.x;
         vt[i][2 * lane + 1] = vy.y;
         kmx = fmaxf(kmx, fmaxf(fabsf(ky.x), fabsf(ky.y)));
@@ -792,20 +799,15 @@ __global__ void __launch_bounds__(256) qkv_split_k(
 #pragma unroll
     for (int w = 1; w < 8; ++w) { kmx = fmaxf(kmx, red[0][w]); vmx = fmaxf(vmx, red[1][w]); }
     const int sk = pow2_shift(kmx), sv = pow2_shift(vmx);
-    for (int e = threadIdx.x; e < BKV * (D / 8); e += 256) {
-      const int j = e / (D / 8), d0 = (e % (D / 8)) * 8;
-      __align__(16) __half h8[8];
-      __align__(16) __half l8[8];
+    // K rows straight from registers: 128 bytes of hi and of lo per row and warp
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float x = ldexpf(kt[j][d0 + i], sk);
-        const __half hh = __float2half_rn(x);
-        h8[i] = hh;
-        l8[i] = __float2half_rn(x - __half2float(hh));
-      }
-      const int64_t off = ((int64_t)bh * Lkt + t0 + j) * D + d0;
-      *reinterpret_cast<uint4*>(khi + off) = *reinterpret_cast<uint4*>(h8);
-      *reinterpret_cast<uint4*>(klo + off) = *reinterpret_cast<uint4*>(l8);
+    for (int r = 0; r < BKV / 8; ++r) {
+      const float a = ldexpf(kreg[r].x, sk), c = ldexpf(kreg[r].y, sk);
+      const __half2 hh = __floats2half2_rn(a, c);
+      const float2 hf = __half22float2(hh);
+      const int64_t off = ((int64_t)bh * Lkt + t0 + warp + 8 * r) * D + 2 * lane;
+      *reinterpret_cast<__half2*>(khi + off) = hh;
+      *reinterpret_cast<__half2*>(klo + off) = __floats2half2_rn(a - hf.x, c - hf.y);
     }
     for (int e = threadIdx.x; e < D * (BKV / 8); e += 256) {
       const int d = e / (BKV / 8), jb = (e % (BKV / 8)) * 8;
@@ -827,28 +829,41 @@ __global__ void __launch_bounds__(256) qkv_split_k(
       vinv[(int64_t)bh * T + tile] = ldexpf(1.0f, -sv);
     }
   }
-  if (kSelected) {
-    for (int j0 = 0; j0 < BKV / 8; j0 += 4) {
-      float2 qx[4], fr[4];
+}
+
+// Selected-query rows of the fused post-process (the q half of qkv_split_k<true>): RMSNorm
+// (and RoPE with the frequency row sel[i]) into the Q planes; one CTA per (bh, 128 queries),
+// no shared memory, so it runs at full occupancy.
+__global__ void __launch_bounds__(256) selected_q_split_k(
+    const float* __restrict__ qsrc, const float* __restrict__ freqs, const int64_t* __restrict__ sel,
+    const float* __restrict__ qg, int H, int Lq, int Lk, int fb, __half* __restrict__ qhi,
+    __half* __restrict__ qlo, float* __restrict__ qinv) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y, b = bh / H, h = bh % H;
+  const int fbb = fb == 1 ? 0 : b;
+  const int tile = blockIdx.x;
+  const float2 gq = reinterpret_cast<const float2*>(qg + (int64_t)h * 64)[lane];
+  for (int j0 = 0; j0 < BKV / 8; j0 += 4) {
+    float2 qx[4], fr[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int qi = tile * BKV + warp + 8 * (j0 + u);
-        qx[u] = make_float2(0.0f, 0.0f);
-        fr[u] = make_float2(1.0f, 0.0f);  // no frequencies: identity rotation
-        if (qi < Lq) {
-          if (freqs) fr[u] = reinterpret_cast<const float2*>(freqs + (((int64_t)fbb * Lk + sel[qi]) * H + h) * 64)[lane];
-          qx[u] = reinterpret_cast<const float2*>(qsrc + (((int64_t)b * Lq + qi) * H + h) * 64)[lane];
-        }
+    for (int u = 0; u < 4; ++u) {
+      const int qi = tile * BKV + warp + 8 * (j0 + u);
+      qx[u] = make_float2(0.0f, 0.0f);
+      fr[u] = make_float2(1.0f, 0.0f);  // no frequencies: identity rotation
+      if (qi < Lq) {
+        if (freqs) fr[u] = reinterpret_cast<const float2*>(freqs + (((int64_t)fbb * Lk + sel[qi]) * H + h) * 64)[lane];
+        qx[u] = reinterpret_cast<const float2*>(qsrc + (((int64_t)b * Lq + qi) * H + h) * 64)[lane];
       }
+    }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int qi = tile * BKV + warp + 8 * (j0 + u);
-        if (qi < Lq) emit_q((int64_t)bh * Lq + qi, rope_rms64(qx[u], fr[u], gq));  // warp-uniform
-      }
+    for (int u = 0; u < 4; ++u) {
+      const int qi = tile * BKV + warp + 8 * (j0 + u);
+      if (qi < Lq) emit_q_row(qhi, qlo, qinv, (int64_t)bh * Lq + qi, rope_rms64(qx[u], fr[u], gq), lane);
     }
   }
 }
-constexpr int QKV_SPLIT_SMEM = 2 * BKV * (D + 1) * 4;
+
+constexpr int QKV_SPLIT_SMEM = BKV * (D + 1) * 4;  // the V staging tile
 
 }  // namespace sdpa
 
@@ -1020,12 +1035,18 @@ static int qkv_sdpa_launch(const float* qsrc, const float* kvsrc, const float* f
     }
   }
   const int q_tiles = (Lq + BKV - 1) / BKV;
-  const int tiles = kSelected ? (sp.T > q_tiles ? sp.T : q_tiles) : sp.T;
+  // key tiles (with, for self-attention, the query rows of the same tokens) through the
+  // shared-memory V staging; selected queries in their own kernel without shared memory
   {
     LaunchScope scope(kKSdpaSplit, stream);
-    qkv_split_k<kSelected><<<dim3(tiles, (unsigned)BH), 256, QKV_SPLIT_SMEM, stream>>>(
+    qkv_split_k<kSelected><<<dim3(sp.T, (unsigned)BH), 256, QKV_SPLIT_SMEM, stream>>>(
         qsrc, kvsrc, freqs, sel, qg, kg, H, Lq, Lk, sp.Lkt, fb, sp.qhi, sp.qlo, sp.qinv, sp.khi, sp.klo,
         sp.vhi, sp.vlo, sp.kinv, sp.vinv);
+  }
+  if (kSelected) {
+    LaunchScope scope(kKSdpaSplit, stream);
+    selected_q_split_k<<<dim3(q_tiles, (unsigned)BH), 256, 0, stream>>>(
+        qsrc, freqs, sel, qg, H, Lq, Lk, fb, sp.qhi, sp.qlo, sp.qinv);
   }
   if ((st = launch_status()) != kOk) return st;
   return sdpa_attend(sp, nullptr, 0, out_blhd, BH, H, Lq, Lk, 1, stream);
