@@ -57,6 +57,9 @@ def parse():
                     help="head-sharded tensor parallelism: each model (the CFG pair, or one "
                          "branch with --parallel cfg) runs on this many GPUs, heads and MLP "
                          "columns split, three NCCL all-reduces per block")
+    ap.add_argument("--tp-reduce", choices=("peer", "nccl"), default="peer",
+                    help="peer: the ranks' partials are summed into the residual by one kernel "
+                         "reading NVLink peer memory; nccl: NCCL all-reduce + residual kernel")
     ap.add_argument("--no-graph", action="store_true",
                     help="issue every kernel from the host each step instead of replaying "
                          "the step's CUDA graph")
@@ -291,12 +294,15 @@ def run_reference(args):
     return 0
 
 
-def parallelism_label(split: bool, tp: int, images: int) -> str:
+def parallelism_label(split: bool, tp: int, images: int, reduce: str = "peer") -> str:
+    reduce_label = ("one kernel reading the ranks' partials over NVLink and updating the residual"
+                    if reduce == "peer" else "NCCL all-reduce + residual kernel")
     parts = []
     if split:
         parts.append("CFG pair split over 2 GPU groups (one NCCL all-gather of the velocity per step)")
     if tp > 1:
-        parts.append(f"heads and MLP columns sharded over {tp} GPUs (3 NCCL all-reduces per block)")
+        parts.append(f"heads and MLP columns sharded over {tp} GPUs (3 reductions per block: "
+                     f"{reduce_label})")
     if not parts:
         return f"replicas x{images} (one image per GPU, no data-path collective)"
     return f"{images} image(s) in parallel; per image: " + "; ".join(parts)
@@ -352,7 +358,7 @@ def main():
         from head_shard import HeadShardedFlowModel
 
         model = HeadShardedFlowModel(weights, rank=tp_rank, tp=T, batch=batch, device=str(dev),
-                                     group=tp_groups[(image, branch)])
+                                     group=tp_groups[(image, branch)], reduce=args.tp_reduce)
     else:
         model = FlowModelB200(weights, batch=batch, device=str(dev))
     if split:
@@ -507,7 +513,7 @@ def main():
                    "heads": spec.heads, "mlp": spec.mlp, "latent_tokens": spec.latent_tokens,
                    "seq": spec.seq, "cond_tokens": Mc, "sampler_steps": SAMPLER_STEPS,
                    "guidance": 3.0, "shift": 3.0, "global_batch": f"{images} image(s) x CFG pair",
-                   "parallelism": parallelism_label(split, T, images),
+                   "parallelism": parallelism_label(split, T, images, args.tp_reduce),
                    "launch": "host-issued kernels" if args.no_graph else "one CUDA graph per sampler step",
                    "l2": "no flush: every step streams 1.4 GB of NF24 weights and ~1 GB of "
                          "activations, far above the 126 MB L2"},
@@ -527,6 +533,11 @@ def main():
         print(json.dumps(line), flush=True)
     if world > 1:
         sampler.graph = None  # release graphs before the process group goes
+        torch.cuda.synchronize()
+        barrier()
+        if hasattr(model, "close"):
+            model.close()  # IPC mappings of the peer reduction
+        barrier()
         dist.destroy_process_group()
     return 0
 

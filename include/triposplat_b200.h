@@ -302,6 +302,24 @@ int triposplat_b200_q_kv_rmsnorm_sdpa_f32(const float* q, const float* kv, const
                                           const float* k_gamma, float* out_blhd, int B, int Lq,
                                           int Lk, int H);
 
+/* ---- Tensor-parallel reduction over NVLink peer memory (no reference counterpart) ----
+ * ipc_alloc: cudaMalloc'd, zeroed buffer plus its 64-byte CUDA IPC handle; ipc_open maps a
+ * handle of another process of the node; ipc_close / ipc_free release them.
+ * peer_barrier: one-warp barrier of `world` ranks through their flag arrays (flag_ptrs[r] =
+ * rank r's array of `world` uint32 as mapped here; counter = this rank's epoch word);
+ * waits are bounded (2 s) and report through triposplat_b200_status().
+ * peer_reduce_residual_f32: x += gate[row / rows_per_batch] * sum_r part_r (mode 2) or
+ * x += sum_r part_r (mode 3), partials read from every rank's memory and summed in rank
+ * order; cols % 4 == 0, 16-byte aligned pointers. */
+int triposplat_b200_ipc_alloc(uint64_t bytes, void** dev_ptr, uint8_t* handle_out);
+int triposplat_b200_ipc_free(void* dev_ptr);
+int triposplat_b200_ipc_open(const uint8_t* handle, void** dev_ptr);
+int triposplat_b200_ipc_close(void* dev_ptr);
+int triposplat_b200_peer_barrier(const uint64_t* flag_ptrs, int rank, int world, uint32_t* counter);
+int triposplat_b200_peer_reduce_residual_f32(const uint64_t* part_ptrs, int world, float* x,
+                                             int64_t rows, int cols, int mode, const float* gate,
+                                             int gate_ld, int64_t rows_per_batch);
+
 #ifdef __cplusplus
 }
 #endif

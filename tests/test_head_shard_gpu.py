@@ -5,8 +5,9 @@ the GEMM's fp16 hi/lo operands, and the partial products are summed across ranks
 velocities must match the single-GPU forward to a relative RMS error far below the 1e-4
 end-of-sampling budget: REL_RMSE = 1e-5 here.  Checked (1) with all ranks driven in lockstep
 by one process on one GPU (partials summed in rank order), at 2 / 4 / 8 ranks, and (2) as
-two processes on two GPUs reducing over NCCL, and (3) the CFG split combined with head
-sharding as four processes on four GPUs, against the batch-2 sampler (each skipped when
+two processes on two GPUs reducing over NCCL and over NVLink peer memory (the fused
+reduce + residual kernel), and (3) the CFG split combined with head sharding (peer
+reduction) as four processes on four GPUs, against the batch-2 sampler (each skipped when
 fewer GPUs are visible).
 """
 import os
@@ -152,7 +153,7 @@ def _cfg_tp_worker(rank, port, out_dir):
         pair_groups = [dist.new_group([0, 2]), dist.new_group([1, 3])]
         branch, tp_rank = rank // 2, rank % 2
         model = HeadShardedFlowModel(w, rank=tp_rank, tp=2, batch=1, device=dev,
-                                     group=tp_groups[branch])
+                                     group=tp_groups[branch], reduce="peer")
         s = CfgSplitSampler(model, branch=branch, group=pair_groups[tp_rank], steps=3)
         g = torch.Generator().manual_seed(4)
         lat = torch.randn(1, spec.latent_tokens, spec.latent_dim, generator=g).to(dev)
@@ -170,6 +171,8 @@ def _cfg_tp_worker(rank, port, out_dir):
             out["ref_lat"], out["ref_cam"] = r_lat.cpu().numpy(), r_cam.cpu().numpy()
         np.savez(os.path.join(out_dir, f"rank{rank}.npz"), **out)
         dist.barrier()
+        model.close()
+        dist.barrier()
     finally:
         dist.destroy_process_group()
 
@@ -184,3 +187,100 @@ def test_cfg_split_with_head_shard_four_gpus(tmp_path):
         assert np.array_equal(r["lat"], rs[0]["lat"]) and np.array_equal(r["cam"], rs[0]["cam"])
     assert _rel_rmse(rs[0]["lat"], rs[0]["ref_lat"]) < REL_RMSE
     assert _rel_rmse(rs[0]["cam"], rs[0]["ref_cam"]) < REL_RMSE
+
+
+def test_peer_reduce_kernel_one_gpu():
+    """The fused reduce + residual kernel over T partial buffers (here all on one GPU, no
+    barrier): x += gate[b] * (p0 + p1 + p2) summed in rank order, and x += sum."""
+    import ctypes
+
+    import _native
+
+    lib = _native.load()
+    _native.use_current_stream(lib)
+    g = torch.Generator().manual_seed(6)
+    B, L, C, T = 2, 37, 64, 3
+    parts = [torch.randn(B * L, C, generator=g).cuda() for _ in range(T)]
+    ptrs = (ctypes.c_uint64 * T)(*[p.data_ptr() for p in parts])
+    gate = torch.randn(B, C, generator=g).cuda()
+    x0 = torch.randn(B * L, C, generator=g).cuda()
+    s = parts[0] + parts[1] + parts[2]
+    x = x0.clone()
+    assert lib.triposplat_b200_peer_reduce_residual_f32(ptrs, T, x.data_ptr(), B * L, C, 2,
+                                                        gate.data_ptr(), C, L) == 0
+    ref = torch.addcmul(x0, gate.repeat_interleave(L, 0), s)
+    torch.cuda.synchronize()
+    assert torch.equal(x, ref)
+    x = x0.clone()
+    assert lib.triposplat_b200_peer_reduce_residual_f32(ptrs, T, x.data_ptr(), B * L, C, 3,
+                                                        None, 0, 1) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(x, x0 + s)
+    assert lib.triposplat_b200_peer_reduce_residual_f32(ptrs, T, x.data_ptr(), B * L, 62, 3,
+                                                        None, 0, 1) == -4
+    assert lib.triposplat_b200_peer_reduce_residual_f32(ptrs, 9, x.data_ptr(), B * L, C, 3,
+                                                        None, 0, 1) == -2
+
+
+def test_peer_barrier_times_out_and_reports():
+    """A barrier whose peer never signals gives up after its 2 s budget and reports through
+    the status word; the context stays usable."""
+    import ctypes
+
+    import _native
+
+    lib = _native.load()
+    _native.use_current_stream(lib)
+    flags = [torch.zeros(16, dtype=torch.int32, device="cuda") for _ in range(2)]
+    ptrs = (ctypes.c_uint64 * 2)(*[f.data_ptr() for f in flags])
+    counter = torch.zeros(1, dtype=torch.int32, device="cuda")
+    assert lib.triposplat_b200_status() == 0
+    assert lib.triposplat_b200_peer_barrier(ptrs, 0, 2, counter.data_ptr()) == 0
+    torch.cuda.synchronize()
+    assert lib.triposplat_b200_status() != 0      # rank 1's slot never reached the epoch
+    assert int(flags[1][0]) == 1 and int(flags[0][0]) == 1  # our own signal went out
+    lib.triposplat_b200_clear_status()
+    assert lib.triposplat_b200_status() == 0
+    y = torch.ones(4, device="cuda") * 2          # the context still runs work
+    assert float(y.sum()) == 8.0
+
+
+def _peer_worker(rank, port, out_dir):
+    import torch.distributed as dist
+
+    _nccl_init(rank, 2, port)
+    try:
+        from flow_model import FlowModelB200, make_weights
+        from head_shard import HeadShardedFlowModel
+
+        dev = f"cuda:{rank}"
+        spec = _spec()
+        w = make_weights(spec, seed=9, device=dev)
+        inp = _inputs(spec, 2, dev)
+        m = HeadShardedFlowModel(w, rank=rank, tp=2, batch=2, device=dev,
+                                 group=dist.group.WORLD, reduce="peer")
+        lat, cam = m.forward(*inp)
+        lat2, cam2 = (t.clone() for t in m.forward(*inp))  # second pass: buffers reused
+        torch.cuda.synchronize(dev)
+        out = {"lat": lat.cpu().numpy(), "cam": cam.cpu().numpy(), "lat2": lat2.cpu().numpy()}
+        if rank == 0:
+            ref = FlowModelB200(w, batch=2, device=dev).forward(*inp)
+            out["ref_lat"], out["ref_cam"] = (t.cpu().numpy() for t in ref)
+        np.savez(os.path.join(out_dir, f"rank{rank}.npz"), **out)
+        dist.barrier()
+        m.close()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_head_shard_two_gpus_peer_reduce(tmp_path):
+    import torch.multiprocessing as mp
+
+    mp.spawn(_peer_worker, args=(_free_port(), str(tmp_path)), nprocs=2, join=True)
+    r0, r1 = (np.load(tmp_path / f"rank{r}.npz") for r in (0, 1))
+    assert np.array_equal(r0["lat"], r1["lat"]) and np.array_equal(r0["cam"], r1["cam"])
+    assert np.array_equal(r0["lat"], r0["lat2"])
+    assert _rel_rmse(r0["lat"], r0["ref_lat"]) < REL_RMSE
+    assert _rel_rmse(r0["cam"], r0["ref_cam"]) < REL_RMSE

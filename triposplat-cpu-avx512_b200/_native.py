@@ -49,6 +49,12 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "triposplat_b200_gemm_nf24_split": ([VP, I, I] + [VP] * 5 + [I, I, I, VP, I, I], I),
     "triposplat_b200_gemm_nf24_split_range": ([VP, I, I] + [VP] * 5 + [I] * 5 + [VP, I, I], I),
     "triposplat_b200_nf24_codes_to_nk": ([VP, VP, I, I, VP, VP], I),
+    "triposplat_b200_ipc_alloc": ([ctypes.c_uint64, VP, VP], I),
+    "triposplat_b200_ipc_free": ([VP], I),
+    "triposplat_b200_ipc_open": ([VP, VP], I),
+    "triposplat_b200_ipc_close": ([VP], I),
+    "triposplat_b200_peer_barrier": ([VP, I, I, VP], I),
+    "triposplat_b200_peer_reduce_residual_f32": ([VP, I, VP, I64, I, I, VP, I, I64], I),
     "triposplat_b200_gemm_nf24_split_nk": ([VP, I, I, VP, VP, I] + [VP] * 3 + [I] * 5 + [VP, I, I], I),
     # exact SDPA
     "triposplat_sdpa_f32_avx512_exact_q8t512": ([VP] * 5 + [I] * 8, I),

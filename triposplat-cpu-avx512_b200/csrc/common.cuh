@@ -23,6 +23,7 @@ enum DeviceError : int {
   kDevTimeoutConsumer = 3,
   kDevTimeoutEpilogue = 4,
   kDevTmemAlloc = 5,
+  kDevTimeoutPeer = 6,  // a tensor-parallel peer did not reach the barrier
 };
 
 // Defined in runtime.cu; points at host-mapped pinned memory (device view).

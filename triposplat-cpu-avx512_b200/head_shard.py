@@ -15,7 +15,9 @@ and ``mlp / tp`` hidden columns:
 * embedders, adaLN and the final layer are replicated, so every rank holds the same
   residual stream ``x`` and ends with the same velocity.
 
-Three all-reduces of the ``[B, L, hidden]`` residual update per block.  ``forward_steps``
+Three reductions of the ``[B, L, hidden]`` residual update per block, either NCCL
+all-reduces followed by the residual kernel, or (``reduce="peer"``) one fused kernel that
+reads every rank's partial over NVLink and updates the residual.  ``forward_steps``
 yields each partial buffer at its reduction point, so a single process can drive several
 ranks in lockstep (the GPU parity tests); ``forward`` hands each one to ``all_reduce``
 (NCCL over the tensor-parallel group by default).  The sum differs from the single-GPU
@@ -56,11 +58,97 @@ def head_shard_plan(spec: FlowSpec, tp: int, rank: int) -> dict:
     }
 
 
+class PeerReduce:
+    """Partial-product buffers shared across one tensor-parallel group through CUDA IPC.
+
+    Every rank allocates two partial buffers (reduction points alternate between them) and
+    a flag array, publishes their IPC handles with one object all-gather over `group`, and
+    maps the other ranks' buffers.  ``reduce(point, x, mode, gate, ...)`` then runs the
+    peer barrier and the fused reduce + residual kernel of the C-ABI on the current stream.
+    """
+
+    def __init__(self, lib, group, rank: int, world: int, numel: int):
+        import ctypes
+
+        import torch.distributed as dist
+
+        self.lib, self.rank, self.world, self.group = lib, rank, world, group
+        self.local, handles = [], []
+        for nbytes in (4 * numel, 4 * numel, 64 * 4):
+            ptr, h = ctypes.c_void_p(), (ctypes.c_uint8 * 64)()
+            st = lib.triposplat_b200_ipc_alloc(nbytes, ctypes.byref(ptr), h)
+            if st:
+                raise RuntimeError(f"ipc_alloc returned {st}")
+            self.local.append(ptr.value)
+            handles.append(bytes(h))
+        allh = [None] * world
+        dist.all_gather_object(allh, handles, group=group)
+        self.opened = []
+        mapped = []  # [rank][buffer] -> pointer in this process
+        for r in range(world):
+            if r == rank:
+                mapped.append(list(self.local))
+                continue
+            row = []
+            for h in allh[r]:
+                ptr = ctypes.c_void_p()
+                st = lib.triposplat_b200_ipc_open((ctypes.c_uint8 * 64).from_buffer_copy(h),
+                                                   ctypes.byref(ptr))
+                if st:
+                    raise RuntimeError(f"ipc_open returned {st} for rank {r}")
+                self.opened.append(ptr.value)
+                row.append(ptr.value)
+            mapped.append(row)
+        arr = ctypes.c_uint64 * world
+        self.parts = [arr(*[mapped[r][k] for r in range(world)]) for k in (0, 1)]
+        self.flags = arr(*[mapped[r][2] for r in range(world)])
+        import torch
+
+        self.counter = torch.zeros(1, dtype=torch.int32, device=f"cuda:{torch.cuda.current_device()}")
+        self.point = 0
+
+    def part_ptr(self) -> int:
+        """This rank's buffer for the next reduction point."""
+        return self.local[self.point % 2]
+
+    def reduce(self, x, mode: int, gate=None, gate_ld: int = 0, rows_per_batch: int = 1):
+        lib = self.lib
+        st = lib.triposplat_b200_peer_barrier(self.flags, self.rank, self.world,
+                                              self.counter.data_ptr())
+        if st:
+            raise RuntimeError(f"peer_barrier returned {st}")
+        rows, cols = x.numel() // x.shape[-1], int(x.shape[-1])
+        st = lib.triposplat_b200_peer_reduce_residual_f32(
+            self.parts[self.point % 2], self.world, x.data_ptr(), rows, cols, mode,
+            None if gate is None else gate.data_ptr(), gate_ld, rows_per_batch)
+        if st:
+            raise RuntimeError(f"peer_reduce_residual returned {st}")
+        self.point += 1
+
+    def close(self):
+        """Unmap the other ranks' buffers, wait for every rank to have done the same, then
+        free this rank's (call with no work of the group in flight)."""
+        import torch.distributed as dist
+
+        for p in self.opened:
+            self.lib.triposplat_b200_ipc_close(p)
+        self.opened = []
+        dist.barrier(group=self.group)
+        for p in self.local:
+            self.lib.triposplat_b200_ipc_free(p)
+        self.local = []
+
+
 class HeadShardedFlowModel(FlowModelB200):
-    """FlowModelB200 forward with the blocks sharded over `tp` ranks (rank `rank`)."""
+    """FlowModelB200 forward with the blocks sharded over `tp` ranks (rank `rank`).
+
+    reduce="nccl": each row-window partial is summed by an NCCL all-reduce (or the
+    caller's `all_reduce`), then the residual kernel runs; reduce="peer": the partials
+    live in IPC-shared buffers and one fused kernel reads all ranks' partials over NVLink
+    and updates the residual (``PeerReduce``)."""
 
     def __init__(self, weights: FlowWeights, rank: int, tp: int, batch: int = 1,
-                 device: str = "cuda", group=None, all_reduce=None):
+                 device: str = "cuda", group=None, all_reduce=None, reduce: str = "nccl"):
         import torch
 
         super().__init__(weights, batch=batch, device=device, fused=True)
@@ -68,6 +156,12 @@ class HeadShardedFlowModel(FlowModelB200):
         self.rank, self.tp, self.group = rank, tp, group
         self.plan = pl = head_shard_plan(s, tp, rank)
         self.all_reduce = all_reduce or self._nccl_all_reduce
+        if reduce not in ("nccl", "peer"):
+            raise ValueError("reduce must be 'nccl' or 'peer'")
+        self.peer = None
+        if reduce == "peer":
+            _native.use_current_stream(self.lib)
+            self.peer = PeerReduce(self.lib, group, rank, tp, batch * s.seq * s.hidden)
         hs, hl = pl["heads"]
         w, f = pl["width"], pl["mlp_width"]
         B, L, h, Mc = batch, s.seq, s.hidden, s.cond_tokens
@@ -97,7 +191,7 @@ class HeadShardedFlowModel(FlowModelB200):
             p.bias.data_ptr(), out_ptr, N, start, count, stride_out, mode, None, 0, 1),
             f"gemm columns {name}")
 
-    def _lin_rows(self, name, split, rows, k0, count, out):
+    def _lin_rows(self, name, split, rows, k0, count, out_ptr):
         """Partial product over input features [k0, k0 + count) into out [rows, N]."""
         p = self.w.linears[name]
         c, q = self.nk[name]
@@ -105,8 +199,26 @@ class HeadShardedFlowModel(FlowModelB200):
         bias = p.bias if self.rank == 0 else self.zero_bias
         self._ok(self.lib.triposplat_b200_gemm_nf24_split_nk(
             split, rows, count, c.data_ptr() + 2 * k0, q.data_ptr() + k0, K,
-            p.scale.data_ptr(), bias.data_ptr(), out.data_ptr(), N, 0, N, N, 0, None, 0, 1),
+            p.scale.data_ptr(), bias.data_ptr(), out_ptr, N, 0, N, N, 0, None, 0, 1),
             f"gemm rows {name}")
+
+    def _part_ptr(self):
+        return self.buf["part"].data_ptr() if self.peer is None else self.peer.part_ptr()
+
+    def _reduce_into_x(self, mode, gate=None):
+        """Sum the ranks' partials into the residual stream: x += gate * sum (mode 2) or
+        x += sum (mode 3).  A generator: the NCCL path yields the partial at the reduction
+        point (see forward_steps); the peer path reduces in place and yields nothing."""
+        x, h, L = self.buf["x"], self.spec.hidden, self.spec.seq
+        if self.peer is not None:
+            self.peer.reduce(x, mode, gate, h, L)
+            return
+        part = self.buf["part"]
+        yield part
+        if mode == 2:
+            self._gated(x, part, gate)
+        else:
+            self._add(x, part)
 
     def _nccl_all_reduce(self, t):
         import torch.distributed as dist
@@ -138,7 +250,7 @@ class HeadShardedFlowModel(FlowModelB200):
         m.copy_(b["mod"])
         self._add(m, self.tables[i])
         shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = (m[j] for j in range(6))
-        x, part = b["x"], b["part"]
+        x = b["x"]
         sph, spo, sphid = self._split_ptr("sp_h"), self._split_ptr("sp_o"), self._split_ptr("sp_hid_l")
         # self-attention over this rank's heads
         self._ln_split(x, sph, shift_msa, scale_msa)
@@ -149,9 +261,8 @@ class HeadShardedFlowModel(FlowModelB200):
             qkv.data_ptr(), self.freqs_l.data_ptr(), g[p + "q_gamma"].data_ptr(),
             g[p + "k_gamma"].data_ptr(), b["o_l"].data_ptr(), B, L, hl, 64, 1), "self_attention")
         self._split(b["o_l"], spo)
-        self._lin_rows(p + "out", spo, rows, *pl["out"], part)
-        yield part
-        self._gated(x, part, gate_msa)
+        self._lin_rows(p + "out", spo, rows, *pl["out"], self._part_ptr())
+        yield from self._reduce_into_x(2, gate_msa)
         # cross-attention over this rank's heads
         self._ln_split(x, sph)
         (c0, n), = pl["cross_q"]
@@ -164,17 +275,22 @@ class HeadShardedFlowModel(FlowModelB200):
             b["yq_l"].data_ptr(), ckv.data_ptr(), g[p + "cq_gamma"].data_ptr(),
             g[p + "ck_gamma"].data_ptr(), b["o_l"].data_ptr(), B, L, Mc, hl), "cross_attention")
         self._split(b["o_l"], spo)
-        self._lin_rows(p + "cross_out", spo, rows, *pl["cross_out"], part)
-        yield part
-        self._add(x, part)
+        self._lin_rows(p + "cross_out", spo, rows, *pl["cross_out"], self._part_ptr())
+        yield from self._reduce_into_x(3)
         # MLP over this rank's hidden columns
         self._ln_split(x, sph, shift_mlp, scale_mlp)
         (c0, n), = pl["fc1"]
         self._lin_cols(p + "fc1", sph, rows, b["hid_l"].data_ptr(), c0, n, n, mode=1)
         self._split(b["hid_l"], sphid)
-        self._lin_rows(p + "fc2", sphid, rows, *pl["fc2"], part)
-        yield part
-        self._gated(x, part, gate_mlp)
+        self._lin_rows(p + "fc2", sphid, rows, *pl["fc2"], self._part_ptr())
+        yield from self._reduce_into_x(2, gate_mlp)
+
+    def close(self):
+        """Release the IPC-shared buffers of the peer path (call before the process group
+        goes away)."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     # collectives per forward: three all-reduces per block
     def all_reduces_per_forward(self) -> int:
