@@ -89,6 +89,7 @@ struct Params {
   int H, Lq, Lk, T;
   int out_blhd;
   int* status;
+  int Qt, BH;  // query tiles per head, heads x batch: work item j = (bh = j / Qt, tile j % Qt)
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -286,7 +287,7 @@ __device__ __forceinline__ void softmax_tile(uint32_t srow, uint32_t orow, bool 
 }
 
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-    sdpa_fwd_tc(const __half* __restrict__ qhi_g, const __half* __restrict__ qlo_g,
+    sdpa_fwd_tc(const __grid_constant__ CUtensorMap tm_qhi, const __grid_constant__ CUtensorMap tm_qlo,
                 const __grid_constant__ CUtensorMap tm_khi, const __grid_constant__ CUtensorMap tm_klo,
                 const __grid_constant__ CUtensorMap tm_vhi, const __grid_constant__ CUtensorMap tm_vlo,
                 const Params p) {
@@ -301,7 +302,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   float* xl = xm + 2 * BQ;             // [2 teams][BQ] final row sums
   float* xo = xl + 2 * BQ;             // [2 teams][BQ][32] output halves for the other team
   uint64_t* bars = reinterpret_cast<uint64_t*>(xo + 2 * BQ * 32);
-  uint64_t* q_full = bars + 0;   // Q rows written to shared memory (8 softmax-warp arrivals)
+  uint64_t* q_full = bars + 0;   // Q tile of the item loaded (TMA bytes)
   uint64_t* k_full = bars + 1;   // [2]
   uint64_t* k_empty = bars + 3;  // [2]
   uint64_t* v_full = bars + 5;   // [2]
@@ -312,17 +313,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* qk_done = bars + 17; // QK issuer's MMAs retired (teardown)
   uint64_t* pv_all = bars + 18;  // P.V issuer's MMAs retired (teardown)
   uint64_t* xbar = bars + 19;    // end-of-row exchange between the teams (8 arrivals)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+  uint64_t* q_empty = bars + 20; // the item's QK MMAs retired: Q shared memory reusable
+  uint64_t* xfree = bars + 21;   // both teams read the exchange buffers (8 arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
-  const int bh = blockIdx.y;
-  const int q0 = blockIdx.x * BQ;
   const int T = p.T;
+  // persistent CTAs: work item j = blockIdx.x + i * gridDim.x (query tiles of one head
+  // consecutive, so CTAs running together share the head's K / V in L2); every role walks
+  // the same items, and stages / barrier phases run on the global tile counter G = i*T + t
+  const int items = p.Qt * p.BH;
+  const int my_items = (int)blockIdx.x < items ? (items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  auto item_of = [&](int i, int& bh, int& q0) {
+    const int j = blockIdx.x + i * gridDim.x;
+    bh = j / p.Qt;
+    q0 = (j - bh * p.Qt) * BQ;
+  };
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 8);
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    mbar_init(xfree, 8);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1);
       mbar_init(&v_full[i], 1); mbar_init(&v_empty[i], 1);
@@ -336,6 +349,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_qhi); tma_prefetch_desc(&tm_qlo);
     tma_prefetch_desc(&tm_khi); tma_prefetch_desc(&tm_klo);
     tma_prefetch_desc(&tm_vhi); tma_prefetch_desc(&tm_vlo);
   }
@@ -358,26 +372,45 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint64_t* empty = is_k ? k_empty : v_empty;
       uint8_t* base = is_k ? k_st : v_st;
       int issued[2] = {-1, -1};
-      for (int t = 0; t < T; ++t) {
-        const int st = t & 1;
-        if (t >= 2 && !mbar_wait(&empty[st], ((t >> 1) & 1) ^ 1, p.status, kDevTimeoutProducer, abort_flag)) break;
-        uint8_t* d = base + st * STAGE;
-        mbar_arrive_expect_tx(&full[st], STAGE);
+      int q_issued = -1;
+      bool ok = true;
+      for (int i = 0; i < my_items && ok; ++i) {
+        int bh, q0;
+        item_of(i, bh, q0);
         if (is_k) {
-          tma_load_3d(d, &tm_khi, &full[st], 0, t * BKV, bh);
-          tma_load_3d(d + PLANE, &tm_klo, &full[st], 0, t * BKV, bh);
-        } else {
-          tma_load_3d(d, &tm_vhi, &full[st], t * BKV, 0, bh);
-          tma_load_3d(d + PLANE / 2, &tm_vhi, &full[st], t * BKV + 64, 0, bh);
-          tma_load_3d(d + PLANE, &tm_vlo, &full[st], t * BKV, 0, bh);
-          tma_load_3d(d + PLANE + PLANE / 2, &tm_vlo, &full[st], t * BKV + 64, 0, bh);
+          // the item's Q tile, once the previous item's QK MMAs have read the old one
+          // (rows past Lq read as zeros)
+          if (i >= 1 && !mbar_wait(q_empty, (i - 1) & 1, p.status, kDevTimeoutProducer, abort_flag)) break;
+          mbar_arrive_expect_tx(q_full, STAGE);
+          tma_load_3d(q_s, &tm_qhi, q_full, 0, q0, bh);
+          tma_load_3d(q_s + PLANE, &tm_qlo, q_full, 0, q0, bh);
+          q_issued = i;
         }
-        issued[st] = t;
+        for (int t = 0; t < T; ++t) {
+          const int G = i * T + t, st = G & 1;
+          if (G >= 2 && !mbar_wait(&empty[st], ((G >> 1) & 1) ^ 1, p.status, kDevTimeoutProducer, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* d = base + st * STAGE;
+          mbar_arrive_expect_tx(&full[st], STAGE);
+          if (is_k) {
+            tma_load_3d(d, &tm_khi, &full[st], 0, t * BKV, bh);
+            tma_load_3d(d + PLANE, &tm_klo, &full[st], 0, t * BKV, bh);
+          } else {
+            tma_load_3d(d, &tm_vhi, &full[st], t * BKV, 0, bh);
+            tma_load_3d(d + PLANE / 2, &tm_vhi, &full[st], t * BKV + 64, 0, bh);
+            tma_load_3d(d + PLANE, &tm_vlo, &full[st], t * BKV, 0, bh);
+            tma_load_3d(d + PLANE + PLANE / 2, &tm_vlo, &full[st], t * BKV + 64, 0, bh);
+          }
+          issued[st] = G;
+        }
       }
       if (*abort_flag) {
         // never leave the CTA while a bulk copy may still write its shared memory
         for (int i = 0; i < 2; ++i)
           if (issued[i] >= 0) mbar_wait(&full[i], (issued[i] >> 1) & 1, p.status, kDevTimeoutProducer, nullptr);
+        if (q_issued >= 0) mbar_wait(q_full, q_issued & 1, p.status, kDevTimeoutProducer, nullptr);
       }
     }
   } else if (warp == 1) {
@@ -387,12 +420,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // team's next tile never wait behind the other team's P.
     if (elect_one()) {
       constexpr uint32_t idesc_s = idesc_f16_f32(BQ, BKV);
-      bool ok = mbar_wait(q_full, 0, p.status, kDevTimeoutMma, abort_flag);
+      bool ok = true;
       const uint32_t qh = smem_u32(q_s), ql = qh + PLANE;
+      for (int i = 0; i < my_items && ok; ++i) {
+      ok = mbar_wait(q_full, i & 1, p.status, kDevTimeoutMma, abort_flag);
       for (int t = 0; t < T && ok; ++t) {
-        const int st = t & 1, sb = t % NSB;
-        ok = mbar_wait(&k_full[st], (t >> 1) & 1, p.status, kDevTimeoutMma, abort_flag) &&
-             (t < NSB || mbar_wait(&pv_done[sb], ((t - NSB) / NSB) & 1, p.status, kDevTimeoutMma, abort_flag));
+        const int G = i * T + t, st = G & 1, sb = G % NSB;
+        ok = mbar_wait(&k_full[st], (G >> 1) & 1, p.status, kDevTimeoutMma, abort_flag) &&
+             (G < NSB || mbar_wait(&pv_done[sb], ((G - NSB) / NSB) & 1, p.status, kDevTimeoutMma, abort_flag));
         if (!ok) break;
         tc_fence_after();
         const uint32_t kh = smem_u32(k_st + st * STAGE), kl = kh + PLANE;
@@ -412,6 +447,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         mma_commit(&k_empty[st]);
         mma_commit(&s_full[sb]);
       }
+      if (ok) mma_commit(q_empty);  // this item's QK MMAs retire -> the next Q may land
+      }
       mma_commit(qk_done);
       mbar_wait(qk_done, 0, p.status, kDevTimeoutMma, nullptr);
     }
@@ -420,14 +457,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (elect_one()) {
       constexpr uint32_t idesc_o = idesc_f16_f32(BQ, D);
       bool ok = true;
+      const int nt0 = (T + 1) / 2, nt1 = T / 2;  // tiles of team 0 / team 1 per item
+      for (int i = 0; i < my_items && ok; ++i)
       for (int t = 0; t < T && ok; ++t) {
-        const int st = t & 1, team = t & 1;
-        ok = mbar_wait(&p_full[team], (t >> 1) & 1, p.status, kDevTimeoutMma, abort_flag) &&
-             mbar_wait(&v_full[st], (t >> 1) & 1, p.status, kDevTimeoutMma, abort_flag);
+        const int G = i * T + t, st = G & 1, team = t & 1;
+        const int c = i * (team ? nt1 : nt0) + (t >> 1);  // the team's global tile count
+        ok = mbar_wait(&p_full[team], c & 1, p.status, kDevTimeoutMma, abort_flag) &&
+             mbar_wait(&v_full[st], (G >> 1) & 1, p.status, kDevTimeoutMma, abort_flag);
         if (!ok) break;
         tc_fence_after();
         const uint32_t vh = smem_u32(v_st + st * STAGE), vl = vh + PLANE;
-        const uint32_t ps = tmem + S_COL + (t % NSB) * BKV;
+        const uint32_t ps = tmem + S_COL + (G % NSB) * BKV;
         const uint32_t od = tmem + O_COL + team * D;
 #pragma unroll 1
         for (int kk = 0; kk < BKV / 16; ++kk) {
@@ -441,7 +481,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           mma_f16_ts(od, pl, b_h, idesc_o, 1);
         }
         mma_commit(&v_empty[st]);
-        mma_commit(&pv_done[t % NSB]);
+        mma_commit(&pv_done[G % NSB]);
       }
       mma_commit(pv_all);
       mbar_wait(pv_all, 0, p.status, kDevTimeoutMma, nullptr);
@@ -454,6 +494,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t sub = warp & 3;
     const int r = sub * 32 + lane;  // query row within the tile == TMEM lane
     const uint32_t trow = tmem + ((sub * 32) << 16);
+    float* bt = bias_s + (warp - 4) * BKV;
+    const uint32_t orow = trow + O_COL + team * D;
+    bool ok = true;
+    for (int i = 0; i < my_items && ok; ++i) {
+    int bh, q0;
+    item_of(i, bh, q0);
     const int qrow = q0 + r;
     const bool row_valid = qrow < p.Lq;
     const float cq = 0.125f * LOG2E * (row_valid ? p.qinv[(int64_t)bh * p.Lq + qrow] : 0.0f);
@@ -462,37 +508,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     float vref = 0.0f;
     for (int t = 0; t < T; ++t) vref = fmaxf(vref, p.vinv[(int64_t)bh * T + t]);
     const int vref_exp = __float_as_int(vref) >> 23;
-    float* bt = bias_s + (warp - 4) * BKV;
-    {
-      // this row's Q plane (team 0: hi, team 1: lo) into shared memory in the MMA's
-      // 128-byte-swizzled K-major layout (16-byte chunk c of row r at chunk c ^ (r & 7))
-      uint8_t* rowp = q_s + team * PLANE + (r >> 3) * 1024 + (r & 7) * 128;
-      const uint4* src = reinterpret_cast<const uint4*>((team == 0 ? qhi_g : qlo_g) + ((int64_t)bh * p.Lq + qrow) * D);
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint4 v = row_valid ? src[c] : make_uint4(0u, 0u, 0u, 0u);
-        *reinterpret_cast<uint4*>(rowp + ((c ^ (r & 7)) << 4)) = v;
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor core
-      __syncwarp();
-      if (lane == 0) mbar_arrive(q_full);
-    }
     float m_run = -INFINITY, l_run = 0.0f;
     float o_acc[D];
 #pragma unroll
     for (int d = 0; d < D; ++d) o_acc[d] = 0.0f;
-    bool ok = true;
-    const uint32_t orow = trow + O_COL + team * D;
-    int n = 0;  // tiles this team has processed
+    int n = 0;  // tiles this team has processed in this item
     for (int t = team; t < T; t += 2, ++n) {
-      const int sb = t % NSB;
+      const int G = i * T + t, sb = G % NSB;
       const bool plain = bias_row == nullptr && (t + 1) * BKV <= p.Lk;  // no bias, no masking
       if (!plain) {
         // key bias (+ -inf past Lk) for this tile, staged in a warp-private buffer
         __syncwarp();
 #pragma unroll
-        for (int i = 0; i < BKV / 32; ++i) {
-          const int jl = i * 32 + lane;
+        for (int ii = 0; ii < BKV / 32; ++ii) {
+          const int jl = ii * 32 + lane;
           const int j = t * BKV + jl;
           bt[jl] = j < p.Lk ? (bias_row ? bias_row[j] * LOG2E : 0.0f) : -INFINITY;
         }
@@ -501,11 +530,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const float c2 = cq * p.kinv[(int64_t)bh * T + t];
       // exponent offset folding this V tile's pre-scale relative to the head reference
       const float vshift = (float)((__float_as_int(p.vinv[(int64_t)bh * T + t]) >> 23) - vref_exp);
-      ok = mbar_wait(&s_full[sb], (t / NSB) & 1, p.status, kDevTimeoutConsumer, abort_flag);
-      // this team's previous O, P.V(t-2), retired long ago; it is folded in with the scores
+      ok = mbar_wait(&s_full[sb], (G / NSB) & 1, p.status, kDevTimeoutConsumer, abort_flag);
+      // this team's previous O, P.V(G-2), retired long ago; it is folded in with the scores
       if (ok && n > 0) {
-        const int tp = t - 2;
-        ok = mbar_wait(&pv_done[tp % NSB], (tp / NSB) & 1, p.status, kDevTimeoutConsumer, abort_flag);
+        const int Gp = G - 2;
+        ok = mbar_wait(&pv_done[Gp % NSB], (Gp / NSB) & 1, p.status, kDevTimeoutConsumer, abort_flag);
       }
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
@@ -520,9 +549,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (lane == 0) mbar_arrive(&p_full[team]);
     }
     if (ok && n > 0) {
-      // the team's last O
-      const int tl = team + 2 * (n - 1);
-      ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[tl % NSB], (tl / NSB) & 1, p.status,
+      // the team's last O of the item
+      const int Gl = i * T + team + 2 * (n - 1);
+      ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[Gl % NSB], (Gl / NSB) & 1, p.status,
                                              kDevTimeoutEpilogue, abort_flag));
       if (ok) {
         tc_fence_after();
@@ -537,6 +566,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
+    // both teams read the previous item's exchange before it is overwritten
+    if (ok && i >= 1)
+      ok = __all_sync(0xffffffffu, mbar_wait(xfree, (i - 1) & 1, p.status, kDevTimeoutEpilogue, abort_flag));
     if (ok) {
       // merge the two teams' partial softmaxes of this row (split-K over the key tiles):
       // common reference m, factors 2^(m_team - m), exact since both references are
@@ -555,7 +587,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(xbar);
-      ok = __all_sync(0xffffffffu, mbar_wait(xbar, 0, p.status, kDevTimeoutEpilogue, abort_flag));
+      ok = __all_sync(0xffffffffu, mbar_wait(xbar, i & 1, p.status, kDevTimeoutEpilogue, abort_flag));
       if (ok && row_valid) {
         const float m_o = xm[(1 - team) * BQ + r], l_o = xl[(1 - team) * BQ + r];
         const float m = fmaxf(m_run, m_o);
@@ -582,7 +614,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                           (res[d + 2] * f_me + ov.z * f_o) * f, (res[d + 3] * f_me + ov.w * f_o) * f);
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(xfree);
     }
+    }  // item loop
   }
 
   tc_fence_before();
@@ -917,9 +952,17 @@ static int sdpa_attend(const SplitPlanesSdpa& sp, const float* bias, int64_t bia
                        float* out, int64_t BH, int H, int Lq, int Lk, int out_blhd,
                        cudaStream_t stream) {
   using namespace sdpa;
-  CUtensorMap m_khi, m_klo, m_vhi, m_vlo;
+  CUtensorMap m_qhi, m_qlo, m_khi, m_klo, m_vhi, m_vlo;
   const uint32_t box_rows[3] = {64, 128, 1};
   const uint32_t box_vt[3] = {64, 64, 1};
+  {
+    // Q planes [BH][Lq][64]: 128-row tiles, rows past Lq of a head read as zeros
+    const uint64_t dims[3] = {D, (uint64_t)Lq, (uint64_t)BH};
+    const uint64_t strides[2] = {D * 2, (uint64_t)Lq * D * 2};
+    if (!encode_tmap(&m_qhi, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, sp.qhi, dims, strides, box_rows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tmap(&m_qlo, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, sp.qlo, dims, strides, box_rows, CU_TENSOR_MAP_SWIZZLE_128B))
+      return kLaunchFailed;
+  }
   {
     const uint64_t dims[3] = {D, (uint64_t)sp.Lkt, (uint64_t)BH};
     const uint64_t strides[2] = {D * 2, (uint64_t)sp.Lkt * D * 2};
@@ -953,12 +996,23 @@ static int sdpa_attend(const SplitPlanesSdpa& sp, const float* bias, int64_t bia
       attr_done |= 1ull << dev;
     }
   }
+  const int Qt = (Lq + BQ - 1) / BQ;
   Params prm{sp.qinv, sp.kinv, sp.vinv, bias, (long long)bias_bh_stride, out, H, Lq, Lk, sp.T, out_blhd,
-             device_status()};
-  dim3 grid((Lq + BQ - 1) / BQ, (unsigned)BH);
+             device_status(), Qt, (int)BH};
+  // persistent: one CTA per SM walking the (head, query tile) items
+  static int sm_count[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (sm_count[dev & 63] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    sm_count[dev & 63] = n > 0 ? n : 148;
+  }
+  const long long items = (long long)Qt * BH;
+  const dim3 grid((unsigned)(items < sm_count[dev & 63] ? items : sm_count[dev & 63]));
   {
     LaunchScope scope(kKSdpaAttn, stream);
-    sdpa_fwd_tc<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(sp.qhi, sp.qlo, m_khi, m_klo, m_vhi, m_vlo, prm);
+    sdpa_fwd_tc<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(m_qhi, m_qlo, m_khi, m_klo, m_vhi, m_vlo, prm);
   }
   return launch_status();
 }
