@@ -504,9 +504,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const bool row_valid = qrow < p.Lq;
     const float cq = 0.125f * LOG2E * (row_valid ? p.qinv[(int64_t)bh * p.Lq + qrow] : 0.0f);
     const float* bias_row = p.bias ? p.bias + (int64_t)bh * p.bias_bh_stride : nullptr;
-    // reference V scale of the head: the largest per-tile inverse pre-scale
+    // reference V scale of the head: the largest per-tile inverse pre-scale (the lanes load
+    // the head's tiles in parallel, then a warp max)
     float vref = 0.0f;
-    for (int t = 0; t < T; ++t) vref = fmaxf(vref, p.vinv[(int64_t)bh * T + t]);
+    for (int t = lane; t < T; t += 32) vref = fmaxf(vref, p.vinv[(int64_t)bh * T + t]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) vref = fmaxf(vref, __shfl_xor_sync(0xffffffffu, vref, o));
     const int vref_exp = __float_as_int(vref) >> 23;
     float m_run = -INFINITY, l_run = 0.0f;
     float o_acc[D];
