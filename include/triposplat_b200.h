@@ -159,6 +159,49 @@ int triposplat_gemm_rnf8_avx512_row_tile(void);
 /* replaces scripts/gemm_nf24_i16_avx512.c:226-228; returns 4 (= nf24_i16) */
 int triposplat_gemm_rnf8_avx512_residual_mode(void);
 
+/* ------------------------------------------------ fused NF24 MLP and QKV projection -----
+ * The reference's fused CPU entry points, on device pointers.  Each stage runs as one
+ * tensor-core launch over all rows; the intermediate (hidden [M, 4096] or qkv [B*L, N])
+ * lives in the library workspace between launches (the chunked MLP uses the caller's
+ * hidden buffer instead). */
+
+/* replaces scripts/native_nf24_mlp_avx512.c:143-205: out = GELU_tanh(x W1 + b1) W2 + b2;
+ * K = 1024, H = 4096, N = 1024 as the reference requires (-1 null, -2 sizes / strides) */
+int triposplat_mlp_nf24_gelu_f32_avx512(const float* x, const uint8_t* w1_code01_t,
+                                        const uint8_t* w1_code2_t, const float* w1_scales,
+                                        const float* w1_bias, const uint8_t* w2_code01_t,
+                                        const uint8_t* w2_code2_t, const float* w2_scales,
+                                        const float* w2_bias, float* out, int M, int K, int H,
+                                        int N, int stride_x, int stride_out, int threads);
+/* replaces scripts/native_nf24_mlp_chunked_avx512.c:3-60: the same over chunks of
+ * chunk_rows rows, hidden [hidden_capacity_rows, H] supplied by the caller (device) */
+int triposplat_mlp_nf24_gelu_chunked_f32_avx512(
+    const float* x, const uint8_t* w1_code01_t, const uint8_t* w1_code2_t,
+    const float* w1_scales, const float* w1_bias, const uint8_t* w2_code01_t,
+    const uint8_t* w2_code2_t, const float* w2_scales, const float* w2_bias, float* hidden,
+    float* out, int M, int K, int H, int N, int stride_x, int stride_out,
+    int hidden_capacity_rows, int chunk_rows, int threads);
+/* replace scripts/native_nf24_mlp_avx512.c:207-213 (row tile of the GEMM; hidden bytes of
+ * one row tile) */
+int triposplat_mlp_nf24_row_tile(void);
+int triposplat_mlp_nf24_hidden_workspace_bytes_per_thread(void);
+/* replaces scripts/gemm_nf24_qkv_direct_avx512.c:87-199: x [B*L, K] . W [K, 3*H*64] + b,
+ * then the RoPE / per-head RMSNorm / pack of
+ * triposplat_qkv_rope_rmsnorm_pack_f32_avx512_v2 (q_bhld [B,H,L,64], packed_k / packed_v
+ * [B,H,64,L_padded], zero tail) */
+int triposplat_gemm_nf24_qkv_rope_rmsnorm_pack_f32_avx512(
+    const float* x, const uint8_t* codes0_t, const uint8_t* codes1_t, const uint8_t* codes2_t,
+    const float* scales0, const float* scales1, const float* scales2, const float* codebook,
+    const float* bias, const float* frequencies, const float* q_gamma, const float* k_gamma,
+    float* q_bhld, float* packed_k, float* packed_v, int B, int L, int K, int N, int H, int D,
+    int L_padded, int frequency_batches, int threads, int stages);
+/* replace scripts/gemm_nf24_qkv_direct_avx512.c:201-207 (row tile; residual mode 4 =
+ * nf24_i16) and scripts/gemm_nf24_qkv_direct_tile_avx512.c:149-151 (qkv bytes of one row
+ * tile) */
+int triposplat_gemm_nf24_qkv_direct_row_tile(void);
+int triposplat_gemm_nf24_qkv_direct_residual_mode(void);
+int triposplat_gemm_nf24_qkv_direct_tile_bytes(void);
+
 /* ---------------------------------------------------------------- exact SDPA ---------
  * O = softmax(0.125 * Q K^T + key_bias) V, head_dim 64, q/k/v/out [B, H, L, 64] fp32. */
 

@@ -303,10 +303,87 @@ def shard_cases(torch):
     pack_nf24_i16_checkpoint(src_path, out, expected_linear_count=3)
 
 
+def mlp_weights(seed):
+    """The fused-MLP fixture's weights, regenerated identically by the tests: numpy's PCG64
+    stream (stable across numpy versions) for W1 [4096, 1024], W2 [1024, 4096] and biases."""
+    g = np.random.default_rng(seed)
+    w1 = (g.standard_normal((4096, 1024), dtype=np.float32) * 0.02).astype(np.float32)
+    w2 = (g.standard_normal((1024, 4096), dtype=np.float32) * 0.02).astype(np.float32)
+    b1 = (g.standard_normal(4096, dtype=np.float32) * 0.01).astype(np.float32)
+    b2 = (g.standard_normal(1024, dtype=np.float32) * 0.01).astype(np.float32)
+    return w1, w2, b1, b2
+
+
+def code_digest(c01, q2):
+    import hashlib
+
+    return hashlib.sha256(np.ascontiguousarray(c01).tobytes() +
+                          np.ascontiguousarray(q2).tobytes()).hexdigest()
+
+
+def fused_cases(torch, pack, codebook):
+    """The reference's fused NF24 entry points: the MLP (plain and chunked,
+    scripts/native_nf24_mlp_avx512.c:143, native_nf24_mlp_chunked_avx512.c:3) and the QKV
+    projection with RoPE / RMSNorm / pack (scripts/gemm_nf24_qkv_direct_avx512.c:87)."""
+    mlp = ctypes.CDLL(str(REF_LIBS / "libref_mlp_nf24.so"))
+    qkvd = ctypes.CDLL(str(REF_LIBS / "libref_gemm_nf24_qkv_direct.so"))
+    plain = bind(mlp, "triposplat_mlp_nf24_gelu_f32_avx512", [VP] * 10 + [I] * 7)
+    chunked = bind(mlp, "triposplat_mlp_nf24_gelu_chunked_f32_avx512", [VP] * 11 + [I] * 9)
+    direct = bind(qkvd, "triposplat_gemm_nf24_qkv_rope_rmsnorm_pack_f32_avx512",
+                  [VP] * 15 + [I] * 10)
+    cb = codebook.numpy()
+
+    # MLP: 11 rows (one 8-row tile + 3 tail rows), padded row strides
+    M, sx, so = 11, 1040, 1056
+    w1, w2, b1, b2 = mlp_weights(41)
+    packed = []
+    for w in (w1, w2):
+        codes, scales, _ = pack(torch.from_numpy(w), codebook)
+        packed.append((codes[0].numpy(), codes[1].numpy(), scales[0].numpy()))
+    (c1, q1, s1), (c2, q2, s2) = packed
+    x = (np.random.default_rng(42).standard_normal((M, sx), dtype=np.float32)).astype(np.float32)
+    out = np.full((M, so), 5.0, np.float32)
+    check(plain(ptr(x), ptr(c1), ptr(q1), ptr(s1), ptr(b1), ptr(c2), ptr(q2), ptr(s2), ptr(b2),
+                ptr(out), M, 1024, 4096, 1024, sx, so, 2), "mlp")
+    out_c = np.full((M, so), 5.0, np.float32)
+    hidden = np.zeros((5, 4096), np.float32)
+    check(chunked(ptr(x), ptr(c1), ptr(q1), ptr(s1), ptr(b1), ptr(c2), ptr(q2), ptr(s2), ptr(b2),
+                  ptr(hidden), ptr(out_c), M, 1024, 4096, 1024, sx, so, 5, 4, 2), "mlp_chunked")
+    np.savez_compressed(HERE / "mlp_nf24.npz", x=x, out=out, out_chunked=out_c, seed=41,
+                        w1_digest=code_digest(c1, q1), w2_digest=code_digest(c2, q2),
+                        stride_x=sx, stride_out=so, chunk_rows=4, hidden_rows=5)
+
+    # QKV projection: B 2, L 11 (padded to 16), K 96, H 2 (N = 384), per-batch frequencies
+    B, L, K, H, D, Lp = 2, 11, 96, 2, 64, 16
+    N = 3 * H * D
+    torch.manual_seed(77)
+    xq = torch.randn(B * L, K, dtype=torch.float32).numpy()
+    w = torch.randn(N, K, dtype=torch.float32) * 0.05
+    bq = (torch.randn(N, dtype=torch.float32) * 0.01).numpy()
+    codes, scales, _ = pack(w, codebook)
+    cq, qq, sq = codes[0].numpy(), codes[1].numpy(), scales[0].numpy()
+    data = dict(x=xq, code01_t=cq, q2_t=qq, scale=sq, bias=bq)
+    rng = np.random.default_rng(78)
+    for fb in (1, B):
+        ang = rng.uniform(0.0, 6.0, (fb, L, H, D // 2)).astype(np.float32)
+        freqs = np.stack([np.cos(ang), np.sin(ang)], -1).reshape(fb, L, H, D).astype(np.float32)
+        qg = (1.0 + 0.1 * rng.standard_normal((H, D))).astype(np.float32)
+        kg = (1.0 + 0.1 * rng.standard_normal((H, D))).astype(np.float32)
+        qo = np.empty((B, H, L, D), np.float32)
+        pk = np.full((B, H, D, Lp), 7.0, np.float32)
+        pv = np.full((B, H, D, Lp), 7.0, np.float32)
+        check(direct(ptr(xq), ptr(cq), ptr(qq), ptr(qq), ptr(sq), ptr(sq), ptr(sq), ptr(cb),
+                     ptr(bq), ptr(freqs), ptr(qg), ptr(kg), ptr(qo), ptr(pk), ptr(pv),
+                     B, L, K, N, H, D, Lp, fb, 2, 3), f"qkv_direct fb={fb}")
+        data.update({f"freqs{fb}": freqs, f"qg{fb}": qg, f"kg{fb}": kg, f"q{fb}": qo,
+                     f"pk{fb}": pk, f"pv{fb}": pv})
+    np.savez_compressed(HERE / "qkv_direct.npz", **data)
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, type=Path)
-    ap.add_argument("--cases", default="gemm,sdpa,elementwise,embeddings,shards",
+    ap.add_argument("--cases", default="gemm,sdpa,elementwise,embeddings,shards,fused",
                     help="comma-separated subset of the fixture groups to (re)write")
     args = ap.parse_args()
     cases = set(args.cases.split(","))
@@ -332,6 +409,8 @@ def main() -> int:
         embedding_cases(torch)
     if "shards" in cases:
         shard_cases(torch)
+    if "fused" in cases:
+        fused_cases(torch, pack, codebook)
     print("golden fixtures written to", HERE)
     return 0
 

@@ -79,3 +79,55 @@ def test_embeddings_oracle_bit_exact(oracle, golden):
     np.testing.assert_array_equal(oracle.mul(g["mul_lhs"], g["mul_rhs"]), g["mul_out"])
     np.testing.assert_array_equal(
         oracle.ab2_update(g["ab2_x"], g["ab2_v"], g["ab2_vp"], g["ab2_dt"], g["ab2_pdt"]), g["ab2_out"])
+
+
+def _make_golden():
+    import importlib.util
+    from pathlib import Path
+
+    path = Path(__file__).resolve().parent / "golden" / "make_golden.py"
+    spec = importlib.util.spec_from_file_location("make_golden", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_fused_mlp_oracle(oracle, golden):
+    """fc1 -> GELU -> fc2 composed from the oracle's GEMM and GELU equals the reference's
+    fused MLP (plain and chunked) on the fixture; the codes this repository's packer makes
+    from the regenerated weights are the reference packer's (digest)."""
+    import torch
+    from nf24_pack import quantize_nf24_i16_per_output_channel
+
+    g = golden("mlp_nf24")
+    mg = _make_golden()
+    w1, w2, b1, b2 = mg.mlp_weights(int(g["seed"]))
+    packed = []
+    for w, digest in ((w1, g["w1_digest"]), (w2, g["w2_digest"])):
+        codes, scales, _ = quantize_nf24_i16_per_output_channel(torch.from_numpy(w))
+        c, q, s = codes[0].numpy(), codes[1].numpy(), scales[0].numpy()
+        assert mg.code_digest(c, q) == str(digest)
+        packed.append((c, q, s))
+    (c1, q1, s1), (c2, q2, s2) = packed
+    x = g["x"][:, :1024]
+    y = oracle.gemm_nf24(oracle.gelu_tanh(oracle.gemm_nf24(x, c1, q1, s1, b1)), c2, q2, s2, b2)
+    # same GEMM order; the GELU's tanh differs from the reference's polynomial by ~1e-7
+    np.testing.assert_allclose(y, g["out"][:, :1024], rtol=2e-5, atol=2e-5)
+    np.testing.assert_array_equal(g["out"], g["out_chunked"])
+    assert (g["out"][:, 1024:] == 5.0).all()  # row padding untouched
+
+
+def test_qkv_direct_oracle(oracle, golden):
+    """The reference's fused QKV projection equals the oracle's GEMM followed by its
+    RoPE / RMSNorm / pack restatement, with shared and per-batch frequencies."""
+    g = golden("qkv_direct")
+    B, H, D = 2, 2, 64
+    qkv = oracle.gemm_nf24(g["x"], g["code01_t"], g["q2_t"], g["scale"], g["bias"])
+    L = qkv.shape[0] // B
+    qkv = qkv.reshape(B, L, 3, H, D)
+    for fb in (1, B):
+        q, pk, pv = oracle.qkv_rope_rmsnorm_pack(qkv, g[f"freqs{fb}"], g[f"qg{fb}"],
+                                                 g[f"kg{fb}"], Lp=16)
+        np.testing.assert_allclose(q, g[f"q{fb}"], rtol=2e-6, atol=2e-6)
+        np.testing.assert_allclose(pk, g[f"pk{fb}"], rtol=2e-6, atol=2e-6)
+        np.testing.assert_array_equal(pv, g[f"pv{fb}"])

@@ -42,6 +42,15 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "triposplat_gemm_rnf8_avx512_tail": ([VP] * 10 + [I] * 7, I),
     "triposplat_gemm_rnf8_avx512_row_tile": ([], I),
     "triposplat_gemm_rnf8_avx512_residual_mode": ([], I),
+    # fused MLP / QKV projection
+    "triposplat_mlp_nf24_gelu_f32_avx512": ([VP] * 10 + [I] * 7, I),
+    "triposplat_mlp_nf24_gelu_chunked_f32_avx512": ([VP] * 11 + [I] * 9, I),
+    "triposplat_mlp_nf24_row_tile": ([], I),
+    "triposplat_mlp_nf24_hidden_workspace_bytes_per_thread": ([], I),
+    "triposplat_gemm_nf24_qkv_rope_rmsnorm_pack_f32_avx512": ([VP] * 15 + [I] * 10, I),
+    "triposplat_gemm_nf24_qkv_direct_row_tile": ([], I),
+    "triposplat_gemm_nf24_qkv_direct_residual_mode": ([], I),
+    "triposplat_gemm_nf24_qkv_direct_tile_bytes": ([], I),
     "triposplat_gemm_nf24_noalloc": ([VP] * 10 + [I] * 7, I),
     "triposplat_b200_split_bytes": ([I, I], ctypes.c_uint64),
     "triposplat_b200_split_f32": ([VP, I, I, I, VP], I),

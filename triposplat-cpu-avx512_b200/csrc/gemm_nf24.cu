@@ -1356,3 +1356,211 @@ int triposplat_gemm_nf24_noalloc(const float* x, const uint8_t* codes0_t, const 
 }
 
 }  // extern "C"
+
+// ===========================================================================
+// The reference's fused NF24 entry points: the MLP (fc1 -> GELU(tanh) -> fc2,
+// scripts/native_nf24_mlp_avx512.c:143-205 and the chunked variant
+// scripts/native_nf24_mlp_chunked_avx512.c:3-60) and the QKV projection with its
+// RoPE / RMSNorm / pack epilogue (scripts/gemm_nf24_qkv_direct_avx512.c:87-199).
+// Same names, argument lists and status codes.  On the GPU the CPU's per-row-tile
+// fusion (a hidden tile kept in cache) is not the win: each stage is one persistent
+// tensor-core launch over all rows, and the intermediate (hidden [M, H] or qkv [M, N])
+// lives in the library workspace -- or, for the chunked MLP, in the caller's hidden
+// buffer -- between launches.
+// ===========================================================================
+extern "C" int triposplat_qkv_rope_rmsnorm_pack_f32_avx512_v2(
+    const float* qkv, const float* frequencies, const float* q_gamma, const float* k_gamma,
+    float* q_bhld, float* packed_k, float* packed_v, int B, int L, int H, int D, int L_padded,
+    int frequency_batches, int threads);
+extern "C" int triposplat_gelu_tanh_f32_avx512(const float* input, float* output, int64_t count,
+                                               int threads);
+
+namespace tsb {
+
+constexpr int kMlpIn = 1024, kMlpHidden = 4096, kMlpOut = 1024;  // native_nf24_mlp_avx512.c:9-15
+
+// One NF24 Linear of fp32 rows x [M, K] (row stride stride_x) into out [M, N] (row stride
+// stride_out), optionally GELU(tanh) applied to the result.  Tensor-core path through the
+// split planes at split_ws (split_bytes(M, K) bytes) when the code planes and the output
+// allow TMA; otherwise the SIMT kernel (then GELU as a separate pass, which needs a
+// contiguous output).
+static int linear_rows(const float* x, int stride_x, int M, int K, const int16_t* c01,
+                       const int8_t* q2, const float* scale, const float* bias, float* out, int N,
+                       int stride_out, bool gelu, uint8_t* split_ws, cudaStream_t stream) {
+  using namespace gemm;
+  const bool tc = (N % 16) == 0 && (stride_out % 4) == 0 &&
+                  ((reinterpret_cast<uintptr_t>(c01) | reinterpret_cast<uintptr_t>(q2) |
+                    reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+  int st;
+  if (tc) {
+    const SplitPlanes sp = split_layout(split_ws, M, K);
+    if ((st = launch_split(x, stride_x, sp, stream)) != kOk) return st;
+    EpilogueArgs ep;
+    ep.mode = gelu ? kGelu : kStore;
+    return launch_tc(sp, c01, q2, scale, bias, out, N, 0, N, stride_out, ep, device_status(),
+                     stream);
+  }
+  if (gelu && stride_out != N) return kBadAlignment;
+  {
+    dim3 grid((N + 127) / 128, M);
+    LaunchScope scope(kKGemmSimt, stream);
+    nf24_gemm_simt<<<grid, 128, 0, stream>>>(x, c01, q2, scale, bias, out, M, K, N, 0, N,
+                                             stride_x, stride_out);
+  }
+  if ((st = launch_status()) != kOk || !gelu) return st;
+  return triposplat_gelu_tanh_f32_avx512(out, out, (int64_t)M * N, 0);
+}
+
+// fc1 -> GELU -> fc2 over `rows` rows; hidden [rows, H] contiguous; workspace split planes
+// for the fc1 input and the fc2 input.
+static int mlp_rows(const float* x, int stride_x, int rows, const int16_t* w1c, const int8_t* w1q,
+                    const float* w1s, const float* w1b, const int16_t* w2c, const int8_t* w2q,
+                    const float* w2s, const float* w2b, float* hidden, float* out, int stride_out,
+                    uint8_t* split_x, uint8_t* split_h, cudaStream_t stream) {
+  int st = linear_rows(x, stride_x, rows, kMlpIn, w1c, w1q, w1s, w1b, hidden, kMlpHidden,
+                       kMlpHidden, true, split_x, stream);
+  if (st != kOk) return st;
+  return linear_rows(hidden, kMlpHidden, rows, kMlpHidden, w2c, w2q, w2s, w2b, out, kMlpOut,
+                     stride_out, false, split_h, stream);
+}
+
+static bool mlp_device_pointers(const void* const* p, int n) {
+  for (int i = 0; i < n; ++i)
+    if (!is_device_pointer(p[i])) return false;
+  return true;
+}
+
+}  // namespace tsb
+
+extern "C" {
+
+// scripts/native_nf24_mlp_avx512.c:143-205: out = GELU_tanh(x W1 + b1) W2 + b2 for
+// K = 1024, H = 4096, N = 1024 (the reference's fixed sizes and checks: -1 null, -2 sizes
+// or strides).  The hidden activations live in the library workspace (M x 4096 floats).
+int triposplat_mlp_nf24_gelu_f32_avx512(const float* x, const uint8_t* w1_code01_t,
+                                        const uint8_t* w1_code2_t, const float* w1_scales,
+                                        const float* w1_bias, const uint8_t* w2_code01_t,
+                                        const uint8_t* w2_code2_t, const float* w2_scales,
+                                        const float* w2_bias, float* out, int M, int K, int H,
+                                        int N, int stride_x, int stride_out, int threads) {
+  using namespace tsb;
+  (void)threads;
+  if (!x || !w1_code01_t || !w1_code2_t || !w1_scales || !w1_bias || !w2_code01_t ||
+      !w2_code2_t || !w2_scales || !w2_bias || !out)
+    return kNullPointer;
+  if (M <= 0 || K != kMlpIn || H != kMlpHidden || N != kMlpOut || stride_x < K ||
+      stride_out < N)
+    return kBadDims;
+  int st = entry_check();
+  if (st != kOk) return st;
+  const void* ptrs[] = {x, w1_code01_t, w1_code2_t, w1_scales, w1_bias, w2_code01_t,
+                        w2_code2_t, w2_scales, w2_bias, out};
+  if (!mlp_device_pointers(ptrs, 10)) return kNotDevicePointer;
+  cudaStream_t stream = current_stream();
+  const size_t sx = align256(split_bytes(M, K)), hb = align256((size_t)M * H * 4);
+  uint8_t* ws = static_cast<uint8_t*>(workspace(sx + hb + split_bytes(M, H), stream));
+  if (!ws) return kWorkspace;
+  return mlp_rows(x, stride_x, M, reinterpret_cast<const int16_t*>(w1_code01_t),
+                  reinterpret_cast<const int8_t*>(w1_code2_t), w1_scales, w1_bias,
+                  reinterpret_cast<const int16_t*>(w2_code01_t),
+                  reinterpret_cast<const int8_t*>(w2_code2_t), w2_scales, w2_bias,
+                  reinterpret_cast<float*>(ws + sx), out, stride_out, ws, ws + sx + hb, stream);
+}
+
+// scripts/native_nf24_mlp_chunked_avx512.c:3-60: the same MLP over chunks of chunk_rows
+// rows, the hidden activations of a chunk in the caller's buffer hidden
+// [hidden_capacity_rows, H] (device memory); -2 also for chunk_rows <= 0 or
+// hidden_capacity_rows < chunk_rows.
+int triposplat_mlp_nf24_gelu_chunked_f32_avx512(
+    const float* x, const uint8_t* w1_code01_t, const uint8_t* w1_code2_t,
+    const float* w1_scales, const float* w1_bias, const uint8_t* w2_code01_t,
+    const uint8_t* w2_code2_t, const float* w2_scales, const float* w2_bias, float* hidden,
+    float* out, int M, int K, int H, int N, int stride_x, int stride_out,
+    int hidden_capacity_rows, int chunk_rows, int threads) {
+  using namespace tsb;
+  (void)threads;
+  if (!x || !w1_code01_t || !w1_code2_t || !w1_scales || !w1_bias || !w2_code01_t ||
+      !w2_code2_t || !w2_scales || !w2_bias || !hidden || !out)
+    return kNullPointer;
+  if (M <= 0 || K != kMlpIn || H != kMlpHidden || N != kMlpOut || stride_x < K ||
+      stride_out < N || chunk_rows <= 0 || hidden_capacity_rows < chunk_rows)
+    return kBadDims;
+  int st = entry_check();
+  if (st != kOk) return st;
+  const void* ptrs[] = {x, w1_code01_t, w1_code2_t, w1_scales, w1_bias, w2_code01_t,
+                        w2_code2_t, w2_scales, w2_bias, hidden, out};
+  if (!mlp_device_pointers(ptrs, 11)) return kNotDevicePointer;
+  cudaStream_t stream = current_stream();
+  const int cr = chunk_rows < M ? chunk_rows : M;
+  const size_t sx = align256(split_bytes(cr, K));
+  uint8_t* ws = static_cast<uint8_t*>(workspace(sx + split_bytes(cr, H), stream));
+  if (!ws) return kWorkspace;
+  for (int start = 0; start < M; start += cr) {
+    const int rows = start + cr <= M ? cr : M - start;
+    st = mlp_rows(x + (int64_t)start * stride_x, stride_x, rows,
+                  reinterpret_cast<const int16_t*>(w1_code01_t),
+                  reinterpret_cast<const int8_t*>(w1_code2_t), w1_scales, w1_bias,
+                  reinterpret_cast<const int16_t*>(w2_code01_t),
+                  reinterpret_cast<const int8_t*>(w2_code2_t), w2_scales, w2_bias, hidden,
+                  out + (int64_t)start * stride_out, stride_out, ws, ws + sx, stream);
+    if (st != kOk) return st;
+  }
+  return kOk;
+}
+
+// scripts/native_nf24_mlp_avx512.c:207-213
+int triposplat_mlp_nf24_row_tile(void) { return tsb::gemm::BM; }
+int triposplat_mlp_nf24_hidden_workspace_bytes_per_thread(void) {
+  return tsb::gemm::BM * tsb::kMlpHidden * (int)sizeof(float);  // one row tile's hidden rows
+}
+
+// scripts/gemm_nf24_qkv_direct_avx512.c:87-199: qkv = x W + b (x [B*L, K] contiguous,
+// W [K, N = 3*H*64]) followed by the RoPE / per-head RMSNorm / pack of
+// triposplat_qkv_rope_rmsnorm_pack_f32_avx512_v2: q_bhld [B, H, L, 64], packed_k / packed_v
+// [B, H, 64, L_padded] with a zero tail.  Status codes as the reference (-1 null; -2 sizes,
+// N != 3*H*D, D != 64, L_padded < L or % 16, frequency_batches not 1 or B, stages != 3).
+// qkv [B*L, N] lives in the library workspace between the two launches.
+int triposplat_gemm_nf24_qkv_rope_rmsnorm_pack_f32_avx512(
+    const float* x, const uint8_t* codes0_t, const uint8_t* codes1_t, const uint8_t* codes2_t,
+    const float* scales0, const float* scales1, const float* scales2, const float* codebook,
+    const float* bias, const float* frequencies, const float* q_gamma, const float* k_gamma,
+    float* q_bhld, float* packed_k, float* packed_v, int B, int L, int K, int N, int H, int D,
+    int L_padded, int frequency_batches, int threads, int stages) {
+  using namespace tsb;
+  (void)threads;
+  if (!x || !codes0_t || !codes1_t || !codes2_t || !scales0 || !scales1 || !scales2 ||
+      !codebook || !bias || !frequencies || !q_gamma || !k_gamma || !q_bhld || !packed_k ||
+      !packed_v)
+    return kNullPointer;
+  if (B <= 0 || L <= 0 || K <= 0 || H <= 0 || D != 64 || (int64_t)N != 3LL * H * D ||
+      L_padded < L || (L_padded & 15) != 0 || (frequency_batches != 1 && frequency_batches != B) ||
+      stages != 3 || (int64_t)B * L > 0x7fffffffLL)
+    return kBadDims;
+  int st = entry_check();
+  if (st != kOk) return st;
+  const void* ptrs[] = {x, codes0_t, codes1_t, scales0, bias, frequencies, q_gamma, k_gamma,
+                        q_bhld, packed_k, packed_v};
+  if (!mlp_device_pointers(ptrs, 11)) return kNotDevicePointer;
+  cudaStream_t stream = current_stream();
+  const int M = B * L;
+  const size_t qb = align256((size_t)M * N * 4);
+  uint8_t* ws = static_cast<uint8_t*>(workspace(qb + split_bytes(M, K), stream));
+  if (!ws) return kWorkspace;
+  float* qkv = reinterpret_cast<float*>(ws);
+  st = linear_rows(x, K, M, K, reinterpret_cast<const int16_t*>(codes0_t),
+                   reinterpret_cast<const int8_t*>(codes1_t), scales0, bias, qkv, N, N, false,
+                   ws + qb, stream);
+  if (st != kOk) return st;
+  return triposplat_qkv_rope_rmsnorm_pack_f32_avx512_v2(qkv, frequencies, q_gamma, k_gamma, q_bhld,
+                                                        packed_k, packed_v, B, L, H, D, L_padded,
+                                                        frequency_batches, 0);
+}
+
+// scripts/gemm_nf24_qkv_direct_avx512.c:201-207 and gemm_nf24_qkv_direct_tile_avx512.c:149-151
+int triposplat_gemm_nf24_qkv_direct_row_tile(void) { return tsb::gemm::BM; }
+int triposplat_gemm_nf24_qkv_direct_residual_mode(void) { return 4; }
+int triposplat_gemm_nf24_qkv_direct_tile_bytes(void) {
+  return tsb::gemm::BM * 3072 * (int)sizeof(float);  // one row tile of the 3072-wide qkv
+}
+
+}  // extern "C"
