@@ -57,7 +57,7 @@ def parse():
                     help="head-sharded tensor parallelism: each model (the CFG pair, or one "
                          "branch with --parallel cfg) runs on this many GPUs, heads and MLP "
                          "columns split, three NCCL all-reduces per block")
-    ap.add_argument("--tp-reduce", choices=("peer", "nccl"), default="nccl",
+    ap.add_argument("--tp-reduce", choices=("peer", "nccl"), default="peer",
                     help="peer: the ranks' partials are summed into the residual by one kernel "
                          "reading NVLink peer memory; nccl: NCCL all-reduce + residual kernel")
     ap.add_argument("--no-graph", action="store_true",
