@@ -17,6 +17,18 @@ pytestmark = pytest.mark.gpu
 
 TOL = dict(rtol=2e-5, atol=2e-5)
 
+# (M, K, H, N, stride_x, stride_out) the reference's MLP rejects with -2
+# (scripts/native_nf24_mlp_avx512.c:164-165); tests/test_reference_status_codes.py checks
+# the reference library returns -2 for the same rows
+MLP_BAD_SIZES = ((0, 1024, 4096, 1024, 1024, 1024), (4, 512, 4096, 1024, 1024, 1024),
+                 (4, 1024, 2048, 1024, 1024, 1024), (4, 1024, 4096, 1024, 1000, 1024),
+                 (4, 1024, 4096, 1024, 1024, 1000))
+# (B, L, K, N, H, D, L_padded, frequency_batches, stages) rejected with -2 by the fused QKV
+# projection (scripts/gemm_nf24_qkv_direct_avx512.c:117-119); base case B 1, L 4, K 64, H 1
+QKV_BAD_SIZES = ((1, 4, 64, 208, 1, 64, 16, 1, 3), (1, 4, 64, 192, 1, 32, 16, 1, 3),
+                 (1, 4, 64, 192, 1, 64, 8, 1, 3), (1, 20, 64, 192, 1, 64, 24, 1, 3),
+                 (1, 4, 64, 192, 1, 64, 16, 3, 3), (1, 4, 64, 192, 1, 64, 16, 1, 2))
+
 
 def _dev(a):
     return torch.from_numpy(np.ascontiguousarray(a)).cuda()
@@ -98,9 +110,7 @@ def test_mlp_status_codes():
     f = lib.triposplat_mlp_nf24_gelu_f32_avx512
     assert f(*p, 4, 1024, 4096, 1024, 1024, 1024, 0) == 0
     assert f(*(p[:9] + [None]), 4, 1024, 4096, 1024, 1024, 1024, 0) == -1
-    for args in ((0, 1024, 4096, 1024, 1024, 1024), (4, 512, 4096, 1024, 1024, 1024),
-                 (4, 1024, 2048, 1024, 1024, 1024), (4, 1024, 4096, 1024, 1000, 1024),
-                 (4, 1024, 4096, 1024, 1024, 1000)):
+    for args in MLP_BAD_SIZES:
         assert f(*p, *args, 0) == -2, args
     host = np.zeros((4, 1024), np.float32)
     assert f(*([host.ctypes.data] + p[1:]), 4, 1024, 4096, 1024, 1024, 1024, 0) == -9
@@ -168,9 +178,7 @@ def test_qkv_direct_status_codes():
     p = [a.data_ptr() for a in p]
     assert f(*p, B, L, K, N, H, D, Lp, 1, 0, 3) == 0
     assert f(*(p[:14] + [None]), B, L, K, N, H, D, Lp, 1, 0, 3) == -1
-    for args in ((B, L, K, N + 16, H, D, Lp, 1, 3), (B, L, K, N, H, 32, Lp, 1, 3),
-                 (B, L, K, N, H, D, 8, 1, 3), (B, 20, K, N, H, D, 24, 1, 3),
-                 (B, L, K, N, H, D, Lp, 3, 3), (B, L, K, N, H, D, Lp, 1, 2)):
+    for args in QKV_BAD_SIZES:
         a = list(args)
         assert f(*p, *a[:8], 0, a[8]) == -2, args
     torch.cuda.synchronize()
