@@ -1424,7 +1424,7 @@ static int mlp_rows(const float* x, int stride_x, int rows, const int16_t* w1c, 
                      stride_out, false, split_h, stream);
 }
 
-static bool mlp_device_pointers(const void* const* p, int n) {
+static bool all_device_pointers(const void* const* p, int n) {
   for (int i = 0; i < n; ++i)
     if (!is_device_pointer(p[i])) return false;
   return true;
@@ -1455,7 +1455,7 @@ int triposplat_mlp_nf24_gelu_f32_avx512(const float* x, const uint8_t* w1_code01
   if (st != kOk) return st;
   const void* ptrs[] = {x, w1_code01_t, w1_code2_t, w1_scales, w1_bias, w2_code01_t,
                         w2_code2_t, w2_scales, w2_bias, out};
-  if (!mlp_device_pointers(ptrs, 10)) return kNotDevicePointer;
+  if (!all_device_pointers(ptrs, 10)) return kNotDevicePointer;
   cudaStream_t stream = current_stream();
   const size_t sx = align256(split_bytes(M, K)), hb = align256((size_t)M * H * 4);
   uint8_t* ws = static_cast<uint8_t*>(workspace(sx + hb + split_bytes(M, H), stream));
@@ -1489,7 +1489,7 @@ int triposplat_mlp_nf24_gelu_chunked_f32_avx512(
   if (st != kOk) return st;
   const void* ptrs[] = {x, w1_code01_t, w1_code2_t, w1_scales, w1_bias, w2_code01_t,
                         w2_code2_t, w2_scales, w2_bias, hidden, out};
-  if (!mlp_device_pointers(ptrs, 11)) return kNotDevicePointer;
+  if (!all_device_pointers(ptrs, 11)) return kNotDevicePointer;
   cudaStream_t stream = current_stream();
   const int cr = chunk_rows < M ? chunk_rows : M;
   const size_t sx = align256(split_bytes(cr, K));
@@ -1540,7 +1540,7 @@ int triposplat_gemm_nf24_qkv_rope_rmsnorm_pack_f32_avx512(
   if (st != kOk) return st;
   const void* ptrs[] = {x, codes0_t, codes1_t, scales0, bias, frequencies, q_gamma, k_gamma,
                         q_bhld, packed_k, packed_v};
-  if (!mlp_device_pointers(ptrs, 11)) return kNotDevicePointer;
+  if (!all_device_pointers(ptrs, 11)) return kNotDevicePointer;
   cudaStream_t stream = current_stream();
   const int M = B * L;
   const size_t qb = align256((size_t)M * N * 4);
