@@ -295,6 +295,18 @@ int triposplat_qkv_rope_rmsnorm_pack_f32_avx512_v2(const float* qkv, const float
                                                    float* packed_v, int B, int L, int H, int D,
                                                    int L_padded, int frequency_batches,
                                                    int threads);
+/* replaces scripts/native_qkv_postprocess_avx512.c:23-116 (the first version: same
+ * arguments and results as _v2) */
+int triposplat_qkv_rope_rmsnorm_pack_f32_avx512(const float* qkv, const float* frequencies,
+                                                const float* q_gamma, const float* k_gamma,
+                                                float* q_bhld, float* packed_k, float* packed_v,
+                                                int B, int L, int H, int D, int L_padded,
+                                                int frequency_batches, int threads);
+/* replace scripts/native_qkv_postprocess_avx512.c:118-120 (tokens per work tile) and
+ * scripts/native_qkv_postprocess_v2_avx512.c:193-195 (returns 1: only the packed tail is
+ * cleared) */
+int triposplat_qkv_postprocess_token_tile(void);
+int triposplat_qkv_postprocess_v2_tail_only_clear(void);
 /* replaces scripts/native_qkv_postprocess_v2_avx512.c:107-191 (selected_indices is a
  * device pointer; it is copied back once to validate it as the reference does) */
 int triposplat_q_kv_selected_rope_rmsnorm_pack_f32_avx512_v2(

@@ -60,6 +60,34 @@ def test_qkv_postprocess(golden):
     np.testing.assert_array_equal(h(pv), g["post_pv"])
 
 
+def test_qkv_postprocess_first_version_symbol(golden):
+    """triposplat_qkv_rope_rmsnorm_pack_f32_avx512 (the reference's first version, same
+    arguments) gives the bits of _v2, zero tail included; the aux queries answer."""
+    import _native
+
+    lib = _native.load()
+    g = golden("elementwise")
+    qkv = c(g["post_qkv"])
+    B, L, _, H, D = (int(x) for x in qkv.shape)
+    fr, qg, kg = c(g["post_freqs"]), c(g["post_qg"]), c(g["post_kg"])
+    outs = []
+    for name in ("triposplat_qkv_rope_rmsnorm_pack_f32_avx512",
+                 "triposplat_qkv_rope_rmsnorm_pack_f32_avx512_v2"):
+        q = torch.full((B, H, L, D), 3.0, device="cuda")
+        pk = torch.full((B, H, D, 32), 3.0, device="cuda")
+        pv = torch.full((B, H, D, 32), 3.0, device="cuda")
+        assert getattr(lib, name)(qkv.data_ptr(), fr.data_ptr(), qg.data_ptr(), kg.data_ptr(),
+                                  q.data_ptr(), pk.data_ptr(), pv.data_ptr(), B, L, H, D, 32,
+                                  int(fr.shape[0]), 0) == 0
+        outs.append((h(q), h(pk), h(pv)))
+    for a, b in zip(*outs):
+        np.testing.assert_array_equal(a, b)
+    np.testing.assert_allclose(outs[0][0], g["post_q"], **TOL)
+    np.testing.assert_array_equal(outs[0][2], g["post_pv"])
+    assert lib.triposplat_qkv_postprocess_token_tile() > 0
+    assert lib.triposplat_qkv_postprocess_v2_tail_only_clear() == 1
+
+
 def test_qkv_selected_postprocess(oracle, golden):
     """Selected-query variant: queries use the frequency row of their selected token."""
     g = golden("elementwise")

@@ -1,6 +1,7 @@
-"""The reference's own fused libraries (oracle/_ref, compiled from its sources) return the
+"""The reference's own libraries (oracle/_ref, compiled from its sources) return the
 status codes this library's GPU tests expect for the same invalid arguments
-(tests/test_fused_entries_gpu.py), so the two agree on error behaviour.  CPU only; skipped
+(tests/test_fused_entries_gpu.py), so the two agree on error behaviour; its first-version
+QKV post-process equals its _v2, which this library exports under both names.  CPU only; skipped
 where oracle/_ref was not built (it needs the reference checkout and an AVX-512 host)."""
 import ctypes
 
@@ -68,3 +69,23 @@ def test_reference_qkv_direct_status_codes():
     for args in QKV_BAD_SIZES:
         a = list(args)
         assert f(*p, *a[:8], 1, a[8]) == -2, args
+
+
+def test_reference_postprocess_first_version_equals_v2(golden):
+    """The reference's first post-process (scripts/native_qkv_postprocess_avx512.c:23) gives
+    the bits of its _v2 on the fixture, so one implementation serves both names."""
+    lib = _lib("libref_qkv_postprocess_v1.so")
+    f = lib.triposplat_qkv_rope_rmsnorm_pack_f32_avx512
+    f.argtypes, f.restype = [VP] * 7 + [I] * 7, I
+    g = golden("elementwise")
+    qkv = np.ascontiguousarray(g["post_qkv"])
+    B, L, _, H, D = qkv.shape
+    q = np.full((B, H, L, D), 3.0, np.float32)
+    pk = np.full((B, H, D, 32), 3.0, np.float32)
+    pv = np.full((B, H, D, 32), 3.0, np.float32)
+    args = [np.ascontiguousarray(g[k]) for k in ("post_freqs", "post_qg", "post_kg")]
+    assert f(_ptr(qkv), *(_ptr(a) for a in args), _ptr(q), _ptr(pk), _ptr(pv),
+             B, L, H, D, 32, 1, 1) == 0
+    np.testing.assert_array_equal(q, g["post_q"])
+    np.testing.assert_array_equal(pk, g["post_pk"])
+    np.testing.assert_array_equal(pv, g["post_pv"])

@@ -92,6 +92,9 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "triposplat_ab2_update_inplace_f32_avx512": ([VP] * 5 + [I, I64, I], I),
     "triposplat_b200_cfg_euler_update_f32": ([VP] * 5 + [I, I64], I),
     "triposplat_qkv_rope_rmsnorm_pack_f32_avx512_v2": ([VP] * 7 + [I] * 7, I),
+    "triposplat_qkv_rope_rmsnorm_pack_f32_avx512": ([VP] * 7 + [I] * 7, I),
+    "triposplat_qkv_postprocess_token_tile": ([], I),
+    "triposplat_qkv_postprocess_v2_tail_only_clear": ([], I),
     "triposplat_q_kv_selected_rope_rmsnorm_pack_f32_avx512_v2": ([VP] * 9 + [I] * 8, I),
     "triposplat_b200_q_kv_rmsnorm_pack_f32": ([VP] * 7 + [I] * 5, I),
     "triposplat_b200_qkv_rope_rmsnorm_sdpa_f32": ([VP] * 5 + [I] * 5, I),

@@ -559,6 +559,26 @@ int triposplat_qkv_rope_rmsnorm_pack_f32_avx512_v2(const float* qkv, const float
   return launch_status();
 }
 
+// scripts/native_qkv_postprocess_avx512.c:23-116: the first version of the post-process,
+// same arguments, checks and results as _v2 (it zeroes all of packed_k / packed_v before
+// filling them, _v2 only their tails; every element ends with the same value)
+int triposplat_qkv_rope_rmsnorm_pack_f32_avx512(const float* qkv, const float* frequencies,
+                                                const float* q_gamma, const float* k_gamma,
+                                                float* q_bhld, float* packed_k, float* packed_v,
+                                                int B, int L, int H, int D, int L_padded,
+                                                int frequency_batches, int threads) {
+  return triposplat_qkv_rope_rmsnorm_pack_f32_avx512_v2(qkv, frequencies, q_gamma, k_gamma, q_bhld,
+                                                        packed_k, packed_v, B, L, H, D, L_padded,
+                                                        frequency_batches, threads);
+}
+
+// scripts/native_qkv_postprocess_avx512.c:118-120: tokens per work tile (64 here)
+int triposplat_qkv_postprocess_token_tile(void) { return 64; }
+
+// scripts/native_qkv_postprocess_v2_avx512.c:193-195: 1 = only the padded tail of the packed
+// K / V rows is cleared (the rest is written)
+int triposplat_qkv_postprocess_v2_tail_only_clear(void) { return 1; }
+
 // scripts/native_qkv_postprocess_v2_avx512.c:107-191
 int triposplat_q_kv_selected_rope_rmsnorm_pack_f32_avx512_v2(
     const float* q, const float* kv, const float* frequencies, const int64_t* selected_indices,
