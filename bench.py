@@ -48,7 +48,6 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--parallel", choices=("replicas", "cfg"), default="replicas",
                     help="replicas: one image per GPU (default); cfg: each image's CFG pair split "
                          "over two GPUs (conditional / unconditional branch), one NCCL all-gather "
@@ -63,6 +62,9 @@ def parse():
     ap.add_argument("--no-graph", action="store_true",
                     help="issue every kernel from the host each step instead of replaying "
                          "the step's CUDA graph")
+    ap.add_argument("--lk", type=int, default=None,
+                    help="sdpa cases: override the key count (the key-tile sweep of the "
+                         "attention kernel's per-item cost)")
     ap.add_argument("--case", default="model",
                     choices=("model", "gemm1", "sdpa2a", "sdpa2b", "sdpa2c", "mlp3", "block4"),
                     help="model = BASELINE config 5 (the headline); the others time one "
@@ -100,6 +102,8 @@ def run_case(args):
     elif args.case.startswith("sdpa"):
         B, H, Lq = 2, 16, 8192
         Lk = 1374 if args.case == "sdpa2c" else 8192
+        if args.lk:
+            Lk = args.lk
         q = torch.randn(B, H, Lq, 64, device=dev, generator=g)
         k = torch.randn(B, H, Lk, 64, device=dev, generator=g)
         v = torch.randn(B, H, Lk, 64, device=dev, generator=g)
@@ -109,6 +113,8 @@ def run_case(args):
         what = {"sdpa2a": "exact SDPA self 2x16x8192^2 (config 2a)",
                 "sdpa2b": "exact SDPA + key bias [2,16,8192] (config 2b)",
                 "sdpa2c": "exact SDPA cross 8192x1374 (config 2c)"}[args.case]
+        if args.lk:
+            what += f", keys overridden to {Lk}"
     elif args.case == "mlp3":
         M, C, F = 8192, 1024, 4096
         x = torch.randn(1, M, C, device=dev, generator=g)
@@ -240,53 +246,74 @@ class ClockSampler:
                 "power_w_max": max((float(r[2]) for r in rows if r[2].replace(".", "").isdigit()), default=None)}
 
 
-def cpu_baseline(spec, seconds):
+def cpu_baseline(spec):
     import cpu_block
 
     try:
-        r = cpu_block.time_sample(spec, min_seconds=seconds, max_reps=3)
+        r = cpu_block.time_sample(spec, block_reps=3)
     except Exception as exc:  # noqa: BLE001 - reported, not fatal
         return {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "unavailable",
-                "sample": f"reference CPU block could not run: {exc}"}
+                "sample": f"reference CPU path could not run: {exc}"}
     return {"value": round(r["sec_per_image"], 2), "unit": UNIT, "cores": r["threads"], "kind": r["kind"],
-            "sample": (f"one full-size block of the CFG-pair forward (B=2, L=8193, 1374 cond tokens) "
-                       f"through the reference's AVX-512 kernels, median of {r['reps']} runs = "
-                       f"{r['block_seconds']:.3f} s; sec/image = 20 steps x forward/block flops "
-                       f"({r['block_flops'] / 1e12:.3f} TFLOP per block)")}
+            "sample": (f"the full-size sampler step's pieces through the reference's AVX-512 kernels "
+                       f"(B=2 CFG pair, L=8193, 1374 cond tokens): embeddings {r['embed_seconds']:.3f} s, "
+                       f"block median of {r['reps']} = {r['block_seconds']:.3f} s (x28), final layer + "
+                       f"CFG/Euler {r['final_seconds']:.3f} s; sec/image = 20 x step")}
+
+
+def reference_schedule(steps: int, pieces: int) -> list[list[int]]:
+    """Pieces of one sampler step run by each of ``steps`` timed steps of the reference arm:
+    with steps <= pieces every piece runs exactly once (consecutive runs per step); with
+    more steps, step i runs piece i mod pieces (the step is covered steps / pieces times)."""
+    if steps <= pieces:
+        return [[j for j in range(pieces) if j * steps // pieces == i] for i in range(steps)]
+    return [[i % pieces] for i in range(steps)]
 
 
 def run_reference(args):
-    """--impl reference: the reference's CPU kernels on the host cores, rank 0 only."""
+    """--impl reference: the reference's CPU kernels on the host cores, rank 0 only.
+
+    The K timed steps together run one whole sampler step of the full-size model (the
+    embeddings, 28 blocks, the final layer and the CFG / Euler update, cut into 30 pieces
+    by reference_schedule) through the reference's kernels; sec/image = 20 x the time of
+    that sampler step.  Warm-up steps run one block each (at most two)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     from flow_model import FlowSpec
     import cpu_block
+    from ref_flow import RefKernels
 
     spec = FlowSpec()
-    if not cpu_block._RefKernels.available():
+    if not RefKernels.available():
         print(json.dumps({"impl": "reference", "unavailable":
                           "reference AVX-512 kernels not built or host CPU lacks AVX-512"}))
         return 0
-    blk = cpu_block.CpuBlock(spec)
-    for _ in range(max(0, min(args.warmup, 1))):
-        blk.run()
-    times = []
-    for _ in range(args.steps):
+    fwd = cpu_block.RefForward(spec)
+    pieces = fwd.pieces()
+    pieces[0]()  # embeddings first: the blocks read the token buffer they fill
+    for _ in range(max(0, min(args.warmup, 2))):
+        pieces[1]()
+    sched = reference_schedule(args.steps, len(pieces))
+    step_times, piece_time = [], {}
+    for plan in sched:
         t0 = time.perf_counter()
-        blk.run()
-        times.append(time.perf_counter() - t0)
-    t_block = sum(times) / len(times)
-    value = cpu_block.sec_per_image_from_block(spec, t_block, blk.block_flops())
-    sample = (f"each step = one full-size block of the CFG-pair forward (B=2, L=8193) through "
-              f"the reference's AVX-512 kernels; sec/image = 20 x forward/block flops x mean block time")
+        for j, t in cpu_block.time_pieces(fwd, plan):
+            piece_time.setdefault(j, []).append(t)
+        step_times.append(time.perf_counter() - t0)
+    sampler_step = sum(sum(v) / len(v) for v in piece_time.values())
+    value = cpu_block.SAMPLER_STEPS * sampler_step
+    sample = (f"the {args.steps} timed steps run one full sampler step of the full-size model "
+              f"(embeddings, 28 blocks, final layer, CFG/Euler; B=2 CFG pair, L=8193) through the "
+              f"reference's AVX-512 kernels, {sampler_step:.2f} s; sec/image = 20 x that step")
     line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "impl": "reference",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(t_block * 1e3, 3), "higher_is_better": False, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "ms_per_step": round(sum(step_times) / len(step_times) * 1e3, 3),
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
             "config": {"workload": "s20 CFG flow sampling, synthetic 28-block NF24 flow model",
-                       "parallelism": "host CPU (OpenMP)"},
-            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": blk.th,
+                       "parallelism": "host CPU (OpenMP)", "sampler_step_seconds": round(sampler_step, 3)},
+            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": fwd.th,
                              "kind": "reference", "sample": sample},
             "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
@@ -528,7 +555,7 @@ def main():
         "finite": finite,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(spec, args.cpu_seconds)
+        line["cpu_baseline"] = cpu_baseline(spec)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

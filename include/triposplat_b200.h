@@ -92,17 +92,22 @@ int triposplat_gemm_rnf8_avx512_tail(const float* x, const uint8_t* codes0_t,
                                      int stride_x, int stride_out, int threads, int stages);
 
 /* No counterpart in the reference.  Same arguments and result as
- * triposplat_gemm_rnf8_avx512, for callers that must not let a library allocate device
- * memory (work being captured into a CUDA graph, hosts whose device memory is owned by
- * their own allocator or a fixed memory plan, loops that cannot absorb cudaMalloc's
- * device-wide synchronisation).  It calls no allocator: its scratch is a fixed 32 MiB
- * __device__ array per device, so it serves split activations of up to 32 MiB
- * (triposplat_b200_split_bytes(M, K); e.g. M <= 8184 at K = 1024), returns -6 beyond, and
- * -4 unless N % 16 == 0 with 16-byte aligned code planes and output (stride_out % 4 == 0).
- * All calls on a device share
- * the scratch: calls whose kernels may overlap on the GPU race, so order them on one
- * stream.  Nothing in the scratch needs to start at zero.  The first call on a device
- * resolves the scratch address; make it before capturing any stream. */
+ * triposplat_gemm_rnf8_avx512, for callers that cannot let a library allocate device
+ * memory: hosts whose device memory belongs to their own allocator or to a fixed plan made
+ * at start-up (a serving process that reserves the GPU's memory up front, an application
+ * that must account for every byte it places on the device), and loops that cannot absorb
+ * cudaMalloc's device-wide synchronisation.  It calls no allocator: its scratch is a fixed
+ * 32 MiB __device__ array that every GPU loading the library holds until exit, so it
+ * serves split activations of up to 32 MiB (triposplat_b200_split_bytes(M, K); e.g.
+ * M <= 8184 at K = 1024), returns -6 beyond, and -4 unless N % 16 == 0 with 16-byte aligned
+ * code planes and output (stride_out % 4 == 0).  All calls on a device share the scratch:
+ * calls whose kernels may overlap on the GPU race, so order them on one stream.  Nothing
+ * in the scratch needs to start at zero.  The first call on a device does its set-up —
+ * resolves the scratch's device address and maps a static status word (cudaHostRegister
+ * of a static page, not an allocation) for the kernels' bounded waits — so make that first
+ * call before any stream capture.  A wait that gives up is reported by
+ * triposplat_b200_status() as for every other entry point, also when this is the first
+ * library call on the device. */
 int triposplat_gemm_nf24_noalloc(const float* x, const uint8_t* codes0_t, const uint8_t* codes1_t,
                                  const uint8_t* codes2_t, const float* scales0,
                                  const float* scales1, const float* scales2,
@@ -304,7 +309,9 @@ int triposplat_qkv_rope_rmsnorm_pack_f32_avx512(const float* qkv, const float* f
                                                 int frequency_batches, int threads);
 /* replace scripts/native_qkv_postprocess_avx512.c:118-120 (tokens per work tile) and
  * scripts/native_qkv_postprocess_v2_avx512.c:193-195 (returns 1: only the packed tail is
- * cleared) */
+ * cleared).  The token tile is this build's: 64 tokens per CTA of the GPU kernel (the
+ * reference's CPU kernel returns its 16-token tile), as the row-tile queries report the
+ * GPU tiles; no caller derives a layout from it. */
 int triposplat_qkv_postprocess_token_tile(void);
 int triposplat_qkv_postprocess_v2_tail_only_clear(void);
 /* replaces scripts/native_qkv_postprocess_v2_avx512.c:107-191 (selected_indices is a

@@ -1,186 +1,107 @@
-"""CPU baseline: one flow-transformer block of the CFG pair, timed on the host cores.
+"""CPU baseline: the synthetic flow model's forward on the reference's own AVX-512 kernels,
+timed on the host cores.
 
 TEST / BASELINE INFRASTRUCTURE ONLY (used by bench.py's cpu_baseline leg and its
-``--impl reference`` arm).  The block is composed from the reference's own AVX-512
-kernels compiled into oracle/_ref (``kind = "reference"``) — the NF24 GEMM
-(scripts/gemm_nf24_i16_avx512.c), QKV post-process v2, the packed q8/tile-512 exact
-SDPA, LayerNorm / RMSNorm, GELU and the block elementwise kernels — exactly as the
-reference's packed-v3 route chains them (scripts/native_qkv_packed_attention_patch_v3.py).
-Without AVX-512 on the host, the oracle restatement (``kind = "port"``) stands in.
+``--impl reference`` arm).  The model is ``ref_flow.RefFlowModel`` — the same forward the
+GPU runs (embeddings, adaLN, 28 blocks with self and cross attention, final layer), every
+op one call of a reference kernel compiled into oracle/_ref — followed by the sampler's
+CFG combine + Euler update (scripts/native_sampler_avx512.c:19,56).  One sampler step is
+cut into 30 pieces: the embeddings, each of the 28 blocks, and the final layer with the
+update; a timed sample runs pieces and sec/image = 20 x (sum of the 30 pieces' times).
 
-The sample is one block at full size (B=2, L=8193, C=1024, 1374 condition tokens);
-sec/image is extrapolated by flops: 20 steps x forward_flops / block_flops x T_block.
-Codes are random int16/int8 (as scripts/bench_native_rnf8_avx512.py:120-131 does):
-the kernels' cost does not depend on the values.
+Codes are random int16 / int8 per Linear with a constant scale (as
+scripts/bench_native_rnf8_avx512.py:120-131 does): the kernels' cost does not depend on
+the values, and generating them takes seconds where packing 477 M weights would take more.
 """
 from __future__ import annotations
 
-import ctypes
-import os
 import time
-from pathlib import Path
 
 import numpy as np
 
-HERE = Path(__file__).resolve().parent
-REF = HERE / "_ref"
-VP, I, I64, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
+from ref_flow import RefFlowModel, RefKernels, _check, _p
+
+SAMPLER_STEPS = 20
 
 
-def _p(a):
-    return None if a is None else a.ctypes.data_as(VP)
-
-
-def _bind(lib, name, args):
-    fn = getattr(lib, name)
-    fn.argtypes = args
-    fn.restype = I
-    return fn
-
-
-class _RefKernels:
-    kind = "reference"
-
-    def __init__(self, threads):
-        self.th = threads
-        g = ctypes.CDLL(str(REF / "libref_gemm_nf24_i16.so"))
-        self.gemm = _bind(g, "triposplat_gemm_rnf8_avx512", [VP] * 10 + [I] * 7)
-        self.gemm_tail = _bind(g, "triposplat_gemm_rnf8_avx512_tail", [VP] * 10 + [I] * 7)
-        nr = ctypes.CDLL(str(REF / "libref_norm_rope.so"))
-        self.ln = _bind(nr, "triposplat_layernorm_f32_avx512", [VP] * 4 + [I64, I, F, I, I])
-        self.rms = _bind(nr, "triposplat_multihead_rmsnorm_f32_avx512", [VP] * 3 + [I64, I, I, F, I])
-        act = ctypes.CDLL(str(REF / "libref_activations.so"))
-        self.gelu = _bind(act, "triposplat_gelu_tanh_f32_avx512", [VP] * 2 + [I64, I])
-        blk = ctypes.CDLL(str(REF / "libref_block_elementwise.so"))
-        self.mod = _bind(blk, "triposplat_modulate_inplace_f32_avx512", [VP] * 3 + [I] * 4)
-        self.gres = _bind(blk, "triposplat_gated_residual_inplace_f32_avx512", [VP] * 3 + [I] * 4)
-        self.add = _bind(blk, "triposplat_add_inplace_f32_avx512", [VP] * 2 + [I64, I])
-        post = ctypes.CDLL(str(REF / "libref_qkv_postprocess_v2.so"))
-        self.post = _bind(post, "triposplat_qkv_rope_rmsnorm_pack_f32_avx512_v2", [VP] * 7 + [I] * 7)
-        sd = ctypes.CDLL(str(REF / "libref_sdpa_q8t512_packed.so"))
-        self.sdpa_packed = _bind(sd, "triposplat_sdpa_f32_avx512_exact_q8t512_packed_blhd",
-                                 [VP] * 5 + [I] * 9)
-
-    @staticmethod
-    def available() -> bool:
-        if not (REF / "libref_sdpa_q8t512_packed.so").is_file():
-            return False
-        try:
-            flags = Path("/proc/cpuinfo").read_text()
-        except OSError:
-            return False
-        return all(f in flags for f in ("avx512f", "avx512dq", "avx512bw", "avx512vl"))
-
-
-def _check(st, what):
-    if st != 0:
-        raise RuntimeError(f"{what} -> {st}")
-
-
-class CpuBlock:
-    """Buffers + weights for one block of the batch-2 pair, on the host."""
+class RefForward:
+    """One batch-2 (CFG pair) sampler step of the full-size model on the reference kernels,
+    as a list of pieces (callables) covering it exactly once."""
 
     def __init__(self, spec, threads=None, seed=0):
-        self.s = spec
-        self.th = threads or len(os.sched_getaffinity(0))
-        if not _RefKernels.available():
+        from flow_model import rope_freqs, timestep_frequencies
+
+        if not RefKernels.available():
             raise RuntimeError("reference kernels unavailable (oracle/_ref missing or no AVX-512)")
-        self.k = _RefKernels(self.th)
+        self.s = spec
         rng = np.random.default_rng(seed)
-        s = spec
-        h, B, L, Mc, H = s.hidden, 2, s.seq, s.cond_tokens, s.heads
-        self.Lp = (L + 15) // 16 * 16
-        self.Mcp = (Mc + 15) // 16 * 16
-        self.lin = {}
-        for name, k, n in (("qkv", h, 3 * h), ("out", h, h), ("cross_q", h, h), ("cross_kv", h, 2 * h),
-                           ("cross_out", h, h), ("fc1", h, s.mlp), ("fc2", s.mlp, h)):
-            self.lin[name] = (rng.integers(-540, 541, size=(k, n), dtype=np.int16),
-                              rng.integers(-128, 128, size=(k, n), dtype=np.int8),
-                              np.full(n, 0.02 / 127 / 1024, np.float32),
-                              (rng.standard_normal(n) * 0.01).astype(np.float32))
         f32 = np.float32
-        self.x = rng.standard_normal((B, L, h)).astype(f32)
-        self.c = rng.standard_normal((B, Mc, h)).astype(f32)
-        self.a = np.empty((B, L, h), f32)
-        self.y = np.empty((B, L, h), f32)
-        self.qkv = np.empty((B, L, 3 * h), f32)
-        self.q = np.empty((B, H, L, 64), f32)
-        self.pk = np.empty((B, H, 64, self.Lp), f32)
-        self.pv = np.empty((B, H, 64, self.Lp), f32)
-        self.o = np.empty((B, L, h), f32)
-        self.ckv = np.empty((B, Mc, 2 * h), f32)
-        self.cpk = np.zeros((B, H, 64, self.Mcp), f32)
-        self.cpv = np.zeros((B, H, 64, self.Mcp), f32)
-        self.hid = np.empty((B, L, s.mlp), f32)
-        self.mod = (rng.standard_normal((6, B, h)) * 0.02).astype(f32)
-        ang = rng.standard_normal((1, L, H, 32))
-        self.freqs = np.stack([np.cos(ang), np.sin(ang)], -1).reshape(1, L, H, 64).astype(f32)
-        self.gam = np.ones((H, 64), f32)
-        self.codebook = np.zeros(256, f32)
+        W = {}
+        for name, k, n in spec.linears():
+            W[name] = {"code01": rng.integers(-540, 541, size=(k, n), dtype=np.int16),
+                       "q2": rng.integers(-128, 128, size=(k, n), dtype=np.int8),
+                       "scale": np.full(n, 0.02 / 127 / 1024, f32),
+                       "bias": rng.standard_normal(n, dtype=f32) * f32(0.01)}
+        H, D = spec.heads, spec.head_dim
+        P = {}
+        for i in range(spec.blocks):
+            p = f"blocks.{i}."
+            P[p + "table"] = rng.standard_normal((6, spec.hidden), dtype=f32) * f32(0.02)
+            for gname in ("q_gamma", "k_gamma", "cq_gamma", "ck_gamma"):
+                P[p + gname] = f32(1.0) + rng.standard_normal((H, D), dtype=f32) * f32(0.02)
+        self.m = RefFlowModel(spec, W, P, rope_freqs(spec), timestep_frequencies(spec),
+                              batch=2, threads=threads)
+        self.th = self.m.k.th
+        self.kind = self.m.k.kind
+        lat = rng.standard_normal((1, spec.latent_tokens, spec.latent_dim), dtype=f32)
+        cam = rng.standard_normal((1, 1, spec.camera_dim), dtype=f32)
+        cond = rng.standard_normal((1, spec.cond_tokens, spec.cond_dim), dtype=f32)
+        self.x_lat, self.x_cam = lat, cam
+        self.cond_pair = np.ascontiguousarray(np.concatenate([cond, np.zeros_like(cond)]))
+        self.t = np.array([750.0, 750.0], f32)
+        self.g = np.array([3.0], f32)
+        self.dt = np.array([0.05], f32)
 
-    def _gemm(self, name, x, out, rows):
-        c01, q2, sc, b = self.lin[name]
-        K, N = c01.shape
-        _check(self.k.gemm(_p(x), _p(c01), _p(q2), _p(q2), _p(sc), _p(sc), _p(sc), _p(self.codebook),
-                           _p(b), _p(out), rows, K, N, K, N, self.th, 3), name)
+    def _embed(self):
+        self.m.embed(np.concatenate([self.x_lat] * 2), np.concatenate([self.x_cam] * 2), self.t,
+                     self.cond_pair)
 
-    def run(self):
-        s, k, th = self.s, self.k, self.th
-        B, L, h, H, Mc = 2, s.seq, s.hidden, s.heads, s.cond_tokens
-        x, a, y, m = self.x, self.a, self.y, self.mod
-        rows, crow = B * L, B * Mc
-        _check(k.ln(_p(x), None, None, _p(a), rows, h, s.eps, 0, th), "ln1")
-        _check(k.mod(_p(a), _p(m[1]), _p(m[0]), B, L, h, th), "mod1")
-        self._gemm("qkv", a, self.qkv, rows)
-        _check(k.post(_p(self.qkv), _p(self.freqs), _p(self.gam), _p(self.gam), _p(self.q), _p(self.pk),
-                      _p(self.pv), B, L, H, 64, self.Lp, 1, th), "post")
-        _check(k.sdpa_packed(_p(self.q), _p(self.pk), _p(self.pv), None, _p(self.o), B, H, L, L, 64,
-                             self.Lp, 0, 0, th), "self_sdpa")
-        self._gemm("out", self.o, y, rows)
-        _check(k.gres(_p(x), _p(y), _p(m[2]), B, L, h, th), "gres1")
-        _check(k.ln(_p(x), None, None, _p(a), rows, h, s.eps, 0, th), "ln2")
-        self._gemm("cross_q", a, y, rows)
-        _check(k.rms(_p(y), _p(self.gam), _p(y), rows, H, 64, 1e-12, th), "rms_q")
-        self._gemm("cross_kv", self.c, self.ckv, crow)
-        # packed condition K/V layout and the query layout conversions the CPU route needs
-        ckv = self.ckv.reshape(B, Mc, 2, H, 64)
-        self.cpk[..., :Mc] = ckv[:, :, 0].transpose(0, 2, 3, 1)
-        self.cpv[..., :Mc] = ckv[:, :, 1].transpose(0, 2, 3, 1)
-        self.q[...] = y.reshape(B, L, H, 64).transpose(0, 2, 1, 3)
-        _check(k.sdpa_packed(_p(self.q), _p(self.cpk), _p(self.cpv), None, _p(self.o), B, H, L, Mc, 64,
-                             self.Mcp, 0, 0, th), "cross_sdpa")
-        self._gemm("cross_out", self.o, y, rows)
-        _check(k.add(_p(x), _p(y), x.size, th), "add")
-        _check(k.ln(_p(x), None, None, _p(a), rows, h, s.eps, 0, th), "ln3")
-        _check(k.mod(_p(a), _p(m[4]), _p(m[3]), B, L, h, th), "mod3")
-        self._gemm("fc1", a, self.hid, rows)
-        _check(k.gelu(_p(self.hid), _p(self.hid), self.hid.size, th), "gelu")
-        self._gemm("fc2", self.hid, y, rows)
-        _check(k.gres(_p(x), _p(y), _p(m[5]), B, L, h, th), "gres3")
+    def _final_and_update(self):
+        k = self.m.k
+        vl, vc = self.m.final_layer()
+        for x, v in ((self.x_lat, vl), (self.x_cam, vc)):
+            pos, neg = np.ascontiguousarray(v[:1]), np.ascontiguousarray(v[1:])
+            _check(k.cfg(_p(pos), _p(neg), _p(self.g), 1, pos.size, k.th), "cfg_combine")
+            _check(k.euler(_p(x), _p(pos), _p(self.dt), 1, x.size, k.th), "euler_update")
 
-    def block_flops(self) -> float:
-        s = self.s
-        B, L, h, Mc = 2, s.seq, s.hidden, s.cond_tokens
-        gemm = 2.0 * B * (L * h * 3 * h + L * h * h * 3 + Mc * h * 2 * h + 2 * L * h * s.mlp)
-        sdpa = 4.0 * B * s.heads * L * (L + Mc) * 64
-        return gemm + sdpa
+    def pieces(self):
+        """[embed, block 0, ..., block 27, final layer + CFG / Euler update]."""
+        blocks = [(lambda i=i: self.m.block(i)) for i in range(self.s.blocks)]
+        return [self._embed] + blocks + [self._final_and_update]
 
 
-def sec_per_image_from_block(spec, block_seconds: float, block_flops: float, steps: int = 20) -> float:
-    fwd = spec.flops_per_forward(batch=2)["total"]
-    return steps * block_seconds * fwd / block_flops
-
-
-def time_sample(spec, min_seconds=10.0, max_reps=3, threads=None):
-    """Run the block until ~min_seconds of CPU work (at least once); return stats."""
-    blk = CpuBlock(spec, threads=threads)
-    times = []
-    t_start = time.perf_counter()
-    while not times or (time.perf_counter() - t_start < min_seconds and len(times) < max_reps):
+def time_pieces(fwd: RefForward, order):
+    """Run pieces in ``order`` (indices into fwd.pieces()); return per-run seconds."""
+    pieces = fwd.pieces()
+    out = []
+    for j in order:
         t0 = time.perf_counter()
-        blk.run()
-        times.append(time.perf_counter() - t0)
-    t_block = float(np.median(times))
-    return {"block_seconds": t_block, "reps": len(times), "threads": blk.th, "kind": blk.k.kind,
-            "block_flops": blk.block_flops(),
-            "sec_per_image": sec_per_image_from_block(spec, t_block, blk.block_flops())}
+        pieces[j]()
+        out.append((j, time.perf_counter() - t0))
+    return out
+
+
+def time_sample(spec, block_reps: int = 3, threads=None):
+    """Bounded sample for bench.py's cpu_baseline leg (~10-30 s of CPU work): the embedding
+    piece once, ``block_reps`` blocks (median), the final piece once; one sampler step =
+    embed + blocks x median block + final (every block has the same shapes)."""
+    fwd = RefForward(spec, threads=threads)
+    n = len(fwd.pieces())
+    runs = time_pieces(fwd, [0] + list(range(1, 1 + block_reps)) + [n - 1])
+    t_embed = runs[0][1]
+    t_block = float(np.median([t for _, t in runs[1:-1]]))
+    t_final = runs[-1][1]
+    step = t_embed + spec.blocks * t_block + t_final
+    return {"embed_seconds": t_embed, "block_seconds": t_block, "final_seconds": t_final,
+            "step_seconds": step, "sec_per_image": SAMPLER_STEPS * step, "threads": fwd.th,
+            "kind": fwd.kind, "reps": block_reps}

@@ -185,3 +185,14 @@ def test_lockstep_driver_rejects_uneven_ranks():
     with pytest.raises(RuntimeError):
         run_lockstep([_Rank(2), _Rank(3)], None, None, None, None)
     assert len(run_lockstep([_Rank(2), _Rank(2)], None, None, None, None)) == 2
+
+
+def test_peer_reduce_refuses_an_odd_number_of_reduction_points():
+    """Three reduction points per block alternate between two partial buffers; with an odd
+    block count the last point of one forward and the first of the next would share a buffer
+    with no barrier between them, so the model refuses to build."""
+    from flow_model import FlowWeights
+    from head_shard import HeadShardedFlowModel
+
+    with pytest.raises(ValueError, match="even number of reduction points"):
+        HeadShardedFlowModel(FlowWeights(_spec()), rank=0, tp=2, device="cpu", reduce="peer")

@@ -8,6 +8,7 @@ CUDA runtime is linked statically so the library needs nothing but the driver.
 from __future__ import annotations
 
 import concurrent.futures as cf
+import hashlib
 import os
 import shutil
 import subprocess
@@ -17,6 +18,7 @@ HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
 BUILD = HERE / "_build"
 LIB = HERE / "libtriposplat_b200.so"
+STAMP = HERE / "libtriposplat_b200.so.sha256"  # digest of the sources the library was built from
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",
          "--expt-relaxed-constexpr", "-DNDEBUG"]
@@ -42,13 +44,21 @@ def _compile(src: Path, verbose: bool) -> Path:
     return obj
 
 
+def source_digest() -> str:
+    """sha256 over the compiler command and every source and header, in name order."""
+    h = hashlib.sha256(" ".join([*ARCH, *FLAGS]).encode())
+    for p in sorted([*CSRC.glob("*.cu"), *CSRC.glob("*.cuh"), *CSRC.glob("*.h")]):
+        h.update(p.name.encode() + b"\0" + p.read_bytes() + b"\0")
+    return h.hexdigest()
+
+
 def build(verbose: bool = False, force: bool = False) -> Path:
+    """Compile and link unless the library was built from exactly these sources (the
+    digest recorded beside it matches); file times are not trusted."""
     sources = sorted(CSRC.glob("*.cu"))
-    deps = sources + sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h"))
-    if LIB.exists() and not force:
-        newest = max(p.stat().st_mtime for p in deps)
-        if LIB.stat().st_mtime >= newest:
-            return LIB
+    digest = source_digest()
+    if LIB.exists() and not force and STAMP.is_file() and STAMP.read_text().strip() == digest:
+        return LIB
     BUILD.mkdir(exist_ok=True)
     with cf.ThreadPoolExecutor(max_workers=min(8, len(sources))) as ex:
         objs = list(ex.map(lambda s: _compile(s, verbose), sources))
@@ -58,6 +68,7 @@ def build(verbose: bool = False, force: bool = False) -> Path:
     if res.returncode != 0:
         raise RuntimeError(f"link failed:\n{res.stderr}")
     os.replace(tmp, LIB)
+    STAMP.write_text(digest + "\n")
     return LIB
 
 

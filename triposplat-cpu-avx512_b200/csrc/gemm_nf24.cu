@@ -46,6 +46,7 @@
 // (scripts/gemm_nf24_i16_avx512_tail.c:32-47) operation for operation.
 #include <cuda_fp16.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -945,23 +946,29 @@ static int launch_tc(const SplitPlanes& sp, const int16_t* c01, const int8_t* q2
   }
   Params prm{sp.rs, scale, bias, out, M, K, N, start, count, stride_out,
              ep.mode, ep.gate, ep.gate_ld, ep.rows_per_batch, status};
-  static uint64_t attr_done[8] = {0};  // per kernel: one bit per device ordinal
-  static int sm_count[64] = {0};
+  // per kernel: one bit per device ordinal once its shared-memory attribute is set; SM
+  // count per device.  Atomic: host threads on their own streams launch concurrently (a
+  // thread that sees a bit unset sets the attribute itself before launching).
+  static std::atomic<uint64_t> attr_done[8];
+  static std::atomic<int> sm_count[64];
   int dev = 0;
   cudaGetDevice(&dev);
-  if (sm_count[dev & 63] == 0) {
+  int sms = sm_count[dev & 63].load(std::memory_order_acquire);
+  if (sms == 0) {
     int n = 0;
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    sm_count[dev & 63] = n > 0 ? n : 148;
+    sms = n > 0 ? n : 148;
+    sm_count[dev & 63].store(sms, std::memory_order_release);
   }
   // one persistent CTA per SM (or one per tile when there are fewer tiles)
   const long long tiles = (long long)((count + BN - 1) / BN) * ((M + BM - 1) / BM);
-  const dim3 grid((unsigned)(tiles < sm_count[dev & 63] ? tiles : sm_count[dev & 63]));
+  const dim3 grid((unsigned)(tiles < sms ? tiles : sms));
   const int smem = SMEM_BYTES;
   auto run = [&](auto kernel, int mode) {
-    if (!(attr_done[mode] >> (dev & 63) & 1)) {
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(attr_done[mode].load(std::memory_order_acquire) & bit)) {
       cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      attr_done[mode] |= 1ull << (dev & 63);
+      attr_done[mode].fetch_or(bit, std::memory_order_acq_rel);
     }
     LaunchScope scope(kKGemmTc, stream);
     kernel<<<grid, NUM_THREADS, smem, stream>>>(m_hi, m_lo, m_c16, m_c8, m_out, prm);
@@ -1348,11 +1355,13 @@ int triposplat_gemm_nf24_noalloc(const float* x, const uint8_t* codes0_t, const 
     return kNotDevicePointer;
   uint8_t* ws = nullptr;
   if ((st = noalloc_scratch(&ws)) != kOk) return st;
+  int* status = device_status_no_alloc();  // first call on a device: maps the status word
+  if (status == nullptr) return kLaunchFailed;
   cudaStream_t stream = current_stream();
   const SplitPlanes sp = split_layout(ws, M, K);
   if ((st = launch_split(x, stride_x, sp, stream)) != kOk) return st;
-  return launch_tc(sp, c01, q2, scales0, bias, out, N, 0, N, stride_out, EpilogueArgs(),
-                   device_status_no_alloc(), stream);
+  return launch_tc(sp, c01, q2, scales0, bias, out, N, 0, N, stride_out, EpilogueArgs(), status,
+                   stream);
 }
 
 }  // extern "C"

@@ -54,6 +54,18 @@ DeviceState* state_for_current_device() {
   return &st;
 }
 
+// Status word of the allocation-free entry points when no DeviceState exists on the
+// device: one page of static host memory, page-locked and mapped (cudaHostRegister: no
+// allocation) by the first such call, read by triposplat_b200_status() like host_status.
+alignas(4096) int g_noalloc_status_page[1024];
+std::mutex g_noalloc_status_mutex;
+bool g_noalloc_status_registered = false;
+int* g_noalloc_status_dev[64] = {};
+
+int noalloc_status_value() {
+  return *reinterpret_cast<volatile int*>(&g_noalloc_status_page[0]);
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
 
@@ -107,8 +119,8 @@ int* device_status() {
 
 int host_status() {
   DeviceState* st = state_for_current_device();
-  if (!st) return 0;
-  return *reinterpret_cast<volatile int*>(st->host_status);
+  const int s = st ? *reinterpret_cast<volatile int*>(st->host_status) : 0;
+  return s != 0 ? s : noalloc_status_value();
 }
 
 int sm_count() {
@@ -155,7 +167,8 @@ bool is_device_pointer(const void* p) {
 int entry_check() {
   DeviceState* st = state_for_current_device();
   if (!st) return kNoDevice;
-  if (*reinterpret_cast<volatile int*>(st->host_status) != 0) return kDeviceFault;
+  if (*reinterpret_cast<volatile int*>(st->host_status) != 0 || noalloc_status_value() != 0)
+    return kDeviceFault;
   return kOk;
 }
 
@@ -178,12 +191,37 @@ int entry_check_no_alloc() {
   }
   DeviceState* st = existing_state();
   if (st && *reinterpret_cast<volatile int*>(st->host_status) != 0) return kDeviceFault;
+  if (noalloc_status_value() != 0) return kDeviceFault;
   return kOk;
 }
 
 int* device_status_no_alloc() {
-  DeviceState* st = existing_state();
-  return st ? st->device_status : nullptr;
+  if (DeviceState* st = existing_state()) return st->device_status;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_status_mutex);
+  if (!g_noalloc_status_registered) {
+    if (cudaHostRegister(g_noalloc_status_page, sizeof(g_noalloc_status_page),
+                         cudaHostRegisterMapped | cudaHostRegisterPortable) != cudaSuccess) {
+      cudaGetLastError();
+      set_last_error("could not map the allocation-free entry's status word");
+      return nullptr;
+    }
+    g_noalloc_status_registered = true;
+  }
+  if (g_noalloc_status_dev[dev] == nullptr) {
+    void* d = nullptr;
+    if (cudaHostGetDevicePointer(&d, g_noalloc_status_page, 0) != cudaSuccess || d == nullptr) {
+      cudaGetLastError();
+      set_last_error("could not map the allocation-free entry's status word");
+      return nullptr;
+    }
+    g_noalloc_status_dev[dev] = static_cast<int*>(d);
+  }
+  return g_noalloc_status_dev[dev];
 }
 
 thread_local char t_last_error[256] = "";
@@ -252,6 +290,7 @@ int triposplat_b200_status(void) { return tsb::host_status(); }
 void triposplat_b200_clear_status(void) {
   tsb::DeviceState* st = tsb::state_for_current_device();
   if (st) *reinterpret_cast<volatile int*>(st->host_status) = 0;
+  *reinterpret_cast<volatile int*>(&tsb::g_noalloc_status_page[0]) = 0;
 }
 
 int triposplat_b200_workspace_reserve(uint64_t bytes) {

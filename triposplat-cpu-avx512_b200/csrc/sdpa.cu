@@ -47,6 +47,8 @@
 // team (t & 1)'s O only after that team folded its previous O into registers (p_full).
 #include <cuda_fp16.h>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "runtime.h"
 
@@ -981,10 +983,10 @@ static int sdpa_attend(const SplitPlanesSdpa& sp, const float* bias, int64_t bia
       return kLaunchFailed;
   }
   {
-    static uint64_t attr_done = 0;
+    static std::atomic<uint64_t> attr_done{0};  // one bit per device ordinal
     int dev = 0;
     cudaGetDevice(&dev);
-    if (!(attr_done >> dev & 1)) {
+    if (!(attr_done.load(std::memory_order_acquire) >> (dev & 63) & 1)) {
       // the warpgroups' setmaxnreg budgets add up to the launch allocation of a kernel
       // compiled with REGS_LAUNCH registers per thread; with fewer, an increase would wait
       // for ever, so refuse to launch instead
@@ -996,23 +998,25 @@ static int sdpa_attend(const SplitPlanesSdpa& sp, const float* bias, int64_t bia
       cudaFuncSetAttribute(sdpa_fwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
       cudaFuncSetAttribute(qkv_split_k<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, QKV_SPLIT_SMEM);
       cudaFuncSetAttribute(qkv_split_k<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, QKV_SPLIT_SMEM);
-      attr_done |= 1ull << dev;
+      attr_done.fetch_or(1ull << (dev & 63), std::memory_order_acq_rel);
     }
   }
   const int Qt = (Lq + BQ - 1) / BQ;
   Params prm{sp.qinv, sp.kinv, sp.vinv, bias, (long long)bias_bh_stride, out, H, Lq, Lk, sp.T, out_blhd,
              device_status(), Qt, (int)BH};
   // persistent: one CTA per SM walking the (head, query tile) items
-  static int sm_count[64] = {0};
+  static std::atomic<int> sm_count[64];
   int dev = 0;
   cudaGetDevice(&dev);
-  if (sm_count[dev & 63] == 0) {
+  int sms = sm_count[dev & 63].load(std::memory_order_acquire);
+  if (sms == 0) {
     int n = 0;
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    sm_count[dev & 63] = n > 0 ? n : 148;
+    sms = n > 0 ? n : 148;
+    sm_count[dev & 63].store(sms, std::memory_order_release);
   }
   const long long items = (long long)Qt * BH;
-  const dim3 grid((unsigned)(items < sm_count[dev & 63] ? items : sm_count[dev & 63]));
+  const dim3 grid((unsigned)(items < sms ? items : sms));
   {
     LaunchScope scope(kKSdpaAttn, stream);
     sdpa_fwd_tc<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(m_qhi, m_qlo, m_khi, m_klo, m_vhi, m_vlo, prm);
@@ -1082,13 +1086,13 @@ static int qkv_sdpa_launch(const float* qsrc, const float* kvsrc, const float* f
   // make sure the attention kernel's attributes (and the fused kernel's shared memory
   // opt-in) are set before the fused kernel's first launch on this device
   {
-    static uint64_t attr_done = 0;
+    static std::atomic<uint64_t> attr_done{0};  // one bit per device ordinal
     int dev = 0;
     cudaGetDevice(&dev);
-    if (!(attr_done >> dev & 1)) {
+    if (!(attr_done.load(std::memory_order_acquire) >> (dev & 63) & 1)) {
       cudaFuncSetAttribute(qkv_split_k<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, QKV_SPLIT_SMEM);
       cudaFuncSetAttribute(qkv_split_k<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, QKV_SPLIT_SMEM);
-      attr_done |= 1ull << dev;
+      attr_done.fetch_or(1ull << (dev & 63), std::memory_order_acq_rel);
     }
   }
   const int q_tiles = (Lq + BKV - 1) / BKV;

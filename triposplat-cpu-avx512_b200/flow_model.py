@@ -153,11 +153,53 @@ class FlowWeights:
         return sum(v.code01.numel() * 3 + v.scale.numel() * 8 for v in self.linears.values())
 
 
-def make_weights(spec: FlowSpec, seed: int = 0, device: str = "cuda") -> FlowWeights:
+def host_float_weights(spec: FlowSpec, seed: int):
+    """Yield ``(kind, name, array)`` for every weight of the model, drawn on the host from
+    numpy's PCG64 stream in a fixed order: for each Linear (``spec.linears()`` order) its
+    float32 ``[out, in]`` weight ~ N(0, 0.02^2) then its bias ~ N(0, 0.01^2); then per block
+    the adaLN table ~ N(0, 0.02^2) and the four RMSNorm gammas ~ 1 + N(0, 0.02^2).
+    The stream depends only on numpy's generator, so a parity fixture produced on one host
+    can be regenerated on another."""
+    rng = np.random.default_rng(seed)
+    f32 = np.float32
+    for name, k, n in spec.linears():
+        w = rng.standard_normal((n, k), dtype=f32) * f32(0.02)
+        b = rng.standard_normal(n, dtype=f32) * f32(0.01)
+        yield "linear", name, (w, b)
+    H, D = spec.heads, spec.head_dim
+    for i in range(spec.blocks):
+        p = f"blocks.{i}."
+        yield "param", p + "table", rng.standard_normal((6, spec.hidden), dtype=f32) * f32(0.02)
+        for gname in ("q_gamma", "k_gamma", "cq_gamma", "ck_gamma"):
+            yield "param", p + gname, f32(1.0) + rng.standard_normal((H, D), dtype=f32) * f32(0.02)
+
+
+def make_weights(spec: FlowSpec, seed: int = 0, device: str = "cuda",
+                 source: str = "torch") -> FlowWeights:
     """Seeded random-init weights (W ~ N(0, 0.02^2), bias ~ N(0, 0.01^2), tables ~ N(0, 0.02^2),
-    gammas ~ 1 + N(0, 0.02^2)) packed to NF24 where they are generated."""
+    gammas ~ 1 + N(0, 0.02^2)) packed to NF24 where they are generated.
+
+    ``source="torch"`` draws on ``device`` with torch's generator (the benchmark's weights);
+    ``source="numpy"`` draws the same distributions on the host (``host_float_weights``) and
+    packs them on ``device``, so the codes are reproducible across machines (full-size parity
+    fixtures)."""
     import torch
 
+    if source == "numpy":
+        cb = make_nf8_codebook(torch).to(device)
+        w = FlowWeights(spec)
+        for kind, name, val in host_float_weights(spec, seed):
+            if kind == "linear":
+                wt = torch.from_numpy(val[0]).to(device)
+                codes, scales, _ = quantize_nf24_i16_any_device(wt, cb, stats=False)
+                w.linears[name] = PackedLinear(codes[0], codes[1], scales[0],
+                                               torch.from_numpy(val[1]).to(device))
+                del wt
+            else:
+                w.params[name] = torch.from_numpy(val).to(device)
+        return w
+    if source != "torch":
+        raise ValueError(f"unknown weight source {source!r}")
     g = torch.Generator(device=device).manual_seed(seed)
     cb = make_nf8_codebook(torch).to(device)
     w = FlowWeights(spec)

@@ -151,6 +151,13 @@ class HeadShardedFlowModel(FlowModelB200):
                  device: str = "cuda", group=None, all_reduce=None, reduce: str = "nccl"):
         import torch
 
+        if reduce == "peer" and (3 * weights.spec.blocks) % 2:
+            # the two partial buffers alternate per reduction point, and a rank rewrites one
+            # only after every rank has passed the next point's barrier; a forward (and so a
+            # replayed CUDA graph of it) must hold an even number of points (3 per block) for
+            # the alternation to carry on across forwards
+            raise ValueError(f"reduce='peer' needs an even number of reduction points per forward "
+                             f"(3 per block); {weights.spec.blocks} blocks give {3 * weights.spec.blocks}")
         super().__init__(weights, batch=batch, device=device, fused=True)
         s = self.spec
         self.rank, self.tp, self.group = rank, tp, group

@@ -211,3 +211,121 @@ def load_flow_weights(root, spec, device: str = "cuda", *, verify_checksums: boo
         w.linears[name] = PackedLinear(lin.code01, lin.q2, lin.scale, lin.bias)
     w.params = dict(sh.non_linear)
     return w
+
+
+def _entry_valid(root: Path, item) -> bool:
+    if not item or "file" not in item or "sha256" not in item:
+        return False
+    path = root / item["file"]
+    return path.is_file() and path.stat().st_size == item.get("bytes") and _sha256(path) == item["sha256"]
+
+
+def pack_nf24_i16_checkpoint(source_checkpoint, output_dir, *, expected_linear_count: int = 206,
+                             device: str = "cpu") -> dict:
+    """A safetensors checkpoint packed into a ``triposplat_nf24_i16_v1`` directory, under the
+    reference packer's name and contract (scripts/native_linear_nf24_prepacked.py:202-335):
+    every 2-D ``*.weight`` tensor is a Linear (their count must equal
+    ``expected_linear_count``), packed by this package's NF24 packer (bit-identical codes;
+    ``device`` selects where the packing runs); a missing bias packs as zeros; every other
+    tensor goes to ``non_linear.safetensors``.  A directory already complete for the same
+    source checkpoint (name, size, sha256) is returned unchanged."""
+    import torch
+    from safetensors import safe_open
+
+    from nf24_pack import make_nf8_codebook, quantize_nf24_i16_any_device
+
+    source = Path(source_checkpoint).resolve()
+    root = Path(output_dir).resolve()
+    source_info = {"name": source.name, "bytes": source.stat().st_size, "sha256": _sha256(source)}
+    manifest_path = root / "manifest.json"
+    if manifest_path.is_file():
+        existing = json.loads(manifest_path.read_text())
+        if existing.get("format") != FORMAT or existing.get("source") != source_info:
+            raise RuntimeError("existing prepacked manifest does not match source checkpoint")
+        if (existing.get("complete") and all(_entry_valid(root, i) for i in existing["linears"].values())
+                and _entry_valid(root, existing.get("non_linear"))):
+            return existing
+    codebook = make_nf8_codebook(torch)
+    with safe_open(source.as_posix(), framework="pt", device="cpu") as handle:
+        keys = sorted(handle.keys())
+        weight_keys = [k for k in keys if k.endswith(".weight") and len(handle.get_slice(k).get_shape()) == 2]
+        if len(weight_keys) != expected_linear_count:
+            raise RuntimeError(f"expected {expected_linear_count} Linear weights, found {len(weight_keys)}")
+        names = [k[:-7] for k in weight_keys]
+        linear_keys = set(weight_keys) | {f"{n}.bias" for n in names if f"{n}.bias" in keys}
+        packed, quant, has_bias = {}, {}, {}
+        for name, wkey in zip(names, weight_keys):
+            weight = handle.get_tensor(wkey).to(torch.float32).contiguous().to(device)
+            codes, scales, error = quantize_nf24_i16_any_device(weight, codebook)
+            bkey = f"{name}.bias"
+            has_bias[name] = bkey in keys
+            bias = (handle.get_tensor(bkey).to(torch.float32).contiguous() if has_bias[name]
+                    else torch.zeros(weight.shape[0], dtype=torch.float32))
+
+            class _P:  # the attribute layout save_nf24_shards reads
+                pass
+            p = _P()
+            p.code01, p.q2, p.scale, p.bias = codes[0].cpu(), codes[1].cpu(), scales[0].cpu(), bias
+            packed[name] = p
+            quant[name] = error
+        non_linear = {k: handle.get_tensor(k).to(torch.float32).contiguous() for k in keys if k not in linear_keys}
+    return save_nf24_shards(packed, root, non_linear=non_linear, source=source_info, quantization=quant,
+                            has_bias=has_bias)
+
+
+def load_nf24_i16_prepacked_model(packed_dir, model_factory, *, verify_checksums: bool = False,
+                                  device: str = "cuda"):
+    """Build ``model_factory()`` with its Linear parameters on the meta device and fill it
+    from a shard directory, under the reference loader's name and contract
+    (scripts/native_linear_nf24_prepacked.py:359-437): the model's Linear set must equal the
+    manifest's, the non-Linear state must account for every other parameter, each Linear
+    gets the ``_native_rnf8_*`` buffers the NF24 patch reads and empty float weights, and
+    the model carries ``_native_rnf8_prepacked_manifest`` / ``_native_rnf8_prepacked_load``.
+    Everything lands on ``device`` (the reference: the host); the source checkpoint is
+    never read."""
+    import torch
+    import torch.nn as nn
+
+    original = nn.Linear.__init__
+
+    def on_meta(module, in_features, out_features, bias=True, device=None, dtype=None):
+        return original(module, in_features, out_features, bias=bias, device="meta", dtype=dtype)
+
+    nn.Linear.__init__ = on_meta
+    try:
+        model = model_factory()
+    finally:
+        nn.Linear.__init__ = original
+    linears = {n: m for n, m in model.named_modules() if isinstance(m, nn.Linear)}
+    manifest = read_manifest(packed_dir)
+    if set(linears) != set(manifest["linears"]):
+        raise RuntimeError("prepacked/model Linear mismatch: "
+                           f"missing={sorted(set(linears) - set(manifest['linears']))} "
+                           f"extra={sorted(set(manifest['linears']) - set(linears))}")
+    shards = load_nf24_shards(packed_dir, device, verify_checksums=verify_checksums)
+    incompatible = model.load_state_dict(shards.non_linear, strict=False, assign=True)
+    expected_missing = {f"{n}.{f}" for n, m in linears.items()
+                        for f in (("weight", "bias") if m.bias is not None else ("weight",))}
+    if set(incompatible.missing_keys) != expected_missing or incompatible.unexpected_keys:
+        raise RuntimeError("non-Linear state mismatch: "
+                           f"missing={incompatible.missing_keys} unexpected={incompatible.unexpected_keys}")
+    for name, module in linears.items():
+        lin = shards.linears[name]
+        module.register_buffer("_native_rnf8_codes0_t", lin.code01, persistent=False)
+        module.register_buffer("_native_rnf8_codes1_t", lin.q2, persistent=False)
+        module.register_buffer("_native_rnf8_codes2_t", lin.q2, persistent=False)
+        module.register_buffer("_native_rnf8_scales0", lin.scale, persistent=False)
+        module.register_buffer("_native_rnf8_scales1", lin.scale, persistent=False)
+        module.register_buffer("_native_rnf8_scales2", lin.scale, persistent=False)
+        module.register_buffer("_native_rnf8_bias", lin.bias, persistent=False)
+        module.weight = nn.Parameter(torch.empty(0, dtype=torch.float32, device=device), requires_grad=False)
+        if module.bias is not None:
+            module.bias = nn.Parameter(torch.empty(0, dtype=torch.float32, device=device), requires_grad=False)
+    model._native_rnf8_prepacked_manifest = manifest
+    model._native_rnf8_prepacked_load = {
+        "enabled": True, "format": FORMAT, "directory": Path(packed_dir).resolve().as_posix(),
+        "linear_count": len(linears), "loaded_bytes": shards.loaded_bytes,
+        "checksums_verified": bool(verify_checksums), "source_checkpoint_loaded": False,
+        "device": str(device),
+    }
+    return model
