@@ -48,10 +48,14 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--parallel", choices=("replicas", "cfg"), default="replicas",
-                    help="replicas: one image per GPU (default); cfg: each image's CFG pair split "
-                         "over two GPUs (conditional / unconditional branch), one NCCL all-gather "
-                         "of the velocity per step")
+    ap.add_argument("--parallel", choices=("auto", "replicas", "cfg"), default="auto",
+                    help="auto (default): one GPU runs the CFG pair; N > 1 GPUs run one image, "
+                         "its CFG pair split over two GPU groups and, with N > 2, each branch's "
+                         "token rows over N / 2 GPUs (--sp); replicas: one image per GPU; cfg: "
+                         "each image's CFG pair split over two GPUs (or 2 x --tp / --sp)")
+    ap.add_argument("--sp", type=int, default=0,
+                    help="query-row sharding: each CFG branch's token rows over this many GPUs "
+                         "(K / V tiles pulled over NVLink once per block); 0 = auto")
     ap.add_argument("--tp", type=int, default=1,
                     help="head-sharded tensor parallelism: each model (the CFG pair, or one "
                          "branch with --parallel cfg) runs on this many GPUs, heads and MLP "
@@ -321,7 +325,7 @@ def run_reference(args):
     return 0
 
 
-def parallelism_label(split: bool, tp: int, images: int, reduce: str = "peer") -> str:
+def parallelism_label(split: bool, tp: int, images: int, reduce: str = "peer", sp: int = 1) -> str:
     reduce_label = ("one kernel reading the ranks' partials over NVLink and updating the residual"
                     if reduce == "peer" else "NCCL all-reduce + residual kernel")
     parts = []
@@ -330,9 +334,41 @@ def parallelism_label(split: bool, tp: int, images: int, reduce: str = "peer") -
     if tp > 1:
         parts.append(f"heads and MLP columns sharded over {tp} GPUs (3 reductions per block: "
                      f"{reduce_label})")
+    if sp > 1:
+        parts.append(f"token rows sharded over {sp} GPUs per branch (query-row sharding; one peer "
+                     f"barrier + K/V tile pull over NVLink per block)")
     if not parts:
         return f"replicas x{images} (one image per GPU, no data-path collective)"
     return f"{images} image(s) in parallel; per image: " + "; ".join(parts)
+
+
+def step0_parity(sampler, weights, dev, rank, inputs):
+    """Relative rmse (and bitwise equality) of the partitioned first-step velocity pair
+    against one GPU's batch-2 forward of the same inputs, computed on rank 0; every rank
+    takes part in the partitioned step (its sampler state is left unchanged).  None on
+    other ranks."""
+    import numpy as np
+    import torch
+
+    from flow_model import FlowModelB200, sampler_schedule
+
+    lat, cam = sampler.velocity_pair(0)
+    if rank != 0:
+        return None
+    h_lat, h_cam, h_cond, h_neg = inputs
+    t1000, _ = sampler_schedule(SAMPLER_STEPS, 3.0)
+    t = torch.tensor([t1000[0], t1000[0]], dtype=torch.float32, device=dev)
+    d = lambda a, b: torch.cat([a, b]).to(dev)  # noqa: E731
+    ref = FlowModelB200(weights, batch=2, device=str(dev))
+    r_lat, r_cam = ref.forward(d(h_lat, h_lat), d(h_cam, h_cam), t, d(h_cond, h_neg))
+    torch.cuda.synchronize()
+    a = torch.cat([lat.reshape(2, -1), cam.reshape(2, -1)], 1).double().cpu().numpy()
+    b = torch.cat([r_lat.reshape(2, -1), r_cam.reshape(2, -1)], 1).double().cpu().numpy()
+    del ref
+    torch.cuda.empty_cache()
+    rel = float(np.sqrt(np.mean((a - b) ** 2)) / np.sqrt(np.mean(b ** 2)))
+    return {"step0_velocity_rel_rmse_vs_1gpu": rel, "bitwise_equal": bool(np.array_equal(a, b)),
+            "reference": "one GPU, batch-2 forward of the same inputs and weights"}
 
 
 def main():
@@ -361,41 +397,60 @@ def main():
     spec = FlowSpec()
     lib = _native.load()
     weights = make_weights(spec, seed=0, device=str(dev))
-    split = args.parallel == "cfg"
-    T = args.tp
-    span = T * (2 if split else 1)  # GPUs per image
+    parallel, T, SP = args.parallel, args.tp, args.sp
+    if parallel == "auto":  # one image over all GPUs: CFG pair split, then query rows
+        parallel = "replicas" if world == 1 else "cfg"
+        if world > 2 and T == 1 and SP == 0:
+            SP = world // 2
+    SP = max(SP, 1)
+    split = parallel == "cfg"
+    if SP > 1 and (T > 1 or not split):
+        raise SystemExit("--sp runs with the CFG split (--parallel cfg) and without --tp")
+    W = max(T, SP)  # GPUs per CFG branch (or per CFG pair without the split)
+    span = W * (2 if split else 1)  # GPUs per image
     if T < 1 or spec.heads % T or world % span or (split and world < 2):
         raise SystemExit(f"--gpus {world} does not split into images of {span} GPU(s) "
-                         f"(--parallel {args.parallel} --tp {T}; tp must divide {spec.heads} heads)")
+                         f"(--parallel {parallel} --tp {T} --sp {SP}; tp must divide {spec.heads} heads)")
     images, image = world // span, rank // span
-    branch, tp_rank = (rank // T) % 2 if split else 0, rank % T
+    branch, w_rank = (rank // W) % 2 if split else 0, rank % W
     # every rank creates every group, in the same order
-    tp_groups, pair_groups = {}, {}
-    if T > 1:
+    w_groups, pair_groups, image_groups = {}, {}, {}
+    if W > 1:
         for im in range(images):
             for br in range(2 if split else 1):
-                base = im * span + br * T
-                tp_groups[(im, br)] = dist.new_group(list(range(base, base + T)))
-    if split:
+                base = im * span + br * W
+                w_groups[(im, br)] = dist.new_group(list(range(base, base + W)))
+    if split and SP == 1:
         for im in range(images):
-            for j in range(T):
-                pair_groups[(im, j)] = dist.new_group([im * span + j, im * span + T + j])
+            for j in range(W):
+                pair_groups[(im, j)] = dist.new_group([im * span + j, im * span + W + j])
+    if SP > 1:
+        for im in range(images):
+            image_groups[im] = dist.new_group(list(range(im * span, (im + 1) * span)))
     batch = 1 if split else 2
-    if T > 1:
-        from head_shard import HeadShardedFlowModel
+    if SP > 1:
+        from seq_shard import SeqCfgSampler, SeqShardedFlowModel
 
-        model = HeadShardedFlowModel(weights, rank=tp_rank, tp=T, batch=batch, device=str(dev),
-                                     group=tp_groups[(image, branch)], reduce=args.tp_reduce)
+        model = SeqShardedFlowModel(weights, rank=w_rank, world=SP, batch=1, device=str(dev),
+                                    group=w_groups[(image, branch)])
+        sampler = SeqCfgSampler(model, branch=branch, image_group=image_groups[image],
+                                steps=SAMPLER_STEPS, guidance=3.0, shift=3.0)
     else:
-        model = FlowModelB200(weights, batch=batch, device=str(dev))
-    if split:
-        from cfg_split import CfgSplitSampler
+        if T > 1:
+            from head_shard import HeadShardedFlowModel
 
-        # branch 0 (conditional) on the first T ranks of the image, branch 1 on the next T
-        sampler = CfgSplitSampler(model, branch=branch, group=pair_groups[(image, tp_rank)],
-                                  steps=SAMPLER_STEPS, guidance=3.0, shift=3.0)
-    else:
-        sampler = CfgEulerSampler(model, steps=SAMPLER_STEPS, guidance=3.0, shift=3.0)
+            model = HeadShardedFlowModel(weights, rank=w_rank, tp=T, batch=batch, device=str(dev),
+                                         group=w_groups[(image, branch)], reduce=args.tp_reduce)
+        else:
+            model = FlowModelB200(weights, batch=batch, device=str(dev))
+        if split:
+            from cfg_split import CfgSplitSampler
+
+            # branch 0 (conditional) on the first T ranks of the image, branch 1 on the next T
+            sampler = CfgSplitSampler(model, branch=branch, group=pair_groups[(image, w_rank)],
+                                      steps=SAMPLER_STEPS, guidance=3.0, shift=3.0)
+        else:
+            sampler = CfgEulerSampler(model, steps=SAMPLER_STEPS, guidance=3.0, shift=3.0)
 
     # per-image seeded inputs in pinned host memory (also the e2e source buffers)
     g = torch.Generator().manual_seed(1000 + image)
@@ -418,6 +473,12 @@ def main():
         t = torch.tensor([x], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
+
+    # ---- multi-GPU correctness: the partitioned first step against one GPU's forward
+    parity = None
+    if world > 1 and parallel != "replicas":
+        parity = step0_parity(sampler, weights, dev, rank, (h_lat, h_cam, h_cond, h_neg))
+        barrier()
 
     # ---- warm-up (untimed)
     for i in range(args.warmup):
@@ -488,11 +549,11 @@ def main():
     ms_step = ms_total / args.steps
     value = ms_step / 1e3 * SAMPLER_STEPS / images
     e2e_value = e2e_ms / args.steps / 1e3 * SAMPLER_STEPS / images
-    # this GPU's share: the pair, or one branch, and 1/T of the block work under --tp
-    flops = spec.flops_per_forward(batch=model.B, tp=T)
+    # this GPU's share: the pair, or one branch, and 1/W of the block work under --tp / --sp
+    flops = spec.flops_per_forward(batch=model.B, tp=W)
     peaks, peak_src = load_peaks()
     attn = prof["sdpa_attn"]
-    L, Mc, BH = spec.seq, spec.cond_tokens, model.B * spec.heads // T
+    L, Mc, BH = spec.seq, spec.cond_tokens, model.B * spec.heads // W
     attn_flops_per_step = spec.blocks * 4.0 * BH * L * (L + Mc) * spec.head_dim
     achieved = None
     if attn["launches"]:
@@ -533,14 +594,15 @@ def main():
     line = {
         "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 3),
-        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": False, "scaling": "weak" if parallel == "replicas" else "strong",
+        "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded Gaussian latent/camera/condition; random-init weights packed to NF24)",
         "config": {"workload": "s20 CFG flow sampling, synthetic 28-block NF24 flow model (BASELINE config 5)",
                    "blocks": spec.blocks, "linears": len(spec.linears()), "hidden": spec.hidden,
                    "heads": spec.heads, "mlp": spec.mlp, "latent_tokens": spec.latent_tokens,
                    "seq": spec.seq, "cond_tokens": Mc, "sampler_steps": SAMPLER_STEPS,
                    "guidance": 3.0, "shift": 3.0, "global_batch": f"{images} image(s) x CFG pair",
-                   "parallelism": parallelism_label(split, T, images, args.tp_reduce),
+                   "parallelism": parallelism_label(split, T, images, args.tp_reduce, SP),
                    "launch": "host-issued kernels" if args.no_graph else "one CUDA graph per sampler step",
                    "l2": "no flush: every step streams 1.4 GB of NF24 weights and ~1 GB of "
                          "activations, far above the 126 MB L2"},
@@ -553,6 +615,7 @@ def main():
         "e2e": {"value": round(e2e_value, 4), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "finite": finite,
+        **({"parity": parity} if parity is not None else {}),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(spec)

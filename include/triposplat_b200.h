@@ -238,6 +238,30 @@ int triposplat_sdpa_f32_cuda_bias_bh(const float* q, const float* k, const float
                                      const float* bias, long long bias_bh_stride, float* out,
                                      int B, int H, int Lq, int Lk, int out_blhd);
 /* replace scripts/native_sdpa_avx512_exact_q8t512.c:64-70 (tile sizes used here) */
+/* No reference counterpart: query-row sharding of one attention over a group of ranks
+ * (one per GPU).  Rank r owns tokens [token_starts[r], token_starts[r+1]) of the L-token
+ * sequence (interior starts multiples of 128).  Per attention each rank splits its own
+ * tokens (RoPE + per-head RMSNorm, as triposplat_b200_qkv_rope_rmsnorm_sdpa_f32) into Q
+ * planes of its rows and its key tiles of a K / V plane set, passes a peer barrier
+ * (triposplat_b200_peer_barrier), pulls the other ranks' key tiles from their plane sets
+ * over NVLink (CUDA IPC mappings, plain loads) and attends its rows to all L keys.  The
+ * outputs are bit-identical to the unsharded fused call.  Plane buffers are caller-owned,
+ * 256-byte aligned, sized by the two queries below. */
+uint64_t triposplat_b200_attn_q_planes_bytes(int BH, int Lq);
+uint64_t triposplat_b200_attn_kv_planes_bytes(int BH, int Lk);
+/* qkv_rows [B, t1 - t0, 3, H, 64] (tokens [t0, t1)); frequencies [fb, L, H, 64]; t0 % 128 == 0,
+ * t1 % 128 == 0 or t1 == L; -3 otherwise */
+int triposplat_b200_qkv_split_rows_f32(const float* qkv_rows, const float* frequencies,
+                                       const float* q_gamma, const float* k_gamma, int B, int L,
+                                       int H, int t0, int t1, int frequency_batches, void* q_planes,
+                                       void* kv_planes);
+/* kv_planes_by_rank[r]: rank r's plane set as mapped here; token_starts: world + 1 entries */
+int triposplat_b200_kv_planes_gather(const uint64_t* kv_planes_by_rank, const int* token_starts,
+                                     int world, int rank, int BH, int L);
+/* Lq query rows (q_planes) against L keys (a complete kv_planes); out [B, Lq, H, 64] */
+int triposplat_b200_attend_rows_f32(const void* q_planes, const void* kv_planes, float* out_blhd,
+                                    int B, int H, int Lq, int L);
+
 int triposplat_sdpa_key_tile(void);
 int triposplat_sdpa_query_block(void);
 /* replace scripts/native_sdpa_avx512_exact_q8t512.c:77-100; GPU timings are host enqueue

@@ -72,6 +72,11 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "triposplat_sdpa_f32_avx512_exact_q8t512_packed_blhd": ([VP] * 5 + [I] * 9, I),
     "triposplat_sdpa_f32_cuda_bias_bh": ([VP] * 4 + [ctypes.c_longlong, VP] + [I] * 5, I),
     "triposplat_sdpa_packed_output_is_blhd": ([], I),
+    "triposplat_b200_attn_q_planes_bytes": ([I, I], ctypes.c_uint64),
+    "triposplat_b200_attn_kv_planes_bytes": ([I, I], ctypes.c_uint64),
+    "triposplat_b200_qkv_split_rows_f32": ([VP] * 4 + [I] * 6 + [VP, VP], I),
+    "triposplat_b200_kv_planes_gather": ([VP, VP, I, I, I, I], I),
+    "triposplat_b200_attend_rows_f32": ([VP, VP, VP, I, I, I, I], I),
     "triposplat_sdpa_key_tile": ([], I),
     "triposplat_sdpa_query_block": ([], I),
     "triposplat_sdpa_q8t512_profile_reset": ([], None),

@@ -95,6 +95,15 @@ class CfgSplitSampler:
         if st:
             raise RuntimeError(f"sampler update returned status {st}")
 
+    def velocity_pair(self, i: int):
+        """Step i's [conditional, unconditional] velocities (latent [2, N, C], camera
+        [2, 1, Cc]) after the exchange, without updating the state."""
+        self.forward_phase(i)
+        self.exchange_phase()
+        s = self.model.spec
+        return (self.recv[:, :self.n_lat].reshape(2, s.latent_tokens, s.latent_dim),
+                self.recv[:, self.n_lat:].reshape(2, 1, s.camera_dim))
+
     def step(self, i: int):
         self.forward_phase(i)
         self.exchange_phase()

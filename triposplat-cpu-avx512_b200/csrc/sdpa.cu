@@ -768,11 +768,15 @@ __device__ __forceinline__ void emit_q_row(__half* __restrict__ qhi, __half* __r
   if (lane == 0) qinv[row] = ldexpf(1.0f, -sq);
 }
 
+// Key tiles tile0 + blockIdx.x of the sequence (Lk tokens).  kvsrc holds src_L token rows
+// per batch starting at token src_t0 (the whole sequence: 0, Lk; a query-row shard: its own
+// token range); self-attention Q rows of token t go to row t - q_t0 of the Q planes.
 template <bool kSelected>
 __global__ void __launch_bounds__(256, 3) qkv_split_k(
     const float* __restrict__ qsrc, const float* __restrict__ kvsrc, const float* __restrict__ freqs,
     const int64_t* __restrict__ sel, const float* __restrict__ qg, const float* __restrict__ kg,
-    int H, int Lq, int Lk, int Lkt, int fb, __half* __restrict__ qhi, __half* __restrict__ qlo,
+    int H, int Lq, int Lk, int Lkt, int fb, int tile0, int src_t0, int src_L, int q_t0,
+    __half* __restrict__ qhi, __half* __restrict__ qlo,
     float* __restrict__ qinv, __half* __restrict__ khi, __half* __restrict__ klo,
     __half* __restrict__ vhi, __half* __restrict__ vlo, float* __restrict__ kinv,
     float* __restrict__ vinv) {
@@ -782,7 +786,8 @@ __global__ void __launch_bounds__(256, 3) qkv_split_k(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.y, b = bh / H, h = bh % H;
   const int fbb = fb == 1 ? 0 : b;
-  const int tile = blockIdx.x, T = Lkt / BKV;
+  const int tile = blockIdx.x + tile0, T = Lkt / BKV;
+  const int t_end = min(Lk, src_t0 + src_L);  // tokens past it read as zeros
   const float2 gq = reinterpret_cast<const float2*>(qg + (int64_t)h * 64)[lane];
   const float2 gk = reinterpret_cast<const float2*>(kg + (int64_t)h * 64)[lane];
   // one q row (rope_rms64 output held as one complex pair per lane) into the Q planes
@@ -802,10 +807,10 @@ __global__ void __launch_bounds__(256, 3) qkv_split_k(
         const int t = t0 + warp + 8 * (j0 + u);
         qx[u] = kx[u] = vx[u] = make_float2(0.0f, 0.0f);
         fr[u] = make_float2(1.0f, 0.0f);
-        if (t < Lk) {
+        if (t < t_end) {
           if (freqs) fr[u] = reinterpret_cast<const float2*>(freqs + (((int64_t)fbb * Lk + t) * H + h) * 64)[lane];
-          const float* ks = kSelected ? kvsrc + (((int64_t)b * Lk + t) * 2 * H + h) * 64
-                                      : kvsrc + (((int64_t)b * Lk + t) * 3 * H + H + h) * 64;
+          const int64_t r = (int64_t)b * src_L + (t - src_t0);
+          const float* ks = kSelected ? kvsrc + (r * 2 * H + h) * 64 : kvsrc + (r * 3 * H + H + h) * 64;
           if (!kSelected) qx[u] = reinterpret_cast<const float2*>(ks - (int64_t)H * 64)[lane];
           kx[u] = reinterpret_cast<const float2*>(ks)[lane];
           vx[u] = reinterpret_cast<const float2*>(ks + (int64_t)H * 64)[lane];
@@ -816,8 +821,8 @@ __global__ void __launch_bounds__(256, 3) qkv_split_k(
         const int i = warp + 8 * (j0 + u);
         const int t = t0 + i;
         float2 ky = make_float2(0.0f, 0.0f), vy = make_float2(0.0f, 0.0f);
-        if (t < Lk) {  // warp-uniform: t depends on the warp only
-          if (!kSelected) emit_q((int64_t)bh * Lq + t, rope_rms64(qx[u], fr[u], gq));
+        if (t < t_end) {  // warp-uniform: t depends on the warp only
+          if (!kSelected) emit_q((int64_t)bh * Lq + (t - q_t0), rope_rms64(qx[u], fr[u], gq));
           ky = rope_rms64(kx[u], fr[u], gk);
           vy = vx[u];
         }
@@ -905,6 +910,58 @@ __global__ void __launch_bounds__(256) selected_q_split_k(
 
 constexpr int QKV_SPLIT_SMEM = BKV * (D + 1) * 4;  // the V staging tile
 
+// Query-row sharding: each rank of a group splits the key tiles of its own tokens into its
+// K / V plane set; after a peer barrier, kv_gather_k copies every other rank's tiles (the
+// key rows, the transposed value rows and the per-tile scales) from that rank's plane set,
+// mapped here over NVLink (CUDA IPC), into this rank's set.  Grid: (x, bh, source rank).
+constexpr int kMaxGatherRanks = 8;
+struct KvGather {
+  const uint8_t* src[kMaxGatherRanks];  // each rank's plane set as mapped in this process
+  int tlo[kMaxGatherRanks], thi[kMaxGatherRanks];  // each rank's key tiles [tlo, thi)
+  unsigned long long off[6];  // byte offsets of khi, klo, vhi, vlo, kinv, vinv in a set
+};
+
+__global__ void __launch_bounds__(256) kv_gather_k(KvGather g, uint8_t* __restrict__ dst, int rank,
+                                                   int Lkt, int T) {
+  const int p = blockIdx.z, bh = blockIdx.y;
+  if (p == rank) return;
+  const int tiles = g.thi[p] - g.tlo[p];
+  if (tiles <= 0) return;
+  const int tok0 = g.tlo[p] * BKV;
+  const uint8_t* src = g.src[p];
+  const int64_t k_units = (int64_t)tiles * BKV * D * 2 / 16;  // 16-byte units per key plane
+  const int64_t v_units = (int64_t)tiles * BKV * 2 / 16;      // per transposed value row
+  const int64_t total = 2 * k_units + 2 * D * v_units;
+  for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < total;
+       u += (int64_t)gridDim.x * blockDim.x) {
+    size_t off;
+    if (u < 2 * k_units) {
+      const int plane = (int)(u / k_units);
+      off = g.off[plane] + ((size_t)bh * Lkt + tok0) * D * 2 + (size_t)(u - plane * k_units) * 16;
+    } else {
+      const int64_t v = u - 2 * k_units;
+      const int plane = (int)(v / (D * v_units));
+      const int64_t w = v - plane * D * v_units;
+      const int d = (int)(w / v_units);
+      off = g.off[2 + plane] + (((size_t)bh * D + d) * Lkt + tok0) * 2 + (size_t)(w - d * v_units) * 16;
+    }
+    uint4 val;
+    asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(val.x), "=r"(val.y), "=r"(val.z), "=r"(val.w)
+                 : "l"(src + off));
+    *reinterpret_cast<uint4*>(dst + off) = val;
+  }
+  if (blockIdx.x == 0) {
+    for (int i = threadIdx.x; i < 2 * tiles; i += blockDim.x) {
+      const int plane = i / tiles, j = i - plane * tiles;
+      const size_t off = g.off[4 + plane] + ((size_t)bh * T + g.tlo[p] + j) * 4;
+      float v;
+      asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(src + off));
+      *reinterpret_cast<float*>(dst + off) = v;
+    }
+  }
+}
+
 }  // namespace sdpa
 
 struct SdpaCounters {
@@ -925,31 +982,67 @@ struct SplitPlanesSdpa {
   int T, Lkt;
 };
 
+static size_t al256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+// Q planes of Lq rows per head: [qhi | qlo | qinv]
+static size_t q_planes_layout(int64_t BH, int Lq, size_t off[2]) {
+  const size_t qplane = (size_t)BH * Lq * sdpa::D * 2;
+  off[0] = al256(qplane);                 // qlo
+  off[1] = off[0] + al256(qplane);        // qinv
+  return off[1] + al256((size_t)BH * Lq * 4);
+}
+
+// K / V planes of a sequence of Lk keys (T tiles of BKV): [khi | klo | vhi | vlo | kinv | vinv]
+static size_t kv_planes_layout(int64_t BH, int Lk, size_t off[6], int& T, int& Lkt) {
+  T = (Lk + sdpa::BKV - 1) / sdpa::BKV;
+  Lkt = T * sdpa::BKV;
+  const size_t kplane = (size_t)BH * Lkt * sdpa::D * 2;
+  off[0] = 0;
+  off[1] = al256(kplane);
+  off[2] = off[1] + al256(kplane);
+  off[3] = off[2] + al256(kplane);
+  off[4] = off[3] + al256(kplane);
+  off[5] = off[4] + al256((size_t)BH * T * 4);
+  return off[5] + al256((size_t)BH * T * 4);
+}
+
+static void planes_from(uint8_t* q, uint8_t* kv, int64_t BH, int Lq, int Lk, SplitPlanesSdpa& sp) {
+  size_t qo[2], ko[6];
+  q_planes_layout(BH, Lq, qo);
+  kv_planes_layout(BH, Lk, ko, sp.T, sp.Lkt);
+  sp.qhi = reinterpret_cast<__half*>(q);
+  sp.qlo = reinterpret_cast<__half*>(q + qo[0]);
+  sp.qinv = reinterpret_cast<float*>(q + qo[1]);
+  sp.khi = reinterpret_cast<__half*>(kv + ko[0]);
+  sp.klo = reinterpret_cast<__half*>(kv + ko[1]);
+  sp.vhi = reinterpret_cast<__half*>(kv + ko[2]);
+  sp.vlo = reinterpret_cast<__half*>(kv + ko[3]);
+  sp.kinv = reinterpret_cast<float*>(kv + ko[4]);
+  sp.vinv = reinterpret_cast<float*>(kv + ko[5]);
+}
+
 static int sdpa_planes(int64_t BH, int Lq, int Lk, cudaStream_t stream, SplitPlanesSdpa& sp) {
-  using namespace sdpa;
-  sp.T = (Lk + BKV - 1) / BKV;
-  sp.Lkt = sp.T * BKV;
-  const size_t qplane = (size_t)BH * Lq * D * 2;
-  const size_t kplane = (size_t)BH * sp.Lkt * D * 2;
-  auto al = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
-  const size_t off_qlo = al(qplane), off_qinv = off_qlo + al(qplane);
-  const size_t off_khi = off_qinv + al((size_t)BH * Lq * 4);
-  const size_t off_klo = off_khi + al(kplane), off_vhi = off_klo + al(kplane);
-  const size_t off_vlo = off_vhi + al(kplane), off_kinv = off_vlo + al(kplane);
-  const size_t off_vinv = off_kinv + al((size_t)BH * sp.T * 4);
-  const size_t total = off_vinv + al((size_t)BH * sp.T * 4);
-  uint8_t* ws = static_cast<uint8_t*>(workspace(total, stream));
+  size_t qo[2], ko[6];
+  int T, Lkt;
+  const size_t qbytes = q_planes_layout(BH, Lq, qo);
+  const size_t kvbytes = kv_planes_layout(BH, Lk, ko, T, Lkt);
+  uint8_t* ws = static_cast<uint8_t*>(workspace(qbytes + kvbytes, stream));
   if (!ws) return kWorkspace;
-  sp.qhi = reinterpret_cast<__half*>(ws);
-  sp.qlo = reinterpret_cast<__half*>(ws + off_qlo);
-  sp.qinv = reinterpret_cast<float*>(ws + off_qinv);
-  sp.khi = reinterpret_cast<__half*>(ws + off_khi);
-  sp.klo = reinterpret_cast<__half*>(ws + off_klo);
-  sp.vhi = reinterpret_cast<__half*>(ws + off_vhi);
-  sp.vlo = reinterpret_cast<__half*>(ws + off_vlo);
-  sp.kinv = reinterpret_cast<float*>(ws + off_kinv);
-  sp.vinv = reinterpret_cast<float*>(ws + off_vinv);
+  planes_from(ws, ws + qbytes, BH, Lq, Lk, sp);
   return kOk;
+}
+
+// Shared-memory opt-in of the fused split kernels, once per device.
+static void ensure_qkv_split_attr() {
+  using namespace sdpa;
+  static std::atomic<uint64_t> attr_done{0};  // one bit per device ordinal
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_done.load(std::memory_order_acquire) >> (dev & 63) & 1)) {
+    cudaFuncSetAttribute(qkv_split_k<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, QKV_SPLIT_SMEM);
+    cudaFuncSetAttribute(qkv_split_k<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, QKV_SPLIT_SMEM);
+    attr_done.fetch_or(1ull << (dev & 63), std::memory_order_acq_rel);
+  }
 }
 
 // The attention kernel on split planes.
@@ -1083,26 +1176,16 @@ static int qkv_sdpa_launch(const float* qsrc, const float* kvsrc, const float* f
   const int64_t BH = (int64_t)B * H;
   SplitPlanesSdpa sp;
   if ((st = sdpa_planes(BH, Lq, Lk, stream, sp)) != kOk) return st;
-  // make sure the attention kernel's attributes (and the fused kernel's shared memory
-  // opt-in) are set before the fused kernel's first launch on this device
-  {
-    static std::atomic<uint64_t> attr_done{0};  // one bit per device ordinal
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!(attr_done.load(std::memory_order_acquire) >> (dev & 63) & 1)) {
-      cudaFuncSetAttribute(qkv_split_k<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, QKV_SPLIT_SMEM);
-      cudaFuncSetAttribute(qkv_split_k<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, QKV_SPLIT_SMEM);
-      attr_done.fetch_or(1ull << (dev & 63), std::memory_order_acq_rel);
-    }
-  }
+  // the fused kernel's shared-memory opt-in before its first launch on this device
+  ensure_qkv_split_attr();
   const int q_tiles = (Lq + BKV - 1) / BKV;
   // key tiles (with, for self-attention, the query rows of the same tokens) through the
   // shared-memory V staging; selected queries in their own kernel without shared memory
   {
     LaunchScope scope(kKSdpaSplit, stream);
     qkv_split_k<kSelected><<<dim3(sp.T, (unsigned)BH), 256, QKV_SPLIT_SMEM, stream>>>(
-        qsrc, kvsrc, freqs, sel, qg, kg, H, Lq, Lk, sp.Lkt, fb, sp.qhi, sp.qlo, sp.qinv, sp.khi, sp.klo,
-        sp.vhi, sp.vlo, sp.kinv, sp.vinv);
+        qsrc, kvsrc, freqs, sel, qg, kg, H, Lq, Lk, sp.Lkt, fb, 0, 0, Lk, 0, sp.qhi, sp.qlo, sp.qinv,
+        sp.khi, sp.klo, sp.vhi, sp.vlo, sp.kinv, sp.vinv);
   }
   if (kSelected) {
     LaunchScope scope(kKSdpaSplit, stream);
@@ -1112,6 +1195,8 @@ static int qkv_sdpa_launch(const float* qsrc, const float* kvsrc, const float* f
   if ((st = launch_status()) != kOk) return st;
   return sdpa_attend(sp, nullptr, 0, out_blhd, BH, H, Lq, Lk, 1, stream);
 }
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace tsb
 
@@ -1206,6 +1291,127 @@ int triposplat_b200_q_kv_rmsnorm_sdpa_f32(const float* q, const float* kv, const
   if (!q || !kv || !q_gamma || !k_gamma || !out_blhd) return tsb::kNullPointer;
   if (B <= 0 || Lq <= 0 || Lk <= 0 || H <= 0) return tsb::kBadDims;
   return tsb::qkv_sdpa_launch<true>(q, kv, nullptr, nullptr, q_gamma, k_gamma, out_blhd, B, H, Lq, Lk, 1);
+}
+
+// ---- query-row sharding (no reference counterpart) -------------------------------------
+// A group of ranks splits one sequence of L tokens by query rows: rank r owns the tokens
+// [starts[r], starts[r+1]) (interior starts multiples of the 128-token key tile).  Per
+// attention: each rank splits its own tokens (triposplat_b200_qkv_split_rows_f32: Q planes
+// of its rows, its key tiles of the shared K / V plane layout), the ranks pass a peer
+// barrier, each pulls the other ranks' key tiles (triposplat_b200_kv_planes_gather), and
+// attends its query rows to all L keys (triposplat_b200_attend_rows_f32).  Every query row
+// sees the same split planes, tiles and warps as in the unsharded call: the outputs are
+// bit-identical to triposplat_b200_qkv_rope_rmsnorm_sdpa_f32 on the whole sequence.
+
+// Bytes of the Q planes of Lq rows x BH heads / of the K / V planes of Lk keys x BH heads.
+uint64_t triposplat_b200_attn_q_planes_bytes(int BH, int Lq) {
+  if (BH <= 0 || Lq <= 0) return 0;
+  size_t off[2];
+  return tsb::q_planes_layout(BH, Lq, off);
+}
+
+uint64_t triposplat_b200_attn_kv_planes_bytes(int BH, int Lk) {
+  if (BH <= 0 || Lk <= 0) return 0;
+  size_t off[6];
+  int T, Lkt;
+  return tsb::kv_planes_layout(BH, Lk, off, T, Lkt);
+}
+
+// RoPE + per-head RMSNorm + split of tokens [t0, t1) of an L-token sequence: qkv_rows
+// [B, t1 - t0, 3, H, 64] (this rank's rows), frequencies [fb, L, H, 64] (the whole
+// sequence's table).  Writes the Q planes of the t1 - t0 rows into q_planes and key tiles
+// [t0 / 128, ceil(t1 / 128)) into the K / V plane set kv_planes (layout of
+// triposplat_b200_attn_kv_planes_bytes(B * H, L)).  t0 % 128 == 0; t1 % 128 == 0 or t1 == L.
+int triposplat_b200_qkv_split_rows_f32(const float* qkv_rows, const float* frequencies,
+                                       const float* q_gamma, const float* k_gamma, int B, int L,
+                                       int H, int t0, int t1, int frequency_batches, void* q_planes,
+                                       void* kv_planes) {
+  using namespace tsb;
+  using namespace tsb::sdpa;
+  if (!qkv_rows || !frequencies || !q_gamma || !k_gamma || !q_planes || !kv_planes) return kNullPointer;
+  if (B <= 0 || L <= 0 || H <= 0 || (frequency_batches != 1 && frequency_batches != B)) return kBadDims;
+  if (t0 < 0 || t1 <= t0 || t1 > L || (t0 % BKV) != 0 || ((t1 % BKV) != 0 && t1 != L)) return kBadRange;
+  if (!aligned16(qkv_rows) || !aligned16(frequencies) || !aligned16(q_gamma) || !aligned16(k_gamma) ||
+      (reinterpret_cast<uintptr_t>(q_planes) & 255) || (reinterpret_cast<uintptr_t>(kv_planes) & 255))
+    return kBadAlignment;
+  int st = entry_check();
+  if (st != kOk) return st;
+  if (!is_device_pointer(qkv_rows) || !is_device_pointer(frequencies) || !is_device_pointer(q_gamma) ||
+      !is_device_pointer(k_gamma) || !is_device_pointer(q_planes) || !is_device_pointer(kv_planes))
+    return kNotDevicePointer;
+  const int64_t BH = (int64_t)B * H;
+  const int Lq = t1 - t0;
+  SplitPlanesSdpa sp;
+  planes_from(static_cast<uint8_t*>(q_planes), static_cast<uint8_t*>(kv_planes), BH, Lq, L, sp);
+  ensure_qkv_split_attr();
+  cudaStream_t stream = current_stream();
+  const int tile0 = t0 / BKV, tiles = (t1 + BKV - 1) / BKV - tile0;
+  {
+    LaunchScope scope(kKSdpaSplit, stream);
+    qkv_split_k<false><<<dim3(tiles, (unsigned)BH), 256, QKV_SPLIT_SMEM, stream>>>(
+        nullptr, qkv_rows, frequencies, nullptr, q_gamma, k_gamma, H, Lq, L, sp.Lkt,
+        frequency_batches, tile0, t0, Lq, t0, sp.qhi, sp.qlo, sp.qinv, sp.khi, sp.klo, sp.vhi,
+        sp.vlo, sp.kinv, sp.vinv);
+  }
+  return launch_status();
+}
+
+// Copy the other ranks' key tiles into this rank's K / V plane set.  kv_planes_by_rank[r]:
+// rank r's set as mapped in this process (this rank's own set at [rank]); token_starts:
+// world + 1 entries, 0 = token_starts[0] < ... < token_starts[world] = L, interior entries
+// multiples of 128.  The caller orders it after a barrier that follows every rank's split.
+int triposplat_b200_kv_planes_gather(const uint64_t* kv_planes_by_rank, const int* token_starts,
+                                     int world, int rank, int BH, int L) {
+  using namespace tsb;
+  using namespace tsb::sdpa;
+  if (!kv_planes_by_rank || !token_starts) return kNullPointer;
+  if (world < 1 || world > kMaxGatherRanks || BH <= 0 || L <= 0) return kBadDims;
+  if (rank < 0 || rank >= world) return kBadRange;
+  if (token_starts[0] != 0 || token_starts[world] != L) return kBadRange;
+  KvGather g{};
+  int T, Lkt;
+  size_t off[6];
+  tsb::kv_planes_layout(BH, L, off, T, Lkt);
+  for (int i = 0; i < 6; ++i) g.off[i] = off[i];
+  for (int r = 0; r < world; ++r) {
+    const int a = token_starts[r], b = token_starts[r + 1];
+    if (b <= a || (a % BKV) != 0) return kBadRange;
+    if (!kv_planes_by_rank[r]) return kNullPointer;
+    if (kv_planes_by_rank[r] & 255) return kBadAlignment;
+    g.src[r] = reinterpret_cast<const uint8_t*>(kv_planes_by_rank[r]);
+    g.tlo[r] = a / BKV;
+    g.thi[r] = (b + BKV - 1) / BKV;
+  }
+  int st = entry_check();
+  if (st != kOk) return st;
+  cudaStream_t stream = current_stream();
+  if (world > 1) {
+    LaunchScope scope(kKElementwise, stream);
+    kv_gather_k<<<dim3(16, (unsigned)BH, (unsigned)world), 256, 0, stream>>>(
+        g, reinterpret_cast<uint8_t*>(kv_planes_by_rank[rank]), rank, Lkt, T);
+  }
+  return launch_status();
+}
+
+// Exact attention of Lq query rows (q_planes, from triposplat_b200_qkv_split_rows_f32) to the
+// L keys of a complete K / V plane set; output [B, Lq, H, 64] (BLHD).
+int triposplat_b200_attend_rows_f32(const void* q_planes, const void* kv_planes, float* out_blhd,
+                                    int B, int H, int Lq, int L) {
+  using namespace tsb;
+  if (!q_planes || !kv_planes || !out_blhd) return kNullPointer;
+  if (B <= 0 || H <= 0 || Lq <= 0 || L <= 0) return kBadDims;
+  if ((reinterpret_cast<uintptr_t>(q_planes) & 255) || (reinterpret_cast<uintptr_t>(kv_planes) & 255) ||
+      !aligned16(out_blhd))
+    return kBadAlignment;
+  int st = entry_check();
+  if (st != kOk) return st;
+  if (!is_device_pointer(q_planes) || !is_device_pointer(kv_planes) || !is_device_pointer(out_blhd))
+    return kNotDevicePointer;
+  const int64_t BH = (int64_t)B * H;
+  SplitPlanesSdpa sp;
+  planes_from(static_cast<uint8_t*>(const_cast<void*>(q_planes)),
+              static_cast<uint8_t*>(const_cast<void*>(kv_planes)), BH, Lq, L, sp);
+  return sdpa_attend(sp, nullptr, 0, out_blhd, BH, H, Lq, L, 1, current_stream());
 }
 
 // scripts/native_sdpa_avx512_exact_q8t512.c:64-70: tile sizes of this implementation

@@ -516,6 +516,15 @@ class CfgEulerSampler:
             if st:
                 raise RuntimeError(f"sampler update returned status {st}")
 
+    def velocity_pair(self, i: int):
+        """Step i's [conditional, unconditional] velocities (latent [2, N, C], camera
+        [2, 1, Cc]), without updating the state."""
+        self.t_cur.copy_(self.t_pair[i])
+        self.x_lat[1].copy_(self.x_lat[0])
+        self.x_cam[1].copy_(self.x_cam[0])
+        v_lat, v_cam = self.model.forward(self.x_lat, self.x_cam, self.t_cur, self.cond_pair)
+        return v_lat.clone(), v_cam.clone()
+
     def step(self, i: int):
         self.t_cur.copy_(self.t_pair[i])
         self.dt_cur.copy_(self.dt[i:i + 1])
