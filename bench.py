@@ -486,6 +486,19 @@ def main():
     torch.cuda.synchronize()
     _native.check_status(lib)
 
+    # ---- the once-per-image condition path (cached across the sampler steps), timed once
+    # and added to sec/image below
+    cond_ms = 0.0
+    if getattr(sampler, "cached", False):
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        c0.record()
+        sampler.refresh_condition()
+        c1.record()
+        torch.cuda.synchronize()
+        cond_ms = c0.elapsed_time(c1)
+    cond_ms = max_over_ranks(cond_ms)
+
     # ---- capture the step into a CUDA graph (the library brackets each kernel with CUDA
     # events inside the graph, so the timed replays still yield live per-kernel times)
     uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
@@ -547,7 +560,7 @@ def main():
 
     # ---- report
     ms_step = ms_total / args.steps
-    value = ms_step / 1e3 * SAMPLER_STEPS / images
+    value = (ms_step * SAMPLER_STEPS + cond_ms) / 1e3 / images
     e2e_value = e2e_ms / args.steps / 1e3 * SAMPLER_STEPS / images
     # this GPU's share: the pair, or one branch, and 1/W of the block work under --tp / --sp
     flops = spec.flops_per_forward(batch=model.B, tp=W)
@@ -604,6 +617,8 @@ def main():
                    "guidance": 3.0, "shift": 3.0, "global_batch": f"{images} image(s) x CFG pair",
                    "parallelism": parallelism_label(split, T, images, args.tp_reduce, SP),
                    "launch": "host-issued kernels" if args.no_graph else "one CUDA graph per sampler step",
+                   "condition_path_ms_per_image": round(cond_ms, 3),
+                   "value_formula": "(ms_per_step x 20 + condition_path_ms_per_image) / images",
                    "l2": "no flush: every step streams 1.4 GB of NF24 weights and ~1 GB of "
                          "activations, far above the 126 MB L2"},
         "tflops_logical_per_gpu": round(flops["total"] / (ms_step / 1e3) / 1e12, 1),

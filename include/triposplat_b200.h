@@ -258,6 +258,16 @@ int triposplat_b200_qkv_split_rows_f32(const float* qkv_rows, const float* frequ
 /* kv_planes_by_rank[r]: rank r's plane set as mapped here; token_starts: world + 1 entries */
 int triposplat_b200_kv_planes_gather(const uint64_t* kv_planes_by_rank, const int* token_starts,
                                      int world, int rank, int BH, int L);
+/* No reference counterpart: cached condition keys.  The condition tokens do not change
+ * across sampler steps: their keys / values are split once per image into a K / V plane
+ * set (per-head RMSNorm of the keys; kv [B, Lk, 2, H, 64]), and each step splits only its
+ * queries (per-head RMSNorm, no rotation; q [B, Lq, H, 64]) before
+ * triposplat_b200_attend_rows_f32.  Bit-identical to triposplat_b200_q_kv_rmsnorm_sdpa_f32. */
+int triposplat_b200_kv_split_f32(const float* kv, const float* k_gamma, int B, int Lk, int H,
+                                 void* kv_planes);
+int triposplat_b200_q_split_f32(const float* q, const float* q_gamma, int B, int Lq, int H,
+                                void* q_planes);
+
 /* Lq query rows (q_planes) against L keys (a complete kv_planes); out [B, Lq, H, 64] */
 int triposplat_b200_attend_rows_f32(const void* q_planes, const void* kv_planes, float* out_blhd,
                                     int B, int H, int Lq, int L);

@@ -121,3 +121,22 @@ def test_graph_replay_matches_eager_steps():
     gl, gc = graphed.run()
     torch.cuda.synchronize()
     assert torch.equal(el, gl) and torch.equal(ec, gc)
+
+
+def test_condition_cache_is_bitwise_the_uncached_forward():
+    """forward() = precompute_condition() + forward_cached(): the condition K / V split
+    once and read by every block gives the bits of the per-step condition path."""
+    from flow_model import FlowModelB200, FlowSpec, make_weights
+
+    spec = FlowSpec(blocks=2)
+    w = make_weights(spec, seed=12, device="cuda")
+    m = FlowModelB200(w)
+    x, cam, cond = _inputs(spec, seed=13)
+    ins = [torch.from_numpy(a).cuda() for a in (x, cam, np.array([640.0, 640.0], np.float32), cond)]
+    vl, vc = (v.clone() for v in m.forward(*ins))
+    m._embed(*ins)
+    for i in range(spec.blocks):
+        m._block_fused(i, cached=False)
+    ul, uc = m._final_layer()
+    torch.cuda.synchronize()
+    assert torch.equal(vl, ul) and torch.equal(vc, uc)

@@ -77,6 +77,8 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "triposplat_b200_qkv_split_rows_f32": ([VP] * 4 + [I] * 6 + [VP, VP], I),
     "triposplat_b200_kv_planes_gather": ([VP, VP, I, I, I, I], I),
     "triposplat_b200_attend_rows_f32": ([VP, VP, VP, I, I, I, I], I),
+    "triposplat_b200_kv_split_f32": ([VP, VP, I, I, I, VP], I),
+    "triposplat_b200_q_split_f32": ([VP, VP, I, I, I, VP], I),
     "triposplat_sdpa_key_tile": ([], I),
     "triposplat_sdpa_query_block": ([], I),
     "triposplat_sdpa_q8t512_profile_reset": ([], None),

@@ -64,9 +64,23 @@ class CfgSplitSampler:
         self.x_cam.copy_(noise_cam.reshape(self.x_cam.shape), non_blocking=True)
         c = cond if self.branch == 0 else neg_cond
         self.cond.copy_(c.reshape(self.cond.shape), non_blocking=True)
+        if self.cached:  # the branch's condition path, once per image
+            self.model.precompute_condition(self.cond)
+
+    @property
+    def cached(self) -> bool:
+        return getattr(self.model, "cond_planes", None) is not None
+
+    def refresh_condition(self):
+        """Re-run the once-per-image condition path on the loaded condition tokens."""
+        if self.cached:
+            self.model.precompute_condition(self.cond)
 
     def _forward_body(self):
-        v_lat, v_cam = self.model.forward(self.x_lat, self.x_cam, self.t_cur, self.cond)
+        if self.cached:
+            v_lat, v_cam = self.model.forward_cached(self.x_lat, self.x_cam, self.t_cur)
+        else:
+            v_lat, v_cam = self.model.forward(self.x_lat, self.x_cam, self.t_cur, self.cond)
         self.send[:self.n_lat].copy_(v_lat.reshape(-1))
         self.send[self.n_lat:].copy_(v_cam.reshape(-1))
 

@@ -1414,6 +1414,73 @@ int triposplat_b200_attend_rows_f32(const void* q_planes, const void* kv_planes,
   return sdpa_attend(sp, nullptr, 0, out_blhd, BH, H, Lq, L, 1, current_stream());
 }
 
+// ---- cached condition keys (no reference counterpart) ----------------------------------
+// The condition tokens do not change across sampler steps, so their keys / values are split
+// once per image (triposplat_b200_kv_split_f32: per-head RMSNorm of the keys, values as
+// they are) into a K / V plane set that every step's cross-attention reads; per step only
+// the queries are split (triposplat_b200_q_split_f32) before triposplat_b200_attend_rows_f32.
+// The three calls run the kernels of triposplat_b200_q_kv_rmsnorm_sdpa_f32 with the same
+// arguments: bit-identical outputs.
+
+// kv [B, Lk, 2, H, 64] -> kv_planes (layout of triposplat_b200_attn_kv_planes_bytes(B * H, Lk))
+int triposplat_b200_kv_split_f32(const float* kv, const float* k_gamma, int B, int Lk, int H,
+                                 void* kv_planes) {
+  using namespace tsb;
+  using namespace tsb::sdpa;
+  if (!kv || !k_gamma || !kv_planes) return kNullPointer;
+  if (B <= 0 || Lk <= 0 || H <= 0) return kBadDims;
+  if (!aligned16(kv) || !aligned16(k_gamma) || (reinterpret_cast<uintptr_t>(kv_planes) & 255))
+    return kBadAlignment;
+  int st = entry_check();
+  if (st != kOk) return st;
+  if (!is_device_pointer(kv) || !is_device_pointer(k_gamma) || !is_device_pointer(kv_planes))
+    return kNotDevicePointer;
+  const int64_t BH = (int64_t)B * H;
+  size_t off[6];
+  int T, Lkt;
+  kv_planes_layout(BH, Lk, off, T, Lkt);
+  uint8_t* base = static_cast<uint8_t*>(kv_planes);
+  ensure_qkv_split_attr();
+  cudaStream_t stream = current_stream();
+  {
+    LaunchScope scope(kKSdpaSplit, stream);
+    qkv_split_k<true><<<dim3(T, (unsigned)BH), 256, QKV_SPLIT_SMEM, stream>>>(
+        nullptr, kv, nullptr, nullptr, k_gamma, k_gamma, H, 0, Lk, Lkt, 1, 0, 0, Lk, 0, nullptr,
+        nullptr, nullptr, reinterpret_cast<__half*>(base + off[0]), reinterpret_cast<__half*>(base + off[1]),
+        reinterpret_cast<__half*>(base + off[2]), reinterpret_cast<__half*>(base + off[3]),
+        reinterpret_cast<float*>(base + off[4]), reinterpret_cast<float*>(base + off[5]));
+  }
+  return launch_status();
+}
+
+// q [B, Lq, H, 64] -> per-head RMSNorm (no rotation) into q_planes
+// (layout of triposplat_b200_attn_q_planes_bytes(B * H, Lq))
+int triposplat_b200_q_split_f32(const float* q, const float* q_gamma, int B, int Lq, int H,
+                                void* q_planes) {
+  using namespace tsb;
+  using namespace tsb::sdpa;
+  if (!q || !q_gamma || !q_planes) return kNullPointer;
+  if (B <= 0 || Lq <= 0 || H <= 0) return kBadDims;
+  if (!aligned16(q) || !aligned16(q_gamma) || (reinterpret_cast<uintptr_t>(q_planes) & 255))
+    return kBadAlignment;
+  int st = entry_check();
+  if (st != kOk) return st;
+  if (!is_device_pointer(q) || !is_device_pointer(q_gamma) || !is_device_pointer(q_planes))
+    return kNotDevicePointer;
+  const int64_t BH = (int64_t)B * H;
+  size_t off[2];
+  q_planes_layout(BH, Lq, off);
+  uint8_t* base = static_cast<uint8_t*>(q_planes);
+  cudaStream_t stream = current_stream();
+  {
+    LaunchScope scope(kKSdpaSplit, stream);
+    selected_q_split_k<<<dim3((Lq + BKV - 1) / BKV, (unsigned)BH), 256, 0, stream>>>(
+        q, nullptr, nullptr, q_gamma, H, Lq, Lq, 1, reinterpret_cast<__half*>(base),
+        reinterpret_cast<__half*>(base + off[0]), reinterpret_cast<float*>(base + off[1]));
+  }
+  return launch_status();
+}
+
 // scripts/native_sdpa_avx512_exact_q8t512.c:64-70: tile sizes of this implementation
 int triposplat_sdpa_key_tile(void) { return tsb::sdpa::BKV; }
 int triposplat_sdpa_query_block(void) { return tsb::sdpa::BQ; }

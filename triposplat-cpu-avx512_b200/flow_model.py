@@ -219,7 +219,16 @@ def make_weights(spec: FlowSpec, seed: int = 0, device: str = "cuda",
 
 
 class FlowModelB200:
-    """Forward of the synthetic flow model on preallocated device buffers (batch = CFG pair)."""
+    """Forward of the synthetic flow model on preallocated device buffers (batch = CFG pair).
+
+    ``forward(x_lat, cam, t1000, cond)`` runs everything.  With the fused path the condition
+    side can be cached across sampler steps, as the reference's attention patch caches its
+    static condition context (scripts/triposplat_attention_patch.py:906-975):
+    ``precompute_condition(cond)`` runs the condition embedder / refiner and every block's
+    cross K / V projection + split once, and ``forward_cached(x_lat, cam, t1000)`` runs the
+    rest; together they give ``forward``'s bits."""
+
+    supports_condition_cache = True
 
     def __init__(self, weights: FlowWeights, batch: int = 2, device: str = "cuda",
                  fused: bool = True):
@@ -275,6 +284,15 @@ class FlowModelB200:
         # per-block adaLN tables, expanded over the batch so they add elementwise
         self.tables = {i: weights.params[f"blocks.{i}.table"][:, None, :].expand(6, B, h).contiguous()
                        for i in range(s.blocks)}
+        # condition cache (fused path): per block the split K / V planes of the condition
+        # tokens, filled once per image by precompute_condition, read by every step
+        self.cond_planes = None
+        if fused and self.supports_condition_cache:
+            kvb = int(self.lib.triposplat_b200_attn_kv_planes_bytes(B * H, Mc))
+            self.cond_planes = torch.empty(s.blocks, kvb + 256, dtype=torch.uint8, device=device)
+            self.cond_plane_bytes = kvb + 256
+            qb = int(self.lib.triposplat_b200_attn_q_planes_bytes(B * H, L))
+            self.buf["cq_planes"] = torch.empty(qb + 256, dtype=torch.uint8, device=device)
 
     # -- helpers -------------------------------------------------------------------------
     def _lin(self, name, x, out, start=0, count=None):
@@ -311,10 +329,42 @@ class FlowModelB200:
     # -- forward -------------------------------------------------------------------------
     def forward(self, x_lat, cam, t1000, cond):
         """x_lat [B,Nl,Cl], cam [B,1,Cc], t1000 [B] (already x1000), cond [B,Mc,Dc]."""
+        if self.cond_planes is not None:
+            self.precompute_condition(cond)
+            return self.forward_cached(x_lat, cam, t1000)
         self._embed(x_lat, cam, t1000, cond)
         for i in range(self.spec.blocks):
             self._block(i)
         return self._final_layer()
+
+    def precompute_condition(self, cond):
+        """The condition path of one image: embedder -> SiLU -> refiner, then per block the
+        cross K / V projection and its split planes (keys RMS-normalised per head)."""
+        s, b, lib = self.spec, self.buf, self.lib
+        B, H, Mc = self.B, s.heads, s.cond_tokens
+        if self.cond_planes is None:
+            raise RuntimeError("the condition cache needs the fused path")
+        _native.use_current_stream(lib)
+        self._lin("cond_embedder", cond, b["c0"])
+        self._silu(b["c0"], b["c0"])
+        self._lin("cond_refiner", b["c0"], b["c"])
+        self._split(b["c"], self._split_ptr("sp_c"))
+        for i in range(s.blocks):
+            p = f"blocks.{i}."
+            self._lin_split(p + "cross_kv", self._split_ptr("sp_c"), B * Mc, b["ckv"])
+            self._ok(lib.triposplat_b200_kv_split_f32(
+                b["ckv"].data_ptr(), self.w.params[p + "ck_gamma"].data_ptr(), B, Mc, H,
+                self._cond_plane_ptr(i)), "condition kv split")
+
+    def forward_cached(self, x_lat, cam, t1000):
+        """forward() after precompute_condition() for this image's condition tokens."""
+        self._embed(x_lat, cam, t1000, None)
+        for i in range(self.spec.blocks):
+            self._block_fused(i, cached=True)
+        return self._final_layer()
+
+    def _cond_plane_ptr(self, i):
+        return (self.cond_planes[i].data_ptr() + 255) & ~255
 
     def _embed(self, x_lat, cam, t1000, cond):
         """Timestep / adaLN / condition / token embeddings into the block inputs."""
@@ -333,12 +383,13 @@ class FlowModelB200:
             self._lin("adaLN", b["stemb"], b["mod"][c], start=c * h, count=h)
         for c in range(2):
             self._lin("final_adaLN", b["stemb"], b["fmod"][c], start=c * h, count=h)
-        # condition tokens
-        self._lin("cond_embedder", cond, b["c0"])
-        self._silu(b["c0"], b["c0"])
-        self._lin("cond_refiner", b["c0"], b["c"])
-        if self.fused:  # every block's cross_kv GEMM reads the same split condition tokens
-            self._split(b["c"], self._split_ptr("sp_c"))
+        # condition tokens (cond None: cached by precompute_condition)
+        if cond is not None:
+            self._lin("cond_embedder", cond, b["c0"])
+            self._silu(b["c0"], b["c0"])
+            self._lin("cond_refiner", b["c0"], b["c"])
+            if self.fused:  # every block's cross_kv GEMM reads the same split condition tokens
+                self._split(b["c"], self._split_ptr("sp_c"))
         # token embedding: [latent | camera]
         x = b["x"]
         for bb in range(B):  # per batch: the camera row sits between the batches' latents
@@ -387,9 +438,10 @@ class FlowModelB200:
             return self._block_fused(i)
         return self._block_reference_ops(i)
 
-    def _block_fused(self, i):
+    def _block_fused(self, i, cached=False):
         """Same block, with LN/modulation fused into the activation split, GELU into the fc1
-        epilogue and the (gated) residual adds into the out / cross_out / fc2 epilogues."""
+        epilogue and the (gated) residual adds into the out / cross_out / fc2 epilogues;
+        cached: the condition keys / values come from precompute_condition."""
         s, b, lib = self.spec, self.buf, self.lib
         B, L, h, H, Mc = self.B, s.seq, s.hidden, s.heads, s.cond_tokens
         rows = B * L
@@ -413,10 +465,17 @@ class FlowModelB200:
         # cross-attention
         self._ln_split(x, sph)
         self._lin_split(p + "cross_q", sph, rows, y)
-        self._lin_split(p + "cross_kv", self._split_ptr("sp_c"), B * Mc, b["ckv"])
-        self._ok(lib.triposplat_b200_q_kv_rmsnorm_sdpa_f32(
-            y.data_ptr(), b["ckv"].data_ptr(), prm[p + "cq_gamma"].data_ptr(),
-            prm[p + "ck_gamma"].data_ptr(), b["o"].data_ptr(), B, L, Mc, H), "cross_attention")
+        if cached:
+            qpl = self._split_ptr("cq_planes")
+            self._ok(lib.triposplat_b200_q_split_f32(y.data_ptr(), prm[p + "cq_gamma"].data_ptr(), B, L, H,
+                                                     qpl), "cross q split")
+            self._ok(lib.triposplat_b200_attend_rows_f32(qpl, self._cond_plane_ptr(i), b["o"].data_ptr(),
+                                                         B, H, L, Mc), "cross_attention")
+        else:
+            self._lin_split(p + "cross_kv", self._split_ptr("sp_c"), B * Mc, b["ckv"])
+            self._ok(lib.triposplat_b200_q_kv_rmsnorm_sdpa_f32(
+                y.data_ptr(), b["ckv"].data_ptr(), prm[p + "cq_gamma"].data_ptr(),
+                prm[p + "ck_gamma"].data_ptr(), b["o"].data_ptr(), B, L, Mc, H), "cross_attention")
         self._split(b["o"], sph)
         self._lin_split(p + "cross_out", sph, rows, x, mode=3)
         # MLP
@@ -496,17 +555,35 @@ class CfgEulerSampler:
         self.graph_stream = None
 
     def load(self, noise_lat, noise_cam, cond, neg_cond):
+        """One image's inputs; with the condition cache the condition path runs here, once
+        per image, and every step reuses it."""
         self.x_lat[0].copy_(noise_lat.reshape(self.x_lat[0].shape), non_blocking=True)
         self.x_cam[0].copy_(noise_cam.reshape(self.x_cam[0].shape), non_blocking=True)
         self.cond_pair[0].copy_(cond.reshape(self.cond_pair[0].shape), non_blocking=True)
         self.cond_pair[1].copy_(neg_cond.reshape(self.cond_pair[1].shape), non_blocking=True)
+        if self.cached:
+            self.model.precompute_condition(self.cond_pair)
+
+    @property
+    def cached(self) -> bool:
+        return getattr(self.model, "cond_planes", None) is not None
+
+    def refresh_condition(self):
+        """Re-run the once-per-image condition path on the loaded condition tokens."""
+        if self.cached:
+            self.model.precompute_condition(self.cond_pair)
+
+    def _forward(self):
+        if self.cached:
+            return self.model.forward_cached(self.x_lat, self.x_cam, self.t_cur)
+        return self.model.forward(self.x_lat, self.x_cam, self.t_cur, self.cond_pair)
 
     def _body(self):
         """One sampler step reading t_cur / dt_cur: everything a CUDA graph captures."""
         m, lib = self.model, self.model.lib
         self.x_lat[1].copy_(self.x_lat[0])
         self.x_cam[1].copy_(self.x_cam[0])
-        v_lat, v_cam = m.forward(self.x_lat, self.x_cam, self.t_cur, self.cond_pair)
+        v_lat, v_cam = self._forward()
         for x, v in ((self.x_lat, v_lat), (self.x_cam, v_cam)):
             # CFG combine + Euler step in one kernel (bit-identical to the reference's
             # triposplat_cfg_combine_inplace + triposplat_euler_update_inplace pair)
@@ -522,7 +599,7 @@ class CfgEulerSampler:
         self.t_cur.copy_(self.t_pair[i])
         self.x_lat[1].copy_(self.x_lat[0])
         self.x_cam[1].copy_(self.x_cam[0])
-        v_lat, v_cam = self.model.forward(self.x_lat, self.x_cam, self.t_cur, self.cond_pair)
+        v_lat, v_cam = self._forward()
         return v_lat.clone(), v_cam.clone()
 
     def step(self, i: int):

@@ -147,6 +147,8 @@ class HeadShardedFlowModel(FlowModelB200):
     live in IPC-shared buffers and one fused kernel reads all ranks' partials over NVLink
     and updates the residual (``PeerReduce``)."""
 
+    supports_condition_cache = False  # the cross K / V are column windows of this rank's heads
+
     def __init__(self, weights: FlowWeights, rank: int, tp: int, batch: int = 1,
                  device: str = "cuda", group=None, all_reduce=None, reduce: str = "nccl"):
         import torch

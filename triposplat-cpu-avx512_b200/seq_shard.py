@@ -184,18 +184,27 @@ class SeqShardedFlowModel(FlowModelB200):
 
     # -- forward ---------------------------------------------------------------------------
     def forward(self, x_lat, cam, t1000, cond):
-        for _ in self.forward_steps(x_lat, cam, t1000, cond):
+        self.precompute_condition(cond)
+        return self.forward_cached(x_lat, cam, t1000)
+
+    def forward_cached(self, x_lat, cam, t1000):
+        for _ in self.forward_steps(x_lat, cam, t1000, None):
             raise RuntimeError("forward() runs the peer exchange; drive lockstep ranks with run_lockstep")
         return self.chunk
 
-    def forward_steps(self, x_lat, cam, t1000, cond):
-        self._embed_rows(x_lat, cam, t1000, cond)
+    def forward_steps(self, x_lat, cam, t1000, cond=None):
+        """The forward as a generator yielding at each exchange point (the plane set index);
+        cond None: the condition cache of precompute_condition is current."""
+        if cond is not None:
+            self.precompute_condition(cond)
+        self._embed_rows(x_lat, cam, t1000)
         for i in range(self.spec.blocks):
             yield from self._block_rows(i)
         self._final_rows()
 
-    def _embed_rows(self, x_lat, cam, t1000, cond):
-        """Replicated timestep / adaLN / condition path, then this rank's token rows."""
+    def _embed_rows(self, x_lat, cam, t1000):
+        """Replicated timestep / adaLN path, then this rank's token rows (the condition path
+        is cached by precompute_condition)."""
         s, b, lib = self.spec, self.buf, self.lib
         B, h = self.B, s.hidden
         _native.use_current_stream(lib)
@@ -210,10 +219,6 @@ class SeqShardedFlowModel(FlowModelB200):
             self._lin("adaLN", b["stemb"], b["mod"][c], start=c * h, count=h)
         for c in range(2):
             self._lin("final_adaLN", b["stemb"], b["fmod"][c], start=c * h, count=h)
-        self._lin("cond_embedder", cond, b["c0"])
-        self._silu(b["c0"], b["c0"])
-        self._lin("cond_refiner", b["c0"], b["c"])
-        self._split(b["c"], self._split_ptr("sp_c"))
         x = self.loc["x"]
         for bb in range(B):
             self._lin("x_embedder", x_lat[bb, self.t0:self.t0 + self.nlat], x[bb, :self.nlat])
@@ -249,13 +254,13 @@ class SeqShardedFlowModel(FlowModelB200):
         self._ok(lib.triposplat_b200_attend_rows_f32(qpl, kv, o.data_ptr(), B, H, Lloc, L), "attend_rows")
         self._split(o, sph)
         self._lin_split(p + "out", sph, rows, x, mode=2, gate=gate_msa, gate_ld=h, rows_per_batch=Lloc)
-        # cross-attention of this rank's rows to the condition tokens
+        # cross-attention of this rank's rows to the cached condition keys / values
         self._ln_split_rows(x, sph)
         self._lin_split(p + "cross_q", sph, rows, y)
-        self._lin_split(p + "cross_kv", self._split_ptr("sp_c"), B * Mc, b["ckv"])
-        self._ok(lib.triposplat_b200_q_kv_rmsnorm_sdpa_f32(
-            y.data_ptr(), b["ckv"].data_ptr(), prm[p + "cq_gamma"].data_ptr(),
-            prm[p + "ck_gamma"].data_ptr(), o.data_ptr(), B, Lloc, Mc, H), "cross_attention")
+        self._ok(lib.triposplat_b200_q_split_f32(y.data_ptr(), prm[p + "cq_gamma"].data_ptr(), B, Lloc, H,
+                                                 qpl), "cross q split")
+        self._ok(lib.triposplat_b200_attend_rows_f32(qpl, self._cond_plane_ptr(i), o.data_ptr(), B, H,
+                                                     Lloc, Mc), "cross_attention")
         self._split(o, sph)
         self._lin_split(p + "cross_out", sph, rows, x, mode=3)
         # MLP
@@ -341,9 +346,16 @@ class SeqCfgSampler:
         self.x_cam.copy_(noise_cam.reshape(self.x_cam.shape), non_blocking=True)
         c = cond if self.branch == 0 else neg_cond
         self.cond.copy_(c.reshape(self.cond.shape), non_blocking=True)
+        self.model.precompute_condition(self.cond)  # once per image
+
+    cached = True
+
+    def refresh_condition(self):
+        """Re-run the once-per-image condition path on the loaded condition tokens."""
+        self.model.precompute_condition(self.cond)
 
     def _forward_body(self):
-        self.model.forward(self.x_lat, self.x_cam, self.t_cur, self.cond)
+        self.model.forward_cached(self.x_lat, self.x_cam, self.t_cur)
 
     def _all_gather(self, send, recv):
         import torch.distributed as dist
