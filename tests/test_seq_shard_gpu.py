@@ -36,10 +36,11 @@ def _inputs(spec, batch, device, seed=31):
 
 
 def _assemble(chunks, spec, world):
-    """Per-rank chunks [B, n_lat/world + cam] -> latent [B, Nl, C] and camera [B, 1, Cc]."""
+    """Per-rank chunks [B, n_lat/world + cam (+ padding)] -> latent [B, Nl, C] and camera
+    [B, 1, Cc]."""
     cl = (spec.latent_tokens // world) * spec.latent_dim
     lat = torch.cat([c[:, :cl] for c in chunks], dim=1).view(-1, spec.latent_tokens, spec.latent_dim)
-    return lat, chunks[-1][:, cl:].reshape(-1, 1, spec.camera_dim)
+    return lat, chunks[-1][:, cl:cl + spec.camera_dim].reshape(-1, 1, spec.camera_dim)
 
 
 @pytest.mark.parametrize("world,batch", [(2, 1), (4, 1), (4, 2)])

@@ -681,8 +681,9 @@ __global__ void __launch_bounds__(256) nf24_split_rows_reg(const float* __restri
   store_split_row<NV>(v, mx, lane, hi + (int64_t)row * K, lo + (int64_t)row * K, rs + row);
 }
 
+// four CTAs (32 rows in flight) per SM: the row loads are the kernel's latency
 template <int NV>
-__global__ void __launch_bounds__(256) ln_modulate_split_reg(
+__global__ void __launch_bounds__(256, 4) ln_modulate_split_reg(
     const float* __restrict__ x, int M, int Mp, float eps, const float* __restrict__ shift,
     const float* __restrict__ scale, int mod_ld, int rows_per_batch, __half* __restrict__ hi,
     __half* __restrict__ lo, float* __restrict__ rs) {

@@ -768,7 +768,7 @@ __device__ __forceinline__ void emit_q_row(__half* __restrict__ qhi, __half* __r
   if (lane == 0) qinv[row] = ldexpf(1.0f, -sq);
 }
 
-// Key tiles tile0 + blockIdx.x of the sequence (Lk tokens).  kvsrc holds src_L token rows
+// Key tiles tile0 + blockIdx.y of the sequence (Lk tokens).  kvsrc holds src_L token rows
 // per batch starting at token src_t0 (the whole sequence: 0, Lk; a query-row shard: its own
 // token range); self-attention Q rows of token t go to row t - q_t0 of the Q planes.
 template <bool kSelected>
@@ -784,9 +784,11 @@ __global__ void __launch_bounds__(256, 3) qkv_split_k(
   float(*vt)[D + 1] = reinterpret_cast<float(*)[D + 1]>(sm_kv);  // [BKV][65]: V for the transpose
   __shared__ float red[2][8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y, b = bh / H, h = bh % H;
+  // heads fastest (blockIdx.x): CTAs running together read the same token rows' heads, so
+  // each token's q / k / v row of all heads streams from DRAM once, in order
+  const int bh = blockIdx.x, b = bh / H, h = bh % H;
   const int fbb = fb == 1 ? 0 : b;
-  const int tile = blockIdx.x + tile0, T = Lkt / BKV;
+  const int tile = blockIdx.y + tile0, T = Lkt / BKV;
   const int t_end = min(Lk, src_t0 + src_L);  // tokens past it read as zeros
   const float2 gq = reinterpret_cast<const float2*>(qg + (int64_t)h * 64)[lane];
   const float2 gk = reinterpret_cast<const float2*>(kg + (int64_t)h * 64)[lane];
@@ -884,9 +886,9 @@ __global__ void __launch_bounds__(256) selected_q_split_k(
     const float* __restrict__ qg, int H, int Lq, int Lk, int fb, __half* __restrict__ qhi,
     __half* __restrict__ qlo, float* __restrict__ qinv) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y, b = bh / H, h = bh % H;
+  const int bh = blockIdx.x, b = bh / H, h = bh % H;  // heads fastest, as qkv_split_k
   const int fbb = fb == 1 ? 0 : b;
-  const int tile = blockIdx.x;
+  const int tile = blockIdx.y;
   const float2 gq = reinterpret_cast<const float2*>(qg + (int64_t)h * 64)[lane];
   for (int j0 = 0; j0 < BKV / 8; j0 += 4) {
     float2 qx[4], fr[4];
@@ -1183,13 +1185,13 @@ static int qkv_sdpa_launch(const float* qsrc, const float* kvsrc, const float* f
   // shared-memory V staging; selected queries in their own kernel without shared memory
   {
     LaunchScope scope(kKSdpaSplit, stream);
-    qkv_split_k<kSelected><<<dim3(sp.T, (unsigned)BH), 256, QKV_SPLIT_SMEM, stream>>>(
+    qkv_split_k<kSelected><<<dim3((unsigned)BH, sp.T), 256, QKV_SPLIT_SMEM, stream>>>(
         qsrc, kvsrc, freqs, sel, qg, kg, H, Lq, Lk, sp.Lkt, fb, 0, 0, Lk, 0, sp.qhi, sp.qlo, sp.qinv,
         sp.khi, sp.klo, sp.vhi, sp.vlo, sp.kinv, sp.vinv);
   }
   if (kSelected) {
     LaunchScope scope(kKSdpaSplit, stream);
-    selected_q_split_k<<<dim3(q_tiles, (unsigned)BH), 256, 0, stream>>>(
+    selected_q_split_k<<<dim3((unsigned)BH, q_tiles), 256, 0, stream>>>(
         qsrc, freqs, sel, qg, H, Lq, Lk, fb, sp.qhi, sp.qlo, sp.qinv);
   }
   if ((st = launch_status()) != kOk) return st;
@@ -1348,7 +1350,7 @@ int triposplat_b200_qkv_split_rows_f32(const float* qkv_rows, const float* frequ
   const int tile0 = t0 / BKV, tiles = (t1 + BKV - 1) / BKV - tile0;
   {
     LaunchScope scope(kKSdpaSplit, stream);
-    qkv_split_k<false><<<dim3(tiles, (unsigned)BH), 256, QKV_SPLIT_SMEM, stream>>>(
+    qkv_split_k<false><<<dim3((unsigned)BH, tiles), 256, QKV_SPLIT_SMEM, stream>>>(
         nullptr, qkv_rows, frequencies, nullptr, q_gamma, k_gamma, H, Lq, L, sp.Lkt,
         frequency_batches, tile0, t0, Lq, t0, sp.qhi, sp.qlo, sp.qinv, sp.khi, sp.klo, sp.vhi,
         sp.vlo, sp.kinv, sp.vinv);
@@ -1444,7 +1446,7 @@ int triposplat_b200_kv_split_f32(const float* kv, const float* k_gamma, int B, i
   cudaStream_t stream = current_stream();
   {
     LaunchScope scope(kKSdpaSplit, stream);
-    qkv_split_k<true><<<dim3(T, (unsigned)BH), 256, QKV_SPLIT_SMEM, stream>>>(
+    qkv_split_k<true><<<dim3((unsigned)BH, T), 256, QKV_SPLIT_SMEM, stream>>>(
         nullptr, kv, nullptr, nullptr, k_gamma, k_gamma, H, 0, Lk, Lkt, 1, 0, 0, Lk, 0, nullptr,
         nullptr, nullptr, reinterpret_cast<__half*>(base + off[0]), reinterpret_cast<__half*>(base + off[1]),
         reinterpret_cast<__half*>(base + off[2]), reinterpret_cast<__half*>(base + off[3]),
@@ -1474,7 +1476,7 @@ int triposplat_b200_q_split_f32(const float* q, const float* q_gamma, int B, int
   cudaStream_t stream = current_stream();
   {
     LaunchScope scope(kKSdpaSplit, stream);
-    selected_q_split_k<<<dim3((Lq + BKV - 1) / BKV, (unsigned)BH), 256, 0, stream>>>(
+    selected_q_split_k<<<dim3((unsigned)BH, (Lq + BKV - 1) / BKV), 256, 0, stream>>>(
         q, nullptr, nullptr, q_gamma, H, Lq, Lq, 1, reinterpret_cast<__half*>(base),
         reinterpret_cast<__half*>(base + off[0]), reinterpret_cast<float*>(base + off[1]));
   }

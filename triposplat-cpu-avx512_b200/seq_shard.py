@@ -113,8 +113,8 @@ class SeqShardedFlowModel(FlowModelB200):
     peer barrier and the pull-gather kernel.  exchange="lockstep": plain device buffers;
     ``forward_steps`` yields at each exchange point and ``run_lockstep`` gathers for all
     ranks (one process, one GPU).  ``forward`` leaves this rank's velocity rows in
-    ``chunk`` [B, (latent_tokens / world) * latent_dim + camera_dim] (camera entries valid
-    on the last rank) and returns it."""
+    ``chunk`` [B, (latent_tokens / world) * latent_dim + camera_dim, padded to 4 floats]
+    (camera entries valid on the last rank) and returns it."""
 
     def __init__(self, weights: FlowWeights, rank: int, world: int, batch: int = 1,
                  device: str = "cuda", group=None, exchange: str = "peer"):
@@ -143,7 +143,9 @@ class SeqShardedFlowModel(FlowModelB200):
                     "o": e(B, Lloc, h, **f32), "qkv": e(B, Lloc, 3 * h, **f32),
                     "hid": e(B, Lloc, s.mlp, **f32)}
         self.chunk_lat = (s.latent_tokens // world) * s.latent_dim
-        self.chunk = torch.zeros(B, self.chunk_lat + s.camera_dim, **f32)
+        # one row per batch, padded to 16 bytes so every row is a tensor-core GEMM output
+        # (the drop-in GEMM sends unaligned outputs to its SIMT kernel, other rounding)
+        self.chunk = torch.zeros(B, (self.chunk_lat + s.camera_dim + 3) // 4 * 4, **f32)
         for name, k in (("sp_hl", h), ("sp_hidl", s.mlp)):
             nbytes = int(self.lib.triposplat_b200_split_bytes(B * Lloc, k))
             self.buf[name] = torch.empty(nbytes + 256, dtype=torch.uint8, device=device)
@@ -277,7 +279,8 @@ class SeqShardedFlowModel(FlowModelB200):
         for bb in range(self.B):
             self._lin("final_linear", a[bb, :self.nlat], self.chunk[bb, :self.nlat * s.latent_dim])
             if self.has_cam:
-                self._lin("camera_head", a[bb, self.nlat:], self.chunk[bb, self.chunk_lat:])
+                self._lin("camera_head", a[bb, self.nlat:],
+                          self.chunk[bb, self.chunk_lat:self.chunk_lat + s.camera_dim])
 
     def close(self):
         if self.peer is not None:
@@ -379,7 +382,7 @@ class SeqCfgSampler:
         _native.use_current_stream(lib)
         parts = [(self.x[r * cl:(r + 1) * cl], self.recv[r, :cl], self.recv[W + r, :cl], cl) for r in range(W)]
         parts.append((self.x[self.n_lat:], self.recv[W - 1, cl:], self.recv[2 * W - 1, cl:],
-                      self.n - self.n_lat))
+                      self.n - self.n_lat))  # the camera entries (the row's padding is not read)
         for x, pos, neg, n in parts:
             st = lib.triposplat_b200_cfg_euler_update_f32(x.data_ptr(), pos.data_ptr(), neg.data_ptr(),
                                                           self.g.data_ptr(), self.dt_cur.data_ptr(), 1, n)
@@ -396,7 +399,7 @@ class SeqCfgSampler:
         m, s = self.model, self.model.spec
         W, cl = m.world, m.chunk_lat
         lat = torch.stack([torch.cat([self.recv[b * W + r, :cl] for r in range(W)]) for b in (0, 1)])
-        cam = torch.stack([self.recv[b * W + W - 1, cl:] for b in (0, 1)])
+        cam = torch.stack([self.recv[b * W + W - 1, cl:cl + s.camera_dim] for b in (0, 1)])
         return lat.view(2, s.latent_tokens, s.latent_dim), cam.view(2, 1, s.camera_dim)
 
     def step(self, i: int):
