@@ -152,9 +152,45 @@ __device__ __forceinline__ uint64_t f2sub(uint64_t a, uint64_t b) {
   return r;
 }
 
+// 2^x on the FMA pipe for a pair of values (the MUFU pipe that ex2 uses is shared by both
+// softmax teams of an SM).  Range reduction x = j + f, j = round-to-nearest(x) by the
+// 1.5 * 2^23 addition, f in [-1/2, 1/2]; 2^f by a degree-5 polynomial whose coefficients
+// minimise the maximum relative error on [-1/2, 1/2] (Remez exchange, computed by
+// csrc/gen_exp2_poly.py: 2.1e-7 in float32 Horner, the order of ex2.approx); 2^j added to
+// the exponent field.  x is clamped at -125 so the result stays a normal float (ex2 gives
+// 0 below -126; both are far below what the fp16 P planes keep).
+// Measured on config 2(a) (B2 H16 L8192, same build): no pairs on the FMA pipe 1.363 ms,
+// a quarter (0x88) 1.445 ms, half (0xAA) 1.572 ms -- the softmax is bound by its dependency
+// chain, not by MUFU throughput, and the polynomial's extra instructions lengthen it; so by
+// default every exponential stays on ex2.
+#ifndef TSB_POLY_PAIRS
+#define TSB_POLY_PAIRS 0x00u  // of each 16-key chunk's 8 pairs, these go to the FMA pipe
+#endif
+constexpr uint32_t kPolyPairs = TSB_POLY_PAIRS;
+__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& p0, float& p1) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  x0 = fmaxf(x0, -125.0f);
+  x1 = fmaxf(x1, -125.0f);
+  const uint64_t xm = f2pack(x0, x1);
+  const uint64_t t = f2add(xm, f2pack(kMagic, kMagic));            // 1.5 * 2^23 + j
+  const uint64_t f = f2sub(xm, f2sub(t, f2pack(kMagic, kMagic)));  // x - j
+  uint64_t r = f2pack(0x1.5c08e6p-10f, 0x1.5c08e6p-10f);
+  r = f2fma(r, f, f2pack(0x1.3d0c52p-7f, 0x1.3d0c52p-7f));
+  r = f2fma(r, f, f2pack(0x1.c6b6e4p-5f, 0x1.c6b6e4p-5f));
+  r = f2fma(r, f, f2pack(0x1.ebf918p-3f, 0x1.ebf918p-3f));
+  r = f2fma(r, f, f2pack(0x1.62e428p-1f, 0x1.62e428p-1f));
+  r = f2fma(r, f, f2pack(0x1.000002p+0f, 0x1.000002p+0f));
+  float r0, r1, t0, t1;
+  f2unpack(r, r0, r1);
+  f2unpack(t, t0, t1);
+  // the low bits of t hold j (two's complement); j << 23 lands on the exponent field
+  p0 = __uint_as_float(__float_as_uint(r0) + (__float_as_uint(t0) << 23));
+  p1 = __uint_as_float(__float_as_uint(r1) + (__float_as_uint(t1) << 23));
+}
+
 // p = 2^(s*c2 (+ bias) + nm) for one 16-key chunk (s[0..15]): two packed partial row sums,
 // fp16 hi/lo split, written over the chunk's scores in tensor memory (8 columns P_hi,
-// 8 columns P_lo).
+// 8 columns P_lo).  The pairs of kPolyPairs take 2^x from exp2_poly2, the others from ex2.
 template <bool PLAIN>
 __device__ __forceinline__ void chunk_exp_store(const uint32_t* s, const float* bt, uint64_t c2x2,
                                                 uint64_t nmx2, uint64_t (&ps)[2], uint32_t taddr) {
@@ -165,7 +201,13 @@ __device__ __forceinline__ void chunk_exp_store(const uint32_t* s, const float* 
     const uint64_t off = PLAIN ? nmx2 : f2add(f2pack(bt[j], bt[j + 1]), nmx2);
     float x0, x1;
     f2unpack(f2fma(sx, c2x2, off), x0, x1);
-    const float p0 = ex2(x0), p1 = ex2(x1);
+    float p0, p1;
+    if ((kPolyPairs >> (j >> 1)) & 1u) {
+      exp2_poly2(x0, x1, p0, p1);
+    } else {
+      p0 = ex2(x0);
+      p1 = ex2(x1);
+    }
     const uint64_t px = f2pack(p0, p1);
     ps[(j >> 1) & 1] = f2add(ps[(j >> 1) & 1], px);
     // hi: p with the 13 low mantissa bits cleared (exact in fp16 for p >= 2^-14),
