@@ -274,6 +274,97 @@ def reference_schedule(steps: int, pieces: int) -> list[list[int]]:
     return [[i % pieces] for i in range(steps)]
 
 
+def run_reference_case(args):
+    """--impl reference --case C: the reference's own AVX-512 kernels for one BASELINE
+    config on the host cores (all of them), median of --steps runs after one warm-up; the
+    same TFLOP/s metric as the b200 case line."""
+    import ctypes
+
+    import numpy as np
+
+    from ref_flow import REF, RefKernels, _bind, _p, host_threads
+
+    if not RefKernels.available():
+        print(json.dumps({"impl": "reference", "case": args.case, "unavailable":
+                          "reference AVX-512 kernels not built or host CPU lacks AVX-512"}))
+        return 0
+    rk = RefKernels()
+    th = rk.th
+    rng = np.random.default_rng(0)
+    f32 = np.float32
+
+    def packed(n, k):  # random codes: the kernels' cost does not depend on the values
+        return {"code01": rng.integers(-540, 541, size=(k, n), dtype=np.int16),
+                "q2": rng.integers(-128, 128, size=(k, n), dtype=np.int8),
+                "scale": np.full(n, 0.02 / 127 / 1024, f32), "bias": rng.standard_normal(n, dtype=f32)}
+
+    if args.case == "gemm1":
+        M, K, N = 4096, 1024, 3072
+        x, w, out = rng.standard_normal((M, K), dtype=f32), packed(N, K), np.empty((M, N), f32)
+        fn = lambda: rk.linear(w, x, out)  # noqa: E731
+        flops, what = 2.0 * M * N * K, "NF24 Linear 4096x1024x3072 (config 1)"
+    elif args.case.startswith("sdpa"):
+        sd = _bind(ctypes.CDLL(str(REF / "libref_sdpa_q8t512.so")), "triposplat_sdpa_f32_avx512_exact_q8t512",
+                   [ctypes.c_void_p] * 5 + [ctypes.c_int] * 8)
+        B, H, Lq = 2, 16, 8192
+        Lk = args.lk or (1374 if args.case == "sdpa2c" else 8192)
+        q = rng.standard_normal((B, H, Lq, 64), dtype=f32)
+        k = rng.standard_normal((B, H, Lk, 64), dtype=f32)
+        v = rng.standard_normal((B, H, Lk, 64), dtype=f32)
+        bias = rng.standard_normal(Lk, dtype=f32) if args.case == "sdpa2b" else None
+        o = np.empty_like(q)
+        fn = lambda: sd(_p(q), _p(k), _p(v), _p(bias), _p(o), B, H, Lq, Lk, 64,  # noqa: E731
+                        int(bias is not None), 0 if bias is None else Lk, th)
+        flops = 4.0 * B * H * Lq * Lk * 64
+        what = {"sdpa2a": "exact SDPA self 2x16x8192^2 (config 2a)",
+                "sdpa2b": "exact SDPA + shared key bias [8192] (config 2b; the reference ABI's bias)",
+                "sdpa2c": "exact SDPA cross 8192x1374 (config 2c)"}[args.case]
+    elif args.case == "mlp3":
+        M, C, F = 8192, 1024, 4096
+        ln = _bind(ctypes.CDLL(str(REF / "libref_norm_rope.so")), "triposplat_layernorm_f32_avx512",
+                   [ctypes.c_void_p] * 4 + [ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_int])
+        x = rng.standard_normal((M, C), dtype=f32)
+        gam, beta = np.ones(C, f32), np.zeros(C, f32)
+        w1, w2 = packed(F, C), packed(C, F)
+        a, hid, y = np.empty_like(x), np.empty((M, F), f32), np.empty((M, C), f32)
+
+        def fn():
+            ln(_p(x), _p(gam), _p(beta), _p(a), M, C, 1e-6, 1, th)
+            rk.linear(w1, a, hid)
+            rk.gelu(_p(hid), _p(hid), hid.size, th)
+            rk.linear(w2, hid, y)
+            rk.add(_p(y), _p(x), y.size, th)
+        flops, what = 2.0 * 2 * M * C * F, "MLP sub-block M=8192 1024-4096-1024 (config 3)"
+    elif args.case == "block4":
+        import cpu_block
+        from flow_model import FlowSpec
+
+        fwd = cpu_block.RefForward(FlowSpec())
+        pieces = fwd.pieces()
+        pieces[0]()
+        fn = pieces[1]
+        L, Mc = 8193, 1374
+        flops = 2.0 * 2 * (L * 1024 * 3072 + 3 * L * 1024 * 1024 + Mc * 1024 * 2048 + 2 * L * 1024 * 4096) \
+            + 4.0 * 2 * 16 * L * (L + Mc) * 64
+        what = "one flow block, B=2 CFG pair, L=8193, 1374 cond tokens (config 4)"
+    else:
+        raise SystemExit(f"no reference case {args.case}")
+    fn()
+    times = []
+    for _ in range(max(1, min(args.steps, 5))):
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+    sec = float(np.median(times))
+    print(json.dumps({"metric": f"{what} TFLOP/s (algorithmic flops)", "value": round(flops / sec / 1e12, 4),
+                      "unit": "TFLOP/s", "impl": "reference", "case": args.case,
+                      "seconds": round(sec, 4), "runs": len(times), "higher_is_better": True,
+                      "cpu_baseline": {"value": round(flops / sec / 1e12, 4), "unit": "TFLOP/s",
+                                       "cores": host_threads(), "kind": "reference",
+                                       "sample": f"median of {len(times)} runs after one warm-up"}}))
+    return 0
+
+
 def run_reference(args):
     """--impl reference: the reference's CPU kernels on the host cores, rank 0 only.
 
@@ -284,6 +375,8 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    if args.case != "model":
+        return run_reference_case(args)
     from flow_model import FlowSpec
     import cpu_block
     from ref_flow import RefKernels
