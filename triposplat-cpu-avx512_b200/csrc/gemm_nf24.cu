@@ -597,6 +597,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // X fp32 [M, K] (row stride stride_x) -> hi, lo fp16 [M, Kp] and inverse row scales rs [Mp].
 // One warp per row; the row is pre-scaled by 2^s so its max lands in [2^14, 2^15) (s clamped
 // to [-60, 60]).  Rows M..Mp-1 only get rs = 0 so every scale the GEMM reads is defined.
+// 2^s (|s| <= 126) built in the exponent field; x * pow2f(s) is the correctly rounded x * 2^s
+__device__ __forceinline__ float pow2f(int s) { return __int_as_float((127 + s) << 23); }
+
 __device__ __forceinline__ int split_shift(float mx) {
   if (!(mx > 0.0f) || !(mx <= 3.402823466e38f)) return 0;
   const int s = 14 - ilogbf(mx);
@@ -622,21 +625,20 @@ __global__ void nf24_split_rows(const float* __restrict__ x, int M, int Mp, int 
   __half* hr = hi + (int64_t)row * Kp;
   __half* lr = lo + (int64_t)row * Kp;
   for (int k = lane * 2; k < Kp; k += 64) {
-    const float a = k < K ? ldexpf(xr[k], shift) : 0.0f;
-    const float b = k + 1 < K ? ldexpf(xr[k + 1], shift) : 0.0f;
+    const float a = k < K ? xr[k] * pow2f(shift) : 0.0f;
+    const float b = k + 1 < K ? xr[k + 1] * pow2f(shift) : 0.0f;
     const __half2 h = __floats2half2_rn(a, b);
     const float2 hf = __half22float2(h);
     *reinterpret_cast<__half2*>(hr + k) = h;
     *reinterpret_cast<__half2*>(lr + k) = __floats2half2_rn(a - hf.x, b - hf.y);
   }
-  if (lane == 0) rs[row] = ldexpf(1.0f, -shift);
+  if (lane == 0) rs[row] = pow2f(-shift);
 }
 
 // Register-resident variants for rows of NV * 128 floats (16-byte aligned rows): the row is
 // read from HBM once (the generic kernels read it two to four times), and the pre-scale is a
 // multiplication by the exact power of two (identical to ldexpf in the normal range the
 // shift keeps the values in).  One warp per row; lane i owns float4 groups i, i+32, ...
-__device__ __forceinline__ float pow2f(int s) { return __int_as_float((127 + s) << 23); }
 
 template <int NV>
 __device__ __forceinline__ void store_split_row(const float4 (&v)[NV], float mx, int lane, __half* hr,
@@ -781,14 +783,14 @@ __global__ void ln_modulate_split(const float* __restrict__ x, int M, int Mp, in
   __half* hr = hi + (int64_t)row * Kp;
   __half* lr = lo + (int64_t)row * Kp;
   for (int k = lane * 2; k < Kp; k += 64) {
-    const float a = k < C ? ldexpf(ln_mod_value(xr, k, mean, inv, sh, sc), shf) : 0.0f;
-    const float bb = k + 1 < C ? ldexpf(ln_mod_value(xr, k + 1, mean, inv, sh, sc), shf) : 0.0f;
+    const float a = k < C ? ln_mod_value(xr, k, mean, inv, sh, sc) * pow2f(shf) : 0.0f;
+    const float bb = k + 1 < C ? ln_mod_value(xr, k + 1, mean, inv, sh, sc) * pow2f(shf) : 0.0f;
     const __half2 h = __floats2half2_rn(a, bb);
     const float2 hf = __half22float2(h);
     *reinterpret_cast<__half2*>(hr + k) = h;
     *reinterpret_cast<__half2*>(lr + k) = __floats2half2_rn(a - hf.x, bb - hf.y);
   }
-  if (lane == 0) rs[row] = ldexpf(1.0f, -shf);
+  if (lane == 0) rs[row] = pow2f(-shf);
 }
 
 // Reference-order scalar kernel: one thread per output, acc = bias, then an in-order

@@ -679,6 +679,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // ---------------------------------------------------------------------------
 // Pre-split kernels
 // ---------------------------------------------------------------------------
+// 2^s for |s| <= 126 built in the exponent field: x * pow2i(s) is the correctly rounded
+// x * 2^s (what ldexpf computes) for a fraction of its instructions
+__device__ __forceinline__ float pow2i(int s) { return __int_as_float((127 + s) << 23); }
+
 __device__ __forceinline__ int pow2_shift(float mx) {
   if (!(mx > 0.0f) || !(mx <= 3.402823466e38f)) return 0;
   int s = 14 - ilogbf(mx);
@@ -696,12 +700,12 @@ __global__ void sdpa_split_q(const float* __restrict__ q, int64_t rows, __half* 
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   const int s = pow2_shift(mx);
-  const float a = ldexpf(v.x, s), b = ldexpf(v.y, s);
+  const float a = v.x * pow2i(s), b = v.y * pow2i(s);
   const __half2 h = __floats2half2_rn(a, b);
   const float2 hf = __half22float2(h);
   *reinterpret_cast<__half2*>(hi + row * D + lane * 2) = h;
   *reinterpret_cast<__half2*>(lo + row * D + lane * 2) = __floats2half2_rn(a - hf.x, b - hf.y);
-  if (lane == 0) qinv[row] = ldexpf(1.0f, -s);
+  if (lane == 0) qinv[row] = pow2i(-s);
 }
 
 // One CTA per (bh, 128-key tile): K -> hi/lo [BH, Lkt, 64]; V -> transposed hi/lo
@@ -752,7 +756,7 @@ __global__ void __launch_bounds__(256) sdpa_split_kv(
     __align__(16) __half l8[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float x = jj < Lk ? ldexpf(kb[(int64_t)jj * j_stride + (int64_t)(d0 + i) * d_stride], sk) : 0.0f;
+      const float x = jj < Lk ? kb[(int64_t)jj * j_stride + (int64_t)(d0 + i) * d_stride] * pow2i(sk) : 0.0f;
       const __half hh = __float2half_rn(x);
       h8[i] = hh;
       l8[i] = __float2half_rn(x - __half2float(hh));
@@ -768,7 +772,7 @@ __global__ void __launch_bounds__(256) sdpa_split_kv(
     __align__(16) __half l8[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float x = ldexpf(vt[jb + i][d], sv);
+      const float x = vt[jb + i][d] * pow2i(sv);
       const __half hh = __float2half_rn(x);
       h8[i] = hh;
       l8[i] = __float2half_rn(x - __half2float(hh));
@@ -778,8 +782,8 @@ __global__ void __launch_bounds__(256) sdpa_split_kv(
     *reinterpret_cast<uint4*>(vlo + off) = *reinterpret_cast<uint4*>(l8);
   }
   if (threadIdx.x == 0) {
-    kinv[(int64_t)bh * T + t] = ldexpf(1.0f, -sk);
-    vinv[(int64_t)bh * T + t] = ldexpf(1.0f, -sv);
+    kinv[(int64_t)bh * T + t] = pow2i(-sk);
+    vinv[(int64_t)bh * T + t] = pow2i(-sv);
   }
 }
 
@@ -802,19 +806,19 @@ __device__ __forceinline__ void emit_q_row(__half* __restrict__ qhi, __half* __r
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   const int sq = pow2_shift(mx);
-  const float a = ldexpf(qy.x, sq), c = ldexpf(qy.y, sq);
+  const float a = qy.x * pow2i(sq), c = qy.y * pow2i(sq);
   const __half2 hh = __floats2half2_rn(a, c);
   const float2 hf = __half22float2(hh);
   *reinterpret_cast<__half2*>(qhi + row * D + lane * 2) = hh;
   *reinterpret_cast<__half2*>(qlo + row * D + lane * 2) = __floats2half2_rn(a - hf.x, c - hf.y);
-  if (lane == 0) qinv[row] = ldexpf(1.0f, -sq);
+  if (lane == 0) qinv[row] = pow2i(-sq);
 }
 
 // Key tiles tile0 + blockIdx.y of the sequence (Lk tokens).  kvsrc holds src_L token rows
 // per batch starting at token src_t0 (the whole sequence: 0, Lk; a query-row shard: its own
 // token range); self-attention Q rows of token t go to row t - q_t0 of the Q planes.
 template <bool kSelected>
-__global__ void __launch_bounds__(256, 3) qkv_split_k(
+__global__ void __launch_bounds__(256, 4) qkv_split_k(
     const float* __restrict__ qsrc, const float* __restrict__ kvsrc, const float* __restrict__ freqs,
     const int64_t* __restrict__ sel, const float* __restrict__ qg, const float* __restrict__ kg,
     int H, int Lq, int Lk, int Lkt, int fb, int tile0, int src_t0, int src_L, int q_t0,
@@ -891,7 +895,7 @@ __global__ void __launch_bounds__(256, 3) qkv_split_k(
     // K rows straight from registers: 128 bytes of hi and of lo per row and warp
 #pragma unroll
     for (int r = 0; r < BKV / 8; ++r) {
-      const float a = ldexpf(kreg[r].x, sk), c = ldexpf(kreg[r].y, sk);
+      const float a = kreg[r].x * pow2i(sk), c = kreg[r].y * pow2i(sk);
       const __half2 hh = __floats2half2_rn(a, c);
       const float2 hf = __half22float2(hh);
       const int64_t off = ((int64_t)bh * Lkt + t0 + warp + 8 * r) * D + 2 * lane;
@@ -904,7 +908,7 @@ __global__ void __launch_bounds__(256, 3) qkv_split_k(
       __align__(16) __half l8[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const float x = ldexpf(vt[jb + i][d], sv);
+        const float x = vt[jb + i][d] * pow2i(sv);
         const __half hh = __float2half_rn(x);
         h8[i] = hh;
         l8[i] = __float2half_rn(x - __half2float(hh));
@@ -914,8 +918,8 @@ __global__ void __launch_bounds__(256, 3) qkv_split_k(
       *reinterpret_cast<uint4*>(vlo + off) = *reinterpret_cast<uint4*>(l8);
     }
     if (threadIdx.x == 0) {
-      kinv[(int64_t)bh * T + tile] = ldexpf(1.0f, -sk);
-      vinv[(int64_t)bh * T + tile] = ldexpf(1.0f, -sv);
+      kinv[(int64_t)bh * T + tile] = pow2i(-sk);
+      vinv[(int64_t)bh * T + tile] = pow2i(-sv);
     }
   }
 }
