@@ -936,10 +936,13 @@ __global__ void __launch_bounds__(256) selected_q_split_k(
   const int fbb = fb == 1 ? 0 : b;
   const int tile = blockIdx.y;
   const float2 gq = reinterpret_cast<const float2*>(qg + (int64_t)h * 64)[lane];
-  for (int j0 = 0; j0 < BKV / 8; j0 += 4) {
-    float2 qx[4], fr[4];
+  // 16 rows per warp in two batches of 8, each batch's loads all issued before its
+  // arithmetic (the kernel is load-latency bound)
+  constexpr int QB = 8;
+  for (int j0 = 0; j0 < BKV / 8; j0 += QB) {
+    float2 qx[QB], fr[QB];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < QB; ++u) {
       const int qi = tile * BKV + warp + 8 * (j0 + u);
       qx[u] = make_float2(0.0f, 0.0f);
       fr[u] = make_float2(1.0f, 0.0f);  // no frequencies: identity rotation
@@ -949,7 +952,7 @@ __global__ void __launch_bounds__(256) selected_q_split_k(
       }
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < QB; ++u) {
       const int qi = tile * BKV + warp + 8 * (j0 + u);
       if (qi < Lq) emit_q_row(qhi, qlo, qinv, (int64_t)bh * Lq + qi, rope_rms64(qx[u], fr[u], gq), lane);
     }
