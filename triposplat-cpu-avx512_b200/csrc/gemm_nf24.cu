@@ -794,23 +794,45 @@ __global__ void ln_modulate_split(const float* __restrict__ x, int M, int Mp, in
 }
 
 // Reference-order scalar kernel: one thread per output, acc = bias, then an in-order
-// fmaf chain over k with w = (float)(256*q01 + q2) * scale[n].
-__global__ void nf24_gemm_simt(const float* __restrict__ x, const int16_t* __restrict__ c01,
-                               const int8_t* __restrict__ q2, const float* __restrict__ scale,
-                               const float* __restrict__ bias, float* __restrict__ out, int M,
-                               int K, int N, int start, int count, int stride_x, int stride_out) {
-  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+// fmaf chain over k with w = (float)(256*q01 + q2) * scale[n] (the reference tail kernel's
+// arithmetic, scripts/gemm_nf24_i16_avx512_tail.c:32-47: bit-identical outputs).
+// The CTA (128 columns of one row) stages SIMT_KC k values of the row and of its columns'
+// combined codes in shared memory, all loads issued together, then each thread runs its
+// in-order chain over the chunk from shared memory (a chain over global memory waits one
+// memory latency per k).
+constexpr int SIMT_KC = 64;
+__global__ void __launch_bounds__(128) nf24_gemm_simt(
+    const float* __restrict__ x, const int16_t* __restrict__ c01, const int8_t* __restrict__ q2,
+    const float* __restrict__ scale, const float* __restrict__ bias, float* __restrict__ out, int M,
+    int K, int N, int start, int count, int stride_x, int stride_out) {
+  __shared__ float xs[SIMT_KC];
+  __shared__ int32_t qs[SIMT_KC][128];
+  const int j0 = blockIdx.x * blockDim.x;
+  const int j = j0 + threadIdx.x;
   const int m = blockIdx.y;
-  if (j >= count || m >= M) return;
-  const int n = start + j;
+  if (m >= M) return;  // CTA-uniform
+  const int cols = min(128, count - j0);
   const float* xr = x + (int64_t)m * stride_x;
-  const float sc = scale[n];
-  float acc = bias[n];
-  for (int k = 0; k < K; ++k) {
-    const int32_t q = (int32_t)c01[(int64_t)k * N + n] * 256 + (int32_t)q2[(int64_t)k * N + n];
-    acc = fmaf(xr[k], __fmul_rn((float)q, sc), acc);
+  const bool active = j < count;
+  const int n = start + (active ? j : 0);
+  const float sc = active ? scale[n] : 0.0f;
+  float acc = active ? bias[n] : 0.0f;
+  for (int k0 = 0; k0 < K; k0 += SIMT_KC) {
+    const int kc = min(SIMT_KC, K - k0);
+    __syncthreads();  // the previous chunk is consumed
+    for (int e = threadIdx.x; e < kc * cols; e += blockDim.x) {
+      const int kk = e / cols, c = e - kk * cols;
+      const int64_t idx = (int64_t)(k0 + kk) * N + start + j0 + c;
+      qs[kk][c] = (int32_t)c01[idx] * 256 + (int32_t)q2[idx];
+    }
+    if (threadIdx.x < kc) xs[threadIdx.x] = xr[k0 + threadIdx.x];
+    __syncthreads();
+    if (active) {
+#pragma unroll 8
+      for (int kk = 0; kk < kc; ++kk) acc = fmaf(xs[kk], __fmul_rn((float)qs[kk][threadIdx.x], sc), acc);
+    }
   }
-  out[(int64_t)m * stride_out + j] = acc;
+  if (active) out[(int64_t)m * stride_out + j] = acc;
 }
 
 }  // namespace gemm
