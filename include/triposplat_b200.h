@@ -127,6 +127,15 @@ int triposplat_b200_split_f32(const float* x, int M, int K, int stride_x, void* 
 int triposplat_b200_ln_modulate_split(const float* x, int M, int C, float eps, const float* shift,
                                       const float* scale, int mod_ld, int rows_per_batch,
                                       void* split);
+/* The same, and in the same pass the row scales of next_split (the split buffer of an
+ * [M, next_K] activation) for a following triposplat_b200_gemm_nf24_split_nk mode 4: per
+ * row 2^-s with GELU(h.W + b) * 2^s < 2^15 for any weight whose columns have euclidean
+ * norm <= wnorm and any bias with |b| <= bmax (Cauchy-Schwarz on the row h as split).
+ * next_split 256-byte aligned; its planes are written by that GEMM. */
+int triposplat_b200_ln_modulate_split_bound(const float* x, int M, int C, float eps,
+                                            const float* shift, const float* scale, int mod_ld,
+                                            int rows_per_batch, void* split, void* next_split,
+                                            int next_K, float wnorm, float bmax);
 /* NF24 GEMM over a split buffer; mode 0 store, 1 GELU(tanh) store, 2 out += gate[b]*y
  * (gate [B, gate_ld], b = row / rows_per_batch), 3 out += y.  N % 16 == 0; out 16-byte
  * aligned with stride_out % 4 == 0 (the outputs leave through TMA stores). */
@@ -152,7 +161,10 @@ int triposplat_b200_nf24_codes_to_nk(const int16_t* code01_t, const int8_t* q2_t
 /* No reference counterpart: triposplat_b200_gemm_nf24_split_range on k-contiguous planes.
  * Row n holds output column n's K codes, rows ldk elements apart (ldk >= K; an offset
  * pointer with ldk > K selects a window of input features).  16-byte aligned planes,
- * ldk % 16 == 0.  Same modes and status codes as the split entry. */
+ * ldk % 16 == 0.  Same modes and status codes as the split entry, plus mode 4: GELU(tanh)
+ * written into `out` read as the split buffer of an [M, count] activation (256-byte
+ * aligned, stride_out == count), under the row scales triposplat_b200_ln_modulate_split_bound
+ * stored there. */
 int triposplat_b200_gemm_nf24_split_nk(const void* split, int M, int K, const int16_t* code01_nk,
                                        const int8_t* q2_nk, int ldk, const float* scale,
                                        const float* bias, float* out, int N, int start, int count,

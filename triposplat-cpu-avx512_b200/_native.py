@@ -55,6 +55,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "triposplat_b200_split_bytes": ([I, I], ctypes.c_uint64),
     "triposplat_b200_split_f32": ([VP, I, I, I, VP], I),
     "triposplat_b200_ln_modulate_split": ([VP, I, I, F, VP, VP, I, I, VP], I),
+    "triposplat_b200_ln_modulate_split_bound": ([VP, I, I, F, VP, VP, I, I, VP, VP, I, F, F], I),
     "triposplat_b200_gemm_nf24_split": ([VP, I, I] + [VP] * 5 + [I, I, I, VP, I, I], I),
     "triposplat_b200_gemm_nf24_split_range": ([VP, I, I] + [VP] * 5 + [I] * 5 + [VP, I, I], I),
     "triposplat_b200_nf24_codes_to_nk": ([VP, VP, I, I, VP, VP], I),

@@ -25,11 +25,14 @@
 //  * Accuracy: the tensor core's fp32 accumulation truncates, so an error that grows
 //    linearly with the number of accumulation steps builds up in a long-lived accumulator
 //    (measured: rmse 1.8e-5 relative at K = 4096, 16x the fp32 reference).  Each k-block
-//    (64 k) is therefore accumulated into a FRESH TMEM partial (double-buffered) and
-//    promoted into round-to-nearest fp32 running sums held in the epilogue warps'
-//    registers, which keeps the error at the level of a 64-long dot product.
+//    (64 k; NK_KPP blocks for the k-contiguous layout) is therefore accumulated into a
+//    FRESH TMEM partial (double-buffered) and promoted into round-to-nearest fp32 running
+//    sums held in the epilogue warps' registers, which keeps the error at the level of a
+//    64- (or 64 * NK_KPP-) long dot product.
 //    Epilogue: y = sum * rowscale[m] * 256*scale[n] + bias[n], then one of: store,
-//    GELU(tanh) + store, gated residual out += gate[b] * y, residual out += y.
+//    GELU(tanh) + store, gated residual out += gate[b] * y, residual out += y, or
+//    GELU(tanh) written straight into the next GEMM's split format (fp16 hi / lo planes
+//    under a per-row power-of-two pre-scale fixed beforehand from a bound on the row).
 //
 // Warp roles (448 threads, one CTA per SM):
 //   warp 0       TMA producer (codes and X planes)
@@ -82,6 +85,16 @@ constexpr int NK_EPI_PAIRS = (BK / 2 - NK_DEC_PAIRS) / 2;
 static_assert(NK_DEC_PAIRS % 2 == 0 && NK_EPI_PAIRS % 2 == 0 &&
               NK_DEC_PAIRS + 2 * NK_EPI_PAIRS == BK / 2, "k-contiguous decode shares");
 constexpr int NK_DEC_ARRIVALS = 4 + (NK_EPI_PAIRS ? NUM_EPI_WARPS : 0);
+// k-blocks accumulated in one TMEM partial before it is promoted, for the k-contiguous
+// layout (whose epilogue warps only promote).  Two halve the promotions and their barrier
+// round trips per k; the partial's truncation error grows with its length (about sqrt(2)
+// over one block's, still well inside fp32 semantics).  The reference layout promotes
+// every block: its epilogue warps' decode share is paced by the per-block completions.
+#ifndef TSB_GEMM_KPP
+#define TSB_GEMM_KPP 2
+#endif
+constexpr int NK_KPP = TSB_GEMM_KPP;
+static_assert(NK_KPP == 1 || NK_KPP == 2 || NK_KPP == 4, "k-blocks per partial");
 constexpr int TMEM_COLS = 512;
 constexpr int ACC_COL = 0;        // 2 partial buffers x BM fp32 columns
 constexpr int A_COL = 2 * BM;     // AS stages x (32 cols A1 + 32 cols A2)
@@ -96,11 +109,11 @@ constexpr int OUT_STAGE_BYTES = NUM_EPI_WARPS * 2 * OUT_CHUNK * 4;  // 24 KB
 static_assert(EPI_COLS % OUT_ROWS == 0, "whole chunks per epilogue warp");
 constexpr int NUM_BARS = 2 * XS + 2 * CS + 2 * AS + 5;
 constexpr int SMEM_BYTES = 1024 /*align slack*/ + XS * X_STAGE + CS * C_STAGE + OUT_STAGE_BYTES +
-                           NUM_EPI_WARPS * EPI_COLS * 4 + NUM_BARS * 8 + 16;
+                           2 * NUM_EPI_WARPS * EPI_COLS * 4 + NUM_BARS * 8 + 16;
 static_assert(SMEM_BYTES <= 232448, "shared memory per block");
 
 
-enum Epilogue : int { kStore = 0, kGelu = 1, kGatedResidual = 2, kResidual = 3 };
+enum Epilogue : int { kStore = 0, kGelu = 1, kGatedResidual = 2, kResidual = 3, kGeluSplit = 4 };
 
 struct Params {
   const float* rscale;  // [Mp] inverse row pre-scale of the split X
@@ -112,6 +125,7 @@ struct Params {
   const float* gate;    // kGatedResidual: gate[(m / rows_per_batch) * gate_ld + n]
   int gate_ld, rows_per_batch;
   int* status;
+  const float* next_rs;  // kGeluSplit: [Mp] inverse pre-scales 2^-s of the split being written
 };
 
 __device__ __forceinline__ float gelu_tanh(float x) {
@@ -285,9 +299,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   constexpr int kCS = CS;  // code stages
   uint8_t* cs = xs + XS * X_STAGE;
   float* ostage = reinterpret_cast<float*>(cs + kCS * C_STAGE);  // output staging slots
-  // [8 epilogue warps][96] row scales
+  // [8 epilogue warps][96] row scales, then (kGeluSplit) [8][96] output pre-scales
   float* rs_s = reinterpret_cast<float*>(cs + kCS * C_STAGE + OUT_STAGE_BYTES);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(rs_s + NUM_EPI_WARPS * EPI_COLS);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(rs_s + 2 * NUM_EPI_WARPS * EPI_COLS);
   uint64_t* x_full = bars;
   uint64_t* x_empty = x_full + XS;
   uint64_t* c_full = x_empty + XS;
@@ -310,6 +324,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int num_tiles = n_tiles * ((p.M + BM - 1) / BM);
   const int my_tiles = blockIdx.x < num_tiles ? (num_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   const int total_g = my_tiles * kblocks;
+  // partials: groups of KPP k-blocks per tile, numbered G across tiles (buffer G & 1)
+  constexpr int KPP = NK ? NK_KPP : 1;
+  const int groups = (kblocks + KPP - 1) / KPP;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < XS; ++i) { mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], 1); }
@@ -387,10 +404,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       constexpr uint32_t idesc = idesc_f16_f32(BN, BM);
       bool ok = true;
       for (int g = 0; g < total_g && ok; ++g) {
-        const int x = g % XS, a = g % AS, b = g & 1;
+        const int kb = g % kblocks;
+        const int G = (g / kblocks) * groups + kb / KPP;
+        const bool first = kb % KPP == 0, last = kb % KPP == KPP - 1 || kb == kblocks - 1;
+        const int x = g % XS, a = g % AS, b = G & 1;
         ok = mbar_wait(&x_full[x], (g / XS) & 1, p.status, kDevTimeoutMma, abort_flag) &&
              mbar_wait(&a_full[a], (g / AS) & 1, p.status, kDevTimeoutMma, abort_flag) &&
-             (g < 2 || mbar_wait(&acc_free[b], ((g >> 1) & 1) ^ 1, p.status, kDevTimeoutMma, abort_flag));
+             (!first || G < 2 ||
+              mbar_wait(&acc_free[b], ((G >> 1) & 1) ^ 1, p.status, kDevTimeoutMma, abort_flag));
         if (!ok) break;
         tc_fence_after();
         const uint32_t hi = smem_u32(xs + x * X_STAGE);
@@ -404,13 +425,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t a1 = a_col + kk * 8;
           const uint32_t a2 = a_col + 32 + kk * 8;
           // S.hi + S.lo + T.hi; the dropped T.lo is below 2^-22 of |x w| per product
-          mma_f16_ts(d, a1, dhi, idesc, kk != 0);  // fresh partial per k-block
+          mma_f16_ts(d, a1, dhi, idesc, !first || kk != 0);  // fresh partial per group
           mma_f16_ts(d, a1, dlo, idesc, 1);
           mma_f16_ts(d, a2, dhi, idesc, 1);
         }
         mma_commit(&x_empty[x]);
         mma_commit(&a_empty[a]);
-        mma_commit(&acc_full[b]);
+        if (last) mma_commit(&acc_full[b]);
       }
       // Retire every issued MMA before teardown frees TMEM (also on the error path).
       mma_commit(mma_done);
@@ -495,21 +516,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // this tile's row pre-scales into the warp's private slice of shared memory (read
     // back at the store; the loads complete while the k-blocks run)
     float* rsw = rs_s + (warp - 6) * EPI_COLS;
+    float* osw = rsw + NUM_EPI_WARPS * EPI_COLS;  // kGeluSplit
     __syncwarp();
     for (int j = lane; j < EPI_COLS; j += 32) {
       const int m = m0 + half * EPI_COLS + j;
       rsw[j] = m < p.M ? p.rscale[m] : 0.0f;
+      // 2^s from the stored 2^-s: exponent field 127 + s = 254 - (127 - s), exact
+      if constexpr (MODE == kGeluSplit)
+        osw[j] = m < p.M ? __int_as_float((254 << 23) - __float_as_int(p.next_rs[m])) : 0.0f;
     }
     __syncwarp();
     float sum[EPI_COLS];
 #pragma unroll
     for (int j = 0; j < EPI_COLS; ++j) sum[j] = 0.0f;
-    for (int kb = 0; kb < kblocks && ok; ++kb) {
-      const int g = i * kblocks + kb, b = g & 1;
-      ok = mbar_wait(&acc_full[b], (g >> 1) & 1, p.status, kDevTimeoutEpilogue, abort_flag);
+    for (int kg = 0; kg < groups && ok; ++kg) {
+      const int G = i * groups + kg, b = G & 1;
+      ok = mbar_wait(&acc_full[b], (G >> 1) & 1, p.status, kDevTimeoutEpilogue, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
-      if (g + AS < total_g && !decode_share(g + AS)) { ok = false; break; }
+      // (KPP == 1 here whenever the epilogue warps decode: G is the k-block counter)
+      if (G + AS < total_g && !decode_share(G + AS)) { ok = false; break; }
       const uint32_t col = tmem + lane_base + ACC_COL + b * BM + half * EPI_COLS;
 #pragma unroll
       for (int q = 0; q < EPI_COLS / 16; ++q) {
@@ -559,18 +585,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             // has finished reading it
             if (lane == 0) bulk_wait_group_read<1>();
             __syncwarp();
+            if constexpr (MODE == kGeluSplit) {
+              // the slot as fp16 [2 planes][OUT_ROWS][32]: a = GELU(y) * 2^s, hi = rn(a),
+              // lo = rn(a - hi) (the split kernels' arithmetic, with s fixed beforehand)
+              __half* hb = reinterpret_cast<__half*>(buf);
 #pragma unroll
-            for (int j = 0; j < OUT_ROWS; ++j) {
-              const int r = c * OUT_ROWS + j;
-              float v = fmaf(sum[r], sc, bi);
-              if constexpr (MODE == kGelu) v = gelu_tanh(v);
-              if constexpr (MODE == kGatedResidual) v *= (r < jb ? g0 : g1);
-              buf[j * 32 + lane] = v;
+              for (int j = 0; j < OUT_ROWS; ++j) {
+                const int r = c * OUT_ROWS + j;
+                const float a = gelu_tanh(fmaf(sum[r], sc, bi)) * osw[r];
+                const __half h = __float2half_rn(a);
+                hb[j * 32 + lane] = h;
+                hb[OUT_ROWS * 32 + j * 32 + lane] = __float2half_rn(a - __half2float(h));
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < OUT_ROWS; ++j) {
+                const int r = c * OUT_ROWS + j;
+                float v = fmaf(sum[r], sc, bi);
+                if constexpr (MODE == kGelu) v = gelu_tanh(v);
+                if constexpr (MODE == kGatedResidual) v *= (r < jb ? g0 : g1);
+                buf[j * 32 + lane] = v;
+              }
             }
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-              if constexpr (MODE == kStore || MODE == kGelu)
+              if constexpr (MODE == kGeluSplit)
+                tma_store_3d(&tm_out, buf, nw0, mbase + c * OUT_ROWS, 0);
+              else if constexpr (MODE == kStore || MODE == kGelu)
                 tma_store_2d(&tm_out, buf, nw0, mbase + c * OUT_ROWS);
               else
                 tma_reduce_add_2d(&tm_out, buf, nw0, mbase + c * OUT_ROWS);
@@ -604,6 +646,18 @@ __device__ __forceinline__ int split_shift(float mx) {
   if (!(mx > 0.0f) || !(mx <= 3.402823466e38f)) return 0;
   const int s = 14 - ilogbf(mx);
   return s < -60 ? -60 : (s > 60 ? 60 : s);
+}
+
+// Inverse pre-scale 2^-s for the split of GELU(X . W + b), chosen before that product exists
+// from the row's euclidean norm: |y_n| <= |x|_2 * max_n |W[:, n]|_2 + max_n |b_n| (Cauchy-
+// Schwarz) and |GELU(y)| <= max(|y|, 0.1701), so with 2^-6 of relative slack for the rounding
+// of the norm and of the product the row's largest GELU output times 2^s stays below 2^15
+// (fp16's range never clips).  A bound above the true maximum only lowers s: the split values
+// carry the same bits times a power of two, except values that become fp16-subnormal, whose
+// absolute error stays below 2^-25 of 2^-s.
+__device__ __forceinline__ float gelu_split_rscale(float sumsq, float wnorm, float bmax) {
+  const float bound = fmaxf(fmaf(sqrtf(sumsq), wnorm, bmax) * (1.0f + 0x1p-6f), 0.25f);
+  return pow2f(-split_shift(bound));
 }
 
 __global__ void nf24_split_rows(const float* __restrict__ x, int M, int Mp, int K, int Kp,
@@ -688,13 +742,17 @@ template <int NV>
 __global__ void __launch_bounds__(256, 4) ln_modulate_split_reg(
     const float* __restrict__ x, int M, int Mp, float eps, const float* __restrict__ shift,
     const float* __restrict__ scale, int mod_ld, int rows_per_batch, __half* __restrict__ hi,
-    __half* __restrict__ lo, float* __restrict__ rs) {
+    __half* __restrict__ lo, float* __restrict__ rs, float* __restrict__ next_rs, float wnorm,
+    float bmax) {
   constexpr int C = NV * 128;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= Mp) return;
   if (row >= M) {
-    if (lane == 0) rs[row] = 0.0f;
+    if (lane == 0) {
+      rs[row] = 0.0f;
+      if (next_rs) next_rs[row] = 0.0f;
+    }
     return;
   }
   const float4* xr = reinterpret_cast<const float4*>(x + (int64_t)row * C);
@@ -720,7 +778,7 @@ __global__ void __launch_bounds__(256, 4) ln_modulate_split_reg(
   const int b = row / rows_per_batch;
   const float4* sh = shift ? reinterpret_cast<const float4*>(shift + (int64_t)b * mod_ld) : nullptr;
   const float4* sc = scale ? reinterpret_cast<const float4*>(scale + (int64_t)b * mod_ld) : nullptr;
-  float mx = 0.0f;
+  float mx = 0.0f, ss = 0.0f;
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     float4 y = make_float4((v[i].x - mean) * inv, (v[i].y - mean) * inv, (v[i].z - mean) * inv, (v[i].w - mean) * inv);
@@ -731,6 +789,12 @@ __global__ void __launch_bounds__(256, 4) ln_modulate_split_reg(
     }
     v[i] = y;
     mx = fmaxf(mx, fmaxf(fmaxf(fabsf(y.x), fabsf(y.y)), fmaxf(fabsf(y.z), fabsf(y.w))));
+    ss = fmaf(y.x, y.x, fmaf(y.y, y.y, fmaf(y.z, y.z, fmaf(y.w, y.w, ss))));
+  }
+  if (next_rs) {  // warp-uniform
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) next_rs[row] = gelu_split_rscale(ss, wnorm, bmax);
   }
   store_split_row<NV>(v, mx, lane, hi + (int64_t)row * C, lo + (int64_t)row * C, rs + row);
 }
@@ -750,12 +814,16 @@ __global__ void ln_modulate_split(const float* __restrict__ x, int M, int Mp, in
                                   float eps, const float* __restrict__ shift,
                                   const float* __restrict__ scale, int mod_ld, int rows_per_batch,
                                   __half* __restrict__ hi, __half* __restrict__ lo,
-                                  float* __restrict__ rs) {
+                                  float* __restrict__ rs, float* __restrict__ next_rs, float wnorm,
+                                  float bmax) {
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= Mp) return;
   if (row >= M) {
-    if (lane == 0) rs[row] = 0.0f;
+    if (lane == 0) {
+      rs[row] = 0.0f;
+      if (next_rs) next_rs[row] = 0.0f;
+    }
     return;
   }
   const float* xr = x + (int64_t)row * C;
@@ -775,10 +843,19 @@ __global__ void ln_modulate_split(const float* __restrict__ x, int M, int Mp, in
   const int b = row / rows_per_batch;
   const float* sh = shift ? shift + (int64_t)b * mod_ld : nullptr;
   const float* sc = scale ? scale + (int64_t)b * mod_ld : nullptr;
-  float mx = 0.0f;
-  for (int c = lane; c < C; c += 32) mx = fmaxf(mx, fabsf(ln_mod_value(xr, c, mean, inv, sh, sc)));
+  float mx = 0.0f, ss = 0.0f;
+  for (int c = lane; c < C; c += 32) {
+    const float a = ln_mod_value(xr, c, mean, inv, sh, sc);
+    mx = fmaxf(mx, fabsf(a));
+    ss = fmaf(a, a, ss);
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (next_rs) {  // warp-uniform
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) next_rs[row] = gelu_split_rscale(ss, wnorm, bmax);
+  }
   const int shf = split_shift(mx);
   __half* hr = hi + (int64_t)row * Kp;
   __half* lr = lo + (int64_t)row * Kp;
@@ -885,6 +962,37 @@ static int launch_split(const float* x, int stride_x, const SplitPlanes& sp, cud
   return launch_status();
 }
 
+static int ln_modulate_split_launch(const float* x, int M, int C, float eps, const float* shift,
+                                    const float* scale, int mod_ld, int rows_per_batch,
+                                    void* split, void* next_split, int next_K, float wnorm,
+                                    float bmax) {
+  if (!x || !split || (!shift) != (!scale)) return kNullPointer;
+  if (M <= 0 || C <= 0 || eps < 0.0f || rows_per_batch <= 0 || (scale && mod_ld < C))
+    return kBadDims;
+  if (reinterpret_cast<uintptr_t>(split) & 255) return kBadAlignment;
+  int st = entry_check();
+  if (st != kOk) return st;
+  const SplitPlanes sp = split_layout(static_cast<uint8_t*>(split), M, C);
+  float* next_rs = next_split ? const_cast<float*>(split_layout(static_cast<uint8_t*>(next_split), M, next_K).rs)
+                              : nullptr;
+  cudaStream_t stream = current_stream();
+  {
+    LaunchScope scope(kKElementwise, stream);
+    const bool vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && C == 1024 && (mod_ld & 3) == 0 &&
+                     ((reinterpret_cast<uintptr_t>(shift) | reinterpret_cast<uintptr_t>(scale)) & 15) == 0;
+    if (vec)
+      gemm::ln_modulate_split_reg<8><<<(sp.Mp + 7) / 8, 256, 0, stream>>>(
+          x, M, sp.Mp, eps, shift, scale, mod_ld, rows_per_batch, const_cast<__half*>(sp.hi),
+          const_cast<__half*>(sp.lo), const_cast<float*>(sp.rs), next_rs, wnorm, bmax);
+    else
+      gemm::ln_modulate_split<<<(sp.Mp + 7) / 8, 256, 0, stream>>>(
+          x, M, sp.Mp, C, sp.Kp, eps, shift, scale, mod_ld, rows_per_batch,
+          const_cast<__half*>(sp.hi), const_cast<__half*>(sp.lo), const_cast<float*>(sp.rs),
+          next_rs, wnorm, bmax);
+  }
+  return launch_status();
+}
+
 struct EpilogueArgs {
   int mode = gemm::kStore;
   const float* gate = nullptr;
@@ -961,7 +1069,21 @@ static int launch_tc(const SplitPlanes& sp, const int16_t* c01, const int8_t* q2
       return kLaunchFailed;
   }
   CUtensorMap m_out;  // the [M, count] output, for the epilogue's TMA stores
-  {
+  const float* next_rs = nullptr;
+  if (ep.mode == kGeluSplit) {
+    // out is the split buffer of an [M, count] activation: its two fp16 planes as one
+    // [2][M][Kp] tensor (the planes are 256-byte aligned, so the plane stride is too)
+    const SplitPlanes nx = split_layout(reinterpret_cast<uint8_t*>(out), M, count);
+    const uint64_t dims[3] = {(uint64_t)count, (uint64_t)M, 2};
+    const uint64_t strides[2] = {(uint64_t)nx.Kp * 2,
+                                 (uint64_t)(reinterpret_cast<const uint8_t*>(nx.lo) -
+                                            reinterpret_cast<const uint8_t*>(nx.hi))};
+    const uint32_t box[3] = {32, OUT_ROWS, 2};
+    if (!encode_tmap(&m_out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<__half*>(nx.hi), dims,
+                     strides, box, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return kLaunchFailed;
+    next_rs = nx.rs;
+  } else {
     const uint64_t dims[2] = {(uint64_t)count, (uint64_t)M};
     const uint64_t strides[1] = {(uint64_t)stride_out * 4};
     const uint32_t box[2] = {32, OUT_ROWS};
@@ -970,11 +1092,11 @@ static int launch_tc(const SplitPlanes& sp, const int16_t* c01, const int8_t* q2
       return kLaunchFailed;
   }
   Params prm{sp.rs, scale, bias, out, M, K, N, start, count, stride_out,
-             ep.mode, ep.gate, ep.gate_ld, ep.rows_per_batch, status};
+             ep.mode, ep.gate, ep.gate_ld, ep.rows_per_batch, status, next_rs};
   // per kernel: one bit per device ordinal once its shared-memory attribute is set; SM
   // count per device.  Atomic: host threads on their own streams launch concurrently (a
   // thread that sees a bit unset sets the attribute itself before launching).
-  static std::atomic<uint64_t> attr_done[8];
+  static std::atomic<uint64_t> attr_done[10];
   static std::atomic<int> sm_count[64];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1003,6 +1125,7 @@ static int launch_tc(const SplitPlanes& sp, const int16_t* c01, const int8_t* q2
       case kGelu: run(nf24_gemm_tc<kGelu, true>, 4 + kGelu); break;
       case kGatedResidual: run(nf24_gemm_tc<kGatedResidual, true>, 4 + kGatedResidual); break;
       case kResidual: run(nf24_gemm_tc<kResidual, true>, 4 + kResidual); break;
+      case kGeluSplit: run(nf24_gemm_tc<kGeluSplit, true>, 8); break;
       default: run(nf24_gemm_tc<kStore, true>, 4 + kStore); break;
     }
   } else {
@@ -1151,29 +1274,27 @@ int triposplat_b200_split_f32(const float* x, int M, int K, int stride_x, void* 
 int triposplat_b200_ln_modulate_split(const float* x, int M, int C, float eps, const float* shift,
                                       const float* scale, int mod_ld, int rows_per_batch,
                                       void* split) {
+  return tsb::ln_modulate_split_launch(x, M, C, eps, shift, scale, mod_ld, rows_per_batch, split,
+                                       nullptr, 0, 0.0f, 0.0f);
+}
+
+// triposplat_b200_ln_modulate_split, and in the same pass the row scales of the split buffer
+// next_split (an [M, next_K] activation) for a following
+// triposplat_b200_gemm_nf24_split_nk mode 4 (GELU into next_split): per row
+// 2^-s with GELU(h . W + b) * 2^s below 2^15 for any W whose columns have euclidean norm at
+// most wnorm and any bias with |b| <= bmax (h = this row as split).  The planes of
+// next_split are left to that GEMM.
+int triposplat_b200_ln_modulate_split_bound(const float* x, int M, int C, float eps,
+                                            const float* shift, const float* scale, int mod_ld,
+                                            int rows_per_batch, void* split, void* next_split,
+                                            int next_K, float wnorm, float bmax) {
   using namespace tsb;
-  if (!x || !split || (!shift) != (!scale)) return kNullPointer;
-  if (M <= 0 || C <= 0 || eps < 0.0f || rows_per_batch <= 0 || (scale && mod_ld < C))
+  if (!next_split) return kNullPointer;
+  if (next_K <= 0 || !(wnorm >= 0.0f) || !(bmax >= 0.0f) || !(wnorm < 3.0e38f) || !(bmax < 3.0e38f))
     return kBadDims;
-  if (reinterpret_cast<uintptr_t>(split) & 255) return kBadAlignment;
-  int st = entry_check();
-  if (st != kOk) return st;
-  const SplitPlanes sp = split_layout(static_cast<uint8_t*>(split), M, C);
-  cudaStream_t stream = current_stream();
-  {
-    LaunchScope scope(kKElementwise, stream);
-    const bool vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && C == 1024 && (mod_ld & 3) == 0 &&
-                     ((reinterpret_cast<uintptr_t>(shift) | reinterpret_cast<uintptr_t>(scale)) & 15) == 0;
-    if (vec)
-      gemm::ln_modulate_split_reg<8><<<(sp.Mp + 7) / 8, 256, 0, stream>>>(
-          x, M, sp.Mp, eps, shift, scale, mod_ld, rows_per_batch, const_cast<__half*>(sp.hi),
-          const_cast<__half*>(sp.lo), const_cast<float*>(sp.rs));
-    else
-      gemm::ln_modulate_split<<<(sp.Mp + 7) / 8, 256, 0, stream>>>(
-          x, M, sp.Mp, C, sp.Kp, eps, shift, scale, mod_ld, rows_per_batch,
-          const_cast<__half*>(sp.hi), const_cast<__half*>(sp.lo), const_cast<float*>(sp.rs));
-  }
-  return launch_status();
+  if (reinterpret_cast<uintptr_t>(next_split) & 255) return kBadAlignment;
+  return ln_modulate_split_launch(x, M, C, eps, shift, scale, mod_ld, rows_per_batch, split,
+                                  next_split, next_K, wnorm, bmax);
 }
 
 // NF24 GEMM on a split buffer (M x K) with one of the epilogues
@@ -1259,6 +1380,10 @@ int triposplat_b200_nf24_codes_to_nk(const int16_t* code01_t, const int8_t* q2_t
 // (triposplat_b200_nf24_codes_to_nk).  Row n of the planes holds the K codes of output column
 // n, rows ldk elements apart (ldk >= K; ldk > K with the planes offset by k0 selects the input
 // features [k0, k0 + K) of a wider weight).  Plane pointers 16-byte aligned, ldk % 16 == 0.
+// mode 4: GELU_tanh(y) written into the split buffer `out` of an [M, count] activation
+// (256-byte aligned, stride_out == count) whose row scales were filled beforehand by
+// triposplat_b200_ln_modulate_split_bound; out[m, :] gets the fp16 planes of
+// GELU(y[m, :]) * 2^s_m for the stored inverse scale 2^-s_m.
 int triposplat_b200_gemm_nf24_split_nk(const void* split, int M, int K, const int16_t* code01_nk,
                                        const int8_t* q2_nk, int ldk, const float* scale,
                                        const float* bias, float* out, int N, int start, int count,
@@ -1266,9 +1391,12 @@ int triposplat_b200_gemm_nf24_split_nk(const void* split, int M, int K, const in
                                        int rows_per_batch) {
   using namespace tsb;
   if (!split || !code01_nk || !q2_nk || !scale || !bias || !out) return kNullPointer;
-  if (M <= 0 || K <= 0 || N <= 0 || count <= 0 || start < 0 || stride_out < count || mode < 0 || mode > 3)
+  if (M <= 0 || K <= 0 || N <= 0 || count <= 0 || start < 0 || stride_out < count || mode < 0 ||
+      mode > gemm::kGeluSplit)
     return kBadDims;
   if (start + count > N || ldk < K) return kBadRange;
+  if (mode == gemm::kGeluSplit && (stride_out != count || (reinterpret_cast<uintptr_t>(out) & 255)))
+    return kBadAlignment;
   if (mode == gemm::kGatedResidual && (!gate || gate_ld < N || rows_per_batch <= 0))
     return kBadRange;
   // outputs leave through TMA stores: 16-byte aligned base and row stride

@@ -257,9 +257,10 @@ class FlowModelB200:
             "pk": e(B, H, 64, self.Lp, **f32), "pv": e(B, H, 64, self.Lp, **f32),
             "o": e(B, L, h, **f32), "ckv": e(B, Mc, 2 * h, **f32),
             "cpk": e(B, H, 64, self.Mcp, **f32), "cpv": e(B, H, 64, self.Mcp, **f32),
-            "hid": e(B, L, s.mlp, **f32),
             "v_lat": e(B, s.latent_tokens, s.latent_dim, **f32), "v_cam": e(B, 1, s.camera_dim, **f32),
         }
+        if not fused:  # the fused path writes the MLP hidden layer straight into "sp_hid"
+            self.buf["hid"] = e(B, L, s.mlp, **f32)
         # split-format activation buffers for the fused path (LN/GELU/residual folded into
         # the GEMMs); 256-byte aligned as the library requires
         rows = B * L
@@ -281,6 +282,9 @@ class FlowModelB200:
                     lin.code01.data_ptr(), lin.q2.data_ptr(), K, N, c.data_ptr(), q.data_ptr()),
                     f"codes_to_nk {name}")
                 self.nk[name] = (c, q)
+        # per block: the fc1 column-norm / bias bound that fixes the split scales of the
+        # MLP hidden layer before fc1 runs (its GELU epilogue writes the fc2 split directly)
+        self.gelu_bounds = {i: self._column_bound(f"blocks.{i}.fc1") for i in range(s.blocks)} if fused else {}
         # per-block adaLN tables, expanded over the batch so they add elementwise
         self.tables = {i: weights.params[f"blocks.{i}.table"][:, None, :].expand(6, B, h).contiguous()
                        for i in range(s.blocks)}
@@ -295,6 +299,16 @@ class FlowModelB200:
             self.buf["cq_planes"] = torch.empty(qb + 256, dtype=torch.uint8, device=device)
 
     # -- helpers -------------------------------------------------------------------------
+    def _column_bound(self, name):
+        """(max over columns of the euclidean norm of the dequantised weight, max |bias|) of a
+        block Linear, rounded up: the constants of the split-scale bound in
+        triposplat_b200_ln_modulate_split_bound."""
+        c, q = self.nk[name]
+        lin = self.w.linears[name]
+        norms = ((c.double() * 256.0 + q.double()) ** 2).sum(1).sqrt() * lin.scale.double().abs()
+        up = 1.0 + 2.0 ** -20
+        return float(norms.max()) * up, float(lin.bias.double().abs().max()) * up
+
     def _lin(self, name, x, out, start=0, count=None):
         p = self.w.linears[name]
         return nf24_linear(x, p.code01, p.q2, p.scale, p.bias, out=out, start=start, count=count,
@@ -412,21 +426,30 @@ class FlowModelB200:
         return (t.data_ptr() + 255) & ~255
 
     def _lin_split(self, name, split, rows, out, mode=0, gate=None, gate_ld=0, rows_per_batch=1):
+        """out: a tensor, or (mode 4) the address of the split buffer the GELU output goes to."""
         p = self.w.linears[name]
         c, q = self.nk[name]
         N, K = int(c.shape[0]), int(c.shape[1])
         st = self.lib.triposplat_b200_gemm_nf24_split_nk(
             split, rows, K, c.data_ptr(), q.data_ptr(), K, p.scale.data_ptr(),
-            p.bias.data_ptr(), out.data_ptr(), N, 0, N, N, mode,
+            p.bias.data_ptr(), out if isinstance(out, int) else out.data_ptr(), N, 0, N, N, mode,
             None if gate is None else gate.data_ptr(), gate_ld, rows_per_batch)
         self._ok(st, f"gemm_split {name}")
 
-    def _ln_split(self, x, split, shift=None, scale=None):
+    def _ln_split(self, x, split, shift=None, scale=None, rows_per_batch=None, bound=None):
+        """bound = (next_split, next_K, (wnorm, bmax)): also fix the row scales of next_split
+        for a GELU-into-split GEMM."""
         s = self.spec
         rows = x.numel() // s.hidden
-        self._ok(self.lib.triposplat_b200_ln_modulate_split(
-            x.data_ptr(), rows, s.hidden, s.eps, None if shift is None else shift.data_ptr(),
-            None if scale is None else scale.data_ptr(), s.hidden, s.seq, split), "ln_split")
+        rpb = s.seq if rows_per_batch is None else rows_per_batch
+        args = (x.data_ptr(), rows, s.hidden, s.eps, None if shift is None else shift.data_ptr(),
+                None if scale is None else scale.data_ptr(), s.hidden, rpb, split)
+        if bound is None:
+            self._ok(self.lib.triposplat_b200_ln_modulate_split(*args), "ln_split")
+        else:
+            nxt, nk, (wn, bm) = bound
+            self._ok(self.lib.triposplat_b200_ln_modulate_split_bound(*args, nxt, nk, wn, bm),
+                     "ln_split_bound")
 
     def _split(self, x, split):
         K = int(x.shape[-1])
@@ -478,10 +501,9 @@ class FlowModelB200:
                 prm[p + "ck_gamma"].data_ptr(), b["o"].data_ptr(), B, L, Mc, H), "cross_attention")
         self._split(b["o"], sph)
         self._lin_split(p + "cross_out", sph, rows, x, mode=3)
-        # MLP
-        self._ln_split(x, sph, shift_mlp, scale_mlp)
-        self._lin_split(p + "fc1", sph, rows, b["hid"], mode=1)
-        self._split(b["hid"], sphid)
+        # MLP: the hidden layer's split scales fixed from a bound, GELU straight into that split
+        self._ln_split(x, sph, shift_mlp, scale_mlp, bound=(sphid, s.mlp, self.gelu_bounds[i]))
+        self._lin_split(p + "fc1", sph, rows, sphid, mode=4)
         self._lin_split(p + "fc2", sphid, rows, x, mode=2, gate=gate_mlp, gate_ld=h, rows_per_batch=L)
 
     def _block_reference_ops(self, i):

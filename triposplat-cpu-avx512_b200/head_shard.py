@@ -178,7 +178,7 @@ class HeadShardedFlowModel(FlowModelB200):
         e = torch.empty
         self.buf.update({
             "qkv_l": e(B, L, 3 * w, **f32), "o_l": e(B, L, w, **f32), "yq_l": e(B, L, w, **f32),
-            "ckv_l": e(B, Mc, 2 * w, **f32), "hid_l": e(B, L, f, **f32), "part": e(B, L, h, **f32),
+            "ckv_l": e(B, Mc, 2 * w, **f32), "part": e(B, L, h, **f32),
         })
         for name, k in (("sp_o", w), ("sp_hid_l", f)):
             nbytes = int(self.lib.triposplat_b200_split_bytes(B * L, k))
@@ -287,10 +287,10 @@ class HeadShardedFlowModel(FlowModelB200):
         self._lin_rows(p + "cross_out", spo, rows, *pl["cross_out"], self._part_ptr())
         yield from self._reduce_into_x(3)
         # MLP over this rank's hidden columns
-        self._ln_split(x, sph, shift_mlp, scale_mlp)
+        # (the bound over all fc1 columns holds for this rank's window)
         (c0, n), = pl["fc1"]
-        self._lin_cols(p + "fc1", sph, rows, b["hid_l"].data_ptr(), c0, n, n, mode=1)
-        self._split(b["hid_l"], sphid)
+        self._ln_split(x, sph, shift_mlp, scale_mlp, bound=(sphid, n, self.gelu_bounds[i]))
+        self._lin_cols(p + "fc1", sph, rows, sphid, c0, n, n, mode=4)
         self._lin_rows(p + "fc2", sphid, rows, *pl["fc2"], self._part_ptr())
         yield from self._reduce_into_x(2, gate_mlp)
 

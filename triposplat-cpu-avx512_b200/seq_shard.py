@@ -140,8 +140,7 @@ class SeqShardedFlowModel(FlowModelB200):
         f32 = dict(dtype=torch.float32, device=device)
         e = torch.empty
         self.loc = {"x": e(B, Lloc, h, **f32), "a": e(B, Lloc, h, **f32), "y": e(B, Lloc, h, **f32),
-                    "o": e(B, Lloc, h, **f32), "qkv": e(B, Lloc, 3 * h, **f32),
-                    "hid": e(B, Lloc, s.mlp, **f32)}
+                    "o": e(B, Lloc, h, **f32), "qkv": e(B, Lloc, 3 * h, **f32)}
         self.chunk_lat = (s.latent_tokens // world) * s.latent_dim
         # one row per batch, padded to 16 bytes so every row is a tensor-core GEMM output
         # (the drop-in GEMM sends unaligned outputs to its SIMT kernel, other rounding)
@@ -169,12 +168,8 @@ class SeqShardedFlowModel(FlowModelB200):
             return self.peer.set_ptr(k)
         return (self.lock_sets[k].data_ptr() + 255) & ~255
 
-    def _ln_split_rows(self, x, split, shift=None, scale=None):
-        s = self.spec
-        rows = x.numel() // s.hidden
-        self._ok(self.lib.triposplat_b200_ln_modulate_split(
-            x.data_ptr(), rows, s.hidden, s.eps, None if shift is None else shift.data_ptr(),
-            None if scale is None else scale.data_ptr(), s.hidden, self.Lloc, split), "ln_split")
+    def _ln_split_rows(self, x, split, shift=None, scale=None, bound=None):
+        self._ln_split(x, split, shift, scale, rows_per_batch=self.Lloc, bound=bound)
 
     def gather(self, set_ptrs):
         """Pull the other ranks' key tiles of the current block into this rank's set
@@ -266,9 +261,8 @@ class SeqShardedFlowModel(FlowModelB200):
         self._split(o, sph)
         self._lin_split(p + "cross_out", sph, rows, x, mode=3)
         # MLP
-        self._ln_split_rows(x, sph, shift_mlp, scale_mlp)
-        self._lin_split(p + "fc1", sph, rows, loc["hid"], mode=1)
-        self._split(loc["hid"], sphid)
+        self._ln_split_rows(x, sph, shift_mlp, scale_mlp, bound=(sphid, s.mlp, self.gelu_bounds[i]))
+        self._lin_split(p + "fc1", sph, rows, sphid, mode=4)
         self._lin_split(p + "fc2", sphid, rows, x, mode=2, gate=gate_mlp, gate_ld=h, rows_per_batch=Lloc)
 
     def _final_rows(self):
