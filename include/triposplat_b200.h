@@ -283,6 +283,10 @@ int triposplat_b200_q_split_f32(const float* q, const float* q_gamma, int B, int
 /* Lq query rows (q_planes) against L keys (a complete kv_planes); out [B, Lq, H, 64] */
 int triposplat_b200_attend_rows_f32(const void* q_planes, const void* kv_planes, float* out_blhd,
                                     int B, int H, int Lq, int L);
+/* The same, output written into a split buffer of [B * Lq, H * 64] (see
+ * triposplat_b200_qkv_rope_rmsnorm_sdpa_split). */
+int triposplat_b200_attend_rows_split(const void* q_planes, const void* kv_planes, int B, int H,
+                                      int Lq, int L, void* out_split);
 
 int triposplat_sdpa_key_tile(void);
 int triposplat_sdpa_query_block(void);
@@ -409,6 +413,18 @@ int triposplat_b200_qkv_rope_rmsnorm_sdpa_f32(const float* qkv, const float* fre
 int triposplat_b200_q_kv_rmsnorm_sdpa_f32(const float* q, const float* kv, const float* q_gamma,
                                           const float* k_gamma, float* out_blhd, int B, int Lq,
                                           int Lk, int H);
+/* No reference counterpart: the two entries above (D = 64) with the output written into
+ * out_split, a split buffer (triposplat_b200_split_bytes(B * Lq, H * 64) bytes, 256-byte
+ * aligned) of the [B * Lq, H * 64] output: the out-projection GEMM's input without an
+ * fp32 round trip.  Row scale 2^-s fixed per batch from the largest V value (every
+ * |O| * 2^s < 2^15); the planes equal the split of the fp32 output under those scales. */
+int triposplat_b200_qkv_rope_rmsnorm_sdpa_split(const float* qkv, const float* frequencies,
+                                                const float* q_gamma, const float* k_gamma, int B,
+                                                int L, int H, int frequency_batches,
+                                                void* out_split);
+int triposplat_b200_q_kv_rmsnorm_sdpa_split(const float* q, const float* kv, const float* q_gamma,
+                                            const float* k_gamma, int B, int Lq, int Lk, int H,
+                                            void* out_split);
 
 /* ---- Tensor-parallel reduction over NVLink peer memory (no reference counterpart) ----
  * ipc_alloc: cudaMalloc'd, zeroed buffer plus its 64-byte CUDA IPC handle; ipc_open maps a

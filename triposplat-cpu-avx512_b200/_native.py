@@ -78,6 +78,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "triposplat_b200_qkv_split_rows_f32": ([VP] * 4 + [I] * 6 + [VP, VP], I),
     "triposplat_b200_kv_planes_gather": ([VP, VP, I, I, I, I], I),
     "triposplat_b200_attend_rows_f32": ([VP, VP, VP, I, I, I, I], I),
+    "triposplat_b200_attend_rows_split": ([VP, VP, I, I, I, I, VP], I),
     "triposplat_b200_kv_split_f32": ([VP, VP, I, I, I, VP], I),
     "triposplat_b200_q_split_f32": ([VP, VP, I, I, I, VP], I),
     "triposplat_sdpa_key_tile": ([], I),
@@ -107,6 +108,8 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "triposplat_b200_q_kv_rmsnorm_pack_f32": ([VP] * 7 + [I] * 5, I),
     "triposplat_b200_qkv_rope_rmsnorm_sdpa_f32": ([VP] * 5 + [I] * 5, I),
     "triposplat_b200_q_kv_rmsnorm_sdpa_f32": ([VP] * 5 + [I] * 4, I),
+    "triposplat_b200_qkv_rope_rmsnorm_sdpa_split": ([VP] * 4 + [I] * 4 + [VP], I),
+    "triposplat_b200_q_kv_rmsnorm_sdpa_split": ([VP] * 4 + [I] * 4 + [VP], I),
     "triposplat_timestep_embedding_f32_avx512": ([VP] * 3 + [I] * 4, I),
     "triposplat_pcd_position_embedding_f32_avx512": ([VP] * 3 + [I64] + [I] * 5, I),
     "triposplat_mul_inplace_f32_avx512": ([VP, VP, I64, I], I),

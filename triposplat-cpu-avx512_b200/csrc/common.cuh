@@ -14,6 +14,27 @@
 namespace tsb {
 
 // ---------------------------------------------------------------------------
+// Split-activation buffer (the NF24 GEMM's X operand, written by its producers): fp16
+// hi plane [M, Kp], fp16 lo plane [M, Kp] (Kp = K rounded up to 8), then the inverse row
+// pre-scales [Mp] (Mp = M rounded up to 4); each region starts 256-byte aligned.
+// ---------------------------------------------------------------------------
+struct SplitLayout {
+  size_t lo_offset, rs_offset, bytes;
+  int Kp, Mp;
+};
+
+inline SplitLayout split_buffer_layout(int M, int K) {
+  SplitLayout l;
+  l.Kp = (K + 7) & ~7;
+  l.Mp = (M + 3) & ~3;
+  const size_t plane = ((size_t)M * l.Kp * 2 + 255) & ~static_cast<size_t>(255);
+  l.lo_offset = plane;
+  l.rs_offset = 2 * plane;
+  l.bytes = 2 * plane + (((size_t)l.Mp * 4 + 255) & ~static_cast<size_t>(255));
+  return l;
+}
+
+// ---------------------------------------------------------------------------
 // status word (host-mapped, written by kernels on a bounded-wait timeout)
 // ---------------------------------------------------------------------------
 enum DeviceError : int {

@@ -25,10 +25,10 @@
 //  * Accuracy: the tensor core's fp32 accumulation truncates, so an error that grows
 //    linearly with the number of accumulation steps builds up in a long-lived accumulator
 //    (measured: rmse 1.8e-5 relative at K = 4096, 16x the fp32 reference).  Each k-block
-//    (64 k; NK_KPP blocks for the k-contiguous layout) is therefore accumulated into a
+//    (64 k; NK_KPP of them for the k-contiguous layout) is therefore accumulated into a
 //    FRESH TMEM partial (double-buffered) and promoted into round-to-nearest fp32 running
 //    sums held in the epilogue warps' registers, which keeps the error at the level of a
-//    64- (or 64 * NK_KPP-) long dot product.
+//    64- (64 * NK_KPP-) long dot product.
 //    Epilogue: y = sum * rowscale[m] * 256*scale[n] + bias[n], then one of: store,
 //    GELU(tanh) + store, gated residual out += gate[b] * y, residual out += y, or
 //    GELU(tanh) written straight into the next GEMM's split format (fp16 hi / lo planes
@@ -86,10 +86,12 @@ static_assert(NK_DEC_PAIRS % 2 == 0 && NK_EPI_PAIRS % 2 == 0 &&
               NK_DEC_PAIRS + 2 * NK_EPI_PAIRS == BK / 2, "k-contiguous decode shares");
 constexpr int NK_DEC_ARRIVALS = 4 + (NK_EPI_PAIRS ? NUM_EPI_WARPS : 0);
 // k-blocks accumulated in one TMEM partial before it is promoted, for the k-contiguous
-// layout (whose epilogue warps only promote).  Two halve the promotions and their barrier
-// round trips per k; the partial's truncation error grows with its length (about sqrt(2)
-// over one block's, still well inside fp32 semantics).  The reference layout promotes
-// every block: its epilogue warps' decode share is paced by the per-block completions.
+// layout of the model path.  Two halve the promotions and their barrier round trips per k;
+// the partial's truncation error grows with its length (about sqrt(2) over one block's,
+// still inside fp32 semantics).  The reference layout behind the drop-in entry points keeps
+// one block per partial (its accuracy against the reference kernel is unchanged).  The
+// epilogue warps' decode shares are paced by each block's MMA completion (a_empty), not by
+// the promotions.
 #ifndef TSB_GEMM_KPP
 #define TSB_GEMM_KPP 2
 #endif
@@ -531,11 +533,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int j = 0; j < EPI_COLS; ++j) sum[j] = 0.0f;
     for (int kg = 0; kg < groups && ok; ++kg) {
       const int G = i * groups + kg, b = G & 1;
+      if constexpr (!(NK && NK_EPI_PAIRS == 0)) {
+        // this warp's decode share of the blocks two ahead of the group's blocks, each as
+        // soon as the MMAs of the block whose A stage it reuses retire (a_empty phase)
+        const int g0 = i * kblocks + kg * KPP, g1 = min(g0 + KPP, (i + 1) * kblocks);
+        for (int gg = g0; gg < g1 && ok; ++gg) {
+          if (gg + AS >= total_g) break;
+          ok = mbar_wait(&a_empty[gg % AS], (gg / AS) & 1, p.status, kDevTimeoutEpilogue, abort_flag);
+          ok = __all_sync(0xffffffffu, ok);
+          if (ok) {
+            tc_fence_after();
+            ok = decode_share(gg + AS);
+          }
+        }
+        if (!ok) break;
+      }
       ok = mbar_wait(&acc_full[b], (G >> 1) & 1, p.status, kDevTimeoutEpilogue, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
-      // (KPP == 1 here whenever the epilogue warps decode: G is the k-block counter)
-      if (G + AS < total_g && !decode_share(G + AS)) { ok = false; break; }
       const uint32_t col = tmem + lane_base + ACC_COL + b * BM + half * EPI_COLS;
 #pragma unroll
       for (int q = 0; q < EPI_COLS / 16; ++q) {
@@ -925,21 +940,18 @@ struct SplitPlanes {
 
 static inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
-static size_t split_bytes(int M, int K) {
-  const size_t Kp = (size_t)((K + 7) & ~7), Mp = (size_t)((M + 3) & ~3);
-  return 2 * align256((size_t)M * Kp * 2) + align256(Mp * 4);
-}
+static size_t split_bytes(int M, int K) { return split_buffer_layout(M, K).bytes; }
 
 static SplitPlanes split_layout(uint8_t* base, int M, int K) {
+  const SplitLayout l = split_buffer_layout(M, K);
   SplitPlanes sp;
   sp.M = M;
   sp.K = K;
-  sp.Kp = (K + 7) & ~7;
-  sp.Mp = (M + 3) & ~3;
-  const size_t plane = align256((size_t)M * sp.Kp * 2);
+  sp.Kp = l.Kp;
+  sp.Mp = l.Mp;
   sp.hi = reinterpret_cast<const __half*>(base);
-  sp.lo = reinterpret_cast<const __half*>(base + plane);
-  sp.rs = reinterpret_cast<const float*>(base + 2 * plane);
+  sp.lo = reinterpret_cast<const __half*>(base + l.lo_offset);
+  sp.rs = reinterpret_cast<const float*>(base + l.rs_offset);
   return sp;
 }
 

@@ -45,6 +45,13 @@
 // then O of team 0 and O of team 1 (64 columns each).
 // Ordering: QK(t) waits only for P.V(t-3), the last reader of its buffer; P.V(t) writes
 // team (t & 1)'s O only after that team folded its previous O into registers (p_full).
+//
+// Output: fp32 (BHLD or BLHD), or straight into the NF24 GEMM's split format for the
+// out-projection ([B*Lq, H*64] fp16 hi / lo planes + one power-of-two scale per row).  A
+// row's scale must be known before any of its heads is written, and O is a convex
+// combination of V rows, so |O| <= max |V| over the batch's keys and heads
+// < 2^15 * (largest inverse V-tile pre-scale of the batch): that bound fixes the scale
+// (value * 2^s < 2^15), and the planes equal the split of the fp32 output under it.
 #include <cuda_fp16.h>
 
 #include <atomic>
@@ -78,7 +85,8 @@ constexpr int PLANE = 128 * D * 2;      // 16 KB: one 128 x 64 fp16 tile
 constexpr int STAGE = 2 * PLANE;        // hi + lo planes of one Q, K or V^T tile
 // Q, 2 K stages, 2 V stages, per-warp bias [8][BKV], team maxima / sums [2][BQ] each,
 // output halves [2 teams][BQ][32], barriers
-constexpr int SMEM_BYTES = 1024 + 5 * STAGE + 8 * BKV * 4 + 4 * BQ * 4 + 2 * BQ * 32 * 4 + 32 * 8 + 16;
+constexpr int SMEM_BYTES = 1024 + 5 * STAGE + 8 * BKV * 4 + 4 * BQ * 4 + 2 * BQ * 32 * 4 + 8 * 4 +
+                           32 * 8 + 16;
 constexpr float LOG2E = 1.4426950408889634f;
 
 struct Params {
@@ -92,7 +100,22 @@ struct Params {
   int out_blhd;
   int* status;
   int Qt, BH;  // query tiles per head, heads x batch: work item j = (bh = j / Qt, tile j % Qt)
+  // nullable: O written as the split planes [B*Lq, H*64] with row scales ors (BLHD rows)
+  __half* ohi;
+  __half* olo;
+  float* ors;
 };
+
+// 2^s for |s| <= 126 built in the exponent field: x * pow2i(s) is the correctly rounded
+// x * 2^s (what ldexpf computes) for a fraction of its instructions
+__device__ __forceinline__ float pow2i(int s) { return __int_as_float((127 + s) << 23); }
+
+// s with mx * 2^s in [2^14, 2^15) (clamped to [-60, 60]; 0 for 0 / non-finite)
+__device__ __forceinline__ int pow2_shift(float mx) {
+  if (!(mx > 0.0f) || !(mx <= 3.402823466e38f)) return 0;
+  int s = 14 - ilogbf(mx);
+  return s < -60 ? -60 : (s > 60 ? 60 : s);
+}
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -345,7 +368,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   float* xm = bias_s + 8 * BKV;        // [2 teams][BQ] final reference maxima
   float* xl = xm + 2 * BQ;             // [2 teams][BQ] final row sums
   float* xo = xl + 2 * BQ;             // [2 teams][BQ][32] output halves for the other team
-  uint64_t* bars = reinterpret_cast<uint64_t*>(xo + 2 * BQ * 32);
+  float* xvb = xo + 2 * BQ * 32;       // [8 softmax warps] partial max of the batch's V scales
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xvb + 8);
   uint64_t* q_full = bars + 0;   // Q tile of the item loaded (TMA bytes)
   uint64_t* k_full = bars + 1;   // [2]
   uint64_t* k_empty = bars + 3;  // [2]
@@ -595,6 +619,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[team]);
     }
+    // output split: this warp's share of the batch's V-tile scales (the loads issue before
+    // the wait for the last P.V; the 8 shares meet in the exchange)
+    float vb_part = 0.0f;
+    if (p.ohi) {
+      const float* vb = p.vinv + (int64_t)(bh / p.H) * p.H * T;
+      const int cnt = p.H * T;
+#pragma unroll 4
+      for (int e = (warp - 4) * 32 + lane; e < cnt; e += 256) vb_part = fmaxf(vb_part, vb[e]);
+    }
     if (ok && n > 0) {
       // the team's last O of the item
       const int Gl = i * T + team + 2 * (n - 1);
@@ -632,6 +665,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int d = 0; d < 32; d += 4)
           *reinterpret_cast<float4*>(mine + d) = make_float4(o_acc[d], o_acc[d + 1], o_acc[d + 2], o_acc[d + 3]);
       }
+      if (p.ohi) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) vb_part = fmaxf(vb_part, __shfl_xor_sync(0xffffffffu, vb_part, o));
+        if (lane == 0) xvb[warp - 4] = vb_part;
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(xbar);
       ok = __all_sync(0xffffffffu, mbar_wait(xbar, i & 1, p.status, kDevTimeoutEpilogue, abort_flag));
@@ -643,8 +681,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const float f = vref / (l_run * f_me + l_o * f_o);
         const float* other = xo + (team * BQ + r) * 32;  // the other team's half of my dims
         const int b = bh / p.H, hh = bh % p.H;
-        float* dst = (p.out_blhd ? p.out + (((int64_t)b * p.Lq + qrow) * p.H + hh) * D
-                                 : p.out + ((int64_t)bh * p.Lq + qrow) * D) + team * 32;
         float res[32];
         if (team == 0) {
 #pragma unroll
@@ -656,9 +692,41 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
         for (int d = 0; d < 32; d += 4) {
           const float4 ov = *reinterpret_cast<const float4*>(other + d);
-          *reinterpret_cast<float4*>(dst + d) =
-              make_float4((res[d] * f_me + ov.x * f_o) * f, (res[d + 1] * f_me + ov.y * f_o) * f,
-                          (res[d + 2] * f_me + ov.z * f_o) * f, (res[d + 3] * f_me + ov.w * f_o) * f);
+          res[d] = (res[d] * f_me + ov.x * f_o) * f;
+          res[d + 1] = (res[d + 1] * f_me + ov.y * f_o) * f;
+          res[d + 2] = (res[d + 2] * f_me + ov.z * f_o) * f;
+          res[d + 3] = (res[d + 3] * f_me + ov.w * f_o) * f;
+        }
+        if (p.ohi) {
+          float vbat = xvb[0];
+#pragma unroll
+          for (int w = 1; w < 8; ++w) vbat = fmaxf(vbat, xvb[w]);
+          // |O| <= max |V| < 2^15 * vbat; 2^-6 of slack for the rounding of P.V and of 1/l
+          const int s = pow2_shift(32768.0f * vbat * (1.0f + 0x1p-6f));
+          const float sc = pow2i(s);
+          const int64_t row = (int64_t)b * p.Lq + qrow;
+          const int64_t off = row * ((int64_t)p.H * D) + hh * D + team * 32;
+#pragma unroll
+          for (int d = 0; d < 32; d += 8) {
+            __align__(16) __half h8[8];
+            __align__(16) __half l8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float a = res[d + e] * sc;
+              const __half hv = __float2half_rn(a);
+              h8[e] = hv;
+              l8[e] = __float2half_rn(a - __half2float(hv));
+            }
+            *reinterpret_cast<uint4*>(p.ohi + off + d) = *reinterpret_cast<const uint4*>(h8);
+            *reinterpret_cast<uint4*>(p.olo + off + d) = *reinterpret_cast<const uint4*>(l8);
+          }
+          if (hh == 0 && team == 0) p.ors[row] = pow2i(-s);
+        } else {
+          float* dst = (p.out_blhd ? p.out + (((int64_t)b * p.Lq + qrow) * p.H + hh) * D
+                                   : p.out + ((int64_t)bh * p.Lq + qrow) * D) + team * 32;
+#pragma unroll
+          for (int d = 0; d < 32; d += 4)
+            *reinterpret_cast<float4*>(dst + d) = make_float4(res[d], res[d + 1], res[d + 2], res[d + 3]);
         }
       }
       __syncwarp();
@@ -679,16 +747,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // ---------------------------------------------------------------------------
 // Pre-split kernels
 // ---------------------------------------------------------------------------
-// 2^s for |s| <= 126 built in the exponent field: x * pow2i(s) is the correctly rounded
-// x * 2^s (what ldexpf computes) for a fraction of its instructions
-__device__ __forceinline__ float pow2i(int s) { return __int_as_float((127 + s) << 23); }
-
-__device__ __forceinline__ int pow2_shift(float mx) {
-  if (!(mx > 0.0f) || !(mx <= 3.402823466e38f)) return 0;
-  int s = 14 - ilogbf(mx);
-  return s < -60 ? -60 : (s > 60 ? 60 : s);
-}
-
 // Q [BH, Lq, 64] fp32 -> hi/lo fp16 [BH, Lq, 64], qinv [BH*Lq].  One warp per row.
 __global__ void sdpa_split_q(const float* __restrict__ q, int64_t rows, __half* __restrict__ hi,
                              __half* __restrict__ lo, float* __restrict__ qinv) {
@@ -924,6 +982,165 @@ __global__ void __launch_bounds__(256, 4) qkv_split_k(
   }
 }
 
+// ---------------------------------------------------------------------------
+// Tail query rows.  When Lq leaves a few rows past its last full 128-row tile (the camera
+// token of an 8193-token sequence), a tensor-core item for them would cost as much as a full
+// one and add a round to the persistent kernel (2080 items on 148 SMs: 15 rounds instead of
+// 14).  Those rows run here instead, on CUDA cores in fp32 from the same split planes:
+// pass 1 computes, per (head, row, chunk of TAIL_KEYS keys), the chunk's maximum m, sum
+// l = sum 2^(x - m) and o = sum 2^(x - m) v in log2 units (x = 0.125 log2(e) q.k); pass 2
+// merges the chunks with exact power-of-two factors and writes the row like the
+// tensor-core kernel does (fp32, or the split format with the batch's V bound).
+// ---------------------------------------------------------------------------
+constexpr int TAIL_MAX = 8;      // rows past the last full query tile handled this way
+constexpr int TAIL_KEYS = 512;   // keys per pass-1 CTA (two per thread)
+constexpr int TAIL_PART = D + 2; // floats per partial: m, l, o[64]
+
+__global__ void __launch_bounds__(256) sdpa_tail_partial(
+    const __half* __restrict__ qhi, const __half* __restrict__ qlo, const float* __restrict__ qinv,
+    const __half* __restrict__ khi, const __half* __restrict__ klo, const float* __restrict__ kinv,
+    const __half* __restrict__ vhi, const __half* __restrict__ vlo, const float* __restrict__ vinv,
+    int Lq, int Lk, int Lkt, int T, int row0, float* __restrict__ part) {
+  __shared__ float qs[D];
+  __shared__ float xs[TAIL_KEYS];
+  __shared__ float red[8][D];
+  __shared__ float mx_s[8], l_s[8];
+  const int c = blockIdx.x, r = blockIdx.y, bh = blockIdx.z;
+  const int chunks = gridDim.x, rows = gridDim.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t qrow = (int64_t)bh * Lq + row0 + r;
+  if (tid < D) qs[tid] = __half2float(qhi[qrow * D + tid]) + __half2float(qlo[qrow * D + tid]);
+  __syncthreads();
+  const float cq = 0.125f * LOG2E * qinv[qrow];
+  const int j0 = c * TAIL_KEYS;
+  float mx = -INFINITY;
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int jl = u * 256 + tid, j = j0 + jl;
+    float x = -INFINITY;
+    if (j < Lk) {
+      const uint4* kh = reinterpret_cast<const uint4*>(khi + ((int64_t)bh * Lkt + j) * D);
+      const uint4* kl = reinterpret_cast<const uint4*>(klo + ((int64_t)bh * Lkt + j) * D);
+      float dot = 0.0f;
+#pragma unroll
+      for (int v = 0; v < D / 8; ++v) {
+        const uint4 a = kh[v], b = kl[v];
+        const __half2* ah = reinterpret_cast<const __half2*>(&a);
+        const __half2* bl = reinterpret_cast<const __half2*>(&b);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 fh = __half22float2(ah[e]), fl = __half22float2(bl[e]);
+          dot = fmaf(qs[v * 8 + 2 * e], fh.x + fl.x, dot);
+          dot = fmaf(qs[v * 8 + 2 * e + 1], fh.y + fl.y, dot);
+        }
+      }
+      x = dot * (cq * kinv[(int64_t)bh * T + j / BKV]);
+    }
+    xs[jl] = x;
+    mx = fmaxf(mx, x);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) mx_s[warp] = mx;
+  __syncthreads();
+  mx = mx_s[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) mx = fmaxf(mx, mx_s[w]);
+  // each thread: its two keys' weights, then their V columns (V^T planes: for a fixed
+  // dimension the lanes' keys are consecutive)
+  float o[D];
+#pragma unroll
+  for (int d = 0; d < D; ++d) o[d] = 0.0f;
+  float l = 0.0f;
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int jl = u * 256 + tid, j = j0 + jl;
+    if (j < Lk) {
+      const float pj = ex2(xs[jl] - mx);
+      l += pj;
+      const float w = pj * vinv[(int64_t)bh * T + j / BKV];
+#pragma unroll
+      for (int d = 0; d < D; ++d) {
+        const int64_t off = ((int64_t)bh * D + d) * Lkt + j;
+        o[d] = fmaf(w, __half2float(vhi[off]) + __half2float(vlo[off]), o[d]);
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+#pragma unroll
+  for (int d = 0; d < D; ++d) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) o[d] += __shfl_xor_sync(0xffffffffu, o[d], off);
+  }
+  if (lane == 0) {
+    l_s[warp] = l;
+#pragma unroll
+    for (int d = 0; d < D; ++d) red[warp][d] = o[d];
+  }
+  __syncthreads();
+  float* dst = part + (((int64_t)bh * rows + r) * chunks + c) * TAIL_PART;
+  if (tid < D) {
+    float acc = red[0][tid];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) acc += red[w][tid];
+    dst[2 + tid] = acc;
+  } else if (tid == D) {
+    float acc = l_s[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) acc += l_s[w];
+    dst[0] = mx;
+    dst[1] = acc;
+  }
+}
+
+// Pass 2: one warp per (head, tail row); lane d owns dimensions d and d + 32.
+__global__ void __launch_bounds__(32) sdpa_tail_merge(
+    const float* __restrict__ part, int chunks, const float* __restrict__ vinv, int H, int Lq, int T,
+    int row0, float* __restrict__ out, int out_blhd, __half* __restrict__ ohi,
+    __half* __restrict__ olo, float* __restrict__ ors) {
+  const int r = blockIdx.x, bh = blockIdx.y, rows = gridDim.x, lane = threadIdx.x;
+  const float* pr = part + ((int64_t)bh * rows + r) * chunks * TAIL_PART;
+  float m = -INFINITY;
+  for (int c = 0; c < chunks; ++c) m = fmaxf(m, pr[c * TAIL_PART]);
+  float l = 0.0f, o0 = 0.0f, o1 = 0.0f;
+  for (int c = 0; c < chunks; ++c) {
+    const float* q = pr + c * TAIL_PART;
+    const float f = q[0] == -INFINITY ? 0.0f : ex2(q[0] - m);  // 2^(m_chunk - m) <= 1
+    l = fmaf(q[1], f, l);
+    o0 = fmaf(q[2 + lane], f, o0);
+    o1 = fmaf(q[2 + 32 + lane], f, o1);
+  }
+  const float inv = 1.0f / l;
+  o0 *= inv;
+  o1 *= inv;
+  const int b = bh / H, hh = bh % H;
+  const int qrow = row0 + r;
+  if (ohi) {
+    float vb = 0.0f;
+    const float* v = vinv + (int64_t)b * H * T;
+    for (int e = lane; e < H * T; e += 32) vb = fmaxf(vb, v[e]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) vb = fmaxf(vb, __shfl_xor_sync(0xffffffffu, vb, off));
+    const int s = pow2_shift(32768.0f * vb * (1.0f + 0x1p-6f));
+    const float sc = pow2i(s);
+    const int64_t row = (int64_t)b * Lq + qrow;
+    const int64_t off = row * ((int64_t)H * D) + hh * D;
+    const float a0 = o0 * sc, a1 = o1 * sc;
+    const __half h0 = __float2half_rn(a0), h1 = __float2half_rn(a1);
+    ohi[off + lane] = h0;
+    ohi[off + 32 + lane] = h1;
+    olo[off + lane] = __float2half_rn(a0 - __half2float(h0));
+    olo[off + 32 + lane] = __float2half_rn(a1 - __half2float(h1));
+    if (hh == 0 && lane == 0) ors[row] = pow2i(-s);
+  } else {
+    float* dst = out_blhd ? out + (((int64_t)b * Lq + qrow) * H + hh) * D
+                          : out + ((int64_t)bh * Lq + qrow) * D;
+    dst[lane] = o0;
+    dst[32 + lane] = o1;
+  }
+}
+
 // Selected-query rows of the fused post-process (the q half of qkv_split_k<true>): RMSNorm
 // (and RoPE with the frequency row sel[i]) into the Q planes; one CTA per (bh, 128 queries),
 // no shared memory, so it runs at full occupancy.
@@ -1031,7 +1248,21 @@ struct SplitPlanesSdpa {
   __half *qhi, *qlo, *khi, *klo, *vhi, *vlo;
   float *qinv, *kinv, *vinv;
   int T, Lkt;
+  float* tail_part = nullptr;  // partials of the tail query rows (sdpa::sdpa_tail_partial)
 };
+
+// Query rows past the last full 128-row tile that go to the CUDA-core tail kernels (0: the
+// tensor-core kernel takes every row).
+static int tail_rows(int Lq, bool has_bias) {
+  const int r = Lq % sdpa::BQ;
+  return (!has_bias && Lq > sdpa::BQ && r != 0 && r <= sdpa::TAIL_MAX) ? r : 0;
+}
+
+static size_t tail_part_bytes(int64_t BH, int Lq, int Lk, bool has_bias) {
+  const int r = tail_rows(Lq, has_bias);
+  const int chunks = (Lk + sdpa::TAIL_KEYS - 1) / sdpa::TAIL_KEYS;
+  return (size_t)BH * r * chunks * sdpa::TAIL_PART * 4;
+}
 
 static size_t al256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
@@ -1072,15 +1303,27 @@ static void planes_from(uint8_t* q, uint8_t* kv, int64_t BH, int Lq, int Lk, Spl
   sp.vinv = reinterpret_cast<float*>(kv + ko[5]);
 }
 
-static int sdpa_planes(int64_t BH, int Lq, int Lk, cudaStream_t stream, SplitPlanesSdpa& sp) {
+// Q / K / V planes (and the tail rows' partials) in the library workspace.
+static int sdpa_planes(int64_t BH, int Lq, int Lk, cudaStream_t stream, SplitPlanesSdpa& sp,
+                       bool has_bias = false) {
   size_t qo[2], ko[6];
   int T, Lkt;
   const size_t qbytes = q_planes_layout(BH, Lq, qo);
   const size_t kvbytes = kv_planes_layout(BH, Lk, ko, T, Lkt);
-  uint8_t* ws = static_cast<uint8_t*>(workspace(qbytes + kvbytes, stream));
+  const size_t tbytes = tail_part_bytes(BH, Lq, Lk, has_bias);
+  uint8_t* ws = static_cast<uint8_t*>(workspace(qbytes + kvbytes + tbytes, stream));
   if (!ws) return kWorkspace;
   planes_from(ws, ws + qbytes, BH, Lq, Lk, sp);
+  sp.tail_part = tbytes ? reinterpret_cast<float*>(ws + qbytes + kvbytes) : nullptr;
   return kOk;
+}
+
+// Tail-row partials in the library workspace, for calls whose planes the caller owns.
+static int tail_workspace(SplitPlanesSdpa& sp, int64_t BH, int Lq, int Lk, cudaStream_t stream) {
+  const size_t tbytes = tail_part_bytes(BH, Lq, Lk, false);
+  if (!tbytes) return kOk;
+  sp.tail_part = static_cast<float*>(workspace(tbytes, stream));
+  return sp.tail_part ? kOk : kWorkspace;
 }
 
 // Shared-memory opt-in of the fused split kernels, once per device.
@@ -1096,10 +1339,28 @@ static void ensure_qkv_split_attr() {
   }
 }
 
+// Output in the NF24 GEMM's split format (hi == nullptr: fp32 output).
+struct OutSplit {
+  __half* hi = nullptr;
+  __half* lo = nullptr;
+  float* rs = nullptr;
+};
+
+// out_split: a split buffer of the [B * Lq, H * 64] output (256-byte aligned)
+static OutSplit out_split_of(void* out_split, int64_t B, int Lq, int H) {
+  const SplitLayout l = split_buffer_layout((int)(B * Lq), H * sdpa::D);
+  uint8_t* base = static_cast<uint8_t*>(out_split);
+  OutSplit o;
+  o.hi = reinterpret_cast<__half*>(base);
+  o.lo = reinterpret_cast<__half*>(base + l.lo_offset);
+  o.rs = reinterpret_cast<float*>(base + l.rs_offset);
+  return o;
+}
+
 // The attention kernel on split planes.
 static int sdpa_attend(const SplitPlanesSdpa& sp, const float* bias, int64_t bias_bh_stride,
                        float* out, int64_t BH, int H, int Lq, int Lk, int out_blhd,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, const OutSplit& osplit = OutSplit()) {
   using namespace sdpa;
   CUtensorMap m_qhi, m_qlo, m_khi, m_klo, m_vhi, m_vlo;
   const uint32_t box_rows[3] = {64, 128, 1};
@@ -1145,9 +1406,11 @@ static int sdpa_attend(const SplitPlanesSdpa& sp, const float* bias, int64_t bia
       attr_done.fetch_or(1ull << (dev & 63), std::memory_order_acq_rel);
     }
   }
-  const int Qt = (Lq + BQ - 1) / BQ;
+  // a few rows past the last full query tile go to the CUDA-core tail kernels
+  const int tail = sp.tail_part ? tail_rows(Lq, bias != nullptr) : 0;
+  const int Qt = tail ? Lq / BQ : (Lq + BQ - 1) / BQ;
   Params prm{sp.qinv, sp.kinv, sp.vinv, bias, (long long)bias_bh_stride, out, H, Lq, Lk, sp.T, out_blhd,
-             device_status(), Qt, (int)BH};
+             device_status(), Qt, (int)BH, osplit.hi, osplit.lo, osplit.rs};
   // persistent: one CTA per SM walking the (head, query tile) items
   static std::atomic<int> sm_count[64];
   int dev = 0;
@@ -1164,6 +1427,17 @@ static int sdpa_attend(const SplitPlanesSdpa& sp, const float* bias, int64_t bia
   {
     LaunchScope scope(kKSdpaAttn, stream);
     sdpa_fwd_tc<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(m_qhi, m_qlo, m_khi, m_klo, m_vhi, m_vlo, prm);
+  }
+  if (tail) {
+    const int chunks = (Lk + TAIL_KEYS - 1) / TAIL_KEYS;
+    const int row0 = Qt * BQ;
+    LaunchScope scope(kKSdpaAttn, stream);
+    sdpa_tail_partial<<<dim3(chunks, tail, (unsigned)BH), 256, 0, stream>>>(
+        sp.qhi, sp.qlo, sp.qinv, sp.khi, sp.klo, sp.kinv, sp.vhi, sp.vlo, sp.vinv, Lq, Lk, sp.Lkt,
+        sp.T, row0, sp.tail_part);
+    sdpa_tail_merge<<<dim3(tail, (unsigned)BH), 32, 0, stream>>>(
+        sp.tail_part, chunks, sp.vinv, H, Lq, sp.T, row0, out, out_blhd, osplit.hi, osplit.lo,
+        osplit.rs);
   }
   return launch_status();
 }
@@ -1184,7 +1458,7 @@ static int sdpa_launch(const float* q, const float* k, const float* v, int64_t b
   cudaStream_t stream = current_stream();
   const int64_t BH = (int64_t)B * H;
   SplitPlanesSdpa sp;
-  if ((st = sdpa_planes(BH, Lq, Lk, stream, sp)) != kOk) return st;
+  if ((st = sdpa_planes(BH, Lq, Lk, stream, sp, bias != nullptr)) != kOk) return st;
   const int64_t qrows = BH * Lq;
   {
     LaunchScope scope(kKSdpaSplit, stream);
@@ -1211,18 +1485,20 @@ static int sdpa_launch(const float* q, const float* k, const float* v, int64_t b
 template <bool kSelected>
 static int qkv_sdpa_launch(const float* qsrc, const float* kvsrc, const float* freqs,
                            const int64_t* sel, const float* qg, const float* kg, float* out_blhd,
-                           int B, int H, int Lq, int Lk, int fb) {
+                           int B, int H, int Lq, int Lk, int fb, void* out_split = nullptr) {
   using namespace sdpa;
   int st = entry_check();
   if (st != kOk) return st;
+  void* out = out_split ? out_split : static_cast<void*>(out_blhd);
   if (!is_device_pointer(kvsrc) || !is_device_pointer(qg) || !is_device_pointer(kg) ||
-      !is_device_pointer(out_blhd) || (qsrc && !is_device_pointer(qsrc)) ||
+      !is_device_pointer(out) || (qsrc && !is_device_pointer(qsrc)) ||
       (freqs && !is_device_pointer(freqs)))
     return kNotDevicePointer;
-  if ((reinterpret_cast<uintptr_t>(kvsrc) | reinterpret_cast<uintptr_t>(out_blhd) |
+  if ((reinterpret_cast<uintptr_t>(kvsrc) | reinterpret_cast<uintptr_t>(out) |
        reinterpret_cast<uintptr_t>(qsrc) | reinterpret_cast<uintptr_t>(freqs) |
        reinterpret_cast<uintptr_t>(qg) | reinterpret_cast<uintptr_t>(kg)) & 15)
     return kBadAlignment;
+  if (out_split && (reinterpret_cast<uintptr_t>(out_split) & 255)) return kBadAlignment;
   cudaStream_t stream = current_stream();
   const int64_t BH = (int64_t)B * H;
   SplitPlanesSdpa sp;
@@ -1244,7 +1520,8 @@ static int qkv_sdpa_launch(const float* qsrc, const float* kvsrc, const float* f
         qsrc, freqs, sel, qg, H, Lq, Lk, fb, sp.qhi, sp.qlo, sp.qinv);
   }
   if ((st = launch_status()) != kOk) return st;
-  return sdpa_attend(sp, nullptr, 0, out_blhd, BH, H, Lq, Lk, 1, stream);
+  return sdpa_attend(sp, nullptr, 0, out_blhd, BH, H, Lq, Lk, 1, stream,
+                     out_split ? out_split_of(out_split, B, Lq, H) : OutSplit());
 }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -1342,6 +1619,34 @@ int triposplat_b200_q_kv_rmsnorm_sdpa_f32(const float* q, const float* kv, const
   if (!q || !kv || !q_gamma || !k_gamma || !out_blhd) return tsb::kNullPointer;
   if (B <= 0 || Lq <= 0 || Lk <= 0 || H <= 0) return tsb::kBadDims;
   return tsb::qkv_sdpa_launch<true>(q, kv, nullptr, nullptr, q_gamma, k_gamma, out_blhd, B, H, Lq, Lk, 1);
+}
+
+// No reference counterpart: triposplat_b200_qkv_rope_rmsnorm_sdpa_f32 (D = 64) with the
+// output written into out_split, a split buffer (triposplat_b200_split_bytes(B * L, H * 64)
+// bytes, 256-byte aligned) of the [B * L, H * 64] attention output: the out-projection's
+// GEMM input without an fp32 round trip.  Row scales: 2^-s with s fixed per batch from the
+// largest V value (so every |O| * 2^s < 2^15); the planes equal the split of the fp32
+// output under those scales.
+int triposplat_b200_qkv_rope_rmsnorm_sdpa_split(const float* qkv, const float* frequencies,
+                                                const float* q_gamma, const float* k_gamma, int B,
+                                                int L, int H, int frequency_batches,
+                                                void* out_split) {
+  if (!qkv || !frequencies || !q_gamma || !k_gamma || !out_split) return tsb::kNullPointer;
+  if (B <= 0 || L <= 0 || H <= 0 || (frequency_batches != 1 && frequency_batches != B))
+    return tsb::kBadDims;
+  return tsb::qkv_sdpa_launch<false>(nullptr, qkv, frequencies, nullptr, q_gamma, k_gamma, nullptr,
+                                     B, H, L, L, frequency_batches, out_split);
+}
+
+// No reference counterpart: triposplat_b200_q_kv_rmsnorm_sdpa_f32 with the output written
+// into a split buffer of [B * Lq, H * 64] (as triposplat_b200_qkv_rope_rmsnorm_sdpa_split).
+int triposplat_b200_q_kv_rmsnorm_sdpa_split(const float* q, const float* kv, const float* q_gamma,
+                                            const float* k_gamma, int B, int Lq, int Lk, int H,
+                                            void* out_split) {
+  if (!q || !kv || !q_gamma || !k_gamma || !out_split) return tsb::kNullPointer;
+  if (B <= 0 || Lq <= 0 || Lk <= 0 || H <= 0) return tsb::kBadDims;
+  return tsb::qkv_sdpa_launch<true>(q, kv, nullptr, nullptr, q_gamma, k_gamma, nullptr, B, H, Lq, Lk,
+                                    1, out_split);
 }
 
 // ---- query-row sharding (no reference counterpart) -------------------------------------
@@ -1462,7 +1767,32 @@ int triposplat_b200_attend_rows_f32(const void* q_planes, const void* kv_planes,
   SplitPlanesSdpa sp;
   planes_from(static_cast<uint8_t*>(const_cast<void*>(q_planes)),
               static_cast<uint8_t*>(const_cast<void*>(kv_planes)), BH, Lq, L, sp);
-  return sdpa_attend(sp, nullptr, 0, out_blhd, BH, H, Lq, L, 1, current_stream());
+  cudaStream_t stream = current_stream();
+  if ((st = tail_workspace(sp, BH, Lq, L, stream)) != kOk) return st;
+  return sdpa_attend(sp, nullptr, 0, out_blhd, BH, H, Lq, L, 1, stream);
+}
+
+// triposplat_b200_attend_rows_f32 with the output written into a split buffer of
+// [B * Lq, H * 64] (as triposplat_b200_qkv_rope_rmsnorm_sdpa_split).
+int triposplat_b200_attend_rows_split(const void* q_planes, const void* kv_planes, int B, int H,
+                                      int Lq, int L, void* out_split) {
+  using namespace tsb;
+  if (!q_planes || !kv_planes || !out_split) return kNullPointer;
+  if (B <= 0 || H <= 0 || Lq <= 0 || L <= 0) return kBadDims;
+  if ((reinterpret_cast<uintptr_t>(q_planes) & 255) || (reinterpret_cast<uintptr_t>(kv_planes) & 255) ||
+      (reinterpret_cast<uintptr_t>(out_split) & 255))
+    return kBadAlignment;
+  int st = entry_check();
+  if (st != kOk) return st;
+  if (!is_device_pointer(q_planes) || !is_device_pointer(kv_planes) || !is_device_pointer(out_split))
+    return kNotDevicePointer;
+  const int64_t BH = (int64_t)B * H;
+  SplitPlanesSdpa sp;
+  planes_from(static_cast<uint8_t*>(const_cast<void*>(q_planes)),
+              static_cast<uint8_t*>(const_cast<void*>(kv_planes)), BH, Lq, L, sp);
+  cudaStream_t stream = current_stream();
+  if ((st = tail_workspace(sp, BH, Lq, L, stream)) != kOk) return st;
+  return sdpa_attend(sp, nullptr, 0, nullptr, BH, H, Lq, L, 1, stream, out_split_of(out_split, B, Lq, H));
 }
 
 // ---- cached condition keys (no reference counterpart) ----------------------------------

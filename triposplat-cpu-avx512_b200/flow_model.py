@@ -479,11 +479,11 @@ class FlowModelB200:
         # self-attention
         self._ln_split(x, sph, shift_msa, scale_msa)
         self._lin_split(p + "qkv", sph, rows, b["qkv"])
-        # RoPE + RMSNorm straight into the attention's split format, then the attention
-        self._ok(lib.triposplat_b200_qkv_rope_rmsnorm_sdpa_f32(
+        # RoPE + RMSNorm straight into the attention's split format, then the attention,
+        # whose output goes straight into the out-projection's split format
+        self._ok(lib.triposplat_b200_qkv_rope_rmsnorm_sdpa_split(
             b["qkv"].data_ptr(), self.freqs.data_ptr(), prm[p + "q_gamma"].data_ptr(),
-            prm[p + "k_gamma"].data_ptr(), b["o"].data_ptr(), B, L, H, 64, 1), "self_attention")
-        self._split(b["o"], sph)
+            prm[p + "k_gamma"].data_ptr(), B, L, H, 1, sph), "self_attention")
         self._lin_split(p + "out", sph, rows, x, mode=2, gate=gate_msa, gate_ld=h, rows_per_batch=L)
         # cross-attention
         self._ln_split(x, sph)
@@ -492,14 +492,13 @@ class FlowModelB200:
             qpl = self._split_ptr("cq_planes")
             self._ok(lib.triposplat_b200_q_split_f32(y.data_ptr(), prm[p + "cq_gamma"].data_ptr(), B, L, H,
                                                      qpl), "cross q split")
-            self._ok(lib.triposplat_b200_attend_rows_f32(qpl, self._cond_plane_ptr(i), b["o"].data_ptr(),
-                                                         B, H, L, Mc), "cross_attention")
+            self._ok(lib.triposplat_b200_attend_rows_split(qpl, self._cond_plane_ptr(i), B, H, L, Mc, sph),
+                     "cross_attention")
         else:
             self._lin_split(p + "cross_kv", self._split_ptr("sp_c"), B * Mc, b["ckv"])
-            self._ok(lib.triposplat_b200_q_kv_rmsnorm_sdpa_f32(
+            self._ok(lib.triposplat_b200_q_kv_rmsnorm_sdpa_split(
                 y.data_ptr(), b["ckv"].data_ptr(), prm[p + "cq_gamma"].data_ptr(),
-                prm[p + "ck_gamma"].data_ptr(), b["o"].data_ptr(), B, L, Mc, H), "cross_attention")
-        self._split(b["o"], sph)
+                prm[p + "ck_gamma"].data_ptr(), B, L, Mc, H, sph), "cross_attention")
         self._lin_split(p + "cross_out", sph, rows, x, mode=3)
         # MLP: the hidden layer's split scales fixed from a bound, GELU straight into that split
         self._ln_split(x, sph, shift_mlp, scale_mlp, bound=(sphid, s.mlp, self.gelu_bounds[i]))

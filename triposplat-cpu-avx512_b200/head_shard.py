@@ -177,7 +177,7 @@ class HeadShardedFlowModel(FlowModelB200):
         f32 = dict(dtype=torch.float32, device=device)
         e = torch.empty
         self.buf.update({
-            "qkv_l": e(B, L, 3 * w, **f32), "o_l": e(B, L, w, **f32), "yq_l": e(B, L, w, **f32),
+            "qkv_l": e(B, L, 3 * w, **f32), "yq_l": e(B, L, w, **f32),
             "ckv_l": e(B, Mc, 2 * w, **f32), "part": e(B, L, h, **f32),
         })
         for name, k in (("sp_o", w), ("sp_hid_l", f)):
@@ -266,10 +266,9 @@ class HeadShardedFlowModel(FlowModelB200):
         qkv = b["qkv_l"]
         for j, (c0, n) in enumerate(pl["qkv"]):
             self._lin_cols(p + "qkv", sph, rows, qkv.data_ptr() + 4 * j * w, c0, n, 3 * w)
-        self._ok(lib.triposplat_b200_qkv_rope_rmsnorm_sdpa_f32(
+        self._ok(lib.triposplat_b200_qkv_rope_rmsnorm_sdpa_split(
             qkv.data_ptr(), self.freqs_l.data_ptr(), g[p + "q_gamma"].data_ptr(),
-            g[p + "k_gamma"].data_ptr(), b["o_l"].data_ptr(), B, L, hl, 64, 1), "self_attention")
-        self._split(b["o_l"], spo)
+            g[p + "k_gamma"].data_ptr(), B, L, hl, 1, spo), "self_attention")
         self._lin_rows(p + "out", spo, rows, *pl["out"], self._part_ptr())
         yield from self._reduce_into_x(2, gate_msa)
         # cross-attention over this rank's heads
@@ -280,10 +279,9 @@ class HeadShardedFlowModel(FlowModelB200):
         for j, (c0, n) in enumerate(pl["cross_kv"]):
             self._lin_cols(p + "cross_kv", self._split_ptr("sp_c"), B * Mc,
                            ckv.data_ptr() + 4 * j * w, c0, n, 2 * w)
-        self._ok(lib.triposplat_b200_q_kv_rmsnorm_sdpa_f32(
+        self._ok(lib.triposplat_b200_q_kv_rmsnorm_sdpa_split(
             b["yq_l"].data_ptr(), ckv.data_ptr(), g[p + "cq_gamma"].data_ptr(),
-            g[p + "ck_gamma"].data_ptr(), b["o_l"].data_ptr(), B, L, Mc, hl), "cross_attention")
-        self._split(b["o_l"], spo)
+            g[p + "ck_gamma"].data_ptr(), B, L, Mc, hl, spo), "cross_attention")
         self._lin_rows(p + "cross_out", spo, rows, *pl["cross_out"], self._part_ptr())
         yield from self._reduce_into_x(3)
         # MLP over this rank's hidden columns

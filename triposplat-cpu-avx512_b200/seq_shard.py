@@ -140,7 +140,7 @@ class SeqShardedFlowModel(FlowModelB200):
         f32 = dict(dtype=torch.float32, device=device)
         e = torch.empty
         self.loc = {"x": e(B, Lloc, h, **f32), "a": e(B, Lloc, h, **f32), "y": e(B, Lloc, h, **f32),
-                    "o": e(B, Lloc, h, **f32), "qkv": e(B, Lloc, 3 * h, **f32)}
+                    "qkv": e(B, Lloc, 3 * h, **f32)}
         self.chunk_lat = (s.latent_tokens // world) * s.latent_dim
         # one row per batch, padded to 16 bytes so every row is a tensor-core GEMM output
         # (the drop-in GEMM sends unaligned outputs to its SIMT kernel, other rounding)
@@ -233,7 +233,7 @@ class SeqShardedFlowModel(FlowModelB200):
         m.copy_(b["mod"])
         self._add(m, self.tables[i])
         shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = (m[j] for j in range(6))
-        x, y, o = loc["x"], loc["y"], loc["o"]
+        x, y = loc["x"], loc["y"]
         sph, sphid = self._split_ptr("sp_hl"), self._split_ptr("sp_hidl")
         qpl = self._split_ptr("qplanes")
         kv = self.kv_set_ptr(i % 2)
@@ -248,17 +248,15 @@ class SeqShardedFlowModel(FlowModelB200):
             self.gather(self.peer.sets[i % 2])
         else:
             yield i % 2
-        self._ok(lib.triposplat_b200_attend_rows_f32(qpl, kv, o.data_ptr(), B, H, Lloc, L), "attend_rows")
-        self._split(o, sph)
+        self._ok(lib.triposplat_b200_attend_rows_split(qpl, kv, B, H, Lloc, L, sph), "attend_rows")
         self._lin_split(p + "out", sph, rows, x, mode=2, gate=gate_msa, gate_ld=h, rows_per_batch=Lloc)
         # cross-attention of this rank's rows to the cached condition keys / values
         self._ln_split_rows(x, sph)
         self._lin_split(p + "cross_q", sph, rows, y)
         self._ok(lib.triposplat_b200_q_split_f32(y.data_ptr(), prm[p + "cq_gamma"].data_ptr(), B, Lloc, H,
                                                  qpl), "cross q split")
-        self._ok(lib.triposplat_b200_attend_rows_f32(qpl, self._cond_plane_ptr(i), o.data_ptr(), B, H,
-                                                     Lloc, Mc), "cross_attention")
-        self._split(o, sph)
+        self._ok(lib.triposplat_b200_attend_rows_split(qpl, self._cond_plane_ptr(i), B, H, Lloc, Mc, sph),
+                 "cross_attention")
         self._lin_split(p + "cross_out", sph, rows, x, mode=3)
         # MLP
         self._ln_split_rows(x, sph, shift_mlp, scale_mlp, bound=(sphid, s.mlp, self.gelu_bounds[i]))
