@@ -982,165 +982,6 @@ __global__ void __launch_bounds__(256, 4) qkv_split_k(
   }
 }
 
-// ---------------------------------------------------------------------------
-// Tail query rows.  When Lq leaves a few rows past its last full 128-row tile (the camera
-// token of an 8193-token sequence), a tensor-core item for them would cost as much as a full
-// one and add a round to the persistent kernel (2080 items on 148 SMs: 15 rounds instead of
-// 14).  Those rows run here instead, on CUDA cores in fp32 from the same split planes:
-// pass 1 computes, per (head, row, chunk of TAIL_KEYS keys), the chunk's maximum m, sum
-// l = sum 2^(x - m) and o = sum 2^(x - m) v in log2 units (x = 0.125 log2(e) q.k); pass 2
-// merges the chunks with exact power-of-two factors and writes the row like the
-// tensor-core kernel does (fp32, or the split format with the batch's V bound).
-// ---------------------------------------------------------------------------
-constexpr int TAIL_MAX = 8;      // rows past the last full query tile handled this way
-constexpr int TAIL_KEYS = 512;   // keys per pass-1 CTA (two per thread)
-constexpr int TAIL_PART = D + 2; // floats per partial: m, l, o[64]
-
-__global__ void __launch_bounds__(256) sdpa_tail_partial(
-    const __half* __restrict__ qhi, const __half* __restrict__ qlo, const float* __restrict__ qinv,
-    const __half* __restrict__ khi, const __half* __restrict__ klo, const float* __restrict__ kinv,
-    const __half* __restrict__ vhi, const __half* __restrict__ vlo, const float* __restrict__ vinv,
-    int Lq, int Lk, int Lkt, int T, int row0, float* __restrict__ part) {
-  __shared__ float qs[D];
-  __shared__ float xs[TAIL_KEYS];
-  __shared__ float red[8][D];
-  __shared__ float mx_s[8], l_s[8];
-  const int c = blockIdx.x, r = blockIdx.y, bh = blockIdx.z;
-  const int chunks = gridDim.x, rows = gridDim.y;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t qrow = (int64_t)bh * Lq + row0 + r;
-  if (tid < D) qs[tid] = __half2float(qhi[qrow * D + tid]) + __half2float(qlo[qrow * D + tid]);
-  __syncthreads();
-  const float cq = 0.125f * LOG2E * qinv[qrow];
-  const int j0 = c * TAIL_KEYS;
-  float mx = -INFINITY;
-#pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    const int jl = u * 256 + tid, j = j0 + jl;
-    float x = -INFINITY;
-    if (j < Lk) {
-      const uint4* kh = reinterpret_cast<const uint4*>(khi + ((int64_t)bh * Lkt + j) * D);
-      const uint4* kl = reinterpret_cast<const uint4*>(klo + ((int64_t)bh * Lkt + j) * D);
-      float dot = 0.0f;
-#pragma unroll
-      for (int v = 0; v < D / 8; ++v) {
-        const uint4 a = kh[v], b = kl[v];
-        const __half2* ah = reinterpret_cast<const __half2*>(&a);
-        const __half2* bl = reinterpret_cast<const __half2*>(&b);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 fh = __half22float2(ah[e]), fl = __half22float2(bl[e]);
-          dot = fmaf(qs[v * 8 + 2 * e], fh.x + fl.x, dot);
-          dot = fmaf(qs[v * 8 + 2 * e + 1], fh.y + fl.y, dot);
-        }
-      }
-      x = dot * (cq * kinv[(int64_t)bh * T + j / BKV]);
-    }
-    xs[jl] = x;
-    mx = fmaxf(mx, x);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if (lane == 0) mx_s[warp] = mx;
-  __syncthreads();
-  mx = mx_s[0];
-#pragma unroll
-  for (int w = 1; w < 8; ++w) mx = fmaxf(mx, mx_s[w]);
-  // each thread: its two keys' weights, then their V columns (V^T planes: for a fixed
-  // dimension the lanes' keys are consecutive)
-  float o[D];
-#pragma unroll
-  for (int d = 0; d < D; ++d) o[d] = 0.0f;
-  float l = 0.0f;
-#pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    const int jl = u * 256 + tid, j = j0 + jl;
-    if (j < Lk) {
-      const float pj = ex2(xs[jl] - mx);
-      l += pj;
-      const float w = pj * vinv[(int64_t)bh * T + j / BKV];
-#pragma unroll
-      for (int d = 0; d < D; ++d) {
-        const int64_t off = ((int64_t)bh * D + d) * Lkt + j;
-        o[d] = fmaf(w, __half2float(vhi[off]) + __half2float(vlo[off]), o[d]);
-      }
-    }
-  }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-#pragma unroll
-  for (int d = 0; d < D; ++d) {
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) o[d] += __shfl_xor_sync(0xffffffffu, o[d], off);
-  }
-  if (lane == 0) {
-    l_s[warp] = l;
-#pragma unroll
-    for (int d = 0; d < D; ++d) red[warp][d] = o[d];
-  }
-  __syncthreads();
-  float* dst = part + (((int64_t)bh * rows + r) * chunks + c) * TAIL_PART;
-  if (tid < D) {
-    float acc = red[0][tid];
-#pragma unroll
-    for (int w = 1; w < 8; ++w) acc += red[w][tid];
-    dst[2 + tid] = acc;
-  } else if (tid == D) {
-    float acc = l_s[0];
-#pragma unroll
-    for (int w = 1; w < 8; ++w) acc += l_s[w];
-    dst[0] = mx;
-    dst[1] = acc;
-  }
-}
-
-// Pass 2: one warp per (head, tail row); lane d owns dimensions d and d + 32.
-__global__ void __launch_bounds__(32) sdpa_tail_merge(
-    const float* __restrict__ part, int chunks, const float* __restrict__ vinv, int H, int Lq, int T,
-    int row0, float* __restrict__ out, int out_blhd, __half* __restrict__ ohi,
-    __half* __restrict__ olo, float* __restrict__ ors) {
-  const int r = blockIdx.x, bh = blockIdx.y, rows = gridDim.x, lane = threadIdx.x;
-  const float* pr = part + ((int64_t)bh * rows + r) * chunks * TAIL_PART;
-  float m = -INFINITY;
-  for (int c = 0; c < chunks; ++c) m = fmaxf(m, pr[c * TAIL_PART]);
-  float l = 0.0f, o0 = 0.0f, o1 = 0.0f;
-  for (int c = 0; c < chunks; ++c) {
-    const float* q = pr + c * TAIL_PART;
-    const float f = q[0] == -INFINITY ? 0.0f : ex2(q[0] - m);  // 2^(m_chunk - m) <= 1
-    l = fmaf(q[1], f, l);
-    o0 = fmaf(q[2 + lane], f, o0);
-    o1 = fmaf(q[2 + 32 + lane], f, o1);
-  }
-  const float inv = 1.0f / l;
-  o0 *= inv;
-  o1 *= inv;
-  const int b = bh / H, hh = bh % H;
-  const int qrow = row0 + r;
-  if (ohi) {
-    float vb = 0.0f;
-    const float* v = vinv + (int64_t)b * H * T;
-    for (int e = lane; e < H * T; e += 32) vb = fmaxf(vb, v[e]);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) vb = fmaxf(vb, __shfl_xor_sync(0xffffffffu, vb, off));
-    const int s = pow2_shift(32768.0f * vb * (1.0f + 0x1p-6f));
-    const float sc = pow2i(s);
-    const int64_t row = (int64_t)b * Lq + qrow;
-    const int64_t off = row * ((int64_t)H * D) + hh * D;
-    const float a0 = o0 * sc, a1 = o1 * sc;
-    const __half h0 = __float2half_rn(a0), h1 = __float2half_rn(a1);
-    ohi[off + lane] = h0;
-    ohi[off + 32 + lane] = h1;
-    olo[off + lane] = __float2half_rn(a0 - __half2float(h0));
-    olo[off + 32 + lane] = __float2half_rn(a1 - __half2float(h1));
-    if (hh == 0 && lane == 0) ors[row] = pow2i(-s);
-  } else {
-    float* dst = out_blhd ? out + (((int64_t)b * Lq + qrow) * H + hh) * D
-                          : out + ((int64_t)bh * Lq + qrow) * D;
-    dst[lane] = o0;
-    dst[32 + lane] = o1;
-  }
-}
-
 // Selected-query rows of the fused post-process (the q half of qkv_split_k<true>): RMSNorm
 // (and RoPE with the frequency row sel[i]) into the Q planes; one CTA per (bh, 128 queries),
 // no shared memory, so it runs at full occupancy.
@@ -1248,21 +1089,7 @@ struct SplitPlanesSdpa {
   __half *qhi, *qlo, *khi, *klo, *vhi, *vlo;
   float *qinv, *kinv, *vinv;
   int T, Lkt;
-  float* tail_part = nullptr;  // partials of the tail query rows (sdpa::sdpa_tail_partial)
 };
-
-// Query rows past the last full 128-row tile that go to the CUDA-core tail kernels (0: the
-// tensor-core kernel takes every row).
-static int tail_rows(int Lq, bool has_bias) {
-  const int r = Lq % sdpa::BQ;
-  return (!has_bias && Lq > sdpa::BQ && r != 0 && r <= sdpa::TAIL_MAX) ? r : 0;
-}
-
-static size_t tail_part_bytes(int64_t BH, int Lq, int Lk, bool has_bias) {
-  const int r = tail_rows(Lq, has_bias);
-  const int chunks = (Lk + sdpa::TAIL_KEYS - 1) / sdpa::TAIL_KEYS;
-  return (size_t)BH * r * chunks * sdpa::TAIL_PART * 4;
-}
 
 static size_t al256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
@@ -1303,27 +1130,15 @@ static void planes_from(uint8_t* q, uint8_t* kv, int64_t BH, int Lq, int Lk, Spl
   sp.vinv = reinterpret_cast<float*>(kv + ko[5]);
 }
 
-// Q / K / V planes (and the tail rows' partials) in the library workspace.
-static int sdpa_planes(int64_t BH, int Lq, int Lk, cudaStream_t stream, SplitPlanesSdpa& sp,
-                       bool has_bias = false) {
+static int sdpa_planes(int64_t BH, int Lq, int Lk, cudaStream_t stream, SplitPlanesSdpa& sp) {
   size_t qo[2], ko[6];
   int T, Lkt;
   const size_t qbytes = q_planes_layout(BH, Lq, qo);
   const size_t kvbytes = kv_planes_layout(BH, Lk, ko, T, Lkt);
-  const size_t tbytes = tail_part_bytes(BH, Lq, Lk, has_bias);
-  uint8_t* ws = static_cast<uint8_t*>(workspace(qbytes + kvbytes + tbytes, stream));
+  uint8_t* ws = static_cast<uint8_t*>(workspace(qbytes + kvbytes, stream));
   if (!ws) return kWorkspace;
   planes_from(ws, ws + qbytes, BH, Lq, Lk, sp);
-  sp.tail_part = tbytes ? reinterpret_cast<float*>(ws + qbytes + kvbytes) : nullptr;
   return kOk;
-}
-
-// Tail-row partials in the library workspace, for calls whose planes the caller owns.
-static int tail_workspace(SplitPlanesSdpa& sp, int64_t BH, int Lq, int Lk, cudaStream_t stream) {
-  const size_t tbytes = tail_part_bytes(BH, Lq, Lk, false);
-  if (!tbytes) return kOk;
-  sp.tail_part = static_cast<float*>(workspace(tbytes, stream));
-  return sp.tail_part ? kOk : kWorkspace;
 }
 
 // Shared-memory opt-in of the fused split kernels, once per device.
@@ -1406,9 +1221,7 @@ static int sdpa_attend(const SplitPlanesSdpa& sp, const float* bias, int64_t bia
       attr_done.fetch_or(1ull << (dev & 63), std::memory_order_acq_rel);
     }
   }
-  // a few rows past the last full query tile go to the CUDA-core tail kernels
-  const int tail = sp.tail_part ? tail_rows(Lq, bias != nullptr) : 0;
-  const int Qt = tail ? Lq / BQ : (Lq + BQ - 1) / BQ;
+  const int Qt = (Lq + BQ - 1) / BQ;
   Params prm{sp.qinv, sp.kinv, sp.vinv, bias, (long long)bias_bh_stride, out, H, Lq, Lk, sp.T, out_blhd,
              device_status(), Qt, (int)BH, osplit.hi, osplit.lo, osplit.rs};
   // persistent: one CTA per SM walking the (head, query tile) items
@@ -1427,17 +1240,6 @@ static int sdpa_attend(const SplitPlanesSdpa& sp, const float* bias, int64_t bia
   {
     LaunchScope scope(kKSdpaAttn, stream);
     sdpa_fwd_tc<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(m_qhi, m_qlo, m_khi, m_klo, m_vhi, m_vlo, prm);
-  }
-  if (tail) {
-    const int chunks = (Lk + TAIL_KEYS - 1) / TAIL_KEYS;
-    const int row0 = Qt * BQ;
-    LaunchScope scope(kKSdpaAttn, stream);
-    sdpa_tail_partial<<<dim3(chunks, tail, (unsigned)BH), 256, 0, stream>>>(
-        sp.qhi, sp.qlo, sp.qinv, sp.khi, sp.klo, sp.kinv, sp.vhi, sp.vlo, sp.vinv, Lq, Lk, sp.Lkt,
-        sp.T, row0, sp.tail_part);
-    sdpa_tail_merge<<<dim3(tail, (unsigned)BH), 32, 0, stream>>>(
-        sp.tail_part, chunks, sp.vinv, H, Lq, sp.T, row0, out, out_blhd, osplit.hi, osplit.lo,
-        osplit.rs);
   }
   return launch_status();
 }
@@ -1458,7 +1260,7 @@ static int sdpa_launch(const float* q, const float* k, const float* v, int64_t b
   cudaStream_t stream = current_stream();
   const int64_t BH = (int64_t)B * H;
   SplitPlanesSdpa sp;
-  if ((st = sdpa_planes(BH, Lq, Lk, stream, sp, bias != nullptr)) != kOk) return st;
+  if ((st = sdpa_planes(BH, Lq, Lk, stream, sp)) != kOk) return st;
   const int64_t qrows = BH * Lq;
   {
     LaunchScope scope(kKSdpaSplit, stream);
@@ -1767,9 +1569,7 @@ int triposplat_b200_attend_rows_f32(const void* q_planes, const void* kv_planes,
   SplitPlanesSdpa sp;
   planes_from(static_cast<uint8_t*>(const_cast<void*>(q_planes)),
               static_cast<uint8_t*>(const_cast<void*>(kv_planes)), BH, Lq, L, sp);
-  cudaStream_t stream = current_stream();
-  if ((st = tail_workspace(sp, BH, Lq, L, stream)) != kOk) return st;
-  return sdpa_attend(sp, nullptr, 0, out_blhd, BH, H, Lq, L, 1, stream);
+  return sdpa_attend(sp, nullptr, 0, out_blhd, BH, H, Lq, L, 1, current_stream());
 }
 
 // triposplat_b200_attend_rows_f32 with the output written into a split buffer of
@@ -1790,9 +1590,8 @@ int triposplat_b200_attend_rows_split(const void* q_planes, const void* kv_plane
   SplitPlanesSdpa sp;
   planes_from(static_cast<uint8_t*>(const_cast<void*>(q_planes)),
               static_cast<uint8_t*>(const_cast<void*>(kv_planes)), BH, Lq, L, sp);
-  cudaStream_t stream = current_stream();
-  if ((st = tail_workspace(sp, BH, Lq, L, stream)) != kOk) return st;
-  return sdpa_attend(sp, nullptr, 0, nullptr, BH, H, Lq, L, 1, stream, out_split_of(out_split, B, Lq, H));
+  return sdpa_attend(sp, nullptr, 0, nullptr, BH, H, Lq, L, 1, current_stream(),
+                     out_split_of(out_split, B, Lq, H));
 }
 
 // ---- cached condition keys (no reference counterpart) ----------------------------------
