@@ -1041,24 +1041,36 @@ __global__ void __launch_bounds__(256) kv_gather_k(KvGather g, uint8_t* __restri
   const int64_t k_units = (int64_t)tiles * BKV * D * 2 / 16;  // 16-byte units per key plane
   const int64_t v_units = (int64_t)tiles * BKV * 2 / 16;      // per transposed value row
   const int64_t total = 2 * k_units + 2 * D * v_units;
-  for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < total;
-       u += (int64_t)gridDim.x * blockDim.x) {
-    size_t off;
+  auto offset_of = [&](int64_t u) -> size_t {
     if (u < 2 * k_units) {
       const int plane = (int)(u / k_units);
-      off = g.off[plane] + ((size_t)bh * Lkt + tok0) * D * 2 + (size_t)(u - plane * k_units) * 16;
-    } else {
-      const int64_t v = u - 2 * k_units;
-      const int plane = (int)(v / (D * v_units));
-      const int64_t w = v - plane * D * v_units;
-      const int d = (int)(w / v_units);
-      off = g.off[2 + plane] + (((size_t)bh * D + d) * Lkt + tok0) * 2 + (size_t)(w - d * v_units) * 16;
+      return g.off[plane] + ((size_t)bh * Lkt + tok0) * D * 2 + (size_t)(u - plane * k_units) * 16;
     }
-    uint4 val;
-    asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(val.x), "=r"(val.y), "=r"(val.z), "=r"(val.w)
-                 : "l"(src + off));
-    *reinterpret_cast<uint4*>(dst + off) = val;
+    const int64_t v = u - 2 * k_units;
+    const int plane = (int)(v / (D * v_units));
+    const int64_t w = v - plane * D * v_units;
+    const int d = (int)(w / v_units);
+    return g.off[2 + plane] + (((size_t)bh * D + d) * Lkt + tok0) * 2 + (size_t)(w - d * v_units) * 16;
+  };
+  // GATHER_ILP 16-byte loads in flight per thread before their stores: a peer's memory is
+  // a few microseconds away, and one outstanding load per thread would leave NVLink idle
+  constexpr int GATHER_ILP = 4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t u0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u0 < total; u0 += GATHER_ILP * stride) {
+    uint4 val[GATHER_ILP];
+    size_t off[GATHER_ILP];
+#pragma unroll
+    for (int e = 0; e < GATHER_ILP; ++e) {
+      const int64_t u = u0 + e * stride;
+      off[e] = u < total ? offset_of(u) : 0;
+      if (u < total)
+        asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(val[e].x), "=r"(val[e].y), "=r"(val[e].z), "=r"(val[e].w)
+                     : "l"(src + off[e]));
+    }
+#pragma unroll
+    for (int e = 0; e < GATHER_ILP; ++e)
+      if (u0 + e * stride < total) *reinterpret_cast<uint4*>(dst + off[e]) = val[e];
   }
   if (blockIdx.x == 0) {
     for (int i = threadIdx.x; i < 2 * tiles; i += blockDim.x) {
