@@ -686,7 +686,7 @@ def main():
                  "tensor_pipe_frac": None if achieved is None else round(3 * achieved / peak, 4),
                  "tensor_pipe_frac_of_burst": None if achieved is None else round(3 * achieved / burst, 4),
                  "ms_per_step": round(attn["ms"] / args.steps, 3),
-                 "traffic": profiled_traffic("sdpa_fwd_tc_config2a.md", "traffic_bytes_per_full_launch")}
+                 "traffic": profiled_traffic("sdpa_fwd_tc_block4.md", "traffic_bytes_per_launch_in_step")}
     roof_gemm = {"kernel": "nf24_gemm_tc (NF24 GEMM, all tensor-core Linears of the step)",
                  "bound": "tensor",
                  "achieved": None if g_achieved is None else round(g_achieved, 1),
@@ -698,8 +698,8 @@ def main():
                  "tensor_pipe_frac": None if g_achieved is None else round(3 * g_achieved / peak, 4),
                  "tensor_pipe_frac_of_burst": None if g_achieved is None else round(3 * g_achieved / burst, 4),
                  "ms_per_step": round(gemm["ms"] / args.steps, 3),
-                 "traffic": profiled_traffic("model_s20_step_launches.md",
-                                             "nf24_gemm_tc_traffic_bytes_per_launch")}
+                 "traffic": profiled_traffic("nf24_gemm_tc_gelu_split_block4.md", "traffic_bytes_per_launch"),
+                 "traffic_launch": "fc1 of a block (the largest Linear; one ncu capture)"}
     roofs = [roof_gemm, roof_attn] if gemm["ms"] >= attn["ms"] else [roof_attn, roof_gemm]
     line = {
         "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
