@@ -209,29 +209,48 @@ class ClockSampler:
     def __init__(self, uuid: str):
         self.uuid = uuid
         self.proc = None
+        self.lines = []
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line)
 
     def __enter__(self):
+        """Start sampling every 100 ms and return once the first sample has arrived (the
+        tool takes a moment to start), so that even a short timed region is sampled."""
+        import threading
+
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", self.uuid, f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return self
+        self.reader = threading.Thread(target=self._read, daemon=True)
+        self.reader.start()
+        t_end = time.time() + 5.0
+        while not self.lines and time.time() < t_end and self.proc.poll() is None:
+            time.sleep(0.02)
+        self.first = len(self.lines)  # samples from here on fall inside the timed region
         return self
 
     def __exit__(self, *exc):
         self.rows = []
         if self.proc is None:
             return False
-        time.sleep(0.25)
+        n_exit = len(self.lines)  # samples that arrived while the region ran
+        time.sleep(0.15)  # for a region shorter than the interval: the next sample
         self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=5)
+            self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-            out, _ = self.proc.communicate()
-        for line in out.splitlines():
+            self.proc.wait()
+        self.reader.join(timeout=5)
+        inside = self.lines[self.first:n_exit] or self.lines[self.first:self.first + 1]
+        for line in inside:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) >= 8:
                 self.rows.append(parts)

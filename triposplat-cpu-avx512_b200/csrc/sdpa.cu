@@ -848,35 +848,20 @@ __global__ void __launch_bounds__(256) sdpa_split_kv(
 
 // Fused QKV post-process -> attention split format (no reference counterpart; the
 // composition of scripts/native_qkv_postprocess_v2_avx512.c:45-191 with the split above).
-// One CTA per (bh, 128-token tile): RoPE + 8/max(||.||,1e-12)*gamma on q and k
-// (rope_rms64), then q rows straight to the Q planes (per-row pre-scale, as
+// One CTA per (bh, 128-token tile), eight lanes per token: RoPE + 8/max(||.||,1e-12)*gamma
+// on q and k (rope_rms64's arithmetic and sum order), then q rows straight to the Q planes
+// (per-row pre-scale, as
 // sdpa_split_q) and the tile's k / v through shared memory to the K and V^T planes (per-tile
 // pre-scales, as sdpa_split_kv): the same bits as the two-kernel path, with q / k / v never
 // written to HBM in fp32.  Source layouts: kSelected = false: qkv [B, L, 3, H, 64]
 // (q, k and v of token t); kSelected = true: q [B, Lq, H, 64] and kv [B, Lk, 2, H, 64], RoPE
 // frequency row of query i = sel[i] (no frequencies: no rotation).
-// One q row (the rope_rms64 output, one complex pair per lane) into the Q planes with its
-// per-row power-of-two pre-scale (as sdpa_split_q).
-__device__ __forceinline__ void emit_q_row(__half* __restrict__ qhi, __half* __restrict__ qlo,
-                                           float* __restrict__ qinv, int64_t row, float2 qy,
-                                           int lane) {
-  float mx = fmaxf(fabsf(qy.x), fabsf(qy.y));
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  const int sq = pow2_shift(mx);
-  const float a = qy.x * pow2i(sq), c = qy.y * pow2i(sq);
-  const __half2 hh = __floats2half2_rn(a, c);
-  const float2 hf = __half22float2(hh);
-  *reinterpret_cast<__half2*>(qhi + row * D + lane * 2) = hh;
-  *reinterpret_cast<__half2*>(qlo + row * D + lane * 2) = __floats2half2_rn(a - hf.x, c - hf.y);
-  if (lane == 0) qinv[row] = pow2i(-sq);
-}
 
 // Key tiles tile0 + blockIdx.y of the sequence (Lk tokens).  kvsrc holds src_L token rows
 // per batch starting at token src_t0 (the whole sequence: 0, Lk; a query-row shard: its own
 // token range); self-attention Q rows of token t go to row t - q_t0 of the Q planes.
 template <bool kSelected>
-__global__ void __launch_bounds__(256, 4) qkv_split_k(
+__global__ void __launch_bounds__(256, 3) qkv_split_k(
     const float* __restrict__ qsrc, const float* __restrict__ kvsrc, const float* __restrict__ freqs,
     const int64_t* __restrict__ sel, const float* __restrict__ qg, const float* __restrict__ kg,
     int H, int Lq, int Lk, int Lkt, int fb, int tile0, int src_t0, int src_L, int q_t0,
@@ -894,50 +879,93 @@ __global__ void __launch_bounds__(256, 4) qkv_split_k(
   const int fbb = fb == 1 ? 0 : b;
   const int tile = blockIdx.y + tile0, T = Lkt / BKV;
   const int t_end = min(Lk, src_t0 + src_L);  // tokens past it read as zeros
-  const float2 gq = reinterpret_cast<const float2*>(qg + (int64_t)h * 64)[lane];
-  const float2 gk = reinterpret_cast<const float2*>(kg + (int64_t)h * 64)[lane];
-  // one q row (rope_rms64 output held as one complex pair per lane) into the Q planes
-  auto emit_q = [&](int64_t row, float2 qy) { emit_q_row(qhi, qlo, qinv, row, qy, lane); };
+  // eight lanes per token, four tokens per warp at a time: lane j of a token holds the
+  // complex pairs j, j + 8, j + 16, j + 24 (the butterfly order of rope_rms64 kept: levels
+  // 16 and 8 are the lane's own adds, 4 / 2 / 1 shuffles inside the token's lanes)
+  const int grp = lane >> 3, jl = lane & 7;
+  const float2* gq2 = reinterpret_cast<const float2*>(qg + (int64_t)h * 64);
+  const float2* gk2 = reinterpret_cast<const float2*>(kg + (int64_t)h * 64);
+  // RoPE + 8/max(||.||, 1e-12) * gamma of one token's row (4 pairs per lane), and its max
+  auto rope_rms8 = [&](const float2 (&x)[4], const float2 (&f)[4], const float2* g,
+                       float2 (&y)[4]) -> float {
+    float sq[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      y[k] = make_float2(fmaf(x[k].x, f[k].x, -(x[k].y * f[k].y)), fmaf(x[k].x, f[k].y, x[k].y * f[k].x));
+      sq[k] = fmaf(y[k].x, y[k].x, y[k].y * y[k].y);
+    }
+    float ss = (sq[0] + sq[2]) + (sq[1] + sq[3]);
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float fac = 8.0f / fmaxf(sqrtf(ss), 1.0e-12f);
+    float mx = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 gg = g[jl + 8 * k];
+      y[k] = make_float2(y[k].x * fac * gg.x, y[k].y * fac * gg.y);
+      mx = fmaxf(mx, fmaxf(fabsf(y[k].x), fabsf(y[k].y)));
+    }
+    return mx;
+  };
   if (tile < T) {
     const int t0 = tile * BKV;
     float kmx = 0.0f, vmx = 0.0f;
-    float2 kreg[BKV / 8];  // this warp's 16 k rows (one complex pair per lane) until the
-                           // tile's scale is known; V goes through shared memory (transpose)
-    // 16 tokens per warp, four at a time with all their loads issued first (the loop is
-    // latency-bound otherwise: one token's loads and warp reductions at a time)
+    float2 kreg[4][4];  // this lane's pairs of its 4 k rows until the tile's scale is known;
+                        // V goes through shared memory (transpose)
 #pragma unroll
-    for (int j0 = 0; j0 < BKV / 8; j0 += 4) {
+    for (int u = 0; u < 4; ++u) {
+      const int i = warp * 16 + u * 4 + grp;  // token within the tile
+      const int t = t0 + i;
       float2 qx[4], kx[4], vx[4], fr[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int t = t0 + warp + 8 * (j0 + u);
-        qx[u] = kx[u] = vx[u] = make_float2(0.0f, 0.0f);
-        fr[u] = make_float2(1.0f, 0.0f);
-        if (t < t_end) {
-          if (freqs) fr[u] = reinterpret_cast<const float2*>(freqs + (((int64_t)fbb * Lk + t) * H + h) * 64)[lane];
-          const int64_t r = (int64_t)b * src_L + (t - src_t0);
-          const float* ks = kSelected ? kvsrc + (r * 2 * H + h) * 64 : kvsrc + (r * 3 * H + H + h) * 64;
-          if (!kSelected) qx[u] = reinterpret_cast<const float2*>(ks - (int64_t)H * 64)[lane];
-          kx[u] = reinterpret_cast<const float2*>(ks)[lane];
-          vx[u] = reinterpret_cast<const float2*>(ks + (int64_t)H * 64)[lane];
-        }
+      for (int k = 0; k < 4; ++k) {
+        qx[k] = kx[k] = vx[k] = make_float2(0.0f, 0.0f);
+        fr[k] = make_float2(1.0f, 0.0f);
       }
+      const bool valid = t < t_end;
+      if (valid) {
+        const int64_t r = (int64_t)b * src_L + (t - src_t0);
+        const float* ks = kSelected ? kvsrc + (r * 2 * H + h) * 64 : kvsrc + (r * 3 * H + H + h) * 64;
+        const float2* f2 = freqs ? reinterpret_cast<const float2*>(freqs + (((int64_t)fbb * Lk + t) * H + h) * 64)
+                                 : nullptr;
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int i = warp + 8 * (j0 + u);
-        const int t = t0 + i;
-        float2 ky = make_float2(0.0f, 0.0f), vy = make_float2(0.0f, 0.0f);
-        if (t < t_end) {  // warp-uniform: t depends on the warp only
-          if (!kSelected) emit_q((int64_t)bh * Lq + (t - q_t0), rope_rms64(qx[u], fr[u], gq));
-          ky = rope_rms64(kx[u], fr[u], gk);
-          vy = vx[u];
+        for (int k = 0; k < 4; ++k) {
+          if (f2) fr[k] = f2[jl + 8 * k];
+          if (!kSelected) qx[k] = reinterpret_cast<const float2*>(ks - (int64_t)H * 64)[jl + 8 * k];
+          kx[k] = reinterpret_cast<const float2*>(ks)[jl + 8 * k];
+          vx[k] = reinterpret_cast<const float2*>(ks + (int64_t)H * 64)[jl + 8 * k];
         }
-        kreg[j0 + u] = ky;
-        vt[i][2 * lane] = vy.x;
-        vt[i][2 * lane + 1] = vy.y;
-        kmx = fmaxf(kmx, fmaxf(fabsf(ky.x), fabsf(ky.y)));
-        vmx = fmaxf(vmx, fmaxf(fabsf(vy.x), fabsf(vy.y)));
       }
+      if (!kSelected) {
+        float2 qy[4];
+        const float qmx = rope_rms8(qx, fr, gq2, qy);
+        float m = qmx;
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (valid) {
+          const int sq2 = pow2_shift(m);
+          const int64_t row = (int64_t)bh * Lq + (t - q_t0);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float a = qy[k].x * pow2i(sq2), c = qy[k].y * pow2i(sq2);
+            const __half2 hh = __floats2half2_rn(a, c);
+            const float2 hf = __half22float2(hh);
+            *reinterpret_cast<__half2*>(qhi + row * D + 2 * (jl + 8 * k)) = hh;
+            *reinterpret_cast<__half2*>(qlo + row * D + 2 * (jl + 8 * k)) = __floats2half2_rn(a - hf.x, c - hf.y);
+          }
+          if (jl == 0) qinv[row] = pow2i(-sq2);
+        }
+      }
+      float2 ky[4];
+      const float km = rope_rms8(kx, fr, gk2, ky);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        kreg[u][k] = valid ? ky[k] : make_float2(0.0f, 0.0f);
+        vt[i][2 * (jl + 8 * k)] = vx[k].x;
+        vt[i][2 * (jl + 8 * k) + 1] = vx[k].y;
+        vmx = fmaxf(vmx, fmaxf(fabsf(vx[k].x), fabsf(vx[k].y)));
+      }
+      if (valid) kmx = fmaxf(kmx, km);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -950,15 +978,18 @@ __global__ void __launch_bounds__(256, 4) qkv_split_k(
 #pragma unroll
     for (int w = 1; w < 8; ++w) { kmx = fmaxf(kmx, red[0][w]); vmx = fmaxf(vmx, red[1][w]); }
     const int sk = pow2_shift(kmx), sv = pow2_shift(vmx);
-    // K rows straight from registers: 128 bytes of hi and of lo per row and warp
+    // K rows straight from registers
 #pragma unroll
-    for (int r = 0; r < BKV / 8; ++r) {
-      const float a = kreg[r].x * pow2i(sk), c = kreg[r].y * pow2i(sk);
-      const __half2 hh = __floats2half2_rn(a, c);
-      const float2 hf = __half22float2(hh);
-      const int64_t off = ((int64_t)bh * Lkt + t0 + warp + 8 * r) * D + 2 * lane;
-      *reinterpret_cast<__half2*>(khi + off) = hh;
-      *reinterpret_cast<__half2*>(klo + off) = __floats2half2_rn(a - hf.x, c - hf.y);
+    for (int u = 0; u < 4; ++u) {
+      const int64_t row = (int64_t)bh * Lkt + t0 + warp * 16 + u * 4 + grp;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float a = kreg[u][k].x * pow2i(sk), c = kreg[u][k].y * pow2i(sk);
+        const __half2 hh = __floats2half2_rn(a, c);
+        const float2 hf = __half22float2(hh);
+        *reinterpret_cast<__half2*>(khi + row * D + 2 * (jl + 8 * k)) = hh;
+        *reinterpret_cast<__half2*>(klo + row * D + 2 * (jl + 8 * k)) = __floats2half2_rn(a - hf.x, c - hf.y);
+      }
     }
     for (int e = threadIdx.x; e < D * (BKV / 8); e += 256) {
       const int d = e / (BKV / 8), jb = (e % (BKV / 8)) * 8;
@@ -985,34 +1016,80 @@ __global__ void __launch_bounds__(256, 4) qkv_split_k(
 // Selected-query rows of the fused post-process (the q half of qkv_split_k<true>): RMSNorm
 // (and RoPE with the frequency row sel[i]) into the Q planes; one CTA per (bh, 128 queries),
 // no shared memory, so it runs at full occupancy.
+// Four rows per warp at a time, eight lanes per row: lane j of a row holds the complex
+// pairs j, j + 8, j + 16, j + 24.  rope_rms64's butterfly adds pair l to pair l + 16, then
+// l + 8, 4, 2, 1: here the first two levels are the lane's own adds and the last three are
+// shuffles inside the row's eight lanes, so the sum (and every result bit) is the same,
+// with three dependent shuffles per reduction instead of five and four rows in flight.
 __global__ void __launch_bounds__(256) selected_q_split_k(
     const float* __restrict__ qsrc, const float* __restrict__ freqs, const int64_t* __restrict__ sel,
     const float* __restrict__ qg, int H, int Lq, int Lk, int fb, __half* __restrict__ qhi,
     __half* __restrict__ qlo, float* __restrict__ qinv) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = lane >> 3, j = lane & 7;
   const int bh = blockIdx.x, b = bh / H, h = bh % H;  // heads fastest, as qkv_split_k
   const int fbb = fb == 1 ? 0 : b;
   const int tile = blockIdx.y;
-  const float2 gq = reinterpret_cast<const float2*>(qg + (int64_t)h * 64)[lane];
-  // 16 rows per warp in two batches of 8, each batch's loads all issued before its
-  // arithmetic (the kernel is load-latency bound)
-  constexpr int QB = 8;
-  for (int j0 = 0; j0 < BKV / 8; j0 += QB) {
-    float2 qx[QB], fr[QB];
+  const float2* g2 = reinterpret_cast<const float2*>(qg + (int64_t)h * 64);
+  float2 gq[4];
 #pragma unroll
-    for (int u = 0; u < QB; ++u) {
-      const int qi = tile * BKV + warp + 8 * (j0 + u);
-      qx[u] = make_float2(0.0f, 0.0f);
-      fr[u] = make_float2(1.0f, 0.0f);  // no frequencies: identity rotation
-      if (qi < Lq) {
-        if (freqs) fr[u] = reinterpret_cast<const float2*>(freqs + (((int64_t)fbb * Lk + sel[qi]) * H + h) * 64)[lane];
-        qx[u] = reinterpret_cast<const float2*>(qsrc + (((int64_t)b * Lq + qi) * H + h) * 64)[lane];
+  for (int k = 0; k < 4; ++k) gq[k] = g2[j + 8 * k];
+  // 16 rows per warp: four passes of four rows, all loads issued first
+  float2 qx[4][4], fr[4][4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int qi = tile * BKV + warp * 16 + u * 4 + grp;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      qx[u][k] = make_float2(0.0f, 0.0f);
+      fr[u][k] = make_float2(1.0f, 0.0f);  // no frequencies: identity rotation
+    }
+    if (qi < Lq) {
+      const float2* src = reinterpret_cast<const float2*>(qsrc + (((int64_t)b * Lq + qi) * H + h) * 64);
+      const float2* f2 = freqs ? reinterpret_cast<const float2*>(freqs + (((int64_t)fbb * Lk + sel[qi]) * H + h) * 64)
+                               : nullptr;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        qx[u][k] = src[j + 8 * k];
+        if (f2) fr[u][k] = f2[j + 8 * k];
       }
     }
+  }
 #pragma unroll
-    for (int u = 0; u < QB; ++u) {
-      const int qi = tile * BKV + warp + 8 * (j0 + u);
-      if (qi < Lq) emit_q_row(qhi, qlo, qinv, (int64_t)bh * Lq + qi, rope_rms64(qx[u], fr[u], gq), lane);
+  for (int u = 0; u < 4; ++u) {
+    const int qi = tile * BKV + warp * 16 + u * 4 + grp;
+    float2 y[4];
+    float sq[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 x = qx[u][k], f = fr[u][k];
+      y[k] = make_float2(fmaf(x.x, f.x, -(x.y * f.y)), fmaf(x.x, f.y, x.y * f.x));
+      sq[k] = fmaf(y[k].x, y[k].x, y[k].y * y[k].y);
+    }
+    float ss = (sq[0] + sq[2]) + (sq[1] + sq[3]);  // butterfly levels 16 and 8
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float fac = 8.0f / fmaxf(sqrtf(ss), 1.0e-12f);
+    float mx = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      y[k] = make_float2(y[k].x * fac * gq[k].x, y[k].y * fac * gq[k].y);
+      mx = fmaxf(mx, fmaxf(fabsf(y[k].x), fabsf(y[k].y)));
+    }
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (qi < Lq) {
+      const int sq2 = pow2_shift(mx);
+      const int64_t row = (int64_t)bh * Lq + qi;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float a = y[k].x * pow2i(sq2), c = y[k].y * pow2i(sq2);
+        const __half2 hh = __floats2half2_rn(a, c);
+        const float2 hf = __half22float2(hh);
+        *reinterpret_cast<__half2*>(qhi + row * D + 2 * (j + 8 * k)) = hh;
+        *reinterpret_cast<__half2*>(qlo + row * D + 2 * (j + 8 * k)) = __floats2half2_rn(a - hf.x, c - hf.y);
+      }
+      if (j == 0) qinv[row] = pow2i(-sq2);
     }
   }
 }
