@@ -51,7 +51,10 @@
 // row's scale must be known before any of its heads is written, and O is a convex
 // combination of V rows, so |O| <= max |V| over the batch's keys and heads
 // < 2^15 * (largest inverse V-tile pre-scale of the batch): that bound fixes the scale
-// (value * 2^s < 2^15), and the planes equal the split of the fp32 output under it.
+// (value * 2^s < 2^15), and the planes equal the split of the fp32 output under it.  Either
+// way the teams merge their halves through shared memory and the item's 128 x 64 output is
+// staged there and written in row order (16 threads per row), not as a 128-byte piece per
+// thread.
 #include <cuda_fp16.h>
 
 #include <atomic>
@@ -85,7 +88,16 @@ constexpr int PLANE = 128 * D * 2;      // 16 KB: one 128 x 64 fp16 tile
 constexpr int STAGE = 2 * PLANE;        // hi + lo planes of one Q, K or V^T tile
 // Q, 2 K stages, 2 V stages, per-warp bias [8][BKV], team maxima / sums [2][BQ] each,
 // output halves [2 teams][BQ][32], barriers
-constexpr int SMEM_BYTES = 1024 + 5 * STAGE + 8 * BKV * 4 + 4 * BQ * 4 + 2 * BQ * 32 * 4 + 8 * 4 +
+// Exchange rows of 32 floats padded to 36: a row's float4 accesses by the eight threads of
+// a quarter warp then fall into eight different 4-bank groups (a 32-float pitch put every
+// thread of the warp on the same banks: 32-way conflicts in the end-of-item exchange).
+constexpr int XO_PITCH = 36;
+// The item's merged 128 x 64 output is staged in the same buffer (rows padded to 68 floats:
+// conflict-free float4 writes by a quarter warp) and written out by all 256 softmax threads
+// in row order, 16 threads per 256-byte row, instead of one 128-byte row piece per thread.
+constexpr int OUT_PITCH = 68;
+static_assert(BQ * OUT_PITCH <= 2 * BQ * XO_PITCH, "staging fits the exchange buffer");
+constexpr int SMEM_BYTES = 1024 + 5 * STAGE + 8 * BKV * 4 + 4 * BQ * 4 + 2 * BQ * XO_PITCH * 4 + 8 * 4 +
                            32 * 8 + 16;
 constexpr float LOG2E = 1.4426950408889634f;
 
@@ -367,8 +379,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   float* bias_s = reinterpret_cast<float*>(v_st + 2 * STAGE);  // [8 warps][BKV], log2 units
   float* xm = bias_s + 8 * BKV;        // [2 teams][BQ] final reference maxima
   float* xl = xm + 2 * BQ;             // [2 teams][BQ] final row sums
-  float* xo = xl + 2 * BQ;             // [2 teams][BQ][32] output halves for the other team
-  float* xvb = xo + 2 * BQ * 32;       // [8 softmax warps] partial max of the batch's V scales
+  float* xo = xl + 2 * BQ;             // [2 teams][BQ][XO_PITCH] output halves for the other team
+  float* xvb = xo + 2 * BQ * XO_PITCH; // [8 softmax warps] partial max of the batch's V scales
   uint64_t* bars = reinterpret_cast<uint64_t*>(xvb + 8);
   uint64_t* q_full = bars + 0;   // Q tile of the item loaded (TMA bytes)
   uint64_t* k_full = bars + 1;   // [2]
@@ -383,7 +395,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* xbar = bars + 19;    // end-of-row exchange between the teams (8 arrivals)
   uint64_t* q_empty = bars + 20; // the item's QK MMAs retired: Q shared memory reusable
   uint64_t* xfree = bars + 21;   // both teams read the exchange buffers (8 arrivals)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 22);
+  uint64_t* xread = bars + 22;   // both teams merged: the exchange buffer becomes the output tile
+  uint64_t* xstage = bars + 23;  // the item's output tile is staged (8 arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const uint32_t warp = warp_id();
@@ -413,6 +427,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     mbar_init(qk_done, 1);
     mbar_init(pv_all, 1);
     mbar_init(xbar, 8);
+    mbar_init(xread, 8);
+    mbar_init(xstage, 8);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -565,19 +581,39 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     float* bt = bias_s + (warp - 4) * BKV;
     const uint32_t orow = trow + O_COL + team * D;
     bool ok = true;
+    // An item's scales — the row's Q pre-scale and this lane's share of the head's V-tile
+    // scales — are loaded one item ahead into registers, so their latency hides behind the
+    // previous item's tiles instead of delaying its first.
+    constexpr int PF_V = 3;
+    float pf_cq = 0.0f, pf_v[PF_V];
+    auto prefetch = [&](int i) {
+      int bh_, q0_;
+      item_of(i, bh_, q0_);
+      const int qr = q0_ + r;
+      pf_cq = qr < p.Lq ? p.qinv[(int64_t)bh_ * p.Lq + qr] : 0.0f;
+#pragma unroll
+      for (int k = 0; k < PF_V; ++k) {
+        const int t = lane + 32 * k;
+        pf_v[k] = t < T ? p.vinv[(int64_t)bh_ * T + t] : 0.0f;
+      }
+    };
+    if (my_items > 0) prefetch(0);
     for (int i = 0; i < my_items && ok; ++i) {
     int bh, q0;
     item_of(i, bh, q0);
     const int qrow = q0 + r;
     const bool row_valid = qrow < p.Lq;
-    const float cq = 0.125f * LOG2E * (row_valid ? p.qinv[(int64_t)bh * p.Lq + qrow] : 0.0f);
+    const float cq = 0.125f * LOG2E * pf_cq;
     const float* bias_row = p.bias ? p.bias + (int64_t)bh * p.bias_bh_stride : nullptr;
-    // reference V scale of the head: the largest per-tile inverse pre-scale (the lanes load
-    // the head's tiles in parallel, then a warp max)
-    float vref = 0.0f;
-    for (int t = lane; t < T; t += 32) vref = fmaxf(vref, p.vinv[(int64_t)bh * T + t]);
+    // reference V scale of the head: the largest per-tile inverse pre-scale (the lanes'
+    // prefetched shares, the rest of a long sequence's tiles, then a warp max)
+    float vref = pf_v[0];
+#pragma unroll
+    for (int k = 1; k < PF_V; ++k) vref = fmaxf(vref, pf_v[k]);
+    for (int t = lane + 32 * PF_V; t < T; t += 32) vref = fmaxf(vref, p.vinv[(int64_t)bh * T + t]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) vref = fmaxf(vref, __shfl_xor_sync(0xffffffffu, vref, o));
+    if (i + 1 < my_items) prefetch(i + 1);
     const int vref_exp = __float_as_int(vref) >> 23;
     float m_run = -INFINITY, l_run = 0.0f;
     float o_acc[D];
@@ -655,7 +691,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // integers (or -inf for a team without tiles)
       xm[team * BQ + r] = m_run;
       xl[team * BQ + r] = l_run;
-      float* mine = xo + ((1 - team) * BQ + r) * 32;  // the half the other team writes out
+      float* mine = xo + ((1 - team) * BQ + r) * XO_PITCH;  // the half the other team writes out
       if (team == 0) {
 #pragma unroll
         for (int d = 0; d < 32; d += 4)
@@ -673,15 +709,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(xbar);
       ok = __all_sync(0xffffffffu, mbar_wait(xbar, i & 1, p.status, kDevTimeoutEpilogue, abort_flag));
+      float res[32];
+#pragma unroll
+      for (int d = 0; d < 32; ++d) res[d] = 0.0f;
       if (ok && row_valid) {
         const float m_o = xm[(1 - team) * BQ + r], l_o = xl[(1 - team) * BQ + r];
         const float m = fmaxf(m_run, m_o);
         const float f_me = m_run == m ? 1.0f : ex2(m_run - m);  // 0 for a team with no tiles
         const float f_o = m_o == m ? 1.0f : ex2(m_o - m);
         const float f = vref / (l_run * f_me + l_o * f_o);
-        const float* other = xo + (team * BQ + r) * 32;  // the other team's half of my dims
-        const int b = bh / p.H, hh = bh % p.H;
-        float res[32];
+        const float* other = xo + (team * BQ + r) * XO_PITCH;  // the other team's half of my dims
         if (team == 0) {
 #pragma unroll
           for (int d = 0; d < 32; ++d) res[d] = o_acc[d];
@@ -697,37 +734,59 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           res[d + 2] = (res[d + 2] * f_me + ov.z * f_o) * f;
           res[d + 3] = (res[d + 3] * f_me + ov.w * f_o) * f;
         }
+      }
+      // both teams have read the exchange halves: stage the merged row in the same buffer
+      __syncwarp();
+      if (lane == 0) mbar_arrive(xread);
+      ok = ok && __all_sync(0xffffffffu, mbar_wait(xread, i & 1, p.status, kDevTimeoutEpilogue, abort_flag));
+      float* stg = xo;  // [BQ][OUT_PITCH]
+      if (ok) {
+#pragma unroll
+        for (int d = 0; d < 32; d += 4)
+          *reinterpret_cast<float4*>(stg + r * OUT_PITCH + team * 32 + d) =
+              make_float4(res[d], res[d + 1], res[d + 2], res[d + 3]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(xstage);
+      ok = ok && __all_sync(0xffffffffu, mbar_wait(xstage, i & 1, p.status, kDevTimeoutEpilogue, abort_flag));
+      if (ok) {
+        // the item's output, row by row: 16 threads per row, 4 consecutive values each
+        const int b = bh / p.H, hh = bh % p.H;
+        const int tid = (warp - 4) * 32 + lane;
+        int s = 0;
+        float sc = 1.0f;
         if (p.ohi) {
           float vbat = xvb[0];
 #pragma unroll
           for (int w = 1; w < 8; ++w) vbat = fmaxf(vbat, xvb[w]);
           // |O| <= max |V| < 2^15 * vbat; 2^-6 of slack for the rounding of P.V and of 1/l
-          const int s = pow2_shift(32768.0f * vbat * (1.0f + 0x1p-6f));
-          const float sc = pow2i(s);
-          const int64_t row = (int64_t)b * p.Lq + qrow;
-          const int64_t off = row * ((int64_t)p.H * D) + hh * D + team * 32;
-#pragma unroll
-          for (int d = 0; d < 32; d += 8) {
-            __align__(16) __half h8[8];
-            __align__(16) __half l8[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float a = res[d + e] * sc;
-              const __half hv = __float2half_rn(a);
-              h8[e] = hv;
-              l8[e] = __float2half_rn(a - __half2float(hv));
-            }
-            *reinterpret_cast<uint4*>(p.ohi + off + d) = *reinterpret_cast<const uint4*>(h8);
-            *reinterpret_cast<uint4*>(p.olo + off + d) = *reinterpret_cast<const uint4*>(l8);
-          }
-          if (hh == 0 && team == 0) p.ors[row] = pow2i(-s);
-        } else {
-          float* dst = (p.out_blhd ? p.out + (((int64_t)b * p.Lq + qrow) * p.H + hh) * D
-                                   : p.out + ((int64_t)bh * p.Lq + qrow) * D) + team * 32;
-#pragma unroll
-          for (int d = 0; d < 32; d += 4)
-            *reinterpret_cast<float4*>(dst + d) = make_float4(res[d], res[d + 1], res[d + 2], res[d + 3]);
+          s = pow2_shift(32768.0f * vbat * (1.0f + 0x1p-6f));
+          sc = pow2i(s);
         }
+#pragma unroll 1
+        for (int f4 = tid; f4 < BQ * (D / 4); f4 += 256) {
+          const int row = f4 / (D / 4), c = (f4 % (D / 4)) * 4;
+          const int qr = q0 + row;
+          if (qr >= p.Lq) continue;
+          const float4 v = *reinterpret_cast<const float4*>(stg + row * OUT_PITCH + c);
+          if (p.ohi) {
+            const int64_t off = ((int64_t)b * p.Lq + qr) * ((int64_t)p.H * D) + hh * D + c;
+            const float a0 = v.x * sc, a1 = v.y * sc, a2 = v.z * sc, a3 = v.w * sc;
+            const __half2 h01 = __floats2half2_rn(a0, a1), h23 = __floats2half2_rn(a2, a3);
+            const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+            const __half2 l01 = __floats2half2_rn(a0 - f01.x, a1 - f01.y);
+            const __half2 l23 = __floats2half2_rn(a2 - f23.x, a3 - f23.y);
+            *reinterpret_cast<uint2*>(p.ohi + off) =
+                make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+            *reinterpret_cast<uint2*>(p.olo + off) =
+                make_uint2(*reinterpret_cast<const uint32_t*>(&l01), *reinterpret_cast<const uint32_t*>(&l23));
+          } else {
+            float* dst = p.out_blhd ? p.out + (((int64_t)b * p.Lq + qr) * p.H + hh) * D + c
+                                    : p.out + ((int64_t)bh * p.Lq + qr) * D + c;
+            *reinterpret_cast<float4*>(dst) = v;
+          }
+        }
+        if (p.ohi && hh == 0 && tid < BQ && q0 + tid < p.Lq) p.ors[(int64_t)b * p.Lq + q0 + tid] = pow2i(-s);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(xfree);
