@@ -581,16 +581,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     float* bt = bias_s + (warp - 4) * BKV;
     const uint32_t orow = trow + O_COL + team * D;
     bool ok = true;
-    // An item's scales — the row's Q pre-scale and this lane's share of the head's V-tile
-    // scales — are loaded one item ahead into registers, so their latency hides behind the
-    // previous item's tiles instead of delaying its first.
+    // An item's scales — the row's Q pre-scale, this lane's share of the head's V-tile
+    // scales and the K scale of the team's first tile — are loaded one item ahead into
+    // registers, so their latency hides behind the previous item's tiles instead of delaying
+    // its first.
     constexpr int PF_V = 3;
-    float pf_cq = 0.0f, pf_v[PF_V];
+    float pf_cq = 0.0f, pf_k0 = 0.0f, pf_v[PF_V];
     auto prefetch = [&](int i) {
       int bh_, q0_;
       item_of(i, bh_, q0_);
       const int qr = q0_ + r;
       pf_cq = qr < p.Lq ? p.qinv[(int64_t)bh_ * p.Lq + qr] : 0.0f;
+      pf_k0 = team < T ? p.kinv[(int64_t)bh_ * T + team] : 0.0f;
 #pragma unroll
       for (int k = 0; k < PF_V; ++k) {
         const int t = lane + 32 * k;
@@ -613,6 +615,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int t = lane + 32 * PF_V; t < T; t += 32) vref = fmaxf(vref, p.vinv[(int64_t)bh * T + t]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) vref = fmaxf(vref, __shfl_xor_sync(0xffffffffu, vref, o));
+    // the team's first tile's K and V scales (tile `team`: lane `team`'s first share)
+    const float k0_cur = pf_k0, v0_cur = __shfl_sync(0xffffffffu, pf_v[0], team);
     if (i + 1 < my_items) prefetch(i + 1);
     const int vref_exp = __float_as_int(vref) >> 23;
     float m_run = -INFINITY, l_run = 0.0f;
@@ -634,9 +638,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         __syncwarp();
       }
-      const float c2 = cq * p.kinv[(int64_t)bh * T + t];
+      const float c2 = cq * (n == 0 ? k0_cur : p.kinv[(int64_t)bh * T + t]);
       // exponent offset folding this V tile's pre-scale relative to the head reference
-      const float vshift = (float)((__float_as_int(p.vinv[(int64_t)bh * T + t]) >> 23) - vref_exp);
+      const float vshift =
+          (float)((__float_as_int(n == 0 ? v0_cur : p.vinv[(int64_t)bh * T + t]) >> 23) - vref_exp);
       ok = mbar_wait(&s_full[sb], (G / NSB) & 1, p.status, kDevTimeoutConsumer, abort_flag);
       // this team's previous O, P.V(G-2), retired long ago; it is folded in with the scores
       if (ok && n > 0) {
