@@ -617,7 +617,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int o = 16; o > 0; o >>= 1) vref = fmaxf(vref, __shfl_xor_sync(0xffffffffu, vref, o));
     // the team's first tile's K and V scales (tile `team`: lane `team`'s first share)
     const float k0_cur = pf_k0, v0_cur = __shfl_sync(0xffffffffu, pf_v[0], team);
-    if (i + 1 < my_items) prefetch(i + 1);
+    // the next item's scales are requested after this item's first tile: right here the
+    // previous item's output stores still fill the load / store queue
+    bool pf_next = i + 1 < my_items;
     const int vref_exp = __float_as_int(vref) >> 23;
     float m_run = -INFINITY, l_run = 0.0f;
     float o_acc[D];
@@ -659,7 +661,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[team]);
+      if (pf_next) {
+        prefetch(i + 1);
+        pf_next = false;
+      }
     }
+    if (pf_next) prefetch(i + 1);  // a team without tiles in this item
     // output split: this warp's share of the batch's V-tile scales (the loads issue before
     // the wait for the last P.V; the 8 shares meet in the exchange)
     float vb_part = 0.0f;
