@@ -86,18 +86,14 @@ constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
 constexpr float P_LIFT = 7.0f;  // p' = p * 2^7 <= 2^15 < fp16 max
 constexpr int PLANE = 128 * D * 2;      // 16 KB: one 128 x 64 fp16 tile
 constexpr int STAGE = 2 * PLANE;        // hi + lo planes of one Q, K or V^T tile
-// Q, 2 K stages, 2 V stages, per-warp bias [8][BKV], team maxima / sums [2][BQ] each,
-// output halves [2 teams][BQ][32], barriers
-// Exchange rows of 32 floats padded to 36: a row's float4 accesses by the eight threads of
-// a quarter warp then fall into eight different 4-bank groups (a 32-float pitch put every
-// thread of the warp on the same banks: 32-way conflicts in the end-of-item exchange).
-constexpr int XO_PITCH = 36;
-// The item's merged 128 x 64 output is staged in the same buffer (rows padded to 68 floats:
-// conflict-free float4 writes by a quarter warp) and written out by all 256 softmax threads
-// in row order, 16 threads per 256-byte row, instead of one 128-byte row piece per thread.
+// Q, 2 K stages, 2 V stages, per-warp bias [8][BKV], team 0's maxima / sums [BQ] each (two
+// arrays of 2 * BQ), the exchange / output tile [BQ][OUT_PITCH], V-scale shares [8], barriers.
+// Rows of the tile are padded to 68 floats: the eight threads of a quarter warp (eight rows)
+// then reach eight different 4-bank groups with their float4 accesses (a 64-float pitch would
+// put them all on the same banks).  Team 0 writes its partial rows there, team 1 merges each
+// row in place and then the whole tile goes out in row order, 16 threads per 256-byte row.
 constexpr int OUT_PITCH = 68;
-static_assert(BQ * OUT_PITCH <= 2 * BQ * XO_PITCH, "staging fits the exchange buffer");
-constexpr int SMEM_BYTES = 1024 + 5 * STAGE + 8 * BKV * 4 + 4 * BQ * 4 + 2 * BQ * XO_PITCH * 4 + 8 * 4 +
+constexpr int SMEM_BYTES = 1024 + 5 * STAGE + 8 * BKV * 4 + 4 * BQ * 4 + BQ * OUT_PITCH * 4 + 8 * 4 +
                            32 * 8 + 16;
 constexpr float LOG2E = 1.4426950408889634f;
 
@@ -379,8 +375,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   float* bias_s = reinterpret_cast<float*>(v_st + 2 * STAGE);  // [8 warps][BKV], log2 units
   float* xm = bias_s + 8 * BKV;        // [2 teams][BQ] final reference maxima
   float* xl = xm + 2 * BQ;             // [2 teams][BQ] final row sums
-  float* xo = xl + 2 * BQ;             // [2 teams][BQ][XO_PITCH] output halves for the other team
-  float* xvb = xo + 2 * BQ * XO_PITCH; // [8 softmax warps] partial max of the batch's V scales
+  float* xo = xl + 2 * BQ;             // [BQ][OUT_PITCH] team 0's partial rows, then the output tile
+  float* xvb = xo + BQ * OUT_PITCH;    // [8 softmax warps] partial max of the batch's V scales
   uint64_t* bars = reinterpret_cast<uint64_t*>(xvb + 8);
   uint64_t* q_full = bars + 0;   // Q tile of the item loaded (TMA bytes)
   uint64_t* k_full = bars + 1;   // [2]
@@ -392,12 +388,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint64_t* p_full = bars + 15;  // [2] per team: P(t) written, its previous O merged
   uint64_t* qk_done = bars + 17; // QK issuer's MMAs retired (teardown)
   uint64_t* pv_all = bars + 18;  // P.V issuer's MMAs retired (teardown)
-  uint64_t* xbar = bars + 19;    // end-of-row exchange between the teams (8 arrivals)
+  uint64_t* xbar = bars + 19;    // team 0's partial of the item is published (4 arrivals)
   uint64_t* q_empty = bars + 20; // the item's QK MMAs retired: Q shared memory reusable
-  uint64_t* xfree = bars + 21;   // both teams read the exchange buffers (8 arrivals)
-  uint64_t* xread = bars + 22;   // both teams merged: the exchange buffer becomes the output tile
-  uint64_t* xstage = bars + 23;  // the item's output tile is staged (8 arrivals)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
+  uint64_t* xfree = bars + 21;   // team 1 has written the item's tile out (4 arrivals)
+  uint64_t* xstage = bars + 22;  // team 1 has staged the merged tile (4 arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 23);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const uint32_t warp = warp_id();
@@ -417,7 +412,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
-    mbar_init(xfree, 8);
+    mbar_init(xfree, 4);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1);
       mbar_init(&v_full[i], 1); mbar_init(&v_empty[i], 1);
@@ -426,9 +421,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int i = 0; i < NSB; ++i) { mbar_init(&s_full[i], 1); mbar_init(&pv_done[i], 1); }
     mbar_init(qk_done, 1);
     mbar_init(pv_all, 1);
-    mbar_init(xbar, 8);
-    mbar_init(xread, 8);
-    mbar_init(xstage, 8);
+    mbar_init(xbar, 4);
+    mbar_init(xstage, 4);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -694,77 +688,61 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
     }
-    // both teams read the previous item's exchange before it is overwritten
-    if (ok && i >= 1)
-      ok = __all_sync(0xffffffffu, mbar_wait(xfree, (i - 1) & 1, p.status, kDevTimeoutEpilogue, abort_flag));
-    if (ok) {
-      // merge the two teams' partial softmaxes of this row (split-K over the key tiles):
-      // common reference m, factors 2^(m_team - m), exact since both references are
-      // integers (or -inf for a team without tiles)
-      xm[team * BQ + r] = m_run;
-      xl[team * BQ + r] = l_run;
-      float* mine = xo + ((1 - team) * BQ + r) * XO_PITCH;  // the half the other team writes out
-      if (team == 0) {
+    // End of the item.  Team 0 (the even tiles; its last tile's scores come first) publishes
+    // its partial softmax of every row — reference max, sum, all 64 O values — and goes on
+    // to the next item; team 1 merges it with its own (common reference, factors
+    // 2^(m_team - m), exact since both references are integers, or -inf for a team without
+    // tiles), stages the merged 128 x 64 tile in place and writes it out in row order.
+    if (p.ohi) {
 #pragma unroll
-        for (int d = 0; d < 32; d += 4)
-          *reinterpret_cast<float4*>(mine + d) = make_float4(o_acc[32 + d], o_acc[33 + d], o_acc[34 + d], o_acc[35 + d]);
-      } else {
-#pragma unroll
-        for (int d = 0; d < 32; d += 4)
-          *reinterpret_cast<float4*>(mine + d) = make_float4(o_acc[d], o_acc[d + 1], o_acc[d + 2], o_acc[d + 3]);
-      }
-      if (p.ohi) {
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) vb_part = fmaxf(vb_part, __shfl_xor_sync(0xffffffffu, vb_part, o));
-        if (lane == 0) xvb[warp - 4] = vb_part;
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(xbar);
-      ok = __all_sync(0xffffffffu, mbar_wait(xbar, i & 1, p.status, kDevTimeoutEpilogue, abort_flag));
-      float res[32];
-#pragma unroll
-      for (int d = 0; d < 32; ++d) res[d] = 0.0f;
-      if (ok && row_valid) {
-        const float m_o = xm[(1 - team) * BQ + r], l_o = xl[(1 - team) * BQ + r];
-        const float m = fmaxf(m_run, m_o);
-        const float f_me = m_run == m ? 1.0f : ex2(m_run - m);  // 0 for a team with no tiles
-        const float f_o = m_o == m ? 1.0f : ex2(m_o - m);
-        const float f = vref / (l_run * f_me + l_o * f_o);
-        const float* other = xo + (team * BQ + r) * XO_PITCH;  // the other team's half of my dims
-        if (team == 0) {
-#pragma unroll
-          for (int d = 0; d < 32; ++d) res[d] = o_acc[d];
-        } else {
-#pragma unroll
-          for (int d = 0; d < 32; ++d) res[d] = o_acc[32 + d];
-        }
-#pragma unroll
-        for (int d = 0; d < 32; d += 4) {
-          const float4 ov = *reinterpret_cast<const float4*>(other + d);
-          res[d] = (res[d] * f_me + ov.x * f_o) * f;
-          res[d + 1] = (res[d + 1] * f_me + ov.y * f_o) * f;
-          res[d + 2] = (res[d + 2] * f_me + ov.z * f_o) * f;
-          res[d + 3] = (res[d + 3] * f_me + ov.w * f_o) * f;
-        }
-      }
-      // both teams have read the exchange halves: stage the merged row in the same buffer
-      __syncwarp();
-      if (lane == 0) mbar_arrive(xread);
-      ok = ok && __all_sync(0xffffffffu, mbar_wait(xread, i & 1, p.status, kDevTimeoutEpilogue, abort_flag));
-      float* stg = xo;  // [BQ][OUT_PITCH]
+      for (int o = 16; o > 0; o >>= 1) vb_part = fmaxf(vb_part, __shfl_xor_sync(0xffffffffu, vb_part, o));
+    }
+    float* xrow = xo + r * OUT_PITCH;  // team 0's partial of row r, then the merged row
+    if (team == 0) {
+      // team 1 has written out the previous item's tile before the buffer is reused
+      if (ok && i >= 1)
+        ok = __all_sync(0xffffffffu, mbar_wait(xfree, (i - 1) & 1, p.status, kDevTimeoutEpilogue, abort_flag));
       if (ok) {
+        xm[r] = m_run;
+        xl[r] = l_run;
 #pragma unroll
-        for (int d = 0; d < 32; d += 4)
-          *reinterpret_cast<float4*>(stg + r * OUT_PITCH + team * 32 + d) =
-              make_float4(res[d], res[d + 1], res[d + 2], res[d + 3]);
+        for (int d = 0; d < D; d += 4)
+          *reinterpret_cast<float4*>(xrow + d) = make_float4(o_acc[d], o_acc[d + 1], o_acc[d + 2], o_acc[d + 3]);
+        if (p.ohi && lane == 0) xvb[warp - 4] = vb_part;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(xbar);
       }
+    } else {
+      if (p.ohi && lane == 0) xvb[warp - 4] = vb_part;
+      if (ok)
+        ok = __all_sync(0xffffffffu, mbar_wait(xbar, i & 1, p.status, kDevTimeoutEpilogue, abort_flag));
+      if (ok && row_valid) {
+        const float m0 = xm[r], l0 = xl[r];
+        const float m = fmaxf(m_run, m0);
+        const float f1 = m_run == m ? 1.0f : ex2(m_run - m);  // 0 for a team with no tiles
+        const float f0 = m0 == m ? 1.0f : ex2(m0 - m);
+        const float f = vref / (l0 * f0 + l_run * f1);
+        // dimensions 0..31 as team 0's own (o0 f0 + o1 f1), 32..63 as team 1's own
+#pragma unroll
+        for (int d = 0; d < D; d += 4) {
+          const float4 o0 = *reinterpret_cast<const float4*>(xrow + d);
+          const float a[4] = {o0.x, o0.y, o0.z, o0.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            if (d < 32) o_acc[d + e] = (a[e] * f0 + o_acc[d + e] * f1) * f;
+            else o_acc[d + e] = (o_acc[d + e] * f1 + a[e] * f0) * f;
+          }
+          *reinterpret_cast<float4*>(xrow + d) = make_float4(o_acc[d], o_acc[d + 1], o_acc[d + 2], o_acc[d + 3]);
+        }
+      }
+      // team 1's four warps have staged their rows
       __syncwarp();
       if (lane == 0) mbar_arrive(xstage);
       ok = ok && __all_sync(0xffffffffu, mbar_wait(xstage, i & 1, p.status, kDevTimeoutEpilogue, abort_flag));
       if (ok) {
         // the item's output, row by row: 16 threads per row, 4 consecutive values each
         const int b = bh / p.H, hh = bh % p.H;
-        const int tid = (warp - 4) * 32 + lane;
+        const int tid = (warp - 8) * 32 + lane;
         int s = 0;
         float sc = 1.0f;
         if (p.ohi) {
@@ -776,11 +754,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           sc = pow2i(s);
         }
 #pragma unroll 1
-        for (int f4 = tid; f4 < BQ * (D / 4); f4 += 256) {
+        for (int f4 = tid; f4 < BQ * (D / 4); f4 += BQ) {
           const int row = f4 / (D / 4), c = (f4 % (D / 4)) * 4;
           const int qr = q0 + row;
           if (qr >= p.Lq) continue;
-          const float4 v = *reinterpret_cast<const float4*>(stg + row * OUT_PITCH + c);
+          const float4 v = *reinterpret_cast<const float4*>(xo + row * OUT_PITCH + c);
           if (p.ohi) {
             const int64_t off = ((int64_t)b * p.Lq + qr) * ((int64_t)p.H * D) + hh * D + c;
             const float a0 = v.x * sc, a1 = v.y * sc, a2 = v.z * sc, a3 = v.w * sc;
@@ -800,6 +778,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         if (p.ohi && hh == 0 && tid < BQ && q0 + tid < p.Lq) p.ors[(int64_t)b * p.Lq + q0 + tid] = pow2i(-s);
       }
+      // the buffer (and the V-scale shares) may be reused for the next item
       __syncwarp();
       if (lane == 0) mbar_arrive(xfree);
     }
