@@ -54,7 +54,8 @@ uint64_t triposplat_b200_launch_count(void);
 void triposplat_b200_profile_enable(int on);
 /* Waits for the bracketed launches recorded so far and returns, per kernel family
  * (0 GEMM tensor-core, 1 GEMM activation split, 2 GEMM scalar tail, 3 SDPA attention,
- * 4 SDPA split, 5 elementwise; n entries), the launch count and summed device ms. */
+ * 4 SDPA split, 5 elementwise, 6 multi-GPU peer barrier, 7 peer K / V gather and partial
+ * reduction; n entries), the launch count and summed device ms. */
 int triposplat_b200_profile_collect(uint64_t* launches, double* total_ms, int n);
 /* Same; keep != 0 leaves the events registered (a captured CUDA graph records into them on
  * every replay, so each read reflects the latest replay). */

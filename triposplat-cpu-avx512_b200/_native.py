@@ -175,7 +175,8 @@ def require_cuda(*tensors, what: str = "tensor") -> None:
         raise RuntimeError("no CUDA device")
 
 
-KERNEL_FAMILIES = ("gemm_tc", "gemm_split", "gemm_simt", "sdpa_attn", "sdpa_split", "elementwise")
+KERNEL_FAMILIES = ("gemm_tc", "gemm_split", "gemm_simt", "sdpa_attn", "sdpa_split", "elementwise",
+                   "peer_wait", "peer_copy")
 
 
 def profile_collect(lib, keep: bool = False) -> dict:

@@ -167,7 +167,7 @@ int triposplat_b200_peer_barrier(const uint64_t* flag_ptrs, int rank, int world,
   if ((st = entry_check()) != kOk) return st;
   cudaStream_t stream = current_stream();
   {
-    LaunchScope scope(kKElementwise, stream);
+    LaunchScope scope(kKPeerWait, stream);
     peer::peer_barrier_k<<<1, 32, 0, stream>>>(pp, rank, world, counter, device_status());
   }
   return launch_status();
@@ -198,7 +198,7 @@ int triposplat_b200_peer_reduce_residual_f32(const uint64_t* part_ptrs, int worl
   const int64_t want = (n4 + 255) / 256;
   const unsigned grid = (unsigned)(want < (int64_t)sms * 8 ? want : (int64_t)sms * 8);
   {
-    LaunchScope scope(kKElementwise, stream);
+    LaunchScope scope(kKPeerCopy, stream);
     if (mode == 2)
       peer::peer_reduce_residual_k<2><<<grid, 256, 0, stream>>>(pp, world, x, gate, gate_ld,
                                                                rows_per_batch, cols, n4);

@@ -66,7 +66,9 @@ enum KernelId : int {
   kKSdpaAttn = 3,    // sdpa_fwd_tc
   kKSdpaSplit = 4,   // sdpa_split_q + sdpa_split_kv
   kKElementwise = 5, // norms, activations, residuals, sampler updates, post-process
-  kKNum = 6,
+  kKPeerWait = 6,    // peer barrier of the multi-GPU exchanges (its time is mostly waiting)
+  kKPeerCopy = 7,    // peer-memory K / V gather and partial-sum reduction
+  kKNum = 8,
 };
 
 // Wrap one kernel launch: counts it and, while profiling is enabled, brackets it with

@@ -1683,7 +1683,7 @@ int triposplat_b200_kv_planes_gather(const uint64_t* kv_planes_by_rank, const in
   if (st != kOk) return st;
   cudaStream_t stream = current_stream();
   if (world > 1) {
-    LaunchScope scope(kKElementwise, stream);
+    LaunchScope scope(kKPeerCopy, stream);
     kv_gather_k<<<dim3(16, (unsigned)BH, (unsigned)world), 256, 0, stream>>>(
         g, reinterpret_cast<uint8_t*>(kv_planes_by_rank[rank]), rank, Lkt, T);
   }
