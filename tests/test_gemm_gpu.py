@@ -109,6 +109,25 @@ def test_gemm_full_config1_vs_oracle(oracle):
     assert float(np.sqrt(np.mean((y - ref) ** 2))) < 1e-6
 
 
+@pytest.mark.parametrize("K,start,count", [(200, 32, 96), (1024, 0, None), (72, 16, 48)])
+def test_gemm_codes_copy_path_is_the_direct_path_row_for_row(oracle, K, start, count):
+    """From 2048 rows on the drop-in entries first copy the codes of the requested columns
+    into k-contiguous planes (K padded to 16, ragged last 64-k tile, column windows); fewer
+    rows read the [K][N] planes directly.  Both decode to the same operands and issue the
+    same MMAs per row, so the first 1000 rows of a 2304-row call equal a 1000-row call bit
+    for bit, and the whole output stays within the oracle tolerance."""
+    g = torch.Generator().manual_seed(K + start)
+    M, N = 2304, 160
+    x = torch.randn(M, K, generator=g).numpy()
+    c01, q2, sc = _pack(torch.randn(N, K, generator=g) * 0.02)
+    b = (torch.randn(N, generator=g) * 0.01).numpy()
+    big = _run(x, c01, q2, sc, b, start=start, count=count)
+    small = _run(x[:1000], c01, q2, sc, b, start=start, count=count)
+    np.testing.assert_array_equal(big[:1000], small)
+    ref = oracle.gemm_nf24(x, c01, q2, sc, b)
+    _assert_close(big, ref[:, start:start + (count or N)])
+
+
 def test_gemm_error_codes():
     import _native
 
