@@ -93,6 +93,28 @@ def test_mlp_equals_unfused_composition():
     torch.testing.assert_close(y, ref, rtol=1e-6, atol=1e-6)
 
 
+def test_mlp_codes_copy_path_is_the_direct_path_row_for_row():
+    """From 2048 rows the fused MLP copies both weights' codes into k-contiguous planes once
+    per call (the chunked variant once for all chunks); fewer rows read the [K][N] planes.
+    Rows are independent and both paths issue the same MMAs per row, so the first 700 rows
+    of a 2300-row call, plain or chunked, equal a 700-row call bit for bit."""
+    from nf24_linear import nf24_mlp_gelu
+
+    g = torch.Generator().manual_seed(5)
+    M = 2300
+    x = torch.randn(M, 1024, generator=g).cuda()
+    w1, _ = _pack_dev(torch.randn(4096, 1024, generator=g) * 0.02,
+                      (torch.randn(4096, generator=g) * 0.01).numpy())
+    w2, _ = _pack_dev(torch.randn(1024, 4096, generator=g) * 0.02,
+                      (torch.randn(1024, generator=g) * 0.01).numpy())
+    y = nf24_mlp_gelu(x, w1, w2)
+    yc = nf24_mlp_gelu(x, w1, w2, chunk_rows=512)
+    ys = nf24_mlp_gelu(x[:700].contiguous(), w1, w2)
+    torch.cuda.synchronize()
+    assert torch.equal(y, yc)
+    assert torch.equal(y[:700], ys)
+
+
 def test_mlp_status_codes():
     import _native
 
@@ -161,6 +183,37 @@ def test_qkv_direct_equals_unfused_composition():
     rq, rpk, rpv = qkv_rope_rmsnorm_pack(qkv, freqs, qg, kg)
     torch.cuda.synchronize()
     assert torch.equal(q, rq) and torch.equal(pk, rpk) and torch.equal(pv, rpv)
+
+
+def test_qkv_direct_codes_copy_path_is_the_direct_path():
+    """From 2048 token rows (B*L) the fused QKV projection reads a k-contiguous copy of its
+    codes; the result still equals nf24_linear + the v2 post-process bit for bit (the
+    unfused GEMM takes the same copy path), and batch 0's first 500 tokens equal a
+    500-token call (per-token arithmetic, positions 0..499 in both)."""
+    from native_ops import qkv_rope_rmsnorm_pack
+    from nf24_linear import nf24_linear, nf24_qkv_rope_rmsnorm_pack
+
+    g = torch.Generator().manual_seed(11)
+    B, L, H, D, K = 2, 1100, 16, 64, 1024
+    x = torch.randn(B * L, K, generator=g).cuda()
+    w, _ = _pack_dev(torch.randn(3 * H * D, K, generator=g) * 0.02,
+                     (torch.randn(3 * H * D, generator=g) * 0.01).numpy())
+    ang = torch.rand(1, L, H, D // 2, generator=g) * 6.0
+    freqs = torch.stack([torch.cos(ang), torch.sin(ang)], -1).reshape(1, L, H, D).cuda()
+    qg = (1.0 + 0.05 * torch.randn(H, D, generator=g)).cuda()
+    kg = (1.0 + 0.05 * torch.randn(H, D, generator=g)).cuda()
+    q, pk, pv = nf24_qkv_rope_rmsnorm_pack(x, *w, freqs, qg, kg, batch=B, heads=H)
+    qkv = nf24_linear(x, *w).view(B, L, 3, H, D)
+    rq, rpk, rpv = qkv_rope_rmsnorm_pack(qkv, freqs, qg, kg)
+    Ls = 500
+    sq, spk, spv = nf24_qkv_rope_rmsnorm_pack(x[:Ls].contiguous(), *w,
+                                              freqs[:, :Ls].contiguous(), qg, kg, batch=1,
+                                              heads=H)
+    torch.cuda.synchronize()
+    assert torch.equal(q, rq) and torch.equal(pk, rpk) and torch.equal(pv, rpv)
+    assert torch.equal(q[0, :, :Ls], sq[0])
+    assert torch.equal(pk[0, :, :, :Ls], spk[0, :, :, :Ls])
+    assert torch.equal(pv[0, :, :, :Ls], spv[0, :, :, :Ls])
 
 
 def test_qkv_direct_status_codes():

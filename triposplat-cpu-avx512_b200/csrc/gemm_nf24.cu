@@ -1192,7 +1192,7 @@ static int launch_tc(const SplitPlanes& sp, const int16_t* c01, const int8_t* q2
   // per kernel: one bit per device ordinal once its shared-memory attribute is set; SM
   // count per device.  Atomic: host threads on their own streams launch concurrently (a
   // thread that sees a bit unset sets the attribute itself before launching).
-  static std::atomic<uint64_t> attr_done[10];
+  static std::atomic<uint64_t> attr_done[11];
   static std::atomic<int> sm_count[64];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1217,8 +1217,11 @@ static int launch_tc(const SplitPlanes& sp, const int16_t* c01, const int8_t* q2
     kernel<<<grid, NUM_THREADS, smem, stream>>>(m_hi, m_lo, m_c16, m_c8, m_out, prm);
   };
   if (nk && kpp_one) {
-    if (ep.mode != kStore) return kLaunchFailed;
-    run(nf24_gemm_tc<kStore, true, 1>, 9);
+    switch (ep.mode) {
+      case kStore: run(nf24_gemm_tc<kStore, true, 1>, 9); break;
+      case kGelu: run(nf24_gemm_tc<kGelu, true, 1>, 10); break;
+      default: return kLaunchFailed;
+    }
   } else if (nk) {
     switch (ep.mode) {
       case kGelu: run(nf24_gemm_tc<kGelu, true, NK_KPP>, 4 + kGelu); break;
@@ -1240,6 +1243,32 @@ static int launch_tc(const SplitPlanes& sp, const int16_t* c01, const int8_t* q2
 
 // Rows from which the drop-in entry points copy the codes into k-contiguous planes.
 constexpr int kNkMinRows = 2048;
+
+// k-contiguous copy of columns [start, start + count) of a weight's code planes, placed in
+// the workspace by the caller (nk_codes_bytes).
+struct NkCodes {
+  const int16_t* c01 = nullptr;
+  const int8_t* q2 = nullptr;
+  int ldk = 0;
+};
+static int nk_ldk(int K) { return (K + 15) & ~15; }
+static size_t nk_codes_bytes(int K, int count) {
+  const size_t n = (size_t)count * nk_ldk(K);
+  return ((n * 2 + 255) & ~static_cast<size_t>(255)) + ((n + 255) & ~static_cast<size_t>(255));
+}
+static int copy_codes_nk(const int16_t* c01, const int8_t* q2, int K, int N, int start, int count,
+                         uint8_t* dst, cudaStream_t stream, NkCodes& nk) {
+  const int ldk = nk_ldk(K);
+  int16_t* d16 = reinterpret_cast<int16_t*>(dst);
+  int8_t* d8 = reinterpret_cast<int8_t*>(dst + (((size_t)count * ldk * 2 + 255) & ~static_cast<size_t>(255)));
+  LaunchScope scope(kKGemmSplit, stream);
+  nf24_codes_window_to_nk<<<dim3((count + 63) / 64, (K + 63) / 64), 256, 0, stream>>>(
+      c01, q2, K, N, start, count, ldk, d16, d8);
+  nk.c01 = d16;
+  nk.q2 = d8;
+  nk.ldk = ldk;
+  return launch_status();
+}
 
 // Host launcher shared by the full / range / tail entry points.
 static int gemm_launch(const float* x, const int16_t* c01, const int8_t* q2, const float* scale,
@@ -1280,23 +1309,14 @@ static int gemm_launch(const float* x, const int16_t* c01, const int8_t* q2, con
                      device_status(), stream);
   }
   const size_t sx = (split_bytes(M, K) + 255) & ~static_cast<size_t>(255);
-  const int ldk = (K + 15) & ~15;
-  const size_t c16 = ((size_t)count * ldk * 2 + 255) & ~static_cast<size_t>(255);
-  const size_t c8 = (size_t)count * ldk;
-  uint8_t* ws = static_cast<uint8_t*>(workspace(sx + c16 + c8, stream));
+  uint8_t* ws = static_cast<uint8_t*>(workspace(sx + nk_codes_bytes(K, count), stream));
   if (!ws) return kWorkspace;
   const SplitPlanes sp = split_layout(ws, M, K);
-  int16_t* c01_nk = reinterpret_cast<int16_t*>(ws + sx);
-  int8_t* q2_nk = reinterpret_cast<int8_t*>(ws + sx + c16);
+  NkCodes nk;
   if ((st = launch_split(x, stride_x, sp, stream)) != kOk) return st;
-  {
-    LaunchScope scope(kKGemmSplit, stream);
-    nf24_codes_window_to_nk<<<dim3((count + 63) / 64, (K + 63) / 64), 256, 0, stream>>>(
-        c01, q2, K, N, start, count, ldk, c01_nk, q2_nk);
-    if ((st = launch_status()) != kOk) return st;
-  }
-  return launch_tc(sp, c01_nk, q2_nk, scale + start, bias + start, out, count, 0, count,
-                   stride_out, EpilogueArgs(), device_status(), stream, ldk, true);
+  if ((st = copy_codes_nk(c01, q2, K, N, start, count, ws + sx, stream, nk)) != kOk) return st;
+  return launch_tc(sp, nk.c01, nk.q2, scale + start, bias + start, out, count, 0, count,
+                   stride_out, EpilogueArgs(), device_status(), stream, nk.ldk, true);
 }
 
 }  // namespace tsb
@@ -1675,19 +1695,26 @@ constexpr int kMlpIn = 1024, kMlpHidden = 4096, kMlpOut = 1024;  // native_nf24_
 // split planes at split_ws (split_bytes(M, K) bytes) when the code planes and the output
 // allow TMA; otherwise the SIMT kernel (then GELU as a separate pass, which needs a
 // contiguous output).
+static bool linear_rows_tc(const int16_t* c01, const int8_t* q2, const float* out, int N,
+                           int stride_out) {
+  return (N % 16) == 0 && (stride_out % 4) == 0 &&
+         ((reinterpret_cast<uintptr_t>(c01) | reinterpret_cast<uintptr_t>(q2) |
+           reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+}
 static int linear_rows(const float* x, int stride_x, int M, int K, const int16_t* c01,
                        const int8_t* q2, const float* scale, const float* bias, float* out, int N,
-                       int stride_out, bool gelu, uint8_t* split_ws, cudaStream_t stream) {
+                       int stride_out, bool gelu, uint8_t* split_ws, cudaStream_t stream,
+                       const NkCodes* nk = nullptr) {
   using namespace gemm;
-  const bool tc = (N % 16) == 0 && (stride_out % 4) == 0 &&
-                  ((reinterpret_cast<uintptr_t>(c01) | reinterpret_cast<uintptr_t>(q2) |
-                    reinterpret_cast<uintptr_t>(out)) & 15) == 0;
   int st;
-  if (tc) {
+  if (linear_rows_tc(c01, q2, out, N, stride_out)) {
     const SplitPlanes sp = split_layout(split_ws, M, K);
     if ((st = launch_split(x, stride_x, sp, stream)) != kOk) return st;
     EpilogueArgs ep;
     ep.mode = gelu ? kGelu : kStore;
+    if (nk)  // the weight's k-contiguous copy (one k-block per partial: the same bits)
+      return launch_tc(sp, nk->c01, nk->q2, scale, bias, out, N, 0, N, stride_out, ep,
+                       device_status(), stream, nk->ldk, true);
     return launch_tc(sp, c01, q2, scale, bias, out, N, 0, N, stride_out, ep, device_status(),
                      stream);
   }
@@ -1707,12 +1734,40 @@ static int linear_rows(const float* x, int stride_x, int M, int K, const int16_t
 static int mlp_rows(const float* x, int stride_x, int rows, const int16_t* w1c, const int8_t* w1q,
                     const float* w1s, const float* w1b, const int16_t* w2c, const int8_t* w2q,
                     const float* w2s, const float* w2b, float* hidden, float* out, int stride_out,
-                    uint8_t* split_x, uint8_t* split_h, cudaStream_t stream) {
+                    uint8_t* split_x, uint8_t* split_h, cudaStream_t stream,
+                    const NkCodes* nk1 = nullptr, const NkCodes* nk2 = nullptr) {
   int st = linear_rows(x, stride_x, rows, kMlpIn, w1c, w1q, w1s, w1b, hidden, kMlpHidden,
-                       kMlpHidden, true, split_x, stream);
+                       kMlpHidden, true, split_x, stream, nk1);
   if (st != kOk) return st;
   return linear_rows(hidden, kMlpHidden, rows, kMlpHidden, w2c, w2q, w2s, w2b, out, kMlpOut,
-                     stride_out, false, split_h, stream);
+                     stride_out, false, split_h, stream, nk2);
+}
+
+// From kNkMinRows rows on, the MLP's two weights are copied into k-contiguous planes once
+// per call (after `off` bytes of the workspace); nk1 / nk2 stay empty otherwise or where a
+// stage takes the scalar kernel.
+static int mlp_nk_codes(int M, const int16_t* w1c, const int8_t* w1q, const int16_t* w2c,
+                        const int8_t* w2q, const float* hidden, const float* out, int stride_out,
+                        uint8_t* ws, size_t off, cudaStream_t stream, NkCodes& nk1, NkCodes& nk2,
+                        bool& use1, bool& use2) {
+  use1 = use2 = false;
+  if (M < kNkMinRows) return kOk;
+  int st;
+  if (linear_rows_tc(w1c, w1q, hidden, kMlpHidden, kMlpHidden)) {
+    if ((st = copy_codes_nk(w1c, w1q, kMlpIn, kMlpHidden, 0, kMlpHidden, ws + off, stream, nk1)) != kOk)
+      return st;
+    use1 = true;
+  }
+  if (linear_rows_tc(w2c, w2q, out, kMlpOut, stride_out)) {
+    if ((st = copy_codes_nk(w2c, w2q, kMlpHidden, kMlpOut, 0, kMlpOut,
+                            ws + off + nk_codes_bytes(kMlpIn, kMlpHidden), stream, nk2)) != kOk)
+      return st;
+    use2 = true;
+  }
+  return kOk;
+}
+static size_t mlp_nk_bytes(int M) {
+  return M < kNkMinRows ? 0 : nk_codes_bytes(kMlpIn, kMlpHidden) + nk_codes_bytes(kMlpHidden, kMlpOut);
 }
 
 static bool all_device_pointers(const void* const* p, int n) {
@@ -1749,13 +1804,22 @@ int triposplat_mlp_nf24_gelu_f32_avx512(const float* x, const uint8_t* w1_code01
   if (!all_device_pointers(ptrs, 10)) return kNotDevicePointer;
   cudaStream_t stream = current_stream();
   const size_t sx = align256(split_bytes(M, K)), hb = align256((size_t)M * H * 4);
-  uint8_t* ws = static_cast<uint8_t*>(workspace(sx + hb + split_bytes(M, H), stream));
+  const size_t sh = align256(split_bytes(M, H));
+  uint8_t* ws = static_cast<uint8_t*>(workspace(sx + hb + sh + mlp_nk_bytes(M), stream));
   if (!ws) return kWorkspace;
-  return mlp_rows(x, stride_x, M, reinterpret_cast<const int16_t*>(w1_code01_t),
-                  reinterpret_cast<const int8_t*>(w1_code2_t), w1_scales, w1_bias,
-                  reinterpret_cast<const int16_t*>(w2_code01_t),
-                  reinterpret_cast<const int8_t*>(w2_code2_t), w2_scales, w2_bias,
-                  reinterpret_cast<float*>(ws + sx), out, stride_out, ws, ws + sx + hb, stream);
+  const auto* w1c = reinterpret_cast<const int16_t*>(w1_code01_t);
+  const auto* w1q = reinterpret_cast<const int8_t*>(w1_code2_t);
+  const auto* w2c = reinterpret_cast<const int16_t*>(w2_code01_t);
+  const auto* w2q = reinterpret_cast<const int8_t*>(w2_code2_t);
+  float* hidden = reinterpret_cast<float*>(ws + sx);
+  NkCodes nk1, nk2;
+  bool u1, u2;
+  if ((st = mlp_nk_codes(M, w1c, w1q, w2c, w2q, hidden, out, stride_out, ws, sx + hb + sh, stream,
+                         nk1, nk2, u1, u2)) != kOk)
+    return st;
+  return mlp_rows(x, stride_x, M, w1c, w1q, w1_scales, w1_bias, w2c, w2q, w2_scales, w2_bias,
+                  hidden, out, stride_out, ws, ws + sx + hb, stream, u1 ? &nk1 : nullptr,
+                  u2 ? &nk2 : nullptr);
 }
 
 // scripts/native_nf24_mlp_chunked_avx512.c:3-60: the same MLP over chunks of chunk_rows
@@ -1783,17 +1847,24 @@ int triposplat_mlp_nf24_gelu_chunked_f32_avx512(
   if (!all_device_pointers(ptrs, 11)) return kNotDevicePointer;
   cudaStream_t stream = current_stream();
   const int cr = chunk_rows < M ? chunk_rows : M;
-  const size_t sx = align256(split_bytes(cr, K));
-  uint8_t* ws = static_cast<uint8_t*>(workspace(sx + split_bytes(cr, H), stream));
+  const size_t sx = align256(split_bytes(cr, K)), sh = align256(split_bytes(cr, H));
+  // the k-contiguous copies (from kNkMinRows rows in total) serve every chunk
+  uint8_t* ws = static_cast<uint8_t*>(workspace(sx + sh + mlp_nk_bytes(M), stream));
   if (!ws) return kWorkspace;
+  const auto* w1c = reinterpret_cast<const int16_t*>(w1_code01_t);
+  const auto* w1q = reinterpret_cast<const int8_t*>(w1_code2_t);
+  const auto* w2c = reinterpret_cast<const int16_t*>(w2_code01_t);
+  const auto* w2q = reinterpret_cast<const int8_t*>(w2_code2_t);
+  NkCodes nk1, nk2;
+  bool u1, u2;
+  if ((st = mlp_nk_codes(M, w1c, w1q, w2c, w2q, hidden, out, stride_out, ws, sx + sh, stream, nk1,
+                         nk2, u1, u2)) != kOk)
+    return st;
   for (int start = 0; start < M; start += cr) {
     const int rows = start + cr <= M ? cr : M - start;
-    st = mlp_rows(x + (int64_t)start * stride_x, stride_x, rows,
-                  reinterpret_cast<const int16_t*>(w1_code01_t),
-                  reinterpret_cast<const int8_t*>(w1_code2_t), w1_scales, w1_bias,
-                  reinterpret_cast<const int16_t*>(w2_code01_t),
-                  reinterpret_cast<const int8_t*>(w2_code2_t), w2_scales, w2_bias, hidden,
-                  out + (int64_t)start * stride_out, stride_out, ws, ws + sx, stream);
+    st = mlp_rows(x + (int64_t)start * stride_x, stride_x, rows, w1c, w1q, w1_scales, w1_bias,
+                  w2c, w2q, w2_scales, w2_bias, hidden, out + (int64_t)start * stride_out,
+                  stride_out, ws, ws + sx, stream, u1 ? &nk1 : nullptr, u2 ? &nk2 : nullptr);
     if (st != kOk) return st;
   }
   return kOk;
@@ -1834,13 +1905,22 @@ int triposplat_gemm_nf24_qkv_rope_rmsnorm_pack_f32_avx512(
   if (!all_device_pointers(ptrs, 11)) return kNotDevicePointer;
   cudaStream_t stream = current_stream();
   const int M = B * L;
-  const size_t qb = align256((size_t)M * N * 4);
-  uint8_t* ws = static_cast<uint8_t*>(workspace(qb + split_bytes(M, K), stream));
+  const size_t qb = align256((size_t)M * N * 4), sx = align256(split_bytes(M, K));
+  const auto* c01 = reinterpret_cast<const int16_t*>(codes0_t);
+  const auto* q2 = reinterpret_cast<const int8_t*>(codes1_t);
+  float* qkv = nullptr;
+  // from kNkMinRows rows on, the projection reads a k-contiguous copy of its codes
+  // (qkv itself is 256-byte aligned in the workspace, its rows N = 3 * H * 64 floats)
+  const bool use_nk = M >= kNkMinRows &&
+                      ((reinterpret_cast<uintptr_t>(c01) | reinterpret_cast<uintptr_t>(q2)) & 15) == 0;
+  uint8_t* ws = static_cast<uint8_t*>(
+      workspace(qb + sx + (use_nk ? nk_codes_bytes(K, N) : 0), stream));
   if (!ws) return kWorkspace;
-  float* qkv = reinterpret_cast<float*>(ws);
-  st = linear_rows(x, K, M, K, reinterpret_cast<const int16_t*>(codes0_t),
-                   reinterpret_cast<const int8_t*>(codes1_t), scales0, bias, qkv, N, N, false,
-                   ws + qb, stream);
+  qkv = reinterpret_cast<float*>(ws);
+  NkCodes nk;
+  if (use_nk && (st = copy_codes_nk(c01, q2, K, N, 0, N, ws + qb + sx, stream, nk)) != kOk) return st;
+  st = linear_rows(x, K, M, K, c01, q2, scales0, bias, qkv, N, N, false, ws + qb, stream,
+                   use_nk ? &nk : nullptr);
   if (st != kOk) return st;
   return triposplat_qkv_rope_rmsnorm_pack_f32_avx512_v2(qkv, frequencies, q_gamma, k_gamma, q_bhld,
                                                         packed_k, packed_v, B, L, H, D, L_padded,
