@@ -130,9 +130,18 @@ struct Params {
   const float* next_rs;  // kGeluSplit: [Mp] inverse pre-scales 2^-s of the split being written
 };
 
+// GELU(tanh) = 0.5 x (1 + tanh(u)), u = sqrt(2/pi) (x + 0.044715 x^3), evaluated through the
+// identity 0.5 (1 + tanh(u)) = 1 / (1 + e^(-2u)) as x / (1 + 2^t), t = -2 u log2(e): one ex2
+// and one fast division instead of a full tanhf, with no cancellation for either sign of x
+// (relative error a few ulp; 2^t overflowing for x below about -9.7 gives -0 where the
+// exact value is below 1e-36 in magnitude).  The epilogue warps evaluate it for every
+// output of a GELU GEMM while they also promote the next tile's partial sums.
 __device__ __forceinline__ float gelu_tanh(float x) {
-  const float inner = 0.7978845608028654f * (x + 0.044715f * (x * x * x));
-  return 0.5f * x * (1.0f + tanhf(inner));
+  constexpr float kT = -2.0f * 0.7978845608028654f * 1.4426950408889634f;
+  const float t = kT * fmaf(0.044715f * x, x * x, x);
+  float e;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(t));
+  return __fdividef(x, 1.0f + e);
 }
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
