@@ -136,12 +136,34 @@ struct Params {
 // (relative error a few ulp; 2^t overflowing for x below about -9.7 gives -0 where the
 // exact value is below 1e-36 in magnitude).  The epilogue warps evaluate it for every
 // output of a GELU GEMM while they also promote the next tile's partial sums.
-__device__ __forceinline__ float gelu_tanh(float x) {
-  constexpr float kT = -2.0f * 0.7978845608028654f * 1.4426950408889634f;
-  const float t = kT * fmaf(0.044715f * x, x * x, x);
+constexpr float kGeluT = -2.0f * 0.7978845608028654f * 1.4426950408889634f;
+__device__ __forceinline__ float ex2_approx(float t) {
   float e;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(t));
-  return __fdividef(x, 1.0f + e);
+  return e;
+}
+__device__ __forceinline__ float rcp_approx(float d) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d));
+  return r;
+}
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float t = kGeluT * fmaf(0.044715f * x, x * x, x);
+  return x * rcp_approx(1.0f + ex2_approx(t));
+}
+// The same for two values at once (packed fp32x2 multiplies / adds, each lane rounded
+// exactly as gelu_tanh rounds it, so both give the same bits).
+__device__ __forceinline__ float2 gelu_tanh2(float2 x) {
+  uint64_t xv, c, xx, in, t;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(xv) : "f"(x.x), "f"(x.y));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(c) : "l"(xv), "l"(0x3d3727133d372713ull));   // 0.044715 x
+  asm("mul.rn.f32x2 %0, %1, %1;" : "=l"(xx) : "l"(xv));                              // x * x
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(in) : "l"(c), "l"(xx), "l"(xv));
+  const uint64_t kt = (uint64_t)__float_as_uint(kGeluT) | ((uint64_t)__float_as_uint(kGeluT) << 32);
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(t) : "l"(in), "l"(kt));
+  float t0, t1;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(t0), "=f"(t1) : "l"(t));
+  return make_float2(x.x * rcp_approx(1.0f + ex2_approx(t0)), x.y * rcp_approx(1.0f + ex2_approx(t1)));
 }
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
@@ -616,12 +638,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               // lo = rn(a - hi) (the split kernels' arithmetic, with s fixed beforehand)
               __half* hb = reinterpret_cast<__half*>(buf);
 #pragma unroll
-              for (int j = 0; j < OUT_ROWS; ++j) {
+              for (int j = 0; j < OUT_ROWS; j += 2) {  // two rows at a time (packed GELU)
                 const int r = c * OUT_ROWS + j;
-                const float a = gelu_tanh(fmaf(sum[r], sc, bi)) * osw[r];
-                const __half h = __float2half_rn(a);
-                hb[j * 32 + lane] = h;
-                hb[OUT_ROWS * 32 + j * 32 + lane] = __float2half_rn(a - __half2float(h));
+                const float2 g = gelu_tanh2(make_float2(fmaf(sum[r], sc, bi), fmaf(sum[r + 1], sc, bi)));
+                const float2 s2 = *reinterpret_cast<const float2*>(&osw[r]);
+                const float a0 = g.x * s2.x, a1 = g.y * s2.y;
+                const __half2 h = __floats2half2_rn(a0, a1);
+                const float2 hf = __half22float2(h);
+                const __half2 l = __floats2half2_rn(a0 - hf.x, a1 - hf.y);
+                hb[j * 32 + lane] = __low2half(h);
+                hb[(j + 1) * 32 + lane] = __high2half(h);
+                hb[OUT_ROWS * 32 + j * 32 + lane] = __low2half(l);
+                hb[OUT_ROWS * 32 + (j + 1) * 32 + lane] = __high2half(l);
               }
             } else {
 #pragma unroll
