@@ -234,28 +234,6 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
       : "memory");
 }
 
-// The same with the A operand kept in the tensor core's collector buffer for the next MMA
-// (fill), or taken from it (lastuse, after a fill with the same A by the SAME issuing
-// thread with no other MMA of the CTA in between: only for kernels with one MMA issuer).
-__device__ __forceinline__ void mma_f16_ts_fill(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                                uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16.collector::a::fill [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void mma_f16_ts_lastuse(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                                   uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16.collector::a::lastuse [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
 // Arrive on an mbarrier once every previously issued tcgen05 op of this thread completes.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile(

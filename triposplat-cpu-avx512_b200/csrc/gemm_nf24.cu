@@ -457,11 +457,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint64_t dlo = sw128_kmajor_desc(lo + kk * 32);
           const uint32_t a1 = a_col + kk * 8;
           const uint32_t a2 = a_col + 32 + kk * 8;
-          // S.hi + S.lo + T.hi; the dropped T.lo is below 2^-22 of |x w| per product.
-          // S serves two MMAs in a row: kept in the collector buffer (this warp is the
-          // kernel's only MMA issuer), read from tensor memory once.
-          mma_f16_ts_fill(d, a1, dhi, idesc, !first || kk != 0);  // fresh partial per group
-          mma_f16_ts_lastuse(d, a1, dlo, idesc, 1);
+          // S.hi + S.lo + T.hi; the dropped T.lo is below 2^-22 of |x w| per product
+          mma_f16_ts(d, a1, dhi, idesc, !first || kk != 0);  // fresh partial per group
+          mma_f16_ts(d, a1, dlo, idesc, 1);
           mma_f16_ts(d, a2, dhi, idesc, 1);
         }
         mma_commit(&x_empty[x]);
