@@ -2,7 +2,7 @@
 
 Every token row sees the arithmetic of the single-GPU model (same split planes, key tiles,
 query tiles, warps and orders), so the comparison is BITWISE:
-(1) all ranks driven in lockstep by one process on one GPU (2 and 4 ranks, batch 1 and 2),
+(1) all ranks driven in lockstep by one process on one GPU (2 and 4 ranks, batch 1),
     the ranks' velocity rows concatenated against FlowModelB200.forward;
 (2) two processes on two GPUs exchanging key tiles over NVLink peer memory (peer barrier +
     pull-gather kernel), a forward run twice through the alternating plane sets;
@@ -43,7 +43,7 @@ def _assemble(chunks, spec, world):
     return lat, chunks[-1][:, cl:cl + spec.camera_dim].reshape(-1, 1, spec.camera_dim)
 
 
-@pytest.mark.parametrize("world,batch", [(2, 1), (4, 1), (4, 2)])
+@pytest.mark.parametrize("world,batch", [(2, 1), (4, 1)])
 def test_seq_shard_lockstep_one_gpu_bitwise(world, batch):
     from flow_model import FlowModelB200, make_weights
     from seq_shard import SeqShardedFlowModel, run_lockstep
