@@ -65,7 +65,11 @@ int triposplat_b200_profile_collect2(uint64_t* launches, double* total_ms, int n
  * Y[M, N] = X[M, K] . W + bias,  W[k, n] = scale[n] * (256*q01[k, n] + q2[k, n]).
  * For NF24: codes0_t = int16 q01 [K, N]; codes1_t = codes2_t = int8 q2 [K, N];
  * scales0 = scales1 = scales2 = scale [N]; codebook is not read (any non-null pointer);
- * stages must be 3.  X fp32 with row stride stride_x; out fp32 with row stride stride_out. */
+ * stages must be 3.  X fp32 with row stride stride_x; out fp32 with row stride stride_out.
+ * Work space (library-owned, per device and stream): the split activation, and from M = 2048
+ * rows on (the tensor-core path) also a k-contiguous copy of the requested columns' codes,
+ * 3 bytes per weight with K rounded up to 16, written by each call before its GEMM; the
+ * result is the same bit for bit as without the copy. */
 
 /* replaces scripts/gemm_nf24_i16_avx512.c:199-220 */
 int triposplat_gemm_rnf8_avx512(const float* x, const uint8_t* codes0_t, const uint8_t* codes1_t,
